@@ -1,0 +1,257 @@
+"""Per-kernel numerics on the GPU: every C-ABI entry point against a plain
+PyTorch fp32 statement of the same op (the kernels are floating point, so a
+torch fp32 reference is the checker here; model-level parity against the
+oracle lives in test_parity_gpu.py).
+
+Tolerances (rel-L2 unless stated): fp32 kernels <= 1e-5; bf16/fp16 outputs
+<= 1e-2 (one rounding of the output to 8/11 mantissa bits dominates).
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-5, torch.bfloat16: 1e-2, torch.float16: 5e-3}
+
+
+@pytest.fixture(scope="module")
+def L():
+    from torch_helion.b200 import lib
+
+    lib.load()
+    return lib
+
+
+def _dev():
+    return torch.device("cuda:0")
+
+
+# ----------------------------------------------------------------- rows
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("rows,cols", [(1, 8), (37, 768), (1000, 4096), (5, 13)])
+def test_rowstat(L, dtype, rows, cols):
+    torch.manual_seed(0)
+    x = torch.randn(rows, cols, device=_dev()).to(dtype)
+    s = L.rowstat(x)
+    ref = (x.float() ** 2).sum(-1)
+    assert rel_l2(s, ref) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_rmsnorm(L, dtype):
+    torch.manual_seed(0)
+    x = torch.randn(333, 1024, device=_dev()).to(dtype)
+    g = torch.rand(1024, device=_dev()) + 0.5
+    y = L.rmsnorm(x, g, 1e-5)
+    xf = x.float()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * g
+    assert rel_l2(y.float(), ref) < TOL[dtype]
+
+
+# ----------------------------------------------------------------- gemm
+def _gemm_ref(a, w):
+    return a.float() @ w.float().t()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("m,n,k", [(128, 128, 64), (300, 384, 200), (512, 1024, 1024), (64, 136, 72), (1000, 3352, 768)])
+def test_gemm_plain(L, dtype, m, n, k):
+    torch.manual_seed(1)
+    a = torch.randn(m, k, device=_dev()).to(dtype)
+    w = (torch.randn(n, k, device=_dev()) * 0.05).to(dtype)
+    out = torch.empty(m, n, device=_dev(), dtype=dtype)
+    L.gemm(a, w, out)
+    torch.cuda.synchronize()
+    assert L.device_error() == 0
+    assert rel_l2(out.float(), _gemm_ref(a, w)) < TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_gemm_rowscale_residual_sumsq(L, dtype):
+    """RMSNorm row scale from rowstat partials, residual add, and the
+    sum-of-squares partials of the stored output."""
+    torch.manual_seed(2)
+    m, n, k = 257, 512, 256
+    x = torch.randn(m, k, device=_dev()).to(dtype)
+    w = (torch.randn(n, k, device=_dev()) * 0.05).to(dtype)
+    res = torch.randn(m, n, device=_dev()).to(dtype)
+    parts = L.rowstat(x).reshape(m, 1)
+    out = torch.empty(m, n, device=_dev(), dtype=dtype)
+    ss = torch.zeros(m, n // 64, device=_dev())
+    L.gemm(x, w, out, rs_parts=parts, rs_inv_k=1.0 / k, rs_eps=1e-6, residual=res, ss_out=ss)
+    xf = x.float()
+    r = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)
+    ref = (xf @ w.float().t()) * r + res.float()
+    assert rel_l2(out.float(), ref) < TOL[dtype]
+    ss_ref = out.float().pow(2).reshape(m, n // 64, 64).sum(-1)
+    assert rel_l2(ss, ss_ref) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_gemm_softplus_tail(L, dtype):
+    """Mamba in_proj: z | xBC stored in the model dtype, dt = softplus(acc + bias)
+    routed to an fp32 side output."""
+    torch.manual_seed(3)
+    m, k = 200, 192
+    nmain, ntail = 256 + 64, 24
+    n = nmain + ntail
+    x = torch.randn(m, k, device=_dev()).to(dtype)
+    w = (torch.randn(n, k, device=_dev()) * 0.1).to(dtype)
+    bias = torch.randn(ntail, device=_dev())
+    out = torch.empty(m, nmain, device=_dev(), dtype=dtype)
+    dt = torch.empty(m, ntail, device=_dev())
+    L.gemm(x, w, out, act=L.ACT_SOFTPLUS, act_begin=nmain, act_end=n, bias=bias, out2=dt, tail_begin=nmain)
+    acc = _gemm_ref(x, w)
+    assert rel_l2(out.float(), acc[:, :nmain]) < TOL[dtype]
+    assert rel_l2(dt, F.softplus(acc[:, nmain:] + bias)) < (1e-5 if dtype == torch.float32 else 1e-3)
+
+
+def _rope_ref(x, cos, sin, hd, seq):
+    t = x.shape[0]
+    pos = torch.arange(t, device=x.device) % seq
+    c, s = cos[pos], sin[pos]
+    xh = x.reshape(t, -1, hd)
+    rot = torch.cat((-xh[..., hd // 2:], xh[..., : hd // 2]), -1)
+    return (xh * c[:, None, :] + rot * s[:, None, :]).reshape(t, -1)
+
+
+@pytest.mark.parametrize("dtype,hd", [(torch.bfloat16, 128), (torch.bfloat16, 64), (torch.float32, 64)])
+def test_gemm_rope(L, dtype, hd):
+    torch.manual_seed(4)
+    seq, b, k = 96, 3, 256
+    m = seq * b
+    nq, nk, nv = 4 * hd, 2 * hd, 2 * hd
+    n = nq + nk + nv
+    x = torch.randn(m, k, device=_dev()).to(dtype)
+    w = (torch.randn(n, k, device=_dev()) * 0.05).to(dtype)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=_dev()).float() / hd))
+    fr = torch.outer(torch.arange(seq, device=_dev()).float(), inv)
+    emb = torch.cat((fr, fr), -1)
+    cos, sin = emb.cos().contiguous(), emb.sin().contiguous()
+    out = torch.empty(m, n, device=_dev(), dtype=dtype)
+    L.gemm(x, w, out, rope_cos=cos, rope_sin=sin, rope_begin=0, rope_end=nq + nk, rope_head_dim=hd)
+    acc = _gemm_ref(x, w)
+    ref = torch.cat((_rope_ref(acc[:, : nq + nk], cos, sin, hd, seq), acc[:, nq + nk:]), -1)
+    assert rel_l2(out.float(), ref) < TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_gemm_swiglu(L, dtype):
+    torch.manual_seed(5)
+    m, k, f = 300, 256, 384
+    x = torch.randn(m, k, device=_dev()).to(dtype)
+    wg = torch.randn(f, k, device=_dev()) * 0.05
+    wu = torch.randn(f, k, device=_dev()) * 0.05
+    # interleave in blocks of 64: [g0..63 | u0..63 | g64..127 | u64..127 | ...]
+    w = torch.stack((wg.reshape(f // 64, 64, k), wu.reshape(f // 64, 64, k)), 1).reshape(2 * f, k).to(dtype)
+    out = torch.empty(m, f, device=_dev(), dtype=dtype)
+    L.gemm(x, w, out, swiglu=True)
+    xf = x.float()
+    ref = F.silu(xf @ wg.to(dtype).float().t()) * (xf @ wu.to(dtype).float().t())
+    assert rel_l2(out.float(), ref) < TOL[dtype]
+
+
+def test_gemm_rejects_bad_alignment(L):
+    a = torch.randn(64, 100, device=_dev(), dtype=torch.bfloat16)  # lda=100: 200 B rows, not 16-B multiple
+    w = torch.randn(64, 100, device=_dev(), dtype=torch.bfloat16)
+    out = torch.empty(64, 64, device=_dev(), dtype=torch.bfloat16)
+    with pytest.raises(L.B200KernelError, match="aligned"):
+        L.gemm(a, w, out)
+
+
+# ------------------------------------------------------------ attention
+def _attn_ref(q, k, v, b, s, hq, hkv, d, scale, causal):
+    q4 = q.float().reshape(b, s, hq, d).transpose(1, 2)
+    k4 = k.float().reshape(b, s, hkv, d).transpose(1, 2).repeat_interleave(hq // hkv, 1)
+    v4 = v.float().reshape(b, s, hkv, d).transpose(1, 2).repeat_interleave(hq // hkv, 1)
+    sc = (q4 @ k4.transpose(-1, -2)) * scale
+    if causal:
+        sc = sc.masked_fill(torch.triu(torch.ones(s, s, dtype=torch.bool, device=q.device), 1), float("-inf"))
+    return (torch.softmax(sc, -1) @ v4).transpose(1, 2).reshape(b * s, hq * d)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("b,s,hq,hkv,d,causal", [(1, 128, 8, 8, 64, False), (2, 100, 4, 2, 64, True),
+                                                 (2, 256, 8, 2, 128, True), (1, 70, 2, 1, 32, False)])
+def test_attention(L, dtype, b, s, hq, hkv, d, causal):
+    torch.manual_seed(6)
+    t = b * s
+    qkv = torch.randn(t, (hq + 2 * hkv) * d, device=_dev()).to(dtype)
+    q, k, v = qkv[:, : hq * d], qkv[:, hq * d: (hq + hkv) * d], qkv[:, (hq + hkv) * d:]
+    o = torch.empty(t, hq * d, device=_dev(), dtype=dtype)
+    scale = d ** -0.5
+    L.attention(q, k, v, o, batch=b, seq=s, hq=hq, hkv=hkv, head_dim=d, scale=scale, causal=causal)
+    ref = _attn_ref(q, k, v, b, s, hq, hkv, d, scale, causal)
+    assert rel_l2(o.float(), ref) < TOL[dtype]
+
+
+# --------------------------------------------------------------- conv1d
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_conv1d_silu(L, dtype):
+    torch.manual_seed(7)
+    b, s, ch, wd = 3, 150, 1792, 4
+    src = torch.randn(b * s, ch + 64, device=_dev()).to(dtype)
+    x = src[:, 32: 32 + ch]  # strided view, like xBC inside the in_proj output
+    w = torch.randn(ch, wd, device=_dev()) * 0.3
+    y = torch.empty(b * s, ch, device=_dev(), dtype=dtype)
+    L.conv1d(x, w, y, batch=b, seq=s)
+    xt = x.float().reshape(b, s, ch).transpose(1, 2)
+    ref = F.silu(F.conv1d(F.pad(xt, (wd - 1, 0)), w.unsqueeze(1), groups=ch)).transpose(1, 2).reshape(b * s, ch)
+    assert rel_l2(y.float(), ref) < TOL[dtype]
+
+
+# ------------------------------------------------------------------ ssd
+def _ssd_recurrence(x, dt, A, B, C, D, b, s, h, p, g, n):
+    """Direct O(S) recurrence (the definition every SSD form must match)."""
+    xr = x.double().reshape(b, s, h, p)
+    Br = B.double().reshape(b, s, g, n).repeat_interleave(h // g, 2)
+    Cr = C.double().reshape(b, s, g, n).repeat_interleave(h // g, 2)
+    dtr = dt.double().reshape(b, s, h)
+    st = torch.zeros(b, h, p, n, dtype=torch.float64, device=x.device)
+    ys = []
+    for t in range(s):
+        dec = torch.exp(dtr[:, t] * A.double()).reshape(b, h, 1, 1)
+        st = dec * st + (dtr[:, t].reshape(b, h, 1, 1) * xr[:, t].unsqueeze(-1) * Br[:, t].unsqueeze(-2))
+        ys.append((st * Cr[:, t].unsqueeze(-2)).sum(-1) + D.double().reshape(1, h, 1) * xr[:, t])
+    return torch.stack(ys, 1).reshape(b * s, h * p)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("b,s,h,p,g,n,chunk", [(2, 200, 4, 32, 1, 16, 64), (1, 256, 2, 64, 2, 128, 128),
+                                               (1, 300, 3, 16, 3, 32, 256)])
+def test_ssd_matches_recurrence(L, dtype, b, s, h, p, g, n, chunk):
+    torch.manual_seed(8)
+    t = b * s
+    x = torch.randn(t, h * p, device=_dev()).to(dtype)
+    B = torch.randn(t, g * n, device=_dev()).to(dtype)
+    C = torch.randn(t, g * n, device=_dev()).to(dtype)
+    dt = torch.rand(t, h, device=_dev()) * 0.099 + 0.001
+    A = -torch.exp(torch.rand(h, device=_dev()) * math.log(16))
+    D = torch.rand(h, device=_dev())
+    z = torch.randn(t, h * p, device=_dev()).to(dtype)
+    out = torch.empty(t, h * p, device=_dev(), dtype=dtype)
+    gss = torch.empty(t, h, device=_dev())
+    L.ssd(x, dt, A, B, C, out, batch=b, seq=s, heads=h, head_dim=p, ngroups=g, state_dim=n, chunk=chunk, D=D, z=z, gss=gss)
+    y = _ssd_recurrence(x, dt, A, B, C, D, b, s, h, p, g, n)
+    ref = y * F.silu(z.double())
+    assert rel_l2(out.float(), ref) < TOL[dtype]
+    assert rel_l2(gss, out.float().pow(2).reshape(t, h, p).sum(-1)) < 1e-5
+
+
+# ------------------------------------------------------------ embedding
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_embedding(L, dtype):
+    torch.manual_seed(9)
+    table = torch.randn(1000, 256, device=_dev()).to(dtype)
+    ids = torch.randint(0, 1000, (77,), device=_dev())
+    out = torch.empty(77, 256, device=_dev(), dtype=dtype)
+    L.embedding(ids, table, out)
+    assert torch.equal(out, table[ids])

@@ -1,0 +1,92 @@
+// Host-side plumbing shared by every entry point: error strings, the device
+// error word, tensor-map encoding and device queries.
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace th {
+
+static thread_local char t_error[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_error, sizeof(t_error), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_error, sizeof(t_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(TH_ELAUNCH, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return TH_OK;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
+                 uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  std::call_once(g_encode_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode) return fail(TH_ELAUNCH, "cuTensorMapEncodeTiled is not available from the driver");
+  if (!aligned16(base)) return fail(TH_EALIGN, "TMA base address %p is not 16-byte aligned", base);
+  if (row_stride_bytes % 16) return fail(TH_EALIGN, "TMA row stride %llu B is not a multiple of 16", (unsigned long long)row_stride_bytes);
+  CUtensorMapDataType dt = dtype == TH_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                           : dtype == TH_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TH_ELAUNCH, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return TH_OK;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+}  // namespace th
+
+extern "C" const char* th_last_error_string(void) { return th::t_error; }
+
+extern "C" const char* th_version(void) { return "th_b200 0.1.0 (sm_100a)"; }
+
+extern "C" int th_device_error(int* out_code, int clear) {
+  if (!out_code) return th::fail(TH_EINVAL, "th_device_error: out_code is NULL");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return th::fail(TH_ELAUNCH, "th_device_error: %s", cudaGetErrorString(e));
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, th::g_device_error, sizeof(int));
+  if (e != cudaSuccess) return th::fail(TH_ELAUNCH, "th_device_error: %s", cudaGetErrorString(e));
+  *out_code = v;
+  if (clear) {
+    int z = 0;
+    e = cudaMemcpyToSymbol(th::g_device_error, &z, sizeof(int));
+    if (e != cudaSuccess) return th::fail(TH_ELAUNCH, "th_device_error: %s", cudaGetErrorString(e));
+  }
+  return TH_OK;
+}

@@ -1,0 +1,366 @@
+// th_gemm: one reference `gemm` KernelSpec (shared LHS, sibling GEMMs
+// concatenated along N, RMSNorm row-scale fold, fused epilogue) on B200.
+//
+//   bf16 / fp16: tcgen05.mma (kind::f16, M=128, N=BN) with the accumulator
+//                in TMEM.  A 4-6 stage shared-memory ring is filled by TMA
+//                (128-byte swizzle, no multicast); one thread issues TMA,
+//                one thread issues MMAs, tcgen05.commit frees ring slots.
+//   fp32:        FFMA tiles (fp32 models need fp32 accuracy, which the
+//                tensor cores' tf32 mode does not give).
+// Both stage the accumulator tile in shared memory and run the same
+// epilogue (row scale, activation segment, RoPE, SwiGLU, residual, stores,
+// sum-of-squares partials), so the two paths have identical semantics.
+#include "common.cuh"
+
+namespace th {
+
+struct EpiParams {
+  void* d;
+  int64_t ldd;
+  int m, n;  // n = accumulator columns (W rows)
+  const float* rs_parts;
+  int rs_nparts;
+  float rs_inv_k, rs_eps;
+  int act, act_begin, act_end;
+  const float* bias;
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_begin, rope_end, rope_hd, rope_seq;
+  int swiglu;
+  const void* residual;
+  int64_t ld_res;
+  float* out2;
+  int64_t ld_out2;
+  int tail_begin;  // in output columns; >= n_out means none
+  float* ss_out;
+  int64_t ss_ld;
+};
+
+// Accumulator value at (local row rl, local col j) with the row scale.
+__device__ __forceinline__ float acc_at(const float* tile, int ldt, int rl, int j, float rs) {
+  return tile[rl * ldt + j] * rs;
+}
+
+// Run the epilogue of one BM x BN accumulator tile that sits in shared
+// memory (fp32, row stride ldt).  All NT threads of the CTA participate.
+// rscale[BM] is scratch for the per-row scale.
+template <typename T, int NT, int BM, int BN>
+__device__ void epilogue_tile(const float* tile, int ldt, float* rscale, const EpiParams& ep, int m0, int n0) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NW = NT / 32;
+  // 1. per-row scale
+  for (int rl = tid; rl < BM; rl += NT) {
+    float r = 1.0f;
+    int row = m0 + rl;
+    if (ep.rs_parts && row < ep.m) {
+      const float* p = ep.rs_parts + (int64_t)row * ep.rs_nparts;
+      float s = 0.f;
+      for (int i = 0; i < ep.rs_nparts; ++i) s += p[i];
+      r = rsqrtf(s * ep.rs_inv_k + ep.rs_eps);
+    }
+    rscale[rl] = r;
+  }
+  __syncthreads();
+  const int bn_out = ep.swiglu ? BN / 2 : BN;
+  const int n_out = ep.swiglu ? ep.n / 2 : ep.n;
+  const int o0 = ep.swiglu ? n0 / 2 : n0;  // first output column of the tile
+  T* d = reinterpret_cast<T*>(ep.d);
+  const T* res = reinterpret_cast<const T*>(ep.residual);
+  for (int rl = warp; rl < BM; rl += NW) {
+    const int row = m0 + rl;
+    if (row >= ep.m) break;
+    const float rs = rscale[rl];
+    for (int base = 0; base < bn_out; base += 256) {  // warp-uniform trip count (shuffles below)
+      const int ol = base + lane * 8;
+      const int oc = o0 + ol;  // global output column of v[0]
+      float v[8];
+      const bool live = ol < bn_out && oc < n_out;
+      if (live) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int jo = ol + e;
+          float x;
+          if (ep.swiglu) {
+            const int g = jo >> 6, w = jo & 63;
+            x = silu_f(acc_at(tile, ldt, rl, g * 128 + w, rs)) * acc_at(tile, ldt, rl, g * 128 + 64 + w, rs);
+          } else {
+            const int c = oc + e;
+            x = acc_at(tile, ldt, rl, jo, rs);
+            if (ep.act != TH_ACT_NONE && c >= ep.act_begin && c < ep.act_end) {
+              if (ep.bias) x += ep.bias[c - ep.act_begin];
+              x = ep.act == TH_ACT_SILU ? silu_f(x) : softplus_f(x);
+            }
+            if (ep.rope_cos && c >= ep.rope_begin && c < ep.rope_end) {
+              const int hd = ep.rope_hd, half = hd >> 1;
+              const int within = (c - ep.rope_begin) % hd;
+              const int partner = within < half ? jo + half : jo - half;
+              const float pv = acc_at(tile, ldt, rl, partner, rs);
+              const float rot = within < half ? -pv : pv;
+              const int64_t t = (int64_t)(row % ep.rope_seq) * hd + within;
+              x = x * ep.rope_cos[t] + rot * ep.rope_sin[t];
+            }
+          }
+          v[e] = x;
+        }
+      }
+      float ss = 0.f;
+      if (live) {
+        if (oc >= ep.tail_begin) {
+          // fp32 tail (tail_begin is a multiple of 8, so a vector never straddles it)
+          float* o2 = ep.out2 + (int64_t)row * ep.ld_out2 + (oc - ep.tail_begin);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (oc + e < n_out) o2[e] = v[e];
+        } else {
+          if (res) {
+            float r8[8];
+            load8<T>(res + (int64_t)row * ep.ld_res + oc, r8);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] += r8[e];
+          }
+          store8<T>(d + (int64_t)row * ep.ldd + oc, v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float q = round_to<T>(v[e]);
+            ss += q * q;
+          }
+        }
+      }
+      if (ep.ss_out) {
+        // 8 lanes x 8 columns = one 64-column group
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+        if ((lane & 7) == 0 && live && oc < ep.tail_begin) ep.ss_out[(int64_t)row * ep.ss_ld + (oc >> 6)] = ss;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------ tcgen05 path
+template <int BN>
+struct TcCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int LDT = BN + 4;  // staged fp32 tile row stride (16-B steps odd -> no bank conflicts)
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+  static_assert(BM * LDT * 4 <= RING_BYTES, "staged tile must fit in the ring");
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + RING_BYTES + 256 /*barriers*/ + BM * 4;
+};
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(128, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiParams ep,
+                   int K) {
+  using C = TcCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* done = empty + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* rscale = reinterpret_cast<float*>(smem + C::RING_BYTES + 256);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * C::BM;
+  const int nk = (K + C::BK - 1) / C::BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  __syncwarp();
+  if (warp == 0) tmem_alloc(tmem_slot, BN);  // warp-wide .sync.aligned
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % C::STAGES;
+      const uint32_t ph = (kb / C::STAGES) & 1;
+      if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) break;
+      uint8_t* sa = smem + s * C::STAGE_BYTES;
+      mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+      tma_load_2d(sa, &tmA, &full[s], kb * C::BK, m0);
+      tma_load_2d(sa + C::A_BYTES, &tmB, &full[s], kb * C::BK, n0);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer
+    constexpr uint32_t idesc = make_idesc_f16(128, BN, DT<T>::id == TH_BF16 ? 1 : 0, 0, 0);
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % C::STAGES;
+      const uint32_t ph = (kb / C::STAGES) & 1;
+      if (!mbar_wait(&full[s], ph, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+      const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+      for (int k = 0; k < C::BK / 16; ++k) {
+        const uint64_t ad = make_desc_sw128(sa + k * 32, 16, 1024);
+        const uint64_t bd = make_desc_sw128(sb + k * 32, 16, 1024);
+        tc_mma_f16(tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+      }
+      tc_commit(&empty[s]);
+    }
+    tc_commit(done);
+  }
+  __syncwarp();
+  const bool ok = mbar_wait(done, 0, abort_flag);
+  __syncwarp();  // tcgen05.ld below is .sync.aligned
+  tc_fence_after();
+  if (ok && !*abort_flag) {
+    // TMEM -> registers -> staged fp32 tile (the ring is idle now)
+    float* tile = reinterpret_cast<float*>(smem);
+    const int rl = warp * 32 + lane;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
+      float4* dst = reinterpret_cast<float4*>(tile + rl * C::LDT + c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    }
+    tc_fence_before();
+    __syncthreads();
+    epilogue_tile<T, 128, C::BM, BN>(tile, C::LDT, rscale, ep, m0, n0);
+  }
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, BN);
+}
+
+// --------------------------------------------------------------- FFMA path
+constexpr int SM_BM = 32, SM_BN = 128, SM_BK = 16, SM_LDT = SM_BN + 4;
+
+template <typename T>
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A, int64_t lda, const T* __restrict__ W,
+                                                        int64_t ldw, EpiParams ep, int K) {
+  __shared__ float As[SM_BK][SM_BM + 4];
+  __shared__ float Ws[SM_BK][SM_BN + 4];
+  __shared__ float tile[SM_BM * SM_LDT];
+  __shared__ float rscale[SM_BM];
+  const int tid = threadIdx.x, tx = tid & 31, ty = tid >> 5;
+  const int m0 = blockIdx.y * SM_BM, n0 = blockIdx.x * SM_BN;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += SM_BK) {
+    for (int i = tid; i < SM_BM * SM_BK; i += 256) {
+      const int r = i / SM_BK, k = i % SM_BK;
+      const int gr = m0 + r, gk = k0 + k;
+      As[k][r] = (gr < ep.m && gk < K) ? to_f32(A[(int64_t)gr * lda + gk]) : 0.f;
+    }
+    for (int i = tid; i < SM_BN * SM_BK; i += 256) {
+      const int r = i / SM_BK, k = i % SM_BK;
+      const int gr = n0 + r, gk = k0 + k;
+      Ws[k][r] = (gr < ep.n && gk < K) ? to_f32(W[(int64_t)gr * ldw + gk]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < SM_BK; ++k) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[k][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Ws[k][tx + 32 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tile[(ty * 4 + i) * SM_LDT + tx + 32 * j] = acc[i][j];
+  __syncthreads();
+  epilogue_tile<T, 256, SM_BM, SM_BN>(tile, SM_LDT, rscale, ep, m0, n0);
+}
+
+// ------------------------------------------------------------------- host
+template <typename T, int BN>
+static int launch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st) {
+  using C = TcCfg<BN>;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, a->a, a->dtype, (uint64_t)a->k, (uint64_t)a->m, (uint64_t)a->lda * 2, 64, C::BM, true);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, a->w, a->dtype, (uint64_t)a->k, (uint64_t)a->n, (uint64_t)a->ldw * 2, 64, BN, true);
+  if (rc) return rc;
+  static bool attr_set = false;  // idempotent; benign race
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemm_tc_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    attr_set = true;
+  }
+  dim3 grid((unsigned)((a->n + BN - 1) / BN), (unsigned)((a->m + C::BM - 1) / C::BM));
+  gemm_tc_kernel<T, BN><<<grid, 128, C::SMEM_BYTES, st>>>(ta, tb, ep, (int)a->k);
+  return check_launch("th_gemm(tcgen05)");
+}
+
+static bool is_al16(const void* p) { return p == nullptr || aligned16(p); }
+
+}  // namespace th
+
+extern "C" int th_gemm(const th_gemm_args* a, void* stream) {
+  using namespace th;
+  if (!a) return fail(TH_EINVAL, "th_gemm: args is NULL");
+  if (!a->a || !a->w || !a->d) return fail(TH_EINVAL, "th_gemm: a/w/d must be non-NULL");
+  if (a->m <= 0 || a->n <= 0 || a->k <= 0) return fail(TH_EINVAL, "th_gemm: bad shape m=%lld n=%lld k=%lld", (long long)a->m, (long long)a->n, (long long)a->k);
+  if (a->m > INT32_MAX || a->n > INT32_MAX || a->k > INT32_MAX) return fail(TH_EINVAL, "th_gemm: extent exceeds int32");
+  if (a->dtype != TH_F32 && a->dtype != TH_BF16 && a->dtype != TH_F16) return fail(TH_EDTYPE, "th_gemm: unknown dtype %d", a->dtype);
+  if (a->lda < a->k || a->ldw < a->k) return fail(TH_EINVAL, "th_gemm: lda/ldw smaller than k");
+  const int64_t n_out = a->swiglu ? a->n / 2 : a->n;
+  if (a->swiglu && a->n % 128) return fail(TH_EINVAL, "th_gemm: swiglu needs n %% 128 == 0 (64 gate | 64 up blocks)");
+  if (n_out % 8) return fail(TH_EALIGN, "th_gemm: output width %lld must be a multiple of 8", (long long)n_out);
+  const int tail = (a->tail_begin > 0 && a->tail_begin < n_out) ? a->tail_begin : (int)n_out;
+  if (tail % 8) return fail(TH_EALIGN, "th_gemm: tail_begin must be a multiple of 8");
+  if (tail < n_out && !a->out2) return fail(TH_EINVAL, "th_gemm: tail requested without out2");
+  if (a->ldd < tail || a->ldd % 8 || !is_al16(a->d)) return fail(TH_EALIGN, "th_gemm: d must be 16-B aligned with ldd %% 8 == 0 and ldd >= width");
+  if (a->residual && (a->ld_res % 8 || !is_al16(a->residual))) return fail(TH_EALIGN, "th_gemm: residual must be 16-B aligned with ld_res %% 8 == 0");
+  if (a->rope_cos) {
+    const int hd = a->rope_head_dim;
+    if (!a->rope_sin || hd <= 0 || hd % 2 || hd > 128 || a->rope_begin % hd || a->rope_end % hd || a->rope_seq <= 0)
+      return fail(TH_EINVAL, "th_gemm: bad rope segment");
+  }
+  if (a->act != TH_ACT_NONE && a->act != TH_ACT_SILU && a->act != TH_ACT_SOFTPLUS) return fail(TH_EINVAL, "th_gemm: bad act");
+  if (a->rs_parts && a->rs_nparts <= 0) return fail(TH_EINVAL, "th_gemm: rs_nparts must be > 0");
+  if (a->ss_out && a->ss_ld < (n_out + 63) / 64) return fail(TH_EINVAL, "th_gemm: ss_ld too small");
+
+  EpiParams ep;
+  ep.d = a->d; ep.ldd = a->ldd; ep.m = (int)a->m; ep.n = (int)a->n;
+  ep.rs_parts = a->rs_parts; ep.rs_nparts = a->rs_nparts; ep.rs_inv_k = a->rs_inv_k; ep.rs_eps = a->rs_eps;
+  ep.act = a->act; ep.act_begin = a->act_begin; ep.act_end = a->act_end; ep.bias = a->bias;
+  ep.rope_cos = a->rope_cos; ep.rope_sin = a->rope_sin; ep.rope_begin = a->rope_begin; ep.rope_end = a->rope_end;
+  ep.rope_hd = a->rope_head_dim; ep.rope_seq = a->rope_seq;
+  ep.swiglu = a->swiglu; ep.residual = a->residual; ep.ld_res = a->ld_res;
+  ep.out2 = a->out2; ep.ld_out2 = a->ld_out2; ep.tail_begin = tail;
+  ep.ss_out = a->ss_out; ep.ss_ld = a->ss_ld;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+
+  if (a->dtype == TH_F32) {
+    if (a->rope_cos && 128 % a->rope_head_dim) return fail(TH_EINVAL, "th_gemm: rope head_dim must divide 128");
+    dim3 grid((unsigned)((a->n + SM_BN - 1) / SM_BN), (unsigned)((a->m + SM_BM - 1) / SM_BM));
+    gemm_simt_kernel<float><<<grid, 256, 0, st>>>(reinterpret_cast<const float*>(a->a), a->lda,
+                                                  reinterpret_cast<const float*>(a->w), a->ldw, ep, (int)a->k);
+    return check_launch("th_gemm(fp32)");
+  }
+  // tcgen05 path: TMA wants 16-B aligned bases and row strides
+  if (!aligned16(a->a) || !aligned16(a->w) || a->lda % 8 || a->ldw % 8)
+    return fail(TH_EALIGN, "th_gemm: a/w must be 16-B aligned with lda, ldw multiples of 8");
+  const bool wide = a->n >= 256 && (!a->rope_cos || 256 % a->rope_head_dim == 0);
+  if (a->dtype == TH_BF16)
+    return wide ? launch_tc<__nv_bfloat16, 256>(a, ep, st) : launch_tc<__nv_bfloat16, 128>(a, ep, st);
+  return wide ? launch_tc<__half, 256>(a, ep, st) : launch_tc<__half, 128>(a, ep, st);
+}

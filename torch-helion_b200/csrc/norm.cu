@@ -1,0 +1,246 @@
+// Memory-bound row kernels: RMSNorm statistics / standalone RMSNorm,
+// depthwise causal conv1d + activation, embedding gather.
+// One warp per row with 16-byte vector loads; grids sized in multiples of
+// the SM count by the launchers.
+#include "common.cuh"
+
+namespace th {
+
+// ------------------------------------------------------------- rowstat
+template <typename T>
+__global__ void __launch_bounds__(256) rowstat_kernel(const T* __restrict__ x, int64_t ldx, float* __restrict__ out,
+                                                      int64_t rows, int cols) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = wid; r < rows; r += nw) {
+    const T* p = x + r * ldx;
+    float s = 0.f;
+    if ((cols & 7) == 0) {
+      for (int c = lane * 8; c < cols; c += 256) {
+        float v[8];
+        load8<T>(p + c, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s = fmaf(v[e], v[e], s);
+      }
+    } else {
+      for (int c = lane; c < cols; c += 32) {
+        float v = to_f32(p[c]);
+        s = fmaf(v, v, s);
+      }
+    }
+    s = warp_sum(s);
+    if (lane == 0) out[r] = s;
+  }
+}
+
+// ------------------------------------------------------------- rmsnorm
+template <typename T>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, int64_t ldx, const float* __restrict__ g,
+                                                      T* __restrict__ y, int64_t ldy, int64_t rows, int cols, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = wid; r < rows; r += nw) {
+    const T* p = x + r * ldx;
+    T* q = y + r * ldy;
+    float s = 0.f;
+    const bool vec = (cols & 7) == 0;
+    if (vec) {
+      for (int c = lane * 8; c < cols; c += 256) {
+        float v[8];
+        load8<T>(p + c, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s = fmaf(v[e], v[e], s);
+      }
+    } else {
+      for (int c = lane; c < cols; c += 32) {
+        float v = to_f32(p[c]);
+        s = fmaf(v, v, s);
+      }
+    }
+    s = warp_sum(s);
+    const float rs = rsqrtf(s / (float)cols + eps);
+    if (vec) {
+      for (int c = lane * 8; c < cols; c += 256) {
+        float v[8];
+        load8<T>(p + c, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = v[e] * rs * (g ? g[c + e] : 1.f);
+        store8<T>(q + c, v);
+      }
+    } else {
+      for (int c = lane; c < cols; c += 32) q[c] = from_f32<T>(to_f32(p[c]) * rs * (g ? g[c] : 1.f));
+    }
+  }
+}
+
+// ------------------------------------------------------ causal conv1d
+// Tile: 64 tokens x (8 * 32) channels per 256-thread block; each thread owns
+// 8 consecutive channels and walks the tokens, keeping the last width-1
+// inputs in registers (the halo is re-read once per tile).
+constexpr int CONV_TOK = 64;
+template <typename T, int W>
+__global__ void __launch_bounds__(256) conv1d_kernel(const T* __restrict__ x, int64_t ldx, const float* __restrict__ w,
+                                                     const float* __restrict__ bias, T* __restrict__ y, int64_t ldy,
+                                                     int seq, int channels, int act) {
+  const int c0 = (blockIdx.x * 256 + threadIdx.x) * 8;
+  if (c0 >= channels) return;
+  const int b = blockIdx.z;
+  const int s0 = blockIdx.y * CONV_TOK;
+  const int64_t base = (int64_t)b * seq;
+  float wt[8][W], bi[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+#pragma unroll
+    for (int j = 0; j < W; ++j) wt[e][j] = w[(int64_t)(c0 + e) * W + j];
+    bi[e] = bias ? bias[c0 + e] : 0.f;
+  }
+  float hist[W][8];  // hist[j] = input at token s-(W-1)+j
+#pragma unroll
+  for (int j = 0; j < W - 1; ++j) {
+    const int s = s0 - (W - 1) + j;
+    if (s >= 0) load8<T>(x + (base + s) * ldx + c0, hist[j]);
+    else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hist[j][e] = 0.f;
+    }
+  }
+  const int s_end = min(seq, s0 + CONV_TOK);
+  for (int s = s0; s < s_end; ++s) {
+    load8<T>(x + (base + s) * ldx + c0, hist[W - 1]);
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float acc = bi[e];
+#pragma unroll
+      for (int j = 0; j < W; ++j) acc = fmaf(wt[e][j], hist[j][e], acc);
+      o[e] = act == TH_ACT_SILU ? silu_f(acc) : acc;
+    }
+    store8<T>(y + (base + s) * ldy + c0, o);
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hist[j][e] = hist[j + 1][e];
+  }
+}
+
+// ------------------------------------------------------------ embedding
+template <typename T>
+__global__ void __launch_bounds__(256) embedding_kernel(const int64_t* __restrict__ ids, const T* __restrict__ table,
+                                                        int64_t ldt, T* __restrict__ out, int64_t ldo, int64_t tokens,
+                                                        int dim, int64_t vocab) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int64_t nw = (int64_t)gridDim.x * 8;
+  for (int64_t t = wid; t < tokens; t += nw) {
+    int64_t id = ids[t];
+    if (id < 0 || id >= vocab) {
+      if (lane == 0) atomicOr(&g_device_error, TH_DEVERR_BAD_ARG);
+      id = 0;
+    }
+    const T* src = table + id * ldt;
+    T* dst = out + t * ldo;
+    for (int c = lane * 8; c < dim; c += 256) *reinterpret_cast<uint4*>(dst + c) = *reinterpret_cast<const uint4*>(src + c);
+  }
+}
+
+static unsigned row_grid(int64_t rows) {
+  const int64_t per_block = 8;  // warps per 256-thread block
+  int64_t want = (rows + per_block - 1) / per_block;
+  const int64_t cap = (int64_t)sm_count() * 16;
+  return (unsigned)(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+}  // namespace th
+
+extern "C" int th_rowstat(const th_rowstat_args* a, void* stream) {
+  using namespace th;
+  if (!a || !a->x || !a->sumsq) return fail(TH_EINVAL, "th_rowstat: NULL argument");
+  if (a->rows <= 0 || a->cols <= 0 || a->ldx < a->cols || a->cols > INT32_MAX) return fail(TH_EINVAL, "th_rowstat: bad shape");
+  if ((a->cols % 8 == 0) && (!aligned16(a->x) || a->ldx % 8)) return fail(TH_EALIGN, "th_rowstat: x must be 16-B aligned with ldx %% 8 == 0");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned g = row_grid(a->rows);
+  switch (a->dtype) {
+    case TH_F32: rowstat_kernel<float><<<g, 256, 0, st>>>((const float*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols); break;
+    case TH_BF16: rowstat_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols); break;
+    case TH_F16: rowstat_kernel<__half><<<g, 256, 0, st>>>((const __half*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols); break;
+    default: return fail(TH_EDTYPE, "th_rowstat: bad dtype %d", a->dtype);
+  }
+  return check_launch("th_rowstat");
+}
+
+extern "C" int th_rmsnorm(const th_rmsnorm_args* a, void* stream) {
+  using namespace th;
+  if (!a || !a->x || !a->y) return fail(TH_EINVAL, "th_rmsnorm: NULL argument");
+  if (a->rows <= 0 || a->cols <= 0 || a->ldx < a->cols || a->ldy < a->cols || a->cols > INT32_MAX) return fail(TH_EINVAL, "th_rmsnorm: bad shape");
+  if ((a->cols % 8 == 0) && (!aligned16(a->x) || !aligned16(a->y) || a->ldx % 8 || a->ldy % 8))
+    return fail(TH_EALIGN, "th_rmsnorm: x/y must be 16-B aligned with ld %% 8 == 0");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned g = row_grid(a->rows);
+  switch (a->dtype) {
+    case TH_F32: rmsnorm_kernel<float><<<g, 256, 0, st>>>((const float*)a->x, a->ldx, a->gain, (float*)a->y, a->ldy, a->rows, (int)a->cols, a->eps); break;
+    case TH_BF16: rmsnorm_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)a->x, a->ldx, a->gain, (__nv_bfloat16*)a->y, a->ldy, a->rows, (int)a->cols, a->eps); break;
+    case TH_F16: rmsnorm_kernel<__half><<<g, 256, 0, st>>>((const __half*)a->x, a->ldx, a->gain, (__half*)a->y, a->ldy, a->rows, (int)a->cols, a->eps); break;
+    default: return fail(TH_EDTYPE, "th_rmsnorm: bad dtype %d", a->dtype);
+  }
+  return check_launch("th_rmsnorm");
+}
+
+template <typename T, int W>
+static void launch_conv(const th_conv1d_args* a, cudaStream_t st) {
+  dim3 grid((unsigned)((a->channels + 2047) / 2048), (unsigned)((a->seq + th::CONV_TOK - 1) / th::CONV_TOK), (unsigned)a->batch);
+  th::conv1d_kernel<T, W><<<grid, 256, 0, st>>>((const T*)a->x, a->ldx, a->w, a->bias, (T*)a->y, a->ldy, a->seq, a->channels, a->act);
+}
+
+template <typename T>
+static int conv_dispatch(const th_conv1d_args* a, cudaStream_t st) {
+  switch (a->width) {
+    case 2: launch_conv<T, 2>(a, st); break;
+    case 3: launch_conv<T, 3>(a, st); break;
+    case 4: launch_conv<T, 4>(a, st); break;
+    default: return th::fail(TH_EUNSUPPORTED, "th_conv1d: width %d not built (2..4)", a->width);
+  }
+  return th::check_launch("th_conv1d");
+}
+
+extern "C" int th_conv1d(const th_conv1d_args* a, void* stream) {
+  using namespace th;
+  if (!a || !a->x || !a->w || !a->y) return fail(TH_EINVAL, "th_conv1d: NULL argument");
+  if (a->batch <= 0 || a->seq <= 0 || a->channels <= 0) return fail(TH_EINVAL, "th_conv1d: bad shape");
+  if (a->channels % 8 || a->ldx % 8 || a->ldy % 8 || !aligned16(a->x) || !aligned16(a->y) || a->ldx < a->channels || a->ldy < a->channels)
+    return fail(TH_EALIGN, "th_conv1d: channels, ldx, ldy must be multiples of 8 and x/y 16-B aligned");
+  if (a->act != TH_ACT_NONE && a->act != TH_ACT_SILU) return fail(TH_EINVAL, "th_conv1d: act must be none or silu");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (a->dtype) {
+    case TH_F32: return conv_dispatch<float>(a, st);
+    case TH_BF16: return conv_dispatch<__nv_bfloat16>(a, st);
+    case TH_F16: return conv_dispatch<__half>(a, st);
+    default: return fail(TH_EDTYPE, "th_conv1d: bad dtype %d", a->dtype);
+  }
+}
+
+extern "C" int th_embedding(const th_embedding_args* a, void* stream) {
+  using namespace th;
+  if (!a || !a->ids || !a->table || !a->out) return fail(TH_EINVAL, "th_embedding: NULL argument");
+  if (a->tokens <= 0 || a->dim <= 0 || a->vocab <= 0) return fail(TH_EINVAL, "th_embedding: bad shape");
+  const int eb = elem_bytes(a->dtype);
+  if ((a->dim * eb) % 16 || (a->ldt * eb) % 16 || (a->ldo * eb) % 16 || !aligned16(a->table) || !aligned16(a->out))
+    return fail(TH_EALIGN, "th_embedding: rows must be 16-B aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned g = row_grid(a->tokens);
+  // copy as 8-element vectors of the element type
+  switch (a->dtype) {
+    case TH_F32:
+      // fp32 rows: treat each pair of floats as one 8-byte unit is unnecessary; reuse the 2-byte kernel on a
+      // half-typed view with doubled width (a pure byte copy).
+      embedding_kernel<__half><<<g, 256, 0, st>>>(a->ids, (const __half*)a->table, a->ldt * 2, (__half*)a->out, a->ldo * 2, a->tokens, (int)(a->dim * 2), a->vocab);
+      break;
+    case TH_BF16:
+    case TH_F16:
+      embedding_kernel<__half><<<g, 256, 0, st>>>(a->ids, (const __half*)a->table, a->ldt, (__half*)a->out, a->ldo, a->tokens, (int)a->dim, a->vocab);
+      break;
+    default: return fail(TH_EDTYPE, "th_embedding: bad dtype %d", a->dtype);
+  }
+  return check_launch("th_embedding");
+}

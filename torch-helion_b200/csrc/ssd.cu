@@ -1,0 +1,290 @@
+// th_ssd: Mamba-2 chunked state-space-duality scan with fp32 state.
+//
+// Reference algorithm: models/mamba.py:163-223 (`ssd_chunked`) plus the
+// D-skip and gate of the mixer forward (mamba.py:297-327).  Three passes:
+//   1. ssd_state_kernel  per (batch, head, chunk): in-chunk cumsum of dt*A
+//      (written to the workspace) and the chunk's own state contribution
+//      states[p, n] = sum_l x[l,p] dt_l exp(cumA_last - cumA_l) B[l,n].
+//   2. ssd_pass_kernel   per (batch, head): the inter-chunk recurrence,
+//      turning each chunk's contribution into the state *entering* it
+//      (S_in(c) = exp(cumA_last(c-1)) S_in(c-1) + states(c-1)), in place.
+//   3. ssd_scan_kernel   per (batch, head, chunk, 64-row block): the
+//      decay-masked intra-chunk product, the inter-chunk term
+//      exp(cumA_i) C_i . S_in, the D skip, the silu(z) gate and the per-head
+//      sum of squares that the gated RMSNorm consumes.
+// This file is the fp32 CUDA-core implementation (all dtypes); exponents
+// are always <= 0 inside a chunk, so nothing overflows at any length.
+#include "common.cuh"
+
+namespace th {
+
+constexpr int SSD_MAXL = 256;  // chunk length limit
+constexpr int SSD_RB = 64;     // rows per scan block
+
+struct SsdGeom {
+  int batch, seq, heads, hd, groups, ns, chunk, nchunks;
+  int64_t states_elems;  // batch*nchunks*heads*hd*ns
+};
+
+__host__ __device__ inline int64_t ssd_cum_index(const SsdGeom& g, int b, int h, int c, int l) {
+  return (((int64_t)b * g.heads + h) * g.nchunks + c) * g.chunk + l;
+}
+
+// ---------------------------------------------------------------- pass 1
+template <typename T>
+__global__ void __launch_bounds__(256) ssd_state_kernel(th_ssd_args p, SsdGeom g, float* __restrict__ states,
+                                                        float* __restrict__ cum) {
+  extern __shared__ float sm[];
+  float* w = sm;                    // [chunk] weights, then scan scratch
+  float* xs = w + SSD_MAXL;         // [32][hd]
+  float* bs = xs + 32 * g.hd;       // [32][ns]
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  const int hg = h / (g.heads / g.groups);
+  const int s0 = c * g.chunk;
+  const int len = min(g.chunk, g.seq - s0);
+  const int64_t t0 = (int64_t)b * g.seq + s0;
+  const float A = p.A[h];
+  // inclusive scan of dt*A over the chunk (Hillis-Steele in shared memory)
+  float dtv = 0.f, v = 0.f;
+  if (tid < g.chunk) {
+    dtv = tid < len ? p.dt[(t0 + tid) * p.lddt + h] : 0.f;
+    v = dtv * A;
+    w[tid] = v;
+  }
+  __syncthreads();
+  for (int off = 1; off < g.chunk; off <<= 1) {
+    float add = 0.f;
+    if (tid < g.chunk && tid >= off) add = w[tid - off];
+    __syncthreads();
+    if (tid < g.chunk) { v += add; w[tid] = v; }
+    __syncthreads();
+  }
+  const float last = w[len - 1];
+  __syncthreads();
+  if (tid < g.chunk) {
+    cum[ssd_cum_index(g, b, h, c, tid)] = v;
+    w[tid] = tid < len ? dtv * __expf(last - v) : 0.f;
+  }
+  __syncthreads();
+  // states[p, n] = sum_l (x[l,p] w[l]) B[l,n]
+  const int PN = g.hd * g.ns;
+  float acc[64];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+  const T* x = reinterpret_cast<const T*>(p.x);
+  const T* B = reinterpret_cast<const T*>(p.B);
+  for (int l0 = 0; l0 < len; l0 += 32) {
+    for (int i = tid; i < 32 * g.hd; i += 256) {
+      const int l = i / g.hd, pp = i % g.hd;
+      xs[i] = (l0 + l < len) ? to_f32(x[(t0 + l0 + l) * p.ldx + (int64_t)h * g.hd + pp]) * w[l0 + l] : 0.f;
+    }
+    for (int i = tid; i < 32 * g.ns; i += 256) {
+      const int l = i / g.ns, n = i % g.ns;
+      bs[i] = (l0 + l < len) ? to_f32(B[(t0 + l0 + l) * p.ldb + (int64_t)hg * g.ns + n]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const int o = tid + 256 * i;
+      if (o < PN) {
+        const int pp = o / g.ns, n = o % g.ns;
+        float a = acc[i];
+        for (int l = 0; l < 32; ++l) a = fmaf(xs[l * g.hd + pp], bs[l * g.ns + n], a);
+        acc[i] = a;
+      }
+    }
+    __syncthreads();
+  }
+  float* dst = states + (((int64_t)b * g.nchunks + c) * g.heads + h) * PN;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    const int o = tid + 256 * i;
+    if (o < PN) dst[o] = acc[i];
+  }
+}
+
+// ---------------------------------------------------------------- pass 2
+__global__ void __launch_bounds__(256) ssd_pass_kernel(SsdGeom g, float* __restrict__ states, const float* __restrict__ cum) {
+  const int PN = g.hd * g.ns;
+  const int e = blockIdx.x * 256 + threadIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  if (e >= PN) return;
+  float S = 0.f;
+  for (int c = 0; c < g.nchunks; ++c) {
+    const int len = min(g.chunk, g.seq - c * g.chunk);
+    const float decay = __expf(cum[ssd_cum_index(g, b, h, c, len - 1)]);
+    float* ptr = states + (((int64_t)b * g.nchunks + c) * g.heads + h) * PN + e;
+    const float contrib = *ptr;
+    *ptr = S;
+    S = S * decay + contrib;
+  }
+}
+
+// ---------------------------------------------------------------- pass 3
+template <typename T>
+__global__ void __launch_bounds__(256) ssd_scan_kernel(th_ssd_args p, SsdGeom g, const float* __restrict__ states,
+                                                       const float* __restrict__ cum) {
+  extern __shared__ float sm[];
+  float* Cs = sm;                          // [RB][ns]
+  float* Bs = Cs + SSD_RB * g.ns;          // [64][ns]   (later S_in [hd][ns])
+  float* xs = Bs + 64 * g.ns;              // [64][hd]
+  float* Gs = xs + 64 * g.hd;              // [RB][65]
+  float* ci = Gs + SSD_RB * 65;            // [RB] cumA of rows
+  float* cj = ci + SSD_RB;                 // [64] cumA of cols
+  float* dj = cj + 64;                     // [64] dt of cols
+  const int rb_per_chunk = g.chunk / SSD_RB;
+  const int c = blockIdx.x / rb_per_chunk, rb = blockIdx.x % rb_per_chunk;
+  const int h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  const int hg = h / (g.heads / g.groups);
+  const int s0 = c * g.chunk;
+  const int len = min(g.chunk, g.seq - s0);
+  const int i0 = rb * SSD_RB;  // first row (within chunk) of this block
+  if (i0 >= len) return;
+  const int64_t t0 = (int64_t)b * g.seq + s0;
+  const T* x = reinterpret_cast<const T*>(p.x);
+  const T* B = reinterpret_cast<const T*>(p.B);
+  const T* Cm = reinterpret_cast<const T*>(p.C);
+  for (int i = tid; i < SSD_RB * g.ns; i += 256) {
+    const int r = i / g.ns, n = i % g.ns;
+    Cs[i] = (i0 + r < len) ? to_f32(Cm[(t0 + i0 + r) * p.ldc + (int64_t)hg * g.ns + n]) : 0.f;
+  }
+  if (tid < SSD_RB) ci[tid] = (i0 + tid < len) ? cum[ssd_cum_index(g, b, h, c, i0 + tid)] : 0.f;
+  const int r = tid >> 2, sub = tid & 3;
+  const int npp = g.hd / 4;  // columns per thread (hd <= 64 -> <= 16)
+  float y[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) y[j] = 0.f;
+  // intra-chunk: rows i in [i0, i0+RB), columns j in [0, i0+RB)
+  for (int j0 = 0; j0 < i0 + SSD_RB && j0 < len; j0 += 64) {
+    __syncthreads();
+    for (int i = tid; i < 64 * g.ns; i += 256) {
+      const int l = i / g.ns, n = i % g.ns;
+      Bs[i] = (j0 + l < len) ? to_f32(B[(t0 + j0 + l) * p.ldb + (int64_t)hg * g.ns + n]) : 0.f;
+    }
+    for (int i = tid; i < 64 * g.hd; i += 256) {
+      const int l = i / g.hd, pp = i % g.hd;
+      xs[i] = (j0 + l < len) ? to_f32(x[(t0 + j0 + l) * p.ldx + (int64_t)h * g.hd + pp]) : 0.f;
+    }
+    if (tid < 64) {
+      const bool ok = j0 + tid < len;
+      cj[tid] = ok ? cum[ssd_cum_index(g, b, h, c, j0 + tid)] : 0.f;
+      dj[tid] = ok ? p.dt[(t0 + j0 + tid) * p.lddt + h] : 0.f;
+    }
+    __syncthreads();
+    // G[r][j] = (C_r . B_j) exp(cum_r - cum_j) dt_j   for j <= r
+#pragma unroll 4
+    for (int jj = 0; jj < 16; ++jj) {
+      const int jl = sub + 4 * jj;
+      float s = 0.f;
+      for (int n = 0; n < g.ns; ++n) s = fmaf(Cs[r * g.ns + n], Bs[jl * g.ns + n], s);
+      const int gi = i0 + r, gj = j0 + jl;
+      const float val = (gj <= gi && gj < len) ? s * __expf(ci[r] - cj[jl]) * dj[jl] : 0.f;
+      Gs[r * 65 + jl] = val;
+    }
+    __syncthreads();
+    for (int jl = 0; jl < 64; ++jl) {
+      const float gv = Gs[r * 65 + jl];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (j < npp) y[j] = fmaf(gv, xs[jl * g.hd + sub + 4 * j], y[j]);
+    }
+  }
+  // inter-chunk: y += exp(cum_i) * sum_n C[i,n] S_in[p,n]
+  __syncthreads();
+  const float* Sin = states + (((int64_t)b * g.nchunks + c) * g.heads + h) * (int64_t)(g.hd * g.ns);
+  for (int i = tid; i < g.hd * g.ns; i += 256) Bs[i] = Sin[i];
+  __syncthreads();
+  const float ei = __expf(ci[r]);
+  for (int j = 0; j < 16; ++j) {
+    if (j >= npp) break;
+    const int pp = sub + 4 * j;
+    float s = 0.f;
+    for (int n = 0; n < g.ns; ++n) s = fmaf(Cs[r * g.ns + n], Bs[pp * g.ns + n], s);
+    y[j] = fmaf(ei, s, y[j]);
+  }
+  // D skip, gate, store, per-head sum of squares
+  const int gi = i0 + r;
+  const bool row_ok = gi < len;
+  const int64_t t = t0 + gi;
+  const float Dh = p.D ? p.D[h] : 0.f;
+  const T* z = reinterpret_cast<const T*>(p.z);
+  T* out = reinterpret_cast<T*>(p.out);
+  float ss = 0.f;
+  if (row_ok) {
+    for (int j = 0; j < npp; ++j) {
+      const int pp = sub + 4 * j;
+      const int64_t col = (int64_t)h * g.hd + pp;
+      float v = y[j] + Dh * to_f32(x[t * p.ldx + col]);
+      if (z) v *= silu_f(to_f32(z[t * p.ldz + col]));
+      const T q = from_f32<T>(v);
+      out[t * p.ldo + col] = q;
+      const float qf = to_f32(q);
+      ss = fmaf(qf, qf, ss);
+    }
+  }
+  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+  if (p.gss && row_ok && sub == 0) p.gss[t * p.ldgss + h] = ss;
+}
+
+static int ssd_geom(const th_ssd_args* a, SsdGeom* g) {
+  if (a->batch <= 0 || a->seq <= 0 || a->heads <= 0 || a->head_dim <= 0 || a->state_dim <= 0 || a->ngroups <= 0 || a->chunk <= 0)
+    return fail(TH_EINVAL, "th_ssd: bad shape");
+  if (a->heads % a->ngroups) return fail(TH_EINVAL, "th_ssd: heads %% ngroups != 0");
+  if (a->chunk > SSD_MAXL || a->chunk % SSD_RB) return fail(TH_EUNSUPPORTED, "th_ssd: chunk must be a multiple of 64 and <= 256");
+  if (a->head_dim > 64 || a->head_dim % 4) return fail(TH_EUNSUPPORTED, "th_ssd: head_dim must be a multiple of 4 and <= 64");
+  if (a->head_dim * a->state_dim > 64 * 256) return fail(TH_EUNSUPPORTED, "th_ssd: head_dim*state_dim > 16384");
+  if (a->state_dim > 256) return fail(TH_EUNSUPPORTED, "th_ssd: state_dim > 256");
+  g->batch = a->batch; g->seq = a->seq; g->heads = a->heads; g->hd = a->head_dim; g->groups = a->ngroups;
+  g->ns = a->state_dim; g->chunk = a->chunk; g->nchunks = (a->seq + a->chunk - 1) / a->chunk;
+  g->states_elems = (int64_t)g->batch * g->nchunks * g->heads * g->hd * g->ns;
+  return TH_OK;
+}
+
+template <typename T>
+static int ssd_launch(const th_ssd_args* a, const SsdGeom& g, cudaStream_t st) {
+  float* states = reinterpret_cast<float*>(a->workspace);
+  float* cum = states + g.states_elems;
+  const size_t sm1 = sizeof(float) * (SSD_MAXL + 32 * g.hd + 32 * g.ns);
+  const size_t sm3 = sizeof(float) * (SSD_RB * g.ns + 64 * g.ns + 64 * g.hd + SSD_RB * 65 + SSD_RB + 64 + 64);
+  cudaFuncSetAttribute(ssd_state_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
+  cudaFuncSetAttribute(ssd_scan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm3);
+  ssd_state_kernel<T><<<dim3(g.nchunks, g.heads, g.batch), 256, sm1, st>>>(*a, g, states, cum);
+  int rc = check_launch("th_ssd(state)");
+  if (rc) return rc;
+  ssd_pass_kernel<<<dim3((g.hd * g.ns + 255) / 256, g.heads, g.batch), 256, 0, st>>>(g, states, cum);
+  rc = check_launch("th_ssd(pass)");
+  if (rc) return rc;
+  ssd_scan_kernel<T><<<dim3(g.nchunks * (g.chunk / SSD_RB), g.heads, g.batch), 256, sm3, st>>>(*a, g, states, cum);
+  return check_launch("th_ssd(scan)");
+}
+
+}  // namespace th
+
+extern "C" size_t th_ssd_workspace_size(int32_t batch, int32_t seq, int32_t heads, int32_t head_dim, int32_t state_dim,
+                                        int32_t chunk) {
+  if (batch <= 0 || seq <= 0 || heads <= 0 || head_dim <= 0 || state_dim <= 0 || chunk <= 0) return 0;
+  const int64_t nch = (seq + chunk - 1) / chunk;
+  const int64_t states = (int64_t)batch * nch * heads * head_dim * state_dim;
+  const int64_t cum = (int64_t)batch * heads * nch * chunk;
+  return (size_t)(states + cum) * sizeof(float);
+}
+
+extern "C" int th_ssd(const th_ssd_args* a, void* stream) {
+  using namespace th;
+  if (!a || !a->x || !a->dt || !a->A || !a->B || !a->C || !a->out) return fail(TH_EINVAL, "th_ssd: NULL argument");
+  SsdGeom g;
+  int rc = ssd_geom(a, &g);
+  if (rc) return rc;
+  const size_t need = th_ssd_workspace_size(a->batch, a->seq, a->heads, a->head_dim, a->state_dim, a->chunk);
+  if (!a->workspace || a->workspace_bytes < need)
+    return fail(TH_EINVAL, "th_ssd: workspace of %zu bytes needed, %zu given", need, a->workspace_bytes);
+  if (a->gss && a->ldgss < a->heads) return fail(TH_EINVAL, "th_ssd: ldgss < heads");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (a->dtype) {
+    case TH_F32: return ssd_launch<float>(a, g, st);
+    case TH_BF16: return ssd_launch<__nv_bfloat16>(a, g, st);
+    case TH_F16: return ssd_launch<__half>(a, g, st);
+    default: return fail(TH_EDTYPE, "th_ssd: bad dtype %d", a->dtype);
+  }
+}
