@@ -1,0 +1,374 @@
+"""Benchmark: tokens/sec per forward of the compiled model on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2|c4|c3|c1]
+
+Default workload (N=1): BASELINE config C2, one Mamba-2 block in bf16,
+batch 4 x seq 2048, d_model 768 (compile_model -> th_* kernels).  With
+N > 1 (torchrun, one rank per GPU) every rank runs the same per-GPU batch
+on its own sequences: Mamba shards by batch with no communication, so the
+scaling is weak and ``value`` is the sum over ranks.
+
+One JSON line on rank 0:
+  value       tokens/s, inputs resident in HBM, L2 flushed between steps,
+              device time from CUDA events (max over ranks)
+  e2e         the same forward through the public entry with pinned HOST
+              buffers: H2D of the step's input and D2H of its output timed in
+  roofline    the dominant kernel's algorithmic bytes (or flops) per launch /
+              its event-timed duration, against MEASURED_PEAKS.json
+  cpu_baseline the CPU oracle (the reference's eager forward restated in
+              oracle/) timed on this host on a bounded sample
+``--impl reference`` prints the reference arm: that CPU forward alone.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "torch-helion_b200"))
+sys.path.insert(0, str(REPO))
+
+L2_FLUSH_BYTES = 256 << 20
+
+
+def _peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def _workload(name: str, rank: int):
+    from workloads import configs
+
+    if name == "c2":
+        cfg = configs.c2_mamba_block_bf16()
+        desc = "C2 Mamba-2 block bf16: B4 S2048 d768 expand2 headdim64 (24 heads) d_state128 ngroups1 conv4 chunk256"
+    elif name == "c4":
+        cfg = configs.c4_mamba24_bf16(batch=2)
+        desc = "C4 Mamba-2 24-layer backbone bf16 (per-GPU batch 2 of 16) S2048 d1024 vocab 50280 tied"
+    elif name == "c1":
+        cfg = configs.c1_llama_fp32()
+        desc = "C1 Llama block fp32: B1 S128 D512 H8 KV8 d64 F1408 causal"
+    elif name == "c3":
+        cfg = configs.c3_llama8b_bf16(batch=1, seq=4096)
+        desc = "C3 Llama-3-8B-geometry block bf16 (per-GPU batch 1) S4096 D4096 Hq32 Hkv8 F14336 causal"
+    else:
+        raise SystemExit(f"unknown workload {name}")
+    model = configs.build(cfg, seed=0)
+    (x,) = model.example_inputs(seed=1 + rank)
+    return cfg, model, x, desc
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while timing."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = [r for r in self.rows if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]) if rows else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def kernel_work(launch, prog, module) -> dict:
+    """Algorithmic bytes and flops of one launch (what the kernel must move /
+    compute, not what it happens to move)."""
+    from torch_helion.b200.lower import GemmPlan
+
+    name, kind = launch.name, launch.kind
+    spec = next((k for k in prog.kernels if k.name == name), None)
+    eb = 2 if module.dtype != torch.float32 else 4
+    if kind == "rowstat":
+        t = module.views[name[len("rowstat("):-1]]
+        return {"bytes": t.numel() * eb + t.shape[0] * 4, "flops": 2.0 * t.numel()}
+    if spec is None:
+        return {"bytes": 0, "flops": 0}
+    a = spec.attrs
+    if kind == "gemm":
+        T, N, K = spec.grid["rows"], spec.grid["cols"], spec.k_extent
+        out = sum(prog.tensors[o.tensor].numel for o in spec.outputs) * eb
+        extra = sum(prog.tensors[x.tensor].numel * eb for x in spec.args if x.role == "extra")
+        return {"bytes": T * K * eb + N * K * eb + out + extra, "flops": 2.0 * T * N * K}
+    if kind == "ssd":
+        T = a["batch"] * a["seq"]
+        H, P, G, N = a["heads"], a["head_dim"], a["ngroups"], a["state_dim"]
+        per_tok = 2 * H * P * eb + 2 * G * N * eb + 4 * H          # x in, y out, B, C, dt (fp32)
+        per_tok += H * P * eb if a.get("gate") else 0               # z gate read
+        per_tok += 4 * H                                            # gss out
+        L = min(256, a["seq"])
+        flops = T * H * (2 * L * P + 4 * P * N + 2 * L * N / max(1, H // G))
+        return {"bytes": T * per_tok, "flops": flops}
+    if kind == "causal_conv1d":
+        t = prog.tensors[spec.outputs[0].tensor]
+        return {"bytes": 2 * t.numel * eb, "flops": 2.0 * a["width"] * t.numel}
+    if kind == "attention":
+        b, s, h, d = a["batch"], a["seq"], a["heads"], a["head_dim"]
+        return {"bytes": (2 * b * s * h * d + 2 * b * s * a.get("kv_heads", h) * d) * eb,
+                "flops": 4.0 * b * h * s * s * d * (0.5 if a.get("causal") else 1.0)}
+    t = prog.tensors[spec.outputs[0].tensor]
+    return {"bytes": 2 * t.numel * eb, "flops": 3.0 * t.numel}
+
+
+def time_kernels(module, flush, iters: int = 5) -> dict[str, float]:
+    """Average device time of every launch, each timed alone (L2 flushed before)."""
+    out = {}
+    st = torch.cuda.current_stream()
+    for l in module.launches:
+        ts = []
+        for _ in range(iters):
+            flush()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            l.fn()
+            e1.record(st)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        out[l.name] = sum(ts) / len(ts)
+    return out
+
+
+def cpu_baseline(cfg, model, x, budget_s: float = 20.0) -> dict:
+    """The reference's eager forward, as restated in the oracle, on this host."""
+    from oracle import models as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    sd = {k: v.detach() for k, v in model.state_dict().items()}
+    dt = cfg.dtype
+    if hasattr(cfg, "d_state"):
+        xb = x[:1]
+
+        def fwd():
+            return O.mamba_forward(sd, xb, n_layers=cfg.n_layers, d_model=cfg.d_model, expand=cfg.expand,
+                                   headdim=cfg.headdim, d_state=cfg.d_state, ngroups=cfg.ngroups, chunk=cfg.chunk,
+                                   eps=cfg.eps, use_conv=cfg.use_conv, d_conv=cfg.d_conv, mode=cfg.mode,
+                                   embedding=cfg.vocab is not None, lm_head=cfg.tie_lm_head, dtype=dt)
+        tokens = xb.shape[0] * xb.shape[1]
+        sample = f"oracle eager forward ({dt}), batch 1 x seq {xb.shape[1]} of the workload"
+    else:
+        xb = x[:1]
+
+        def fwd():
+            return O.llama_block_forward(sd, xb, heads=cfg.heads, kv_heads=cfg.kv_heads, eps=cfg.eps,
+                                         rope_theta=cfg.rope_theta, causal=cfg.causal, model_dtype=dt, dtype=dt)
+        tokens = xb.shape[0] * xb.shape[1]
+        sample = f"oracle eager forward ({dt}), batch 1 x seq {xb.shape[1]} of the workload"
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        fwd()
+        once = time.perf_counter() - t0
+        reps = max(1, min(20, int(budget_s / max(once, 1e-3))))
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fwd()
+            ts.append(time.perf_counter() - t0)
+    med = statistics.median(ts)
+    return {"value": tokens / med, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{sample}; median of {reps} after 1 warm-up ({med * 1e3:.1f} ms each)"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    metric, unit = "tokens/sec per forward", "tokens/s"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cfg, model, x, desc = _workload(args.workload, 0)
+        torch.set_num_threads(os.cpu_count() or 1)
+        cb = None
+        vals = []
+        for i in range(args.warmup + args.steps):
+            cb = cpu_baseline(cfg, model, x, budget_s=3.0)
+            if i >= args.warmup:
+                vals.append(cb["value"])
+        v = statistics.median(vals)
+        line = {"metric": metric, "value": v, "unit": unit, "impl": "reference", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": str(cfg.dtype).replace("torch.", ""),
+                "data": "synthetic", "config": {"workload": desc, "global_batch": 1, "seq_len": x.shape[1]},
+                "cpu_baseline": {**cb, "value": v}, "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0,
+                                                             "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+
+    from torch_helion import CompileConfig, compile_model
+
+    cfg, model, x, desc = _workload(args.workload, rank)
+    res = compile_model(model, (x,), CompileConfig(run_name=f"bench_{args.workload}_r{rank}", device=str(dev),
+                                                   verify_passes=False, reference_check=False,
+                                                   results_dir=REPO / "results"))
+    mod, prog = res.module, res.program
+    tokens = x.shape[0] * x.shape[1]
+    flushbuf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    flush = lambda: flushbuf.fill_(1.0)
+    xd = x.to(dev)
+    mod.load_inputs([xd])
+    st = torch.cuda.current_stream()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    # ---- device-resident forward
+    for _ in range(max(3, args.warmup)):
+        flush()
+        mod.launch_all()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        for e0, e1 in ev:
+            flush()
+            e0.record(st)
+            mod.launch_all()
+            e1.record(st)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+
+    # ---- end to end through the public entry with pinned host buffers
+    xh = x.pin_memory()
+    out_view = mod.output_views()[0]
+    oh = torch.empty(out_view.shape, dtype=out_view.dtype, pin_memory=True)
+    for _ in range(max(3, args.warmup)):
+        mod.load_inputs([xh])
+        mod.launch_all()
+        oh.copy_(mod.output_views()[0], non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for e0, e1 in ev2:
+        flush()
+        e0.record(st)
+        mod.load_inputs([xh])
+        mod.launch_all()
+        oh.copy_(mod.output_views()[0], non_blocking=True)
+        e1.record(st)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ms_e2e = sum(a.elapsed_time(b) for a, b in ev2) / args.steps
+
+    # ---- per-kernel times and the dominant kernel's roofline
+    ktimes = time_kernels(mod, flush)
+    peaks, peak_src = _peaks()
+    top = max(mod.launches, key=lambda l: ktimes[l.name])
+    work = kernel_work(top, prog, mod)
+    ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    t_top = ktimes[top.name] / 1e3
+    tensor_kind = top.kind == "gemm" and work["flops"] / max(work["bytes"], 1) > ridge and mod.dtype != torch.float32
+    if tensor_kind:
+        achieved, peak, ru, bound = work["flops"] / t_top / 1e12, peaks["bf16_tflops"], "TFLOP/s", "tensor"
+    else:
+        achieved, peak, ru, bound = work["bytes"] / t_top / 1e9, peaks["hbm_gbs"], "GB/s", "hbm"
+    traffic = None
+    tf = REPO / "profiles" / f"traffic_{args.workload}.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(top.kind)
+
+    # ---- aggregate over ranks (max time)
+    t = torch.tensor([ms, ms_e2e], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_e2e = float(t[0]), float(t[1])
+    n = world
+    if rank == 0:
+        cb = None if args.no_cpu_baseline else cpu_baseline(cfg, model, x)
+        line = {
+            "metric": metric, "value": n * tokens / (ms / 1e3), "unit": unit, "n_gpus": n, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[mod.dtype],
+            "data": "synthetic",
+            "config": {"workload": desc, "global_batch": n * x.shape[0], "seq_len": x.shape[1],
+                       "parallelism": f"dp{n} (batch-sharded, no communication)" if n > 1 else "single GPU",
+                       "l2": "flushed between steps (256 MiB write, untimed)", "kernels_per_forward": mod.n_launches},
+            "roofline": {"bound": bound, "kernel": f"{top.name} ({top.kind})", "achieved": achieved, "peak": peak,
+                         "unit": ru, "frac": achieved / peak, "peak_source": peak_src,
+                         "algorithmic_bytes": work["bytes"], "algorithmic_flops": work["flops"],
+                         "launch_ms": ktimes[top.name], "traffic": traffic},
+            "e2e": {"value": n * tokens / (ms_e2e / 1e3), "unit": unit, "ms_per_step": ms_e2e,
+                    "h2d_bytes_per_step": xh.numel() * xh.element_size(),
+                    "d2h_bytes_per_step": oh.numel() * oh.element_size()},
+            "gpu_launches": mod.n_launches * args.steps,
+            "clocks": clocks.summary(),
+            "kernels_ms": ktimes,
+            "cpu_baseline": cb,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

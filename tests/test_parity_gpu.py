@@ -1,0 +1,129 @@
+"""Model-level parity on the GPU: ``compile_model`` -> B200 kernels vs the CPU
+oracle on the same seeded weights and inputs.
+
+Tolerances (rel-L2, from the north-star statement): fp32 models <= 1e-5;
+bf16/fp16 models <= 2e-2 against the oracle evaluated in fp32 on the
+model's (rounded) weights and inputs.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import rel_l2
+from oracle import models as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2, torch.float16: 2e-2}
+
+
+def _compile(model, args, tmp_path, **kw):
+    from torch_helion import CompileConfig, compile_model
+
+    cfg = CompileConfig(run_name="t", results_dir=tmp_path, **kw)
+    return compile_model(model, args, cfg)
+
+
+def _sd(model):
+    return {k: v.detach() for k, v in model.state_dict().items()}
+
+
+def _llama(cfg_kwargs, tmp_path, seed=0):
+    from workloads.llama_block import LlamaBlockConfig, build_llama_block
+
+    cfg = LlamaBlockConfig(**cfg_kwargs)
+    m = build_llama_block(cfg, seed)
+    (x,) = m.example_inputs(seed=1)
+    res = _compile(m, (x,), tmp_path, verify_passes=cfg.tokens <= 4096)
+    out = res.run(x)[0].float().cpu()
+    assert out.shape == x.shape
+    ref = O.llama_block_forward(_sd(m), x, heads=cfg.heads, kv_heads=cfg.kv_heads, eps=cfg.eps,
+                                rope_theta=cfg.rope_theta, causal=cfg.causal, model_dtype=cfg.dtype)
+    return res, out, ref, cfg
+
+
+@pytest.mark.parametrize("kw", [
+    dict(batch=2, seq=32, hidden=64, heads=2, intermediate=128, dtype=torch.float32),
+    dict(batch=2, seq=96, hidden=128, heads=4, kv_heads=2, intermediate=256, causal=True, dtype=torch.float32),
+    dict(batch=2, seq=64, hidden=256, heads=4, kv_heads=1, intermediate=512, causal=True, dtype=torch.bfloat16),
+    dict(batch=2, seq=256, hidden=256, heads=4, intermediate=512, dtype=torch.float16),  # reference defaults
+], ids=["mha_fp32", "gqa_causal_fp32", "mqa_causal_bf16", "reference_default_fp16"])
+def test_llama_block(kw, tmp_path):
+    res, out, ref, cfg = _llama(kw, tmp_path)
+    assert rel_l2(out, ref) < TOL[cfg.dtype], res.program.summary()
+    assert res.reference_check["ok"], res.reference_check
+    kinds = [k.kind for k in res.program.kernels]
+    assert kinds == ["gemm", "attention", "gemm", "gemm", "gemm"]
+
+
+def test_c1_llama_fp32(tmp_path):
+    from workloads import configs
+
+    cfg = configs.c1_llama_fp32()
+    res, out, ref, _ = _llama(cfg.__dict__, tmp_path)
+    assert rel_l2(out, ref) < 1e-5
+
+
+def _mamba(cfg, tmp_path, baseline_a=True, verify=True):
+    from workloads import configs
+    from workloads.mamba import build_mamba_model
+
+    m = configs.build(cfg) if baseline_a else build_mamba_model(cfg)
+    (u,) = m.example_inputs(seed=1)
+    res = _compile(m, (u,), tmp_path, verify_passes=verify)
+    out = res.run(u)[0].float().cpu()
+    ref = O.mamba_forward(_sd(m), u, n_layers=cfg.n_layers, d_model=cfg.d_model, expand=cfg.expand,
+                          headdim=cfg.headdim, d_state=cfg.d_state, ngroups=cfg.ngroups, chunk=cfg.chunk,
+                          eps=cfg.eps, use_conv=cfg.use_conv, d_conv=cfg.d_conv, mode=cfg.mode,
+                          embedding=cfg.vocab is not None, lm_head=cfg.tie_lm_head)
+    return res, out, ref
+
+
+@pytest.mark.parametrize("kw", [
+    dict(batch=2, seq=128, d_model=128, headdim=32, d_state=32, chunk=64, n_layers=2, mode="chunked", ngroups=1,
+         use_conv=True, dtype=torch.float32),
+    dict(batch=2, seq=200, d_model=128, headdim=64, d_state=64, chunk=40, n_layers=1, mode="quadratic",
+         use_conv=False, dtype=torch.float32),
+    dict(batch=2, seq=256, d_model=512, headdim=32, d_state=32, chunk=64, n_layers=2, dtype=torch.float16),
+    dict(batch=2, seq=256, d_model=256, headdim=64, d_state=128, chunk=128, n_layers=2, mode="chunked", ngroups=1,
+         use_conv=True, dtype=torch.bfloat16, vocab=1000, tie_lm_head=True),
+], ids=["chunked_conv_g1_fp32", "quadratic_fp32", "reference_default_fp16", "lm_tied_bf16"])
+def test_mamba(kw, tmp_path):
+    from workloads.mamba import MambaConfig
+
+    cfg = MambaConfig(**kw)
+    res, out, ref = _mamba(cfg, tmp_path, baseline_a=kw.get("mode") == "chunked")
+    assert rel_l2(out, ref) < TOL[cfg.dtype], res.program.summary()
+    assert any(k.kind == "ssd" for k in res.program.kernels)
+
+
+def test_c2_mamba_block_bf16(tmp_path):
+    from workloads import configs
+
+    cfg = configs.c2_mamba_block_bf16()
+    res, out, ref = _mamba(cfg, tmp_path, verify=False)
+    assert rel_l2(out, ref) < 2e-2
+    gold = torch.load(__import__("pathlib").Path(__file__).parent / "golden" / "c2_mamba.pt", weights_only=False)
+    assert rel_l2(out[:, ::97, ::13], gold["y_sel"]) < 2e-2
+    kinds = [k.kind for k in res.program.kernels]
+    assert kinds == ["gemm", "causal_conv1d", "ssd", "gemm", "rmsnorm"], kinds
+
+
+def test_cuda_graph_replay_matches_eager(tmp_path):
+    from workloads.mamba import MambaConfig
+
+    cfg = MambaConfig(batch=2, seq=128, d_model=128, headdim=32, d_state=32, chunk=64, n_layers=2, mode="chunked",
+                      ngroups=1, use_conv=True, dtype=torch.bfloat16)
+    from workloads import configs
+
+    m = configs.build(cfg)
+    (u,) = m.example_inputs(seed=1)
+    res = _compile(m, (u,), tmp_path)
+    eager = res.run(u)[0].clone()
+    res.module.capture_graph()
+    u2 = torch.randn_like(u)
+    res.run(u2)
+    again = res.run(u)[0]
+    assert torch.equal(eager, again)

@@ -97,7 +97,11 @@ __global__ void __launch_bounds__(256) attention_simt_kernel(th_attention_args p
 template <typename T, int D>
 static int launch_attention(const th_attention_args* a, cudaStream_t st) {
   const size_t smem = sizeof(float) * (AT_BQ * (D + 1) + AT_BK * (D + 1) + AT_BK * D + AT_BQ * (AT_BK + 1));
-  cudaFuncSetAttribute(attention_simt_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static bool attr_set = false;  // once per instantiation (keeps it out of CUDA-graph captures)
+  if (!attr_set) {
+    cudaFuncSetAttribute(attention_simt_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr_set = true;
+  }
   dim3 grid((unsigned)((a->seq + AT_BQ - 1) / AT_BQ), (unsigned)a->hq, (unsigned)a->batch);
   attention_simt_kernel<T, D><<<grid, 256, smem, st>>>(*a);
   return check_launch("th_attention");
@@ -106,10 +110,11 @@ static int launch_attention(const th_attention_args* a, cudaStream_t st) {
 template <typename T>
 static int attention_dispatch(const th_attention_args* a, cudaStream_t st) {
   switch (a->head_dim) {
+    case 16: return launch_attention<T, 16>(a, st);
     case 32: return launch_attention<T, 32>(a, st);
     case 64: return launch_attention<T, 64>(a, st);
     case 128: return launch_attention<T, 128>(a, st);
-    default: return fail(TH_EUNSUPPORTED, "th_attention: head_dim %d not built (32/64/128)", a->head_dim);
+    default: return fail(TH_EUNSUPPORTED, "th_attention: head_dim %d not built (16/32/64/128)", a->head_dim);
   }
 }
 

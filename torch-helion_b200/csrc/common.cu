@@ -63,10 +63,14 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, 
 }
 
 int sm_count() {
-  int dev = 0, n = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
+  static int cached = 0;  // every GPU of a node is the same part
+  if (cached == 0) {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached = n > 0 ? n : 148;
+  }
+  return cached;
 }
 
 }  // namespace th

@@ -247,8 +247,9 @@ static int ssd_launch(const th_ssd_args* a, const SsdGeom& g, cudaStream_t st) {
   float* cum = states + g.states_elems;
   const size_t sm1 = sizeof(float) * (SSD_MAXL + 32 * g.hd + 32 * g.ns);
   const size_t sm3 = sizeof(float) * (SSD_RB * g.ns + 64 * g.ns + 64 * g.hd + SSD_RB * 65 + SSD_RB + 64 + 64);
-  cudaFuncSetAttribute(ssd_state_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
-  cudaFuncSetAttribute(ssd_scan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm3);
+  static size_t set1 = 0, set3 = 0;  // raise the limit only when a larger one is needed
+  if (sm1 > set1) { cudaFuncSetAttribute(ssd_state_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1); set1 = sm1; }
+  if (sm3 > set3) { cudaFuncSetAttribute(ssd_scan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm3); set3 = sm3; }
   ssd_state_kernel<T><<<dim3(g.nchunks, g.heads, g.batch), 256, sm1, st>>>(*a, g, states, cum);
   int rc = check_launch("th_ssd(state)");
   if (rc) return rc;

@@ -1,1 +1,9 @@
-"""torch-helion on B200: the torch-helion front end with sm_100a kernels."""
+"""torch-helion on B200: the torch-helion front end (capture, OpGraph,
+optimizer, planner) with hand-written sm_100a kernels as the backend."""
+
+from .config import CompileConfig
+from .pipeline import CompileResult, compile_model
+
+__version__ = "0.1.0.dev0+b200"
+
+__all__ = ["CompileConfig", "CompileResult", "compile_model", "__version__"]

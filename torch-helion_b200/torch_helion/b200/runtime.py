@@ -1,0 +1,338 @@
+"""Execute an OpIR Program on a B200 through the C ABI.
+
+The B200 twin of the reference interpreter (src/torch_helion/codegen/
+interpret.py:54-65, ``run_program``): it walks ``program.kernels`` in order
+and launches each one -- but on the GPU, through ``libth_b200.so``.
+Everything is prepared once in :class:`CompiledProgram`:
+
+* parameters are uploaded in the layout the kernels want (GEMM weights
+  transposed to [N, K] and concatenated per kernel, SwiGLU gate/up
+  interleaved in 64-row blocks, rope/conv/scan constants in fp32);
+* every intermediate gets a device buffer; a GEMM's sibling outputs are
+  column views of one buffer, its fp32 tail (the scan's dt) a second one;
+* the RMSNorm row statistics come from the cheapest producer: the
+  ``ss_out`` partials of the GEMM that wrote the tensor, the scan's
+  per-head ``gss``, or a ``th_rowstat`` launch;
+* each kernel becomes a closure with fixed pointers, so the whole forward
+  can also be captured in one CUDA graph.
+
+There is no CPU fallback: without a CUDA device or the built library this
+raises :class:`~torch_helion.b200.lib.B200KernelError`.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Callable, Sequence
+
+import torch
+
+from ..optimizer.opir import KernelArg, Program
+from . import lib
+from .lower import GemmPlan, MacroPlan, fp32_outputs, lower_gemm, lower_macro
+
+_TORCH_DTYPES = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16, "int64": torch.int64}
+
+
+def _round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+@dataclass
+class KernelLaunch:
+    name: str
+    kind: str
+    fn: Callable[[], None]
+
+
+class CompiledProgram:
+    """A Program bound to device memory on one GPU."""
+
+    def __init__(self, program: Program, params: dict[str, torch.Tensor], device: str | torch.device = "cuda",
+                 tp_rank: int = 0, tp_world: int = 1, allreduce: Callable[[torch.Tensor], None] | None = None) -> None:
+        if not torch.cuda.is_available():
+            raise lib.B200KernelError("CompiledProgram needs a CUDA device (there is no CPU fallback)")
+        lib.load()
+        self.program = program
+        self.device = torch.device(device)
+        self.dtype = _TORCH_DTYPES[program.metadata.get("dtype", "float32")]
+        self.params = params
+        self.views: dict[str, torch.Tensor] = {}
+        self.launches: list[KernelLaunch] = []
+        self._dev_params: dict[tuple, torch.Tensor] = {}
+        self._graph: torch.cuda.CUDAGraph | None = None
+        self._ssd_ws: torch.Tensor | None = None
+        self.tp_rank, self.tp_world, self.allreduce = tp_rank, tp_world, allreduce
+        with torch.cuda.device(self.device):
+            self._build()
+
+    # ------------------------------------------------------------ parameters
+    def _param(self, name: str, kind: str = "raw", dtype: torch.dtype | None = None) -> torch.Tensor:
+        key = (name, kind, dtype)
+        if key not in self._dev_params:
+            v = self.params[name]
+            if kind == "f32vec":
+                v = v.float().reshape(-1)
+            elif kind == "f32":
+                v = v.float()
+            t = v.to(device=self.device, dtype=dtype or v.dtype).contiguous()
+            self._dev_params[key] = t
+        return self._dev_params[key]
+
+    def _gemm_weight(self, plan: GemmPlan, n_main_pad: int, n_tail_pad: int) -> torch.Tensor:
+        """[N_total, K] weight in the column order of the plan (rows padded)."""
+        key = ("gemm_w", tuple(s.rhs for s in plan.segments), n_main_pad, n_tail_pad)
+        if key in self._dev_params:
+            return self._dev_params[key]
+        K = plan.k
+        dt = self.dtype
+        if plan.swiglu is not None:
+            from ..optimizer.param_transforms import swiglu_interleave
+
+            wg = self.params[plan.swiglu[0]].t().float()
+            wu = self.params[plan.swiglu[1]].t().float()
+            w = swiglu_interleave(wg, wu).to(dt)
+        else:
+            main = [self.params[s.rhs].t().float() for s in plan.segments if s.kind != "tail"]
+            tail = [self.params[s.rhs].t().float() for s in plan.segments if s.kind == "tail"]
+            rows = []
+            m = torch.cat(main, 0) if main else torch.zeros(0, K)
+            rows.append(m)
+            if n_main_pad > m.shape[0]:
+                rows.append(torch.zeros(n_main_pad - m.shape[0], K))
+            if tail:
+                t = torch.cat(tail, 0)
+                rows.append(t)
+                if n_tail_pad > t.shape[0]:
+                    rows.append(torch.zeros(n_tail_pad - t.shape[0], K))
+            w = torch.cat(rows, 0).to(dt)
+        w = w.to(self.device).contiguous()
+        self._dev_params[key] = w
+        return w
+
+    # --------------------------------------------------------------- buffers
+    def _empty(self, rows: int, cols: int, dtype: torch.dtype) -> torch.Tensor:
+        return torch.empty(rows, cols, device=self.device, dtype=dtype)
+
+    def _view(self, arg: KernelArg) -> torch.Tensor:
+        if arg.tensor in self.program.params:
+            raise lib.B200KernelError(f"{arg.tensor} is a constant, not an activation")
+        v = self.views[arg.tensor]
+        return v[:, arg.cols[0]:arg.cols[1]] if arg.cols else v
+
+    def _build(self) -> None:
+        prog = self.program
+        T_of = lambda name: prog.tensors[name].shape[0]
+        for name in prog.inputs:
+            t = prog.tensors[name]
+            dt = _TORCH_DTYPES[t.dtype]
+            cols = t.shape[1] if dt == torch.int64 else _round_up(t.shape[1], 8)
+            buf = self._empty(t.shape[0], cols, dt)
+            self.views[name] = buf if dt == torch.int64 else buf[:, : t.shape[1]]
+        f32 = fp32_outputs(prog)
+        plans = {}
+        for spec in prog.kernels:
+            plans[spec.name] = lower_gemm(spec, prog.tensors, f32) if spec.kind == "gemm" else lower_macro(spec, prog.tensors)
+        # who computes the row statistics of each GEMM LHS
+        need_ss = {next(a.tensor for a in s.args if a.role == "lhs") for s in prog.kernels if s.kind == "gemm" and s.sumsq}
+        self._ss_parts: dict[str, torch.Tensor] = {}
+        ss_by_producer: dict[str, str] = {}
+        for tname in need_ss:
+            prod = prog.producer(tname)
+            if prod is None:
+                continue
+            p = plans[prod.name]
+            if isinstance(p, GemmPlan) and p.outputs.get(tname, (None,))[0] == "main" and p.outputs[tname][1] == 0 \
+                    and p.outputs[tname][2] == p.n_main and not self._allreduced(prod):
+                ss_by_producer[tname] = prod.name
+            elif isinstance(p, MacroPlan) and p.kind == "ssd" and p.attrs.get("gate"):
+                ss_by_producer[tname] = prod.name
+        for spec in prog.kernels:
+            p = plans[spec.name]
+            if isinstance(p, GemmPlan):
+                self._add_gemm(spec.name, spec, p, need_ss, ss_by_producer)
+            else:
+                self._add_macro(spec.name, p, need_ss, ss_by_producer)
+        self.outputs = list(prog.outputs)
+
+    def _allreduced(self, spec) -> bool:
+        return self.tp_world > 1 and spec.attrs.get("tp_allreduce", False)
+
+    def _row_parts(self, tname: str, ss_by_producer: dict[str, str]) -> torch.Tensor:
+        """fp32 [T, nparts] whose row sums are sum(x^2) of tensor ``tname``."""
+        if tname in self._ss_parts:
+            return self._ss_parts[tname]
+        # no producer writes it: a th_rowstat launch right before the consumer
+        x = self.views[tname]
+        parts = self._empty(x.shape[0], 1, torch.float32)
+        self.launches.append(KernelLaunch(f"rowstat({tname})", "rowstat", lambda x=x, parts=parts: lib.rowstat(x, parts.view(-1))))
+        self._ss_parts[tname] = parts
+        return parts
+
+    def _add_gemm(self, kname: str, spec, p: GemmPlan, need_ss, ss_by_producer) -> None:
+        T = p.rows
+        n_main_pad = _round_up(p.n_main, 8)
+        n_tail = p.n_tail
+        n_tail_pad = _round_up(n_tail, 8) if n_tail else 0
+        W = self._gemm_weight(p, n_main_pad, n_tail_pad)
+        out = self._empty(T, max(n_main_pad, 8), self.dtype)
+        tail = self._empty(T, n_tail_pad, torch.float32) if n_tail else None
+        for tname, (where, c0, c1) in p.outputs.items():
+            self.views[tname] = (out if where == "main" else tail)[:, c0:c1]
+        lhs = self._view(p.lhs)
+        kw: dict = {}
+        if p.rowscale is not None:
+            kw.update(rs_parts=self._row_parts(p.lhs.tensor, ss_by_producer), rs_inv_k=p.rowscale[0], rs_eps=p.rowscale[1])
+        # activation segment (acc column space == output column space without SwiGLU)
+        col = 0
+        for s in p.segments:
+            if s.kind == "act":
+                kw.update(act=lib.ACT_SILU if p.act == "silu" else lib.ACT_SOFTPLUS, act_begin=col, act_end=col + s.width)
+            if s.kind != "tail":
+                col += s.width
+        if n_tail:
+            act_code = lib.ACT_SILU if p.act == "silu" else lib.ACT_SOFTPLUS
+            kw.update(act=act_code, act_begin=n_main_pad, act_end=n_main_pad + n_tail, out2=tail, tail_begin=n_main_pad)
+        if p.bias is not None:
+            kw["bias"] = self._param(p.bias, "f32vec", torch.float32)
+        if p.rope is not None:
+            r0 = sum(s.width for s in p.segments if s.kind == "rope")
+            kw.update(rope_cos=self._param(p.rope[0], "f32", torch.float32),
+                      rope_sin=self._param(p.rope[1], "f32", torch.float32), rope_begin=0, rope_end=r0,
+                      rope_head_dim=p.rope[2])
+        if p.swiglu is not None:
+            kw["swiglu"] = True
+        if p.residual is not None:
+            kw["residual"] = self._view(p.residual)
+        # row statistics for a consumer, from this kernel's epilogue
+        for tname, prod in ss_by_producer.items():
+            if prod == kname:
+                parts = self._empty(T, (n_main_pad + 63) // 64, torch.float32)
+                self._ss_parts[tname] = parts
+                kw["ss_out"] = parts
+        d = out if n_tail == 0 else out[:, :n_main_pad]
+        self.launches.append(KernelLaunch(kname, "gemm", lambda lhs=lhs, W=W, d=d, kw=kw: lib.gemm(lhs, W, d, **kw)))
+        if self._allreduced(spec):
+            buf = out[:, :p.n_main]
+            self.launches.append(KernelLaunch(f"allreduce({kname})", "nccl", lambda buf=buf: self.allreduce(buf)))
+
+    def _add_macro(self, kname: str, p: MacroPlan, need_ss, ss_by_producer) -> None:
+        prog = self.program
+        a = p.attrs
+        out_t = prog.tensors[p.output]
+        T, C = out_t.shape
+        out = self._empty(T, _round_up(C, 8), self.dtype)[:, :C]
+        self.views[p.output] = out
+        A = p.args
+        if p.kind == "attention":
+            q, k, v = self._view(A["q"]), self._view(A["k"]), self._view(A["v"])
+            fn = lambda: lib.attention(q, k, v, out, batch=a["batch"], seq=a["seq"], hq=a["heads"],
+                                       hkv=a.get("kv_heads", a["heads"]), head_dim=a["head_dim"], scale=a["scale"],
+                                       causal=bool(a.get("causal")))
+        elif p.kind == "causal_conv1d":
+            x = self._view(A["x"])
+            w = self._param(A["w"].tensor, "f32", torch.float32)
+            act = lib.ACT_SILU if a.get("act") == "silu" else lib.ACT_NONE
+            fn = lambda: lib.conv1d(x, w, out, batch=a["batch"], seq=a["seq"], act=act)
+        elif p.kind == "rmsnorm":
+            x = self._view(A["x"])
+            gain = self._param(A["gain"].tensor, "f32vec", torch.float32)
+            fn = lambda: lib.rmsnorm(x, gain, a["eps"], out=out)
+        elif p.kind == "embedding":
+            ids = self.views[A["ids"].tensor].reshape(-1)
+            table = self._param(A["table"].tensor, "raw", self.dtype)
+            fn = lambda: lib.embedding(ids, table, out)
+        elif p.kind == "ssd":
+            x, dt, B, C_ = self._view(A["x"]), self._view(A["dt"]), self._view(A["B"]), self._view(A["C"])
+            if dt.dtype != torch.float32:
+                raise lib.B200KernelError(f"{kname}: dt must be fp32")
+            Av = self._param(A["A"].tensor, "f32vec", torch.float32)
+            Dv = self._param(A["D"].tensor, "f32vec", torch.float32) if "D" in A else None
+            z = self._view(A["z"]) if "z" in A else None
+            chunk = 256 if a["seq"] >= 256 else _round_up(a["seq"], 64)
+            need = lib.ssd_workspace_size(a["batch"], a["seq"], a["heads"], a["head_dim"], a["state_dim"], chunk)
+            if self._ssd_ws is None or self._ssd_ws.numel() < need:
+                self._ssd_ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+            ws = self._ssd_ws
+            gss = None
+            if ss_by_producer.get(p.output) == kname:
+                gss = self._empty(T, a["heads"], torch.float32)
+                self._ss_parts[p.output] = gss
+            fn = lambda: lib.ssd(x, dt, Av, B, C_, out, batch=a["batch"], seq=a["seq"], heads=a["heads"],
+                                 head_dim=a["head_dim"], ngroups=a["ngroups"], state_dim=a["state_dim"], chunk=chunk,
+                                 D=Dv, z=z, gss=gss, workspace=ws)
+        else:
+            raise lib.B200KernelError(f"{kname}: unknown kind {p.kind}")
+        self.launches.append(KernelLaunch(kname, p.kind, fn))
+
+    # ------------------------------------------------------------------ run
+    def load_inputs(self, inputs: Sequence[torch.Tensor]) -> None:
+        if len(inputs) != len(self.program.inputs):
+            raise ValueError(f"expected {len(self.program.inputs)} inputs, got {len(inputs)}")
+        for name, x in zip(self.program.inputs, inputs):
+            dst = self.views[name]
+            src = x.reshape(dst.shape) if dst.dim() == 1 else x.reshape(dst.shape[0], -1)
+            dst.copy_(src, non_blocking=True)
+
+    def launch_all(self) -> None:
+        if self._graph is not None:
+            self._graph.replay()
+            return
+        for l in self.launches:
+            l.fn()
+
+    def output_views(self) -> list[torch.Tensor]:
+        shapes = self.program.metadata.get("output_shapes", {})
+        outs = []
+        for o in self.outputs:
+            v = self.views[o]
+            outs.append(v.reshape(shapes[o]) if o in shapes and v.is_contiguous() else
+                        (v.contiguous().reshape(shapes[o]) if o in shapes else v))
+        return outs
+
+    def __call__(self, *inputs: torch.Tensor) -> list[torch.Tensor]:
+        with torch.cuda.device(self.device):
+            self.load_inputs(inputs)
+            self.launch_all()
+            return self.output_views()
+
+    def capture_graph(self) -> None:
+        """Record every launch of the forward into one CUDA graph (after one
+        eager run, so one-time host set-up stays out of the capture)."""
+        with torch.cuda.device(self.device):
+            for l in self.launches:
+                l.fn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for l in self.launches:
+                    l.fn()
+            self._graph = g
+
+    @property
+    def n_launches(self) -> int:
+        return sum(1 for l in self.launches if l.kind != "nccl")
+
+    def launch_names(self) -> list[str]:
+        return [l.name for l in self.launches]
+
+
+def run_program(program: Program, params: dict[str, torch.Tensor], inputs, device="cuda") -> dict[str, torch.Tensor]:
+    """Reference-shaped entry (interpret.py:54-65): run all kernels, return
+    the produced tensors by name (device tensors)."""
+    cp = CompiledProgram(program, params, device)
+    if isinstance(inputs, dict):
+        inputs = [inputs[n] for n in program.inputs]
+    cp(*inputs)
+    return dict(cp.views)
+
+
+def program_outputs(program: Program, params: dict[str, torch.Tensor], inputs, device="cuda") -> list[torch.Tensor]:
+    cp = CompiledProgram(program, params, device)
+    if isinstance(inputs, dict):
+        inputs = [inputs[n] for n in program.inputs]
+    return [o.clone() for o in cp(*inputs)]
+
+
+__all__ = ["CompiledProgram", "KernelLaunch", "run_program", "program_outputs", "math"]

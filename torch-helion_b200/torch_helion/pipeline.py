@@ -1,0 +1,236 @@
+"""End-to-end pipeline: PyTorch model -> OpGraph -> OpIR -> sm_100a kernels.
+
+::
+
+    from torch_helion import compile_model, CompileConfig
+    res = compile_model(model, example_args, CompileConfig(run_name="llama_block"))
+    out = res.run(*inputs)            # forward on the B200
+    print(res.program.summary())
+
+The stages and their artefacts follow the reference pipeline
+(src/torch_helion/pipeline.py:60-145): capture, canonicalise (numerically
+verified pass by pass), plan (partition + cost model), codegen artefacts,
+a reference check against the eager model, cost reports, timings.  The
+B200 backend replaces Helion/Loom emission and validation with a device
+program (:class:`torch_helion.b200.runtime.CompiledProgram`) built from the
+hand-written kernels, and adds an optional device-timed measurement.
+"""
+
+from __future__ import annotations
+
+import copy
+import logging
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any, Sequence
+
+import torch
+
+from .capture import CapturedFx, OpGraph, capture
+from .codegen.emit import emit_program
+from .config import CompileConfig
+from .cost_models.b200 import B200Spec
+from .optimizer.evaluate import max_rel_err, rel_l2
+from .optimizer.opir import Program
+from .optimizer.passes import canonicalize
+from .optimizer.planner import PlanResult, plan
+from .results import ResultsWriter
+
+log = logging.getLogger("torch_helion")
+
+
+@dataclass
+class CompileResult:
+    config: CompileConfig
+    run_dir: Path
+    fx: CapturedFx
+    raw_graph: OpGraph
+    graph: OpGraph
+    hw: B200Spec
+    plan: PlanResult
+    program: Program
+    kernel_files: dict[str, Path]
+    validation: dict[str, Any] = field(default_factory=dict)
+    reference_check: dict[str, Any] = field(default_factory=dict)
+    loom_results: dict[str, Any] = field(default_factory=dict)
+    timings: dict[str, float] = field(default_factory=dict)
+    module: Any = None
+    measured: dict[str, Any] = field(default_factory=dict)
+
+    @property
+    def estimated_us(self) -> float:
+        return self.program.metadata.get("plan", {}).get("total_us", float("nan"))
+
+    @property
+    def estimated_cycles(self) -> float:
+        """Reference name; the B200 model estimates microseconds."""
+        return self.estimated_us
+
+    def run(self, *inputs: torch.Tensor) -> list[torch.Tensor]:
+        """Run the compiled forward on the GPU (inputs on CPU or GPU); returns device tensors."""
+        if self.module is None:
+            from .b200.runtime import CompiledProgram
+
+            self.module = CompiledProgram(self.program, self.graph.params, self.config.device)
+        return self.module(*inputs)
+
+
+def _stage(timings: dict[str, float], name: str):
+    class _T:
+        def __enter__(self):
+            self.t = time.time()
+            log.info("stage %s", name)
+
+        def __exit__(self, *a):
+            timings[name] = time.time() - self.t
+
+    return _T()
+
+
+def compile_model(model: torch.nn.Module, example_args: Sequence[Any], config: CompileConfig | None = None) -> CompileResult:
+    config = config or CompileConfig()
+    if config.backend != "b200":
+        raise ValueError(f"unknown backend {config.backend!r} (this package implements 'b200')")
+    rw = ResultsWriter(config.run_dir)
+    timings: dict[str, float] = {}
+
+    with _stage(timings, "capture"):
+        fx, raw = capture(model, example_args)
+        rw.write_text("00_model.txt", f"{model!r}\n\nconfig: {config!r}\n")
+        rw.write_text("01_fx_graph.txt", fx.text())
+        rw.write_json("01_fx_op_histogram.json", fx.op_histogram())
+        raw.to_json(rw.path("02_opgraph_raw.json"))
+        rw.write_text("02_opgraph_raw.txt", raw.summary())
+
+    with _stage(timings, "canonicalize"):
+        graph, pass_log = canonicalize(raw, verify_inputs=list(example_args) if config.verify_passes else None)
+        graph.to_json(rw.path("03_opgraph_canonical.json"))
+        rw.write_text("03_opgraph_canonical.txt", graph.summary())
+        rw.write_json("03_pass_log.json", pass_log)
+
+    with _stage(timings, "plan"):
+        hw = B200Spec.load(config.hw_spec)
+        rw.write_json("04_hw_spec.json", hw.summary())
+        result = plan(graph, hw, config, name=config.run_name)
+        program = result.program
+        rw.write_json("05_plan/candidates.json", [c.to_dict() for c in result.candidates])
+        rw.write_text("05_plan/plan.md", plan_report(result, hw, config))
+        program.to_json(rw.path("06_opir.json"))
+        rw.write_text("06_opir.txt", program.summary())
+
+    with _stage(timings, "codegen"):
+        kernel_files = emit_program(program, config, rw.path("kernels"))
+        rw.write_json("07_launch_plan.json", {k: str(v) for k, v in kernel_files.items()})
+        if config.save_params:
+            torch.save({n: graph.params[n] for n in program.params}, rw.path("params.pt"))
+
+    res = CompileResult(config, rw.run_dir, fx, raw, graph, hw, result, program, kernel_files, timings=timings)
+
+    if config.execute:
+        from .b200.runtime import CompiledProgram
+
+        with _stage(timings, "build_device_program"):
+            res.module = CompiledProgram(program, graph.params, config.device)
+            if config.cuda_graph:
+                res.module.capture_graph()
+        if config.reference_check:
+            with _stage(timings, "reference_check"):
+                res.reference_check = reference_check(model, example_args, res, config.tolerance)
+                rw.write_json("08_reference_check.json", res.reference_check)
+        if config.measure_iters > 0:
+            with _stage(timings, "measure"):
+                res.measured = measure(res, example_args, config.measure_iters)
+                rw.write_json("10_measured.json", res.measured)
+
+    rw.write_json("09_cost_report.json", cost_report_json(program, hw, config))
+    rw.write_text("09_cost_report.md", cost_report_md(program, hw, config, res.measured))
+    rw.write_json("timings.json", timings)
+    return res
+
+
+def reference_check(model, example_args, res: CompileResult, tolerance: float) -> dict[str, Any]:
+    """B200 output vs the eager model.  For low-precision models the primary
+    comparison is the eager forward in fp32 on the model's (rounded)
+    weights; the eager low-precision forward is recorded beside it."""
+    outs = [o.float().cpu() for o in res.run(*example_args)]
+    with torch.no_grad():
+        ref = model(*example_args)
+        refs = ref if isinstance(ref, (list, tuple)) else [ref]
+        low = any(r.dtype in (torch.bfloat16, torch.float16) for r in refs)
+        if low:
+            m32 = copy.deepcopy(model).float()
+            args32 = [a.float() if torch.is_tensor(a) and a.is_floating_point() else a for a in example_args]
+            r32 = m32(*args32)
+            r32 = r32 if isinstance(r32, (list, tuple)) else [r32]
+        else:
+            r32 = refs
+    e32 = [max_rel_err(o.reshape(-1), r.float().reshape(-1)) for o, r in zip(outs, r32)]
+    l2 = [rel_l2(o.reshape(-1), r.float().reshape(-1)) for o, r in zip(outs, r32)]
+    d = {"max_rel_err": max(e32), "per_output": e32, "rel_l2": l2, "tolerance": tolerance, "ok": max(e32) <= tolerance,
+         "oracle": "eager fp32 on the model's weights" if low else "eager model"}
+    if low:
+        d["vs_eager_model_dtype"] = [max_rel_err(o.reshape(-1), r.float().reshape(-1)) for o, r in zip(outs, refs)]
+    return d
+
+
+def measure(res: CompileResult, example_args, iters: int) -> dict[str, Any]:
+    mod = res.module
+    dev_args = [a.to(res.config.device) for a in example_args]
+    for _ in range(3):
+        mod(*dev_args)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        mod(*dev_args)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / iters
+    tokens = res.program.tensors[res.program.inputs[0]].shape[0]
+    return {"ms_per_forward": ms, "tokens": tokens, "tokens_per_s": tokens / (ms / 1e3), "iters": iters,
+            "kernels": mod.n_launches, "cuda_graph": mod._graph is not None}
+
+
+# ---------------------------------------------------------------- reports
+def plan_report(result: PlanResult, hw: B200Spec, config: CompileConfig) -> str:
+    lines = [f"# Partition plan ({config.run_name})", "",
+             f"Hardware: {hw.name} ({hw.source} peaks): {hw.sm_count} SMs, HBM {hw.hbm_gbs:,.0f} GB/s, "
+             f"bf16 {hw.bf16_tflops:,.0f} TFLOP/s",
+             f"Candidates: {len(result.candidates)} (legal: {sum(c.legal for c in result.candidates)}), planner mode: "
+             f"{config.planner_mode}", "", "| # | kernels | est. us | legal | note |", "|---|---|---|---|---|"]
+    for c in sorted(result.candidates, key=lambda c: (not c.legal, c.total_us)):
+        note = c.error or "; ".join(c.violations[:2]) or ("best" if c is result.best else "")
+        est = f"{c.total_us:,.1f}" if c.legal else "-"
+        lines.append(f"| {c.index} | {len(c.program.kernels) if c.program else '-'} | {est} | {'yes' if c.legal else 'no'} | {note} |")
+    lines += ["", "## Chosen program", "", "```", result.program.summary(), "```"]
+    return "\n".join(lines)
+
+
+def cost_report_json(program: Program, hw: B200Spec, config: CompileConfig) -> dict[str, Any]:
+    kernels = [{"name": k.name, "kind": k.kind, "tiles": k.tiles, "us": k.cost.get("us"),
+                "breakdown": k.cost.get("breakdown", {})} for k in program.kernels]
+    inter = program.intermediates()
+    link = {t: program.tensors[t].nbytes for t in inter}
+    return {"hw": hw.summary(), "kernel_launch_overhead_us": config.kernel_launch_overhead_us, "kernels": kernels,
+            "total_us": program.metadata.get("plan", {}).get("total_us"), "intermediate_tensors": link,
+            "intermediate_bytes": sum(link.values())}
+
+
+def cost_report_md(program: Program, hw: B200Spec, config: CompileConfig, measured: dict | None = None) -> str:
+    total = program.metadata.get("plan", {}).get("total_us", 0.0)
+    lines = [f"# Cost report ({program.name})", "",
+             f"B200 roofline model ({hw.source} peaks): estimated forward **{total:,.1f} us** incl. "
+             f"{config.kernel_launch_overhead_us} us per launch.", ""]
+    if measured:
+        lines += [f"Measured on the device: **{measured['ms_per_forward'] * 1e3:,.1f} us** per forward "
+                  f"({measured['tokens_per_s']:,.0f} tokens/s).", ""]
+    lines += ["| kernel | kind | tiles | est. us | bound | flops | bytes |", "|---|---|---|---|---|---|---|"]
+    for k in program.kernels:
+        b = k.cost.get("breakdown", {})
+        lines.append(f"| {k.name} | {k.kind} | {k.tiles} | {k.cost.get('us', 0):,.2f} | {b.get('bound', '-')} | "
+                     f"{b.get('flops', 0):.3g} | {b.get('bytes', 0):.3g} |")
+    inter = program.intermediates()
+    lines += ["", f"Kernel-to-kernel links: {len(inter)} tensors, "
+                  f"{sum(program.tensors[t].nbytes for t in inter):,} bytes through HBM."]
+    return "\n".join(lines) + "\n"
