@@ -208,6 +208,24 @@ size_t th_ssd_workspace_size(int32_t batch, int32_t seq, int32_t heads, int32_t 
                              int32_t state_dim, int32_t chunk);
 int th_ssd(const th_ssd_args* a, void* stream);
 
+/* th_ssd_noalloc -- no counterpart in the reference.
+ * The same scan as th_ssd for callers that cannot allocate device memory
+ * where they call it (a host framework that keeps all device memory in its
+ * own pool and forbids libraries from calling the CUDA allocator, a caller
+ * that cannot afford the synchronisation a cudaFree implies, a plugin given
+ * only input and output pointers).  `workspace`/`workspace_bytes` are
+ * ignored: the chunk-state scratch is a file-scope device array of
+ * TH_SSD_NOALLOC_MAX_BYTES that every GPU loading the library keeps until
+ * exit; shapes needing more (see th_ssd_workspace_size) are rejected with
+ * TH_EINVAL.  Inputs and outputs are still the caller's.  The first call on
+ * a device looks up the array's device address with that device current
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the one array and it keeps the previous call's contents
+ * (nothing in it needs to start at zero), so calls whose work overlaps on
+ * the GPU -- concurrent streams, or threads sharing a device -- race. */
+#define TH_SSD_NOALLOC_MAX_BYTES (32u << 20)
+int th_ssd_noalloc(const th_ssd_args* a, void* stream);
+
 /* -------------------------------------------------------------- embedding
  * out[t, :] = table[ids[t], :]  (aten.embedding capture, Mamba LM front). */
 typedef struct {

@@ -14,6 +14,8 @@
 //      sum of squares that the gated RMSNorm consumes.
 // This file is the fp32 CUDA-core implementation (all dtypes); exponents
 // are always <= 0 inside a chunk, so nothing overflows at any length.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace th {
@@ -287,5 +289,72 @@ extern "C" int th_ssd(const th_ssd_args* a, void* stream) {
     case TH_BF16: return ssd_launch<__nv_bfloat16>(a, g, st);
     case TH_F16: return ssd_launch<__half>(a, g, st);
     default: return fail(TH_EDTYPE, "th_ssd: bad dtype %d", a->dtype);
+  }
+}
+
+// ------------------------------------------------------- allocation-free SSD
+// th_ssd_noalloc: the same scan for callers that cannot allocate device
+// memory at the call site -- a host framework that owns every byte of
+// device memory through its own pool and does not let libraries call the
+// CUDA allocator, a caller that must not pay the device-wide synchronisation
+// a cudaFree implies, or a C plugin that is handed only its input and output
+// pointers.  The chunk-state scratch lives in the fixed-size array below,
+// which every GPU that loads this library keeps until the process exits.
+namespace th {
+
+static __device__ __align__(256) unsigned char g_ssd_noalloc_scratch[TH_SSD_NOALLOC_MAX_BYTES];
+
+// Device address of the scratch array, looked up once per device.  On the
+// host, the array's name is only a stand-in symbol (not a device address),
+// so the kernels are given the address cudaGetSymbolAddress returns.
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64] = {};
+
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(TH_ELAUNCH, "th_ssd_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(TH_EUNSUPPORTED, "th_ssd_noalloc: device ordinal %d >= 64", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_ssd_noalloc_scratch);  // with `dev` current
+    if (e != cudaSuccess || !p)
+      return fail(TH_ELAUNCH, "th_ssd_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return TH_OK;
+}
+
+}  // namespace th
+
+extern "C" int th_ssd_noalloc(const th_ssd_args* a, void* stream) {
+  using namespace th;
+  if (!a || !a->x || !a->dt || !a->A || !a->B || !a->C || !a->out) return fail(TH_EINVAL, "th_ssd_noalloc: NULL argument");
+  SsdGeom g;
+  int rc = ssd_geom(a, &g);
+  if (rc) return rc;
+  const size_t need = th_ssd_workspace_size(a->batch, a->seq, a->heads, a->head_dim, a->state_dim, a->chunk);
+  if (need > (size_t)TH_SSD_NOALLOC_MAX_BYTES)
+    return fail(TH_EINVAL,
+                "th_ssd_noalloc: this shape needs %zu bytes of scratch, more than the built-in %u bytes "
+                "(TH_SSD_NOALLOC_MAX_BYTES); use th_ssd with a caller-provided workspace",
+                need, (unsigned)TH_SSD_NOALLOC_MAX_BYTES);
+  if (a->gss && a->ldgss < a->heads) return fail(TH_EINVAL, "th_ssd_noalloc: ldgss < heads");
+  void* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  // Nothing in the scratch has to start at zero: the first pass writes every
+  // chunk state and cumulative sum that the later passes read.
+  th_ssd_args b = *a;
+  b.workspace = scratch;
+  b.workspace_bytes = need;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (a->dtype) {
+    case TH_F32: return ssd_launch<float>(&b, g, st);
+    case TH_BF16: return ssd_launch<__nv_bfloat16>(&b, g, st);
+    case TH_F16: return ssd_launch<__half>(&b, g, st);
+    default: return fail(TH_EDTYPE, "th_ssd_noalloc: bad dtype %d", a->dtype);
   }
 }
