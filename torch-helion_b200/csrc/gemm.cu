@@ -138,6 +138,14 @@ __device__ void epilogue_tile(const float* tile, int ldt, float* rscale, const E
 }
 
 // ------------------------------------------------------------ tcgen05 path
+// Persistent, warp-specialised kernel (192 threads, one CTA per SM):
+//   warp 0  TMA producer: A/B tiles (128-byte swizzle) into a STAGES-deep ring
+//   warp 1  MMA issuer:   tcgen05.mma 128xBNx16 into one of two TMEM accumulators
+//   warps 2-5 epilogue:   thread = accumulator row; tcgen05.ld 32 columns at a
+//           time, all fused stages in registers, direct stores
+// The two accumulators (2*BN TMEM columns) let the epilogue of tile i overlap
+// the mainloop of tile i+1.  Every wait is bounded (mbar_wait): a stuck
+// pipeline sets the device error word and the kernel drains and exits.
 template <int BN>
 struct TcCfg {
   static constexpr int BM = 128, BK = 64;
@@ -145,34 +153,148 @@ struct TcCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int LDT = BN + 4;  // staged fp32 tile row stride (16-B steps odd -> no bank conflicts)
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
-  static_assert(BM * LDT * 4 <= RING_BYTES, "staged tile must fit in the ring");
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + RING_BYTES + 256 /*barriers*/ + BM * 4;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + RING_BYTES + 256 /*barriers*/;
 };
 
+// Residual add, store, fp32 tail and sum-of-squares partials of a 32-value
+// row chunk whose first element is output column `oc`.  Returns the chunk's
+// sum of squares of the stored (rounded) values.
+template <typename T>
+__device__ __forceinline__ float finish_chunk(float* v, int row, int oc, int n_out, const EpiParams& ep) {
+  T* d = reinterpret_cast<T*>(ep.d);
+  const T* res = reinterpret_cast<const T*>(ep.residual);
+  float ss = 0.f;
+#pragma unroll
+  for (int e8 = 0; e8 < 32; e8 += 8) {
+    const int c = oc + e8;
+    if (c >= n_out) break;
+    if (c >= ep.tail_begin) {
+      float* o2 = ep.out2 + (int64_t)row * ep.ld_out2 + (c - ep.tail_begin);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (c + e < n_out) o2[e] = v[e8 + e];
+      continue;
+    }
+    if (res) {
+      float r8[8];
+      load8<T>(res + (int64_t)row * ep.ld_res + c, r8);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e8 + e] += r8[e];
+    }
+    store8<T>(d + (int64_t)row * ep.ldd + c, v + e8);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float q = round_to<T>(v[e8 + e]);
+      ss += q * q;
+    }
+  }
+  return ss;
+}
+
+// Epilogue of one accumulator row (this thread) of a 128 x BN tile.
 template <typename T, int BN>
-__global__ void __launch_bounds__(128, 1)
+__device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_ok, float rs, int n0,
+                                             const EpiParams& ep) {
+  if (ep.swiglu) {
+    const int n_out = ep.n / 2;
+    for (int g = 0; g < BN / 128; ++g) {
+      float ss = 0.f;
+      for (int q = 0; q < 2; ++q) {
+        float gv[32], uv[32];
+        tmem_ld32(tbase + g * 128 + q * 32, gv);
+        tmem_ld32(tbase + g * 128 + 64 + q * 32, uv);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) gv[e] = silu_f(gv[e] * rs) * (uv[e] * rs);
+        const int oc = n0 / 2 + g * 64 + q * 32;
+        if (row_ok) ss += finish_chunk<T>(gv, row, oc, n_out, ep);
+      }
+      const int oc = n0 / 2 + g * 64;
+      if (ep.ss_out && row_ok && oc < n_out) ep.ss_out[(int64_t)row * ep.ss_ld + (oc >> 6)] = ss;
+    }
+    return;
+  }
+  const int n_out = ep.n;
+  float ss = 0.f;
+  for (int c = 0; c < BN; c += 32) {
+    float v[32];
+    tmem_ld32(tbase + c, v);
+    const int col = n0 + c;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] *= rs;
+    if (ep.act != TH_ACT_NONE && col < ep.act_end && col + 32 > ep.act_begin) {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int cc = col + e;
+        if (cc >= ep.act_begin && cc < ep.act_end) {
+          float x = v[e] + (ep.bias ? ep.bias[cc - ep.act_begin] : 0.f);
+          v[e] = ep.act == TH_ACT_SILU ? silu_f(x) : softplus_f(x);
+        }
+      }
+    }
+    if (ep.rope_cos && col < ep.rope_end && col + 32 > ep.rope_begin) {
+      const int hd = ep.rope_hd, half = hd >> 1;
+      const int64_t pos = row_ok ? (int64_t)(row % ep.rope_seq) * hd : 0;
+      if (half >= 32) {  // the partner 32 columns are a whole chunk away
+        const int within0 = (col - ep.rope_begin) % hd;
+        const bool first = within0 < half;
+        float pv[32];
+        tmem_ld32(tbase + (first ? c + half : c - half), pv);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float rot = first ? -pv[e] * rs : pv[e] * rs;
+          v[e] = v[e] * ep.rope_cos[pos + within0 + e] + rot * ep.rope_sin[pos + within0 + e];
+        }
+      } else {  // heads of <= 32 columns: partner inside this chunk
+        float t[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) t[e] = v[e];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int within = (col + e - ep.rope_begin) % hd;
+          const bool first = within < half;
+          const float pv = first ? t[(e + half) & 31] : t[(e - half) & 31];
+          v[e] = t[e] * ep.rope_cos[pos + within] + (first ? -pv : pv) * ep.rope_sin[pos + within];
+        }
+      }
+    }
+    if (row_ok) ss += finish_chunk<T>(v, row, col, n_out, ep);
+    if (((c + 32) & 63) == 0) {
+      const int g0 = col - 32;  // first column of this 64-column group
+      if (ep.ss_out && row_ok && g0 < n_out && g0 < ep.tail_begin) ep.ss_out[(int64_t)row * ep.ss_ld + (g0 >> 6)] = ss;
+      ss = 0.f;
+    }
+  }
+}
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiParams ep,
-                   int K) {
+                   int K, int tiles_m, int tiles_n) {
   using C = TcCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING_BYTES);
   uint64_t* empty = full + C::STAGES;
-  uint64_t* done = empty + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* rscale = reinterpret_cast<float*>(smem + C::RING_BYTES + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * C::BM;
+  const int ntiles = tiles_m * tiles_n;
   const int nk = (K + C::BK - 1) / C::BK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);  // one arrive per epilogue warp
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -181,66 +303,93 @@ __global__ void __launch_bounds__(128, 1)
     tma_prefetch_desc(&tmB);
   }
   __syncwarp();
-  if (warp == 0) tmem_alloc(tmem_slot, BN);  // warp-wide .sync.aligned
+  if (warp == 0) tmem_alloc(tmem_slot, C::TMEM_COLS);  // warp-wide .sync.aligned
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // TMA producer
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % C::STAGES;
-      const uint32_t ph = (kb / C::STAGES) & 1;
-      if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) break;
-      uint8_t* sa = smem + s * C::STAGE_BYTES;
-      mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-      tma_load_2d(sa, &tmA, &full[s], kb * C::BK, m0);
-      tma_load_2d(sa + C::A_BYTES, &tmB, &full[s], kb * C::BK, n0);
-    }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer
-    constexpr uint32_t idesc = make_idesc_f16(128, BN, DT<T>::id == TH_BF16 ? 1 : 0, 0, 0);
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % C::STAGES;
-      const uint32_t ph = (kb / C::STAGES) & 1;
-      if (!mbar_wait(&full[s], ph, abort_flag)) break;
-      tc_fence_after();
-      const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
-      const uint32_t sb = sa + C::A_BYTES;
-#pragma unroll
-      for (int k = 0; k < C::BK / 16; ++k) {
-        const uint64_t ad = make_desc_sw128(sa + k * 32, 16, 1024);
-        const uint64_t bd = make_desc_sw128(sb + k * 32, 16, 1024);
-        tc_mma_f16(tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+        const int m0 = (tile / tiles_n) * C::BM, n0 = (tile % tiles_n) * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+          uint8_t* sa = smem + s * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+          tma_load_2d(sa, &tmA, &full[s], kb * C::BK, m0);
+          tma_load_2d(sa + C::A_BYTES, &tmB, &full[s], kb * C::BK, n0);
+        }
       }
-      tc_commit(&empty[s]);
     }
-    tc_commit(done);
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      constexpr uint32_t idesc = make_idesc_f16(128, BN, DT<T>::id == TH_BF16 ? 1 : 0, 0, 0);
+      int it = 0, i = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++i) {
+        const int acc = i & 1, use = i >> 1;
+        if (!mbar_wait(&tempty[acc], (use & 1) ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < C::BK / 16; ++k) {
+            const uint64_t ad = make_desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = make_desc_sw128(sb + k * 32, 16, 1024);
+            tc_mma_f16(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+        }
+        if (ok) tc_commit(&tfull[acc]);
+      }
+      tc_commit(done);  // tracks every MMA this thread issued
+    }
+  } else {  // ---- epilogue warps 2..5
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    const int rl = q * 32 + lane;
+    int i = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++i) {
+      const int acc = i & 1, use = i >> 1;
+      const int m0 = (tile / tiles_n) * C::BM, n0 = (tile % tiles_n) * BN;
+      if (!mbar_wait(&tfull[acc], use & 1, abort_flag)) break;
+      __syncwarp();
+      tc_fence_after();
+      const int row = m0 + rl;
+      const bool row_ok = row < ep.m;
+      float rs = 1.f;
+      if (ep.rs_parts && row_ok) {
+        const float* pp = ep.rs_parts + (int64_t)row * ep.rs_nparts;
+        float sacc = 0.f;
+        for (int k = 0; k < ep.rs_nparts; ++k) sacc += pp[k];
+        rs = rsqrtf(sacc * ep.rs_inv_k + ep.rs_eps);
+      }
+      __syncwarp();
+      epilogue_row<T, BN>(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN), row, row_ok, rs, n0, ep);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
   }
   __syncwarp();
-  const bool ok = mbar_wait(done, 0, abort_flag);
-  __syncwarp();  // tcgen05.ld below is .sync.aligned
-  tc_fence_after();
-  if (ok && !*abort_flag) {
-    // TMEM -> registers -> staged fp32 tile (the ring is idle now)
-    float* tile = reinterpret_cast<float*>(smem);
-    const int rl = warp * 32 + lane;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      float v[32];
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
-      float4* dst = reinterpret_cast<float4*>(tile + rl * C::LDT + c);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-    }
-    tc_fence_before();
-    __syncthreads();
-    epilogue_tile<T, 128, C::BM, BN>(tile, C::LDT, rscale, ep, m0, n0);
+  // teardown: wait (bounded) for the MMAs to retire before freeing TMEM
+  if (threadIdx.x == 64) {
+    volatile int dummy = 0;
+    mbar_wait(done, 0, &dummy);
   }
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, BN);
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
 // --------------------------------------------------------------- FFMA path
@@ -299,13 +448,15 @@ static int launch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st
   if (rc) return rc;
   rc = make_tmap_2d(&tb, a->w, a->dtype, (uint64_t)a->k, (uint64_t)a->n, (uint64_t)a->ldw * 2, 64, BN, true);
   if (rc) return rc;
-  static bool attr_set = false;  // idempotent; benign race
+  static bool attr_set = false;  // once per instantiation (keeps it out of CUDA-graph captures)
   if (!attr_set) {
     cudaFuncSetAttribute(gemm_tc_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     attr_set = true;
   }
-  dim3 grid((unsigned)((a->n + BN - 1) / BN), (unsigned)((a->m + C::BM - 1) / C::BM));
-  gemm_tc_kernel<T, BN><<<grid, 128, C::SMEM_BYTES, st>>>(ta, tb, ep, (int)a->k);
+  const int tiles_m = (int)((a->m + C::BM - 1) / C::BM), tiles_n = (int)((a->n + BN - 1) / BN);
+  const int ntiles = tiles_m * tiles_n;
+  const int grid = ntiles < sm_count() ? ntiles : sm_count();
+  gemm_tc_kernel<T, BN><<<grid, 192, C::SMEM_BYTES, st>>>(ta, tb, ep, (int)a->k, tiles_m, tiles_n);
   return check_launch("th_gemm(tcgen05)");
 }
 

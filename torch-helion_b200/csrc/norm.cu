@@ -76,10 +76,10 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, i
 }
 
 // ------------------------------------------------------ causal conv1d
-// Tile: 64 tokens x (8 * 32) channels per 256-thread block; each thread owns
+// Tile: 16 tokens x (8 * 256) channels per 256-thread block; each thread owns
 // 8 consecutive channels and walks the tokens, keeping the last width-1
 // inputs in registers (the halo is re-read once per tile).
-constexpr int CONV_TOK = 64;
+constexpr int CONV_TOK = 16;
 template <typename T, int W>
 __global__ void __launch_bounds__(256) conv1d_kernel(const T* __restrict__ x, int64_t ldx, const float* __restrict__ w,
                                                      const float* __restrict__ bias, T* __restrict__ y, int64_t ldy,

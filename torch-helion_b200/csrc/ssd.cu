@@ -15,6 +15,7 @@
 // This file is the fp32 CUDA-core implementation (all dtypes); exponents
 // are always <= 0 inside a chunk, so nothing overflows at any length.
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -243,10 +244,21 @@ static int ssd_geom(const th_ssd_args* a, SsdGeom* g) {
   return TH_OK;
 }
 
+}  // namespace th
+
+#include "ssd_mma.cu"  // tensor-core passes for 2-byte dtypes (uses ssd_pass_kernel above)
+
+namespace th {
+
 template <typename T>
 static int ssd_launch(const th_ssd_args* a, const SsdGeom& g, cudaStream_t st) {
   float* states = reinterpret_cast<float*>(a->workspace);
   float* cum = states + g.states_elems;
+  if constexpr (!std::is_same<T, float>::value) {
+    int rc = TH_OK;
+    if ((reinterpret_cast<uintptr_t>(a->out) & 3) == 0 && a->ldo % 2 == 0 && ssd_mma_try<T>(a, states, cum, st, &rc) == 0)
+      return rc;
+  }
   const size_t sm1 = sizeof(float) * (SSD_MAXL + 32 * g.hd + 32 * g.ns);
   const size_t sm3 = sizeof(float) * (SSD_RB * g.ns + 64 * g.ns + 64 * g.hd + SSD_RB * 65 + SSD_RB + 64 + 64);
   static size_t set1 = 0, set3 = 0;  // raise the limit only when a larger one is needed
