@@ -226,7 +226,10 @@ def _ssd_recurrence(x, dt, A, B, C, D, b, s, h, p, g, n):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("b,s,h,p,g,n,chunk", [(2, 200, 4, 32, 1, 16, 64), (1, 256, 2, 64, 2, 128, 128),
-                                               (1, 300, 3, 16, 3, 32, 256)])
+                                               (1, 300, 3, 16, 3, 32, 256),
+                                               # tcgen05 scan path: head_dim 64, chunk 256 (full and ragged chunks)
+                                               (2, 512, 4, 64, 1, 128, 256), (1, 700, 4, 64, 2, 64, 256),
+                                               (3, 300, 2, 64, 1, 128, 256)])
 def test_ssd_matches_recurrence(L, dtype, b, s, h, p, g, n, chunk):
     torch.manual_seed(8)
     t = b * s

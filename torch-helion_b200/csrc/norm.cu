@@ -76,52 +76,67 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, i
 }
 
 // ------------------------------------------------------ causal conv1d
-// Tile: 16 tokens x (8 * 256) channels per 256-thread block; each thread owns
-// 8 consecutive channels and walks the tokens, keeping the last width-1
-// inputs in registers (the halo is re-read once per tile).
-constexpr int CONV_TOK = 16;
+// One thread = CONV_TPT consecutive tokens x 8 consecutive channels.  A 32x8
+// block covers 256 channels x (8*CONV_TPT) tokens: a warp reads 512
+// contiguous bytes of a row, the weights (8 channels x width taps) are read
+// once per thread as float4s, and the CONV_TPT+width-1 input rows a thread
+// needs are independent loads.
+constexpr int CONV_TPT = 4;
 template <typename T, int W>
 __global__ void __launch_bounds__(256) conv1d_kernel(const T* __restrict__ x, int64_t ldx, const float* __restrict__ w,
                                                      const float* __restrict__ bias, T* __restrict__ y, int64_t ldy,
-                                                     int seq, int channels, int act) {
-  const int c0 = (blockIdx.x * 256 + threadIdx.x) * 8;
-  if (c0 >= channels) return;
-  const int b = blockIdx.z;
-  const int s0 = blockIdx.y * CONV_TOK;
-  const int64_t base = (int64_t)b * seq;
-  float wt[8][W], bi[8];
+                                                     int batch, int seq, int channels, int act) {
+  const int c0 = (blockIdx.x * 32 + threadIdx.x) * 8;
+  const int64_t t0 = ((int64_t)blockIdx.y * 8 + threadIdx.y) * CONV_TPT;  // first token (global row)
+  const int64_t T_ = (int64_t)batch * seq;
+  if (c0 >= channels || t0 >= T_) return;
+  float wt[8][W];
+  if constexpr (W == 4) {
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
+    for (int e = 0; e < 8; ++e) {
+      const float4 q = *reinterpret_cast<const float4*>(w + (int64_t)(c0 + e) * 4);
+      wt[e][0] = q.x; wt[e][1] = q.y; wt[e][2] = q.z; wt[e][3] = q.w;
+    }
+  } else {
 #pragma unroll
-    for (int j = 0; j < W; ++j) wt[e][j] = w[(int64_t)(c0 + e) * W + j];
-    bi[e] = bias ? bias[c0 + e] : 0.f;
+    for (int e = 0; e < 8; ++e)
+#pragma unroll
+      for (int j = 0; j < W; ++j) wt[e][j] = w[(int64_t)(c0 + e) * W + j];
   }
-  float hist[W][8];  // hist[j] = input at token s-(W-1)+j
+  float bi[8];
 #pragma unroll
-  for (int j = 0; j < W - 1; ++j) {
-    const int s = s0 - (W - 1) + j;
-    if (s >= 0) load8<T>(x + (base + s) * ldx + c0, hist[j]);
-    else {
+  for (int e = 0; e < 8; ++e) bi[e] = bias ? bias[c0 + e] : 0.f;
+  // global rows t0-(W-1) .. t0+CONV_TPT-1 (a thread's tokens may straddle two
+  // sequences; taps that would reach into the previous sequence are masked)
+  constexpr int R = CONV_TPT + W - 1;
+  float in[R][8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) hist[j][e] = 0.f;
+  for (int r = 0; r < R; ++r) {
+    const int64_t tr = t0 - (W - 1) + r;
+    if (tr >= 0 && tr < T_) {
+      load8<T>(x + tr * ldx + c0, in[r]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) in[r][e] = 0.f;
     }
   }
-  const int s_end = min(seq, s0 + CONV_TOK);
-  for (int s = s0; s < s_end; ++s) {
-    load8<T>(x + (base + s) * ldx + c0, hist[W - 1]);
+#pragma unroll
+  for (int k = 0; k < CONV_TPT; ++k) {
+    const int64_t t = t0 + k;
+    if (t >= T_) break;
+    const int sk = (int)(t % seq);  // position of this token in its sequence
     float o[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       float acc = bi[e];
 #pragma unroll
-      for (int j = 0; j < W; ++j) acc = fmaf(wt[e][j], hist[j][e], acc);
+      for (int j = 0; j < W; ++j) {
+        const bool in_seq = sk - (W - 1) + j >= 0;  // zero left padding of the causal conv
+        acc = in_seq ? fmaf(wt[e][j], in[k + j][e], acc) : acc;
+      }
       o[e] = act == TH_ACT_SILU ? silu_f(acc) : acc;
     }
-    store8<T>(y + (base + s) * ldy + c0, o);
-#pragma unroll
-    for (int j = 0; j < W - 1; ++j)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) hist[j][e] = hist[j + 1][e];
+    store8<T>(y + t * ldy + c0, o);
   }
 }
 
@@ -189,8 +204,10 @@ extern "C" int th_rmsnorm(const th_rmsnorm_args* a, void* stream) {
 
 template <typename T, int W>
 static void launch_conv(const th_conv1d_args* a, cudaStream_t st) {
-  dim3 grid((unsigned)((a->channels + 2047) / 2048), (unsigned)((a->seq + th::CONV_TOK - 1) / th::CONV_TOK), (unsigned)a->batch);
-  th::conv1d_kernel<T, W><<<grid, 256, 0, st>>>((const T*)a->x, a->ldx, a->w, a->bias, (T*)a->y, a->ldy, a->seq, a->channels, a->act);
+  const int64_t T_ = (int64_t)a->batch * a->seq;
+  dim3 grid((unsigned)((a->channels + 255) / 256), (unsigned)((T_ + 8 * th::CONV_TPT - 1) / (8 * th::CONV_TPT)));
+  th::conv1d_kernel<T, W><<<grid, dim3(32, 8), 0, st>>>((const T*)a->x, a->ldx, a->w, a->bias, (T*)a->y, a->ldy,
+                                                        a->batch, a->seq, a->channels, a->act);
 }
 
 template <typename T>

@@ -107,19 +107,36 @@ __global__ void __launch_bounds__(256) ssd_state_kernel(th_ssd_args p, SsdGeom g
 }
 
 // ---------------------------------------------------------------- pass 2
+// One thread per state element; the chunk values are loaded eight at a time
+// before the dependent recurrence so the loads overlap instead of queueing
+// behind each store.
 __global__ void __launch_bounds__(256) ssd_pass_kernel(SsdGeom g, float* __restrict__ states, const float* __restrict__ cum) {
   const int PN = g.hd * g.ns;
   const int e = blockIdx.x * 256 + threadIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
   if (e >= PN) return;
+  const int64_t stride = (int64_t)g.heads * PN;  // between consecutive chunks
+  float* base = states + ((int64_t)b * g.nchunks * g.heads + h) * PN + e;
   float S = 0.f;
-  for (int c = 0; c < g.nchunks; ++c) {
-    const int len = min(g.chunk, g.seq - c * g.chunk);
-    const float decay = __expf(cum[ssd_cum_index(g, b, h, c, len - 1)]);
-    float* ptr = states + (((int64_t)b * g.nchunks + c) * g.heads + h) * PN + e;
-    const float contrib = *ptr;
-    *ptr = S;
-    S = S * decay + contrib;
+  for (int c0 = 0; c0 < g.nchunks; c0 += 8) {
+    float v[8], dec[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int c = c0 + k;
+      if (c < g.nchunks) {
+        const int len = min(g.chunk, g.seq - c * g.chunk);
+        v[k] = base[c * stride];
+        dec[k] = __expf(cum[ssd_cum_index(g, b, h, c, len - 1)]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int c = c0 + k;
+      if (c < g.nchunks) {
+        base[c * stride] = S;
+        S = S * dec[k] + v[k];
+      }
+    }
   }
 }
 

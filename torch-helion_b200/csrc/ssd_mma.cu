@@ -75,6 +75,27 @@ __device__ __forceinline__ uint32_t b_kmajor_t(uint32_t base, int ld, int n0, in
   return base + (uint32_t)(((k0 + i + 8 * (mat & 1)) * ld + n0 + 8 * (mat >> 1)) * 2);
 }
 
+// Asynchronous 16-byte global->shared copies (zero-filled when !valid).
+__device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(sdst)), "l"(gsrc), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Asynchronous version of stage_rows (same layout, rows >= valid zero-filled).
+template <typename T>
+__device__ __forceinline__ void stage_rows_async(T* s, int lds, const T* g, int64_t ldg, int nrows, int ncols,
+                                                 int valid, int tid, int nthreads) {
+  const int vpr = ncols / 8;
+  for (int v = tid; v < nrows * vpr; v += nthreads) {
+    const int r = v / vpr, c = (v % vpr) * 8;
+    const bool ok = r < valid;
+    cp_async16(s + r * lds + c, ok ? (const void*)(g + (int64_t)r * ldg + c) : (const void*)g, ok);
+  }
+}
+
 // Copy rows [r0, r0+nrows) x cols [0, ncols) of a strided global matrix into
 // smem (row stride lds elements), zero-filling rows >= valid.  16-B vectors.
 template <typename T>
@@ -171,7 +192,9 @@ __global__ void __launch_bounds__(256) ssd_state_mma(th_ssd_args p, MmaGeom g, f
       }
       store8<T>(xs + r * LDX + cc, f);
     }
-    stage_rows<T>(bs, LDB, bg + (t0 + l0) * p.ldb, p.ldb, MS_LH, ncols, rows, tid, 256);
+    stage_rows_async<T>(bs, LDB, bg + (t0 + l0) * p.ldb, p.ldb, MS_LH, ncols, rows, tid, 256);
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncthreads();
     const int kmax = (rows + 15) / 16;
     for (int kk = 0; kk < kmax; ++kk) {
@@ -205,20 +228,25 @@ __global__ void __launch_bounds__(256) ssd_state_mma(th_ssd_args p, MmaGeom g, f
 
 // ------------------------------------------------------------- scan pass
 // grid (nchunks * chunk/64, heads, batch), 128 threads (4 warps x 16 rows).
+// C rows and S_in are staged once; the (B, x) blocks of the intra-chunk
+// loop are double-buffered with cp.async so block j+1 loads while block j
+// multiplies.  S_in stays fp32 in shared memory and its MMA fragments are
+// packed straight from it.
 template <typename T, int P>
 __global__ void __launch_bounds__(128) ssd_scan_mma(th_ssd_args p, MmaGeom g, const float* __restrict__ states,
                                                     const float* __restrict__ cum) {
   using namespace mma;
   extern __shared__ __align__(16) uint8_t smraw[];
-  const int LDN = g.ns + 8;
+  const int LDN = g.ns + 8;       // bf16 row stride of C/B tiles
+  const int LDS = g.ns + 4;       // fp32 row stride of the S_in tile
   constexpr int LDP = P + 8;
-  T* Cs = reinterpret_cast<T*>(smraw);          // [64][LDN]
-  T* Bs = Cs + MS_RB * LDN;                     // [64][LDN]
-  T* Ss = Bs + MS_RB * LDN;                     // [P][LDN]
-  T* xs = Ss + P * LDN;                         // [64][LDP]
-  float* ci = reinterpret_cast<float*>(xs + MS_RB * LDP);  // [64]
-  float* cj = ci + MS_RB;                       // [64]
-  float* dj = cj + MS_RB;                       // [64]
+  T* Cs = reinterpret_cast<T*>(smraw);                              // [64][LDN]
+  float* Sf = reinterpret_cast<float*>(Cs + MS_RB * LDN);           // [P][LDS]
+  T* Bs = reinterpret_cast<T*>(Sf + P * LDS);                       // [2][64][LDN]
+  T* xs = Bs + 2 * MS_RB * LDN;                                     // [2][64][LDP]
+  float* ci = reinterpret_cast<float*>(xs + 2 * MS_RB * LDP);       // [64]
+  float* cj = ci + MS_RB;                                           // [2][64]
+  float* dj = cj + 2 * MS_RB;                                       // [2][64]
   const int rb_per = g.chunk / MS_RB;
   const int c = blockIdx.x / rb_per, rb = blockIdx.x % rb_per;
   const int h = blockIdx.y, b = blockIdx.z;
@@ -232,51 +260,68 @@ __global__ void __launch_bounds__(128) ssd_scan_mma(th_ssd_args p, MmaGeom g, co
   const T* xg = reinterpret_cast<const T*>(p.x) + (int64_t)h * P;
   const T* Bg = reinterpret_cast<const T*>(p.B) + (int64_t)hg * g.ns;
   const T* Cg = reinterpret_cast<const T*>(p.C) + (int64_t)hg * g.ns;
-  // stage C rows of this block, S_in (as T), row cumsums
-  stage_rows<T>(Cs, LDN, Cg + (t0 + i0) * p.ldc, p.ldc, MS_RB, g.ns, len - i0, tid, 128);
   const float* Sin = states + (((int64_t)b * g.nchunks + c) * g.heads + h) * (int64_t)(P * g.ns);
-  for (int e = tid; e < P * (g.ns / 8); e += 128) {
-    const int r = e / (g.ns / 8), cc = (e % (g.ns / 8)) * 8;
-    float f[8];
-    load8<float>(Sin + (int64_t)r * g.ns + cc, f);
-    store8<T>(Ss + r * LDN + cc, f);
+  const int nj = i0 / MS_RB + 1;  // intra-chunk blocks j0 = 0 .. i0
+
+  auto stage_j = [&](int jb, int buf) {
+    const int j0 = jb * MS_RB;
+    stage_rows_async<T>(Bs + buf * MS_RB * LDN, LDN, Bg + (t0 + j0) * p.ldb, p.ldb, MS_RB, g.ns, len - j0, tid, 128);
+    stage_rows_async<T>(xs + buf * MS_RB * LDP, LDP, xg + (t0 + j0) * p.ldx, p.ldx, MS_RB, P, len - j0, tid, 128);
+    if (tid < MS_RB) {
+      const bool ok = j0 + tid < len;
+      cj[buf * MS_RB + tid] = ok ? cum[mg_cum(g, b, h, c, j0 + tid)] : 0.f;
+      dj[buf * MS_RB + tid] = ok ? p.dt[(t0 + j0 + tid) * p.lddt + h] : 0.f;
+    }
+  };
+  // group 0: C rows + S_in ; group 1: first (B, x) block
+  stage_rows_async<T>(Cs, LDN, Cg + (t0 + i0) * p.ldc, p.ldc, MS_RB, g.ns, len - i0, tid, 128);
+  for (int v = tid; v < P * (g.ns / 4); v += 128) {
+    const int r = v / (g.ns / 4), cc = (v % (g.ns / 4)) * 4;
+    cp_async16(Sf + r * LDS + cc, Sin + (int64_t)r * g.ns + cc, true);
   }
   if (tid < MS_RB) ci[tid] = (i0 + tid < len) ? cum[mg_cum(g, b, h, c, i0 + tid)] : 0.f;
+  cp_async_commit();
+  stage_j(0, 0);
+  cp_async_commit();
+  cp_async_wait<1>();
   __syncthreads();
-  const uint32_t Cs_a = smem_u32(Cs), Bs_a = smem_u32(Bs), Ss_a = smem_u32(Ss), xs_a = smem_u32(xs);
+
+  const uint32_t Cs_a = smem_u32(Cs);
   constexpr int PT = P / 8;  // n-tiles of y
   float y[PT][4];
 #pragma unroll
   for (int j = 0; j < PT; ++j) y[j][0] = y[j][1] = y[j][2] = y[j][3] = 0.f;
-  // y_off = C . S_in^T   (B[k=n][p] = S[p][n], n contiguous -> non-trans)
+  // y_off = C . S_in^T : B fragment (k = state n, col = p) packed from fp32 S[p][n]
   for (int kk = 0; kk < g.ns / 16; ++kk) {
     uint32_t a[4];
     ldsm_x4(a_rowmajor(Cs_a, LDN, warp * 16, kk * 16, lane), a);
 #pragma unroll
-    for (int j = 0; j < PT; j += 2) {
-      uint32_t bb[4];
-      ldsm_x4(b_nmajor(Ss_a, LDN, j * 8, kk * 16, lane), bb);
+    for (int j = 0; j < PT; ++j) {
+      const float* sp = Sf + (j * 8 + gr) * LDS + kk * 16 + tq * 2;
+      const float2 lo = *reinterpret_cast<const float2*>(sp);
+      const float2 hi = *reinterpret_cast<const float2*>(sp + 8);
+      uint32_t bb[2] = {pack2<T>(lo.x, lo.y), pack2<T>(hi.x, hi.y)};
       mma16816<T>(y[j], a, bb);
-      mma16816<T>(y[j + 1], a, bb + 2);
     }
   }
-  const int rA = warp * 16 + gr, rB = rA + 8;  // this thread's two rows (block-local)
-  const float eA = __expf(ci[rA]), eB = __expf(ci[rB]);
+  const int rA = warp * 16 + gr, rB = rA + 8;
+  const float ciA = ci[rA], ciB = ci[rB];
+  const float eA = __expf(ciA), eB = __expf(ciB);
 #pragma unroll
   for (int j = 0; j < PT; ++j) {
     y[j][0] *= eA; y[j][1] *= eA; y[j][2] *= eB; y[j][3] *= eB;
   }
-  // intra-chunk blocks j0 <= i0
-  for (int j0 = 0; j0 <= i0 && j0 < len; j0 += MS_RB) {
+  const int giA = i0 + rA, giB = i0 + rB;
+  for (int jb = 0; jb < nj; ++jb) {
+    const int buf = jb & 1;
+    if (jb + 1 < nj) stage_j(jb + 1, buf ^ 1);  // prefetch the next block
+    cp_async_commit();
+    cp_async_wait<1>();
     __syncthreads();
-    stage_rows<T>(Bs, LDN, Bg + (t0 + j0) * p.ldb, p.ldb, MS_RB, g.ns, len - j0, tid, 128);
-    stage_rows<T>(xs, LDP, xg + (t0 + j0) * p.ldx, p.ldx, MS_RB, P, len - j0, tid, 128);
-    if (tid < MS_RB) {
-      const bool ok = j0 + tid < len;
-      cj[tid] = ok ? cum[mg_cum(g, b, h, c, j0 + tid)] : 0.f;
-      dj[tid] = ok ? p.dt[(t0 + j0 + tid) * p.lddt + h] : 0.f;
-    }
-    __syncthreads();
+    const uint32_t Bs_a = smem_u32(Bs + buf * MS_RB * LDN), xs_a = smem_u32(xs + buf * MS_RB * LDP);
+    const float* cjb = cj + buf * MS_RB;
+    const float* djb = dj + buf * MS_RB;
+    const int j0 = jb * MS_RB;
     float G[8][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j) G[j][0] = G[j][1] = G[j][2] = G[j][3] = 0.f;
@@ -291,19 +336,16 @@ __global__ void __launch_bounds__(128) ssd_scan_mma(th_ssd_args p, MmaGeom g, co
         mma16816<T>(G[j + 1], a, bb + 2);
       }
     }
-    // decay mask: G[i][j] *= exp(cum_i - cum_j) dt_j for j <= i
-    const int giA = i0 + rA, giB = i0 + rB;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         const int jl = j * 8 + tq * 2 + q, gj = j0 + jl;
-        const float wj = dj[jl], cjv = cj[jl];
-        G[j][q] = (gj <= giA) ? G[j][q] * __expf(ci[rA] - cjv) * wj : 0.f;
-        G[j][2 + q] = (gj <= giB) ? G[j][2 + q] * __expf(ci[rB] - cjv) * wj : 0.f;
+        const float wj = djb[jl], cjv = cjb[jl];
+        G[j][q] = (gj <= giA) ? G[j][q] * __expf(ciA - cjv) * wj : 0.f;
+        G[j][2 + q] = (gj <= giB) ? G[j][2 + q] * __expf(ciB - cjv) * wj : 0.f;
       }
     }
-    // y += G . x_j   (A from G's registers, B[k=j][p] = xs[j][p] -> trans)
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       uint32_t a[4];
@@ -319,8 +361,11 @@ __global__ void __launch_bounds__(128) ssd_scan_mma(th_ssd_args p, MmaGeom g, co
         mma16816<T>(y[j + 1], a, bb + 2);
       }
     }
+    __syncthreads();  // buffer `buf` is refilled two iterations later
   }
-  // epilogue: D skip, gate, store, per-head sum of squares
+  // epilogue: D skip (x of the diagonal block is still staged), gate, store,
+  // per-head sum of squares
+  const T* xd = xs + ((nj - 1) & 1) * MS_RB * LDP;
   const float Dh = p.D ? p.D[h] : 0.f;
   const T* zg = reinterpret_cast<const T*>(p.z);
   T* out = reinterpret_cast<T*>(p.out);
@@ -334,16 +379,15 @@ __global__ void __launch_bounds__(128) ssd_scan_mma(th_ssd_args p, MmaGeom g, co
 #pragma unroll
     for (int j = 0; j < PT; ++j) {
       const int col = j * 8 + tq * 2;
-      const T* xp = xg + t * p.ldx + col;
-      float v0 = y[j][2 * half] + Dh * to_f32(xp[0]);
-      float v1 = y[j][2 * half + 1] + Dh * to_f32(xp[1]);
+      float v0 = y[j][2 * half] + Dh * to_f32(xd[rl * LDP + col]);
+      float v1 = y[j][2 * half + 1] + Dh * to_f32(xd[rl * LDP + col + 1]);
       if (zg) {
-        const T* zp = zg + t * p.ldz + (int64_t)h * P + col;
+        const uint32_t zz = *reinterpret_cast<const uint32_t*>(zg + t * p.ldz + (int64_t)h * P + col);
+        const T* zp = reinterpret_cast<const T*>(&zz);
         v0 *= silu_f(to_f32(zp[0]));
         v1 *= silu_f(to_f32(zp[1]));
       }
-      const uint32_t pk = pack2<T>(v0, v1);
-      *reinterpret_cast<uint32_t*>(out + t * p.ldo + (int64_t)h * P + col) = pk;
+      *reinterpret_cast<uint32_t*>(out + t * p.ldo + (int64_t)h * P + col) = pack2<T>(v0, v1);
       const float q0 = round_to<T>(v0), q1 = round_to<T>(v1);
       if (half) ssB += q0 * q0 + q1 * q1; else ssA += q0 * q0 + q1 * q1;
     }
@@ -353,17 +397,23 @@ __global__ void __launch_bounds__(128) ssd_scan_mma(th_ssd_args p, MmaGeom g, co
   ssB += __shfl_xor_sync(0xffffffffu, ssB, 1);
   ssB += __shfl_xor_sync(0xffffffffu, ssB, 2);
   if (p.gss && tq == 0) {
-    if (i0 + rA < len) p.gss[(t0 + i0 + rA) * p.ldgss + h] = ssA;
-    if (i0 + rB < len) p.gss[(t0 + i0 + rB) * p.ldgss + h] = ssB;
+    if (giA < len) p.gss[(t0 + giA) * p.ldgss + h] = ssA;
+    if (giB < len) p.gss[(t0 + giB) * p.ldgss + h] = ssB;
   }
 }
 
 // The inter-chunk pass is shared with the fp32 path (ssd.cu: ssd_pass_kernel).
 
+}  // namespace th
+
+#include "ssd_tc.cu"  // tcgen05 scan pass (head_dim 64, chunk 256)
+
+namespace th {
+
 template <typename T, int P>
 static int ssd_mma_launch(const th_ssd_args* a, const MmaGeom& g, float* states, float* cum, cudaStream_t st) {
   const size_t sm1 = sizeof(float) * MS_L + sizeof(T) * (MS_LH * (P + 8) + MS_LH * (MS_NS + 8));
-  const size_t sm3 = sizeof(T) * ((2 * MS_RB + P) * (g.ns + 8) + MS_RB * (P + 8)) + sizeof(float) * 3 * MS_RB;
+  const size_t sm3 = sizeof(T) * (3 * MS_RB * (g.ns + 8) + 2 * MS_RB * (P + 8)) + sizeof(float) * (P * (g.ns + 4) + 5 * MS_RB);
   static size_t set1 = 0, set3 = 0;
   if (sm1 > set1) { cudaFuncSetAttribute(ssd_state_mma<T, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1); set1 = sm1; }
   if (sm3 > set3) { cudaFuncSetAttribute(ssd_scan_mma<T, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm3); set3 = sm3; }
@@ -375,6 +425,7 @@ static int ssd_mma_launch(const th_ssd_args* a, const MmaGeom& g, float* states,
   ssd_pass_kernel<<<dim3((g.hd * g.ns + 255) / 256, g.heads, g.batch), 256, 0, st>>>(sg, states, cum);
   rc = check_launch("th_ssd(pass)");
   if (rc) return rc;
+  if (P == TS_P && ssd_scan_tc_try<T>(a, g.nchunks, states, cum, st, &rc) == 0) return rc;
   ssd_scan_mma<T, P><<<dim3(g.nchunks * (g.chunk / MS_RB), g.heads, g.batch), 128, sm3, st>>>(*a, g, states, cum);
   return check_launch("th_ssd(scan, mma)");
 }
@@ -389,6 +440,7 @@ static int ssd_mma_try(const th_ssd_args* a, float* states, float* cum, cudaStre
   if (P != 16 && P != 32 && P != 64) return 1;
   auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   if (!al(a->x) || !al(a->B) || !al(a->C) || a->ldx % 8 || a->ldb % 8 || a->ldc % 8) return 1;
+  if (a->z && ((reinterpret_cast<uintptr_t>(a->z) & 3) || a->ldz % 2)) return 1;
   MmaGeom g{a->batch, a->seq, a->heads, P, a->ngroups, N, a->chunk, (a->seq + a->chunk - 1) / a->chunk,
             (N + MS_NS - 1) / MS_NS};
   switch (P) {
