@@ -180,7 +180,10 @@ def _attn_ref(q, k, v, b, s, hq, hkv, d, scale, causal):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("b,s,hq,hkv,d,causal", [(1, 128, 8, 8, 64, False), (2, 100, 4, 2, 64, True),
-                                                 (2, 256, 8, 2, 128, True), (1, 70, 2, 1, 32, False)])
+                                                 (2, 256, 8, 2, 128, True), (1, 70, 2, 1, 32, False),
+                                                 # tcgen05 path: several KV blocks, ragged tails, GQA
+                                                 (2, 640, 8, 2, 128, True), (1, 1000, 4, 4, 64, False),
+                                                 (3, 333, 4, 1, 128, True), (1, 2048, 2, 2, 64, True)])
 def test_attention(L, dtype, b, s, hq, hkv, d, causal):
     torch.manual_seed(6)
     t = b * s

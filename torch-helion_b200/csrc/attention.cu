@@ -7,6 +7,8 @@
 // per (batch, head), here additionally masked to j <= i when causal.
 #include <float.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace th {
@@ -107,8 +109,18 @@ static int launch_attention(const th_attention_args* a, cudaStream_t st) {
   return check_launch("th_attention");
 }
 
+}  // namespace th
+
+#include "attention_tc.cu"  // tcgen05 path for bf16/fp16, head_dim 64/128
+
+namespace th {
+
 template <typename T>
 static int attention_dispatch(const th_attention_args* a, cudaStream_t st) {
+  if constexpr (!std::is_same<T, float>::value) {
+    int rc = TH_OK;
+    if (attention_tc_try<T>(a, st, &rc) == 0) return rc;
+  }
   switch (a->head_dim) {
     case 16: return launch_attention<T, 16>(a, st);
     case 32: return launch_attention<T, 32>(a, st);

@@ -1,0 +1,295 @@
+// tcgen05 flash attention (forward) for bf16/fp16, head_dim 64 or 128.
+//
+// One CTA = 128 query rows of one (batch, query head); KV blocks of 128 rows.
+// 192 threads, warp-specialised:
+//   warp 0    TMA: the Q tile once, K/V tiles of each KV block into a 2-stage ring
+//   warp 1    MMA: S_j = Q K_j^T into one of two TMEM S buffers (so S_{j+1} is
+//             computed while the softmax warps work on S_j), then O += P_j V_j
+//             (V is an MN-major operand: head_dim is its contiguous axis)
+//   warps 2-5 softmax, one thread per query row: read S_j from TMEM, masked
+//             online softmax in the log2 domain, P_j (bf16) written to shared
+//             memory in the 128-byte-swizzled K-major operand layout.  O is
+//             rescaled in TMEM only when the running max grows by more than
+//             2^8 (a lazy rescale: P stays <= 256, the final O/l is exact).
+// Causal masking skips KV blocks above the diagonal and masks the diagonal
+// block; grouped-query heads read K/V head h / (hq/hkv).  Rows of a tile that
+// run past the sequence (into the next batch element) are masked.
+// TMEM: S buffers at columns [0,128) and [128,256), O at [256, 256+D).
+#include "common.cuh"
+
+namespace th {
+
+template <int D>
+struct AtCfg {
+  static constexpr int BM = 128, BN = 128;
+  static constexpr int DA = D / 64;                // 64-column atoms of head_dim
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KV_BYTES = BN * D * 2;      // one K or one V tile
+  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int STAGES = 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = Q_BYTES;
+  static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int SMEM = 1024 + OFF_BAR + 256;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+
+__device__ __forceinline__ uint32_t at_sw128(int row, int col, int rows) {
+  const int atom = col >> 6, chunk = (col & 63) >> 3, e = col & 7;
+  return (uint32_t)(atom * rows * 128 + row * 128 + ((chunk ^ (row & 7)) << 4) + e * 2);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(192, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, th_attention_args p) {
+  using C = AtCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;        // [2]
+  uint64_t* kv_empty = bars + 3;       // [2]
+  uint64_t* s_full = bars + 5;         // [2]
+  uint64_t* s_free = bars + 7;         // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* pv_done = bars + 10;
+  uint64_t* mma_done = bars + 11;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = (p.seq + C::BM - 1) / C::BM;
+  const int qb = nqb - 1 - (int)blockIdx.x;  // heaviest (most KV blocks) first when causal
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.hq / p.hkv);
+  const int q0 = qb * C::BM;
+  const int64_t row0 = (int64_t)b * p.seq;
+  const int nkv_all = (p.seq + C::BN - 1) / C::BN;
+  const int nkv = p.causal ? min(nkv_all, (q0 + C::BM - 1) / C::BN + 1) : nkv_all;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  __syncwarp();
+  if (warp == 0) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ------------------------------------------- TMA
+      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+      for (int a = 0; a < C::DA; ++a)
+        tma_load_2d(sm + C::OFF_Q + a * C::BM * 128, &tmQ, q_full, h * D + a * 64, (int)(row0 + q0));
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * C::KV_BYTES);
+        for (int a = 0; a < C::DA; ++a) {
+          tma_load_2d(sm + C::OFF_K + s * C::KV_BYTES + a * C::BN * 128, &tmK, &kv_full[s], hk * D + a * 64,
+                      (int)(row0 + j * C::BN));
+          tma_load_2d(sm + C::OFF_V + s * C::KV_BYTES + a * C::BN * 128, &tmV, &kv_full[s], hk * D + a * 64,
+                      (int)(row0 + j * C::BN));
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ------------------------------------------- MMA
+      constexpr int fmt = DT<T>::id == TH_BF16 ? 1 : 0;
+      constexpr uint32_t id_s = make_idesc_f16(128, C::BN, fmt, 0, 0);
+      constexpr uint32_t id_o = make_idesc_f16(128, D, fmt, 0, 1);  // V: MN-major
+      const uint32_t qa = smem_u32(sm + C::OFF_Q), pa = smem_u32(sm + C::OFF_P);
+      bool ok = mbar_wait(q_full, 0, abort_flag);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag)) return false;
+        if (!mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(sm + C::OFF_K + s * C::KV_BYTES);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (uint32_t)((k >> 2) * C::BM * 128 + (k & 3) * 32);
+          const uint32_t koff = (uint32_t)((k >> 2) * C::BN * 128 + (k & 3) * 32);
+          tc_mma_f16(tmem + s * 128, make_desc_sw128(qa + off, 16, 1024), make_desc_sw128(ka + koff, 16, 1024), id_s,
+                     k ? 1u : 0u);
+        }
+        tc_commit(&s_full[s]);
+        return true;
+      };
+      if (ok && nkv > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < nkv; ++j) {
+        if (j + 1 < nkv && !issue_s(j + 1)) break;
+        if (!mbar_wait(p_full, j & 1, abort_flag)) break;
+        tc_fence_after();
+        const int s = j & 1;
+        const uint32_t va = smem_u32(sm + C::OFF_V + s * C::KV_BYTES);
+#pragma unroll
+        for (int k = 0; k < C::BN / 16; ++k) {
+          // A = P rows x kv (K-major, 2 atoms of 128 rows); B = V kv x D (MN-major, atoms 128 rows apart)
+          const uint32_t poff = (uint32_t)((k >> 2) * C::BM * 128 + (k & 3) * 32);
+          tc_mma_f16(tO, make_desc_sw128(pa + poff, 16, 1024),
+                     make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o, (j | k) ? 1u : 0u);
+        }
+        tc_commit(pv_done);
+        tc_commit(&kv_empty[s]);
+      }
+      tc_commit(mma_done);
+    }
+  } else {  // ------------------------------------------- softmax warps 2..5
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;          // row within the tile (TMEM lane)
+    const int qi = q0 + r;                 // query position
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const float sl2 = p.scale * 1.4426950408889634f;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int s = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[s], (j >> 1) & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t sb = tmem + lane_off + s * 128;
+      const int k0 = j * C::BN;
+      const bool diag = p.causal && (k0 + C::BN - 1 > q0);
+      // pass 1: row max of the masked, scaled scores
+      float mx = -INFINITY;
+      for (int c = 0; c < C::BN; c += 32) {
+        float v[32];
+        tmem_ld32(sb + c, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int kj = k0 + c + e;
+          const bool masked = kj >= p.seq || (diag && kj > qi);
+          mx = masked ? mx : fmaxf(mx, v[e] * sl2);
+        }
+      }
+      float m_new = fmaxf(m_ref, mx);
+      const bool rescale = j > 0 && m_new > m_ref + 8.0f;
+      const bool any_rescale = __any_sync(0xffffffffu, rescale);
+      // P_{j-1} must be consumed (and O complete) before P_j / O are touched
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+      }
+      if (j == 0) {
+        m_ref = m_new;
+      } else if (any_rescale) {
+        const float f = rescale ? exp2f(m_ref - m_new) : 1.f;
+        for (int c = 0; c < D; c += 32) {
+          float o[32];
+          tmem_ld32(tO + lane_off + c, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] *= f;
+          tmem_st32(tO + lane_off + c, o);
+        }
+        if (rescale) {
+          l *= f;
+          m_ref = m_new;
+        }
+      }
+      const float mref = (m_ref == -INFINITY) ? 0.f : m_ref;  // fully masked row: P = 0
+      // pass 2: P = exp2(s*scale - m_ref) -> bf16 operand tile, running sum
+      uint8_t* pt = sm + C::OFF_P;
+      for (int c = 0; c < C::BN; c += 32) {
+        float v[32];
+        tmem_ld32(sb + c, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int kj = k0 + c + e;
+          const bool masked = kj >= p.seq || (diag && kj > qi);
+          const float pe = masked ? 0.f : exp2f(v[e] * sl2 - mref);
+          v[e] = pe;
+          l += pe;
+        }
+#pragma unroll
+        for (int e8 = 0; e8 < 32; e8 += 8) store8<T>(reinterpret_cast<T*>(pt + at_sw128(r, c + e8, C::BM)), v + e8);
+      }
+      tc_fence_before();
+      fence_proxy_async();  // P (generic writes) -> visible to the tensor cores
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_free[s]);
+        mbar_arrive(p_full);
+      }
+    }
+    // epilogue: O / l
+    if (ok && nkv > 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (nkv - 1) & 1, abort_flag));
+      tc_fence_after();
+    }
+    if (ok) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* orow = reinterpret_cast<T*>(p.o) + (row0 + qi) * p.ldo + (int64_t)h * D;
+      for (int c = 0; c < D; c += 32) {
+        float o[32];
+        tmem_ld32(tO + lane_off + c, o);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] *= inv;
+        if (qi < p.seq) {
+#pragma unroll
+          for (int e8 = 0; e8 < 32; e8 += 8) store8<T>(orow + c + e8, o + e8);
+        }
+      }
+    }
+  }
+  __syncwarp();
+  if (threadIdx.x == 64) {  // TMEM must be idle before it is freed
+    volatile int dummy = 0;
+    mbar_wait(mma_done, 0, &dummy);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// bf16/fp16, head_dim 64/128, 16-byte aligned rows; returns 1 (not taken) otherwise.
+template <typename T>
+static int attention_tc_try(const th_attention_args* a, cudaStream_t st, int* rc) {
+  const int D = a->head_dim;
+  if (D != 64 && D != 128) return 1;
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o) || a->ldq % 8 || a->ldk % 8 ||
+      a->ldv % 8 || a->ldo % 8)
+    return 1;
+  const int64_t T_ = (int64_t)a->batch * a->seq;
+  if (T_ >= INT32_MAX) return 1;
+  CUtensorMap tq, tk, tv;
+  int r = make_tmap_2d(&tq, a->q, a->dtype, (uint64_t)a->hq * D, (uint64_t)T_, (uint64_t)a->ldq * 2, 64, 128, true);
+  if (!r) r = make_tmap_2d(&tk, a->k, a->dtype, (uint64_t)a->hkv * D, (uint64_t)T_, (uint64_t)a->ldk * 2, 64, 128, true);
+  if (!r) r = make_tmap_2d(&tv, a->v, a->dtype, (uint64_t)a->hkv * D, (uint64_t)T_, (uint64_t)a->ldv * 2, 64, 128, true);
+  if (r) { *rc = r; return 0; }
+  dim3 grid((unsigned)((a->seq + 127) / 128), (unsigned)a->hq, (unsigned)a->batch);
+  if (D == 128) {
+    static bool set = false;
+    if (!set) { cudaFuncSetAttribute(attention_tc_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, AtCfg<128>::SMEM); set = true; }
+    attention_tc_kernel<T, 128><<<grid, 192, AtCfg<128>::SMEM, st>>>(tq, tk, tv, *a);
+  } else {
+    static bool set = false;
+    if (!set) { cudaFuncSetAttribute(attention_tc_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AtCfg<64>::SMEM); set = true; }
+    attention_tc_kernel<T, 64><<<grid, 192, AtCfg<64>::SMEM, st>>>(tq, tk, tv, *a);
+  }
+  *rc = check_launch("th_attention(tcgen05)");
+  return 0;
+}
+
+}  // namespace th
