@@ -214,7 +214,7 @@ class CompiledProgram:
         d = out if n_tail == 0 else out[:, :n_main_pad]
         self.launches.append(KernelLaunch(kname, "gemm", lambda lhs=lhs, W=W, d=d, kw=kw: lib.gemm(lhs, W, d, **kw)))
         if self._allreduced(spec):
-            buf = out[:, :p.n_main]
+            buf = out  # the whole (contiguous) buffer; zero-weight pad columns sum to zero
             self.launches.append(KernelLaunch(f"allreduce({kname})", "nccl", lambda buf=buf: self.allreduce(buf)))
 
     def _add_macro(self, kname: str, p: MacroPlan, need_ss, ss_by_producer) -> None:

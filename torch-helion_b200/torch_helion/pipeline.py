@@ -70,10 +70,29 @@ class CompileResult:
     def run(self, *inputs: torch.Tensor) -> list[torch.Tensor]:
         """Run the compiled forward on the GPU (inputs on CPU or GPU); returns device tensors."""
         if self.module is None:
-            from .b200.runtime import CompiledProgram
-
-            self.module = CompiledProgram(self.program, self.graph.params, self.config.device)
+            self.module = device_module(self.program, self.graph.params, self.config)
         return self.module(*inputs)
+
+
+def device_module(program: Program, params: dict[str, torch.Tensor], config: CompileConfig):
+    """The device program for ``config``: one GPU, or this rank's tensor-parallel
+    shard when ``world_size > 1`` (``torch.distributed`` initialised, NCCL)."""
+    from .b200.runtime import CompiledProgram
+
+    if config.world_size <= 1:
+        return CompiledProgram(program, params, config.device)
+    import torch.distributed as dist
+
+    from .b200.tp import shard_program
+
+    if config.tp_mode not in (None, "heads"):
+        raise ValueError(f"unknown tp_mode {config.tp_mode!r} (supported: 'heads')")
+    if not dist.is_initialized() or dist.get_world_size() != config.world_size:
+        raise RuntimeError(f"world_size={config.world_size} needs an initialised process group of that size")
+    rank = dist.get_rank()
+    sharded, sparams = shard_program(program, params, config.world_size, rank)
+    return CompiledProgram(sharded, sparams, config.device, tp_rank=rank, tp_world=config.world_size,
+                           allreduce=lambda t: dist.all_reduce(t))
 
 
 def _stage(timings: dict[str, float], name: str):
@@ -128,10 +147,8 @@ def compile_model(model: torch.nn.Module, example_args: Sequence[Any], config: C
     res = CompileResult(config, rw.run_dir, fx, raw, graph, hw, result, program, kernel_files, timings=timings)
 
     if config.execute:
-        from .b200.runtime import CompiledProgram
-
         with _stage(timings, "build_device_program"):
-            res.module = CompiledProgram(program, graph.params, config.device)
+            res.module = device_module(program, graph.params, config)
             if config.cuda_graph:
                 res.module.capture_graph()
         if config.reference_check:
