@@ -1,0 +1,167 @@
+"""Front end on the CPU (no GPU): capture -> canonicalisation -> partition ->
+plan -> OpIR, checked the way the reference checks its optimizer
+(tests/test_llama_fusion.py, tests/test_mamba_block.py: structure of the
+partition, numerics of the canonical graph and of the interpreted program
+against the eager model).  The programs are interpreted in fp64 by
+``oracle.interpret`` and compared with the eager oracle."""
+
+from __future__ import annotations
+
+import json
+
+import pytest
+import torch
+
+from conftest import rel_l2
+from oracle import interpret as I
+from oracle import models as O
+
+
+def _compile(model, args, tmp_path, **kw):
+    from torch_helion import CompileConfig, compile_model
+
+    return compile_model(model, args, CompileConfig(run_name="fe", results_dir=tmp_path, execute=False, **kw))
+
+
+def _llama(**kw):
+    from workloads.llama_block import LlamaBlockConfig, build_llama_block
+
+    base = dict(batch=2, seq=32, hidden=128, heads=4, intermediate=256, dtype=torch.float32)
+    cfg = LlamaBlockConfig(**{**base, **kw})
+    m = build_llama_block(cfg, 0)
+    return cfg, m, m.example_inputs(seed=1)
+
+
+def _mamba(**kw):
+    from workloads.mamba import MambaConfig, apply_baseline_init, build_mamba_model
+
+    base = dict(batch=2, seq=128, d_model=64, expand=2, headdim=16, d_state=16, chunk=64, n_layers=1, mode="chunked",
+                ngroups=1, d_conv=4, use_conv=True, dtype=torch.float32)
+    cfg = MambaConfig(**{**base, **kw})
+    m = apply_baseline_init(build_mamba_model(cfg, 0), 0)
+    return cfg, m, m.example_inputs(1)
+
+
+def _sd(m):
+    return {k: v.detach() for k, v in m.state_dict().items()}
+
+
+def _mamba_ref(m, u, cfg):
+    return O.mamba_forward(_sd(m), u, n_layers=cfg.n_layers, d_model=cfg.d_model, expand=cfg.expand,
+                           headdim=cfg.headdim, d_state=cfg.d_state, ngroups=cfg.ngroups, chunk=cfg.chunk, eps=cfg.eps,
+                           use_conv=cfg.use_conv, d_conv=cfg.d_conv, mode=cfg.mode, embedding=cfg.vocab is not None,
+                           lm_head=cfg.tie_lm_head, dtype=torch.float64)
+
+
+# ------------------------------------------------------------------ Llama
+@pytest.mark.parametrize("kw", [dict(), dict(kv_heads=2, causal=True), dict(kv_heads=1, causal=True)],
+                         ids=["mha", "gqa_causal", "mqa_causal"])
+def test_llama_partition(tmp_path, kw):
+    cfg, m, args = _llama(**kw)
+    res = _compile(m, args, tmp_path)
+    p = res.program
+    assert [k.kind for k in p.kernels] == ["gemm", "attention", "gemm", "gemm", "gemm"]
+    qkv, att, o, mlp, down = p.kernels
+    assert len(qkv.gemms) == 3 and qkv.sumsq  # q|k|v share the normalised LHS; RMSNorm folded
+    assert any(op.op == "rope" for op in qkv.epilogue)
+    assert att.attrs["heads"] == cfg.heads and att.attrs["kv_heads"] == (cfg.kv_heads or cfg.heads)
+    assert att.attrs["causal"] == cfg.causal and att.attrs["head_dim"] == cfg.hidden // cfg.heads
+    assert len(mlp.gemms) == 2 and mlp.sumsq  # gate|up with SwiGLU epilogue
+    assert {op.op for op in mlp.epilogue} >= {"silu", "mul"}
+    assert any(a.role == "extra" for a in o.args) and any(a.role == "extra" for a in down.args)  # residuals
+    # numerics: the interpreted program vs the eager oracle
+    (x,) = args
+    out = I.program_outputs(p, res.graph.params, [x])[0].reshape(x.shape)
+    ref = O.llama_block_forward(_sd(m), x, heads=cfg.heads, kv_heads=cfg.kv_heads, eps=cfg.eps,
+                                rope_theta=cfg.rope_theta, causal=cfg.causal, dtype=torch.float64)
+    assert rel_l2(out, ref) < 1e-8  # fp32-rounded constants (RoPE tables, scale) in the graph
+
+
+def test_pass_log_is_verified(tmp_path):
+    _, m, args = _llama(kv_heads=2, causal=True)
+    res = _compile(m, args, tmp_path)
+    log = json.loads((res.run_dir / "03_pass_log.json").read_text())
+    applied = [e for e in log if e.get("rewrites", 0) > 0]
+    assert {e["pass"] for e in applied} >= {"match_rope", "match_rmsnorm", "match_attention"}
+    for e in applied:
+        assert e.get("max_rel_err", 0.0) < 1e-5, e
+
+
+def test_artifacts_and_opir_roundtrip(tmp_path):
+    from torch_helion.optimizer.opir import Program
+
+    _, m, args = _llama()
+    res = _compile(m, args, tmp_path)
+    for f in ("01_fx_graph.txt", "02_opgraph_raw.json", "03_opgraph_canonical.json", "05_plan/plan.md", "06_opir.json",
+              "07_launch_plan.json", "09_cost_report.md", "timings.json"):
+        assert (res.run_dir / f).exists(), f
+    loaded = Program.from_json(res.run_dir / "06_opir.json")
+    assert json.dumps(loaded.to_dict(), sort_keys=True, default=str) == \
+        json.dumps(json.loads(json.dumps(res.program.to_dict(), default=str)), sort_keys=True, default=str)
+    assert len(res.kernel_files) == len(res.program.kernels)
+    for path in res.kernel_files.values():
+        plan = json.loads(path.read_text())
+        assert plan["entry_point"].startswith("th_")
+
+
+def test_planner_exhaustive_llama(tmp_path):
+    _, m, args = _llama()
+    res = _compile(m, args, tmp_path)
+    meta = res.program.metadata["plan"]
+    # sibling sets {q,k,v} (Bell(3)=5 partitions) and {gate,up} (Bell(2)=2)
+    assert meta["search"] == "exhaustive" and meta["candidates"] == 10
+    best = res.plan.best
+    assert best.total_us == min(c.total_us for c in res.plan.candidates if c.legal)
+
+
+def test_planner_descent_deep_mamba(tmp_path):
+    cfg, m, args = _mamba(n_layers=4, use_conv=False, ngroups=8, chunk=32, seq=64, vocab=100)
+    res = _compile(m, args, tmp_path)
+    meta = res.program.metadata["plan"]
+    assert meta["search"] == "coordinate descent" and meta["search_space"] > 512
+    kinds = [k.kind for k in res.program.kernels]
+    assert kinds[0] == "embedding" and kinds[-1] == "rmsnorm"
+    assert kinds.count("ssd") == 4 and kinds.count("gemm") == 8  # in_proj merged, out_proj per layer
+    (u,) = args
+    out = I.program_outputs(res.program, res.graph.params, [u])[0]
+    ref = _mamba_ref(m, u, cfg)
+    assert rel_l2(out.reshape(ref.shape), ref) < 1e-6  # fp32-rounded constants (A, dt_bias folds)
+
+
+# ------------------------------------------------------------------ Mamba
+@pytest.mark.parametrize("kw", [dict(), dict(ngroups=None), dict(mode="quadratic", seq=64)],
+                         ids=["conv_g1", "conv_per_head_groups", "quadratic"])
+def test_mamba_partition(tmp_path, kw):
+    cfg, m, args = _mamba(**kw)
+    res = _compile(m, args, tmp_path)
+    p = res.program
+    assert [k.kind for k in p.kernels] == ["gemm", "causal_conv1d", "ssd", "gemm", "rmsnorm"]
+    inp, conv, ssd, outp, norm_f = p.kernels
+    assert conv.attrs.get("act") == "silu"
+    assert ssd.attrs["gate"] and ssd.attrs["has_D"] and ssd.attrs["ngroups"] == cfg.groups
+    assert ssd.attrs["heads"] == cfg.d_model * cfg.expand // cfg.headdim
+    assert {a.role for a in ssd.args} == {"x", "dt", "A", "B", "C", "D", "z"}
+    (u,) = args
+    out = I.program_outputs(p, res.graph.params, [u])[0]
+    ref = _mamba_ref(m, u, cfg)
+    assert rel_l2(out.reshape(ref.shape), ref) < 1e-6  # fp32-rounded constants (A, dt_bias folds)
+
+
+def test_legality_rejects_unbuilt_head_dim(tmp_path):
+    from torch_helion.optimizer.legality import check_program
+
+    _, m, args = _llama()
+    res = _compile(m, args, tmp_path)
+    prog = res.program
+    att = next(k for k in prog.kernels if k.kind == "attention")
+    att.attrs["head_dim"] = 48
+    rep = check_program(prog)
+    assert not rep.ok and "head_dim" in str(rep)
+
+
+def test_unknown_backend_raises():
+    from torch_helion import CompileConfig, compile_model
+
+    _, m, args = _llama()
+    with pytest.raises(ValueError):
+        compile_model(m, args, CompileConfig(backend="loom"))

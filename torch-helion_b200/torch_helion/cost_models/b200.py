@@ -118,11 +118,13 @@ def gemm_cost(spec: KernelSpec, tensors: dict[str, TensorType], hw: B200Spec, bn
     out_bytes = sum(tensors[o.tensor].numel * eb for o in spec.outputs)
     byts = T * K * eb + N * K * eb + out_bytes + _arg_bytes(spec, tensors, ("extra",))
     if dt == "float32":
+        # 32x128 tiles, several resident per SM; an SM's share of the tiles
+        # runs at its share of the SIMT throughput
         tiles_m, bn_eff = math.ceil(T / 32), 128
         tiles = tiles_m * math.ceil(N / bn_eff)
         waves = math.ceil(tiles / (hw.sm_count * 4))
-        per_wave = 32 * bn_eff * K * 2 * hw.sm_count * 4 / (hw.fp32_tflops * 1e12 * hw.eff_simt)
-        t_c = waves * per_wave * 1e6
+        per_tile = 32 * bn_eff * K * 2 / (hw.fp32_tflops * 1e12 / hw.sm_count * hw.eff_simt)
+        t_c = math.ceil(tiles / hw.sm_count) * per_tile * 1e6
     else:
         if bn not in hw.eff_tc:
             raise CostModelError(f"tile width {bn} not built")
