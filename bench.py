@@ -11,8 +11,10 @@ scaling is weak and ``value`` is the sum over ranks.
 One JSON line on rank 0:
   value       tokens/s, inputs resident in HBM, L2 flushed between steps,
               device time from CUDA events (max over ranks)
-  e2e         the same forward through the public entry with pinned HOST
-              buffers: H2D of the step's input and D2H of its output timed in
+  e2e         the same forward through the public serving entry
+              (CompileResult.streaming_runner) with pinned HOST buffers: the
+              H2D of every step's input and the D2H of its output are inside
+              the timed region, overlapped with neighbouring forwards
   roofline    the dominant kernel's algorithmic bytes (or flops) per launch /
               its event-timed duration, against MEASURED_PEAKS.json
   cpu_baseline the CPU oracle (the reference's eager forward restated in
@@ -154,24 +156,6 @@ def kernel_work(launch, prog, module) -> dict:
     return {"bytes": 2 * t.numel * eb, "flops": 3.0 * t.numel}
 
 
-def time_kernels(module, flush, iters: int = 5) -> dict[str, float]:
-    """Average device time of every launch, each timed alone (L2 flushed before)."""
-    out = {}
-    st = torch.cuda.current_stream()
-    for l in module.launches:
-        ts = []
-        for _ in range(iters):
-            flush()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            l.fn()
-            e1.record(st)
-            e1.synchronize()
-            ts.append(e0.elapsed_time(e1))
-        out[l.name] = sum(ts) / len(ts)
-    return out
-
-
 def cpu_baseline(cfg, model, x, budget_s: float = 20.0) -> dict:
     """The reference's eager forward, as restated in the oracle, on this host."""
     from oracle import models as O
@@ -283,7 +267,8 @@ def main() -> None:
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    mk = lambda: torch.cuda.Event(enable_timing=True)
+    ev = [(mk(), mk()) for _ in range(args.steps)]
     with ClockSampler(local) as clocks:
         for e0, e1 in ev:
             flush()
@@ -291,36 +276,51 @@ def main() -> None:
             mod.launch_all()
             e1.record(st)
         torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+        barrier()
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+        # the same K steps again with every launch bracketed by events (on the
+        # launching stream): the per-kernel times behind the roofline; kept
+        # out of `value` because each event record adds a small gap
+        kev = [[(mk(), mk()) for _ in mod.launches] for _ in range(args.steps)]
+        for kl in kev:
+            flush()
+            for l, (k0, k1) in zip(mod.launches, kl):
+                k0.record(st)
+                l.fn()
+                k1.record(st)
+        torch.cuda.synchronize()
+    ktimes: dict[str, float] = {}
+    for j, l in enumerate(mod.launches):
+        ktimes[l.name] = sum(kl[j][0].elapsed_time(kl[j][1]) for kl in kev) / args.steps
 
-    # ---- end to end through the public entry with pinned host buffers
+    # ---- end to end through the public serving entry (CompileResult.streaming_runner):
+    # every step copies its input from pinned host memory and its output back;
+    # step i's copies overlap the forward of its neighbours (two slots, three
+    # streams).  The L2 flush runs on the compute stream before each forward.
+    runner = res.streaming_runner(depth=2)
     xh = x.pin_memory()
-    out_view = mod.output_views()[0]
-    oh = torch.empty(out_view.shape, dtype=out_view.dtype, pin_memory=True)
-    for _ in range(max(3, args.warmup)):
-        mod.load_inputs([xh])
-        mod.launch_all()
-        oh.copy_(mod.output_views()[0], non_blocking=True)
+    outs = [runner.output_buffers() for _ in range(2)]
+    for i in range(max(3, args.warmup)):
+        runner.submit(i, [xh], outs[i % 2], before_forward=flush)
+    runner.synchronize()
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for e0, e1 in ev2:
-        flush()
-        e0.record(st)
-        mod.load_inputs([xh])
-        mod.launch_all()
-        oh.copy_(mod.output_views()[0], non_blocking=True)
-        e1.record(st)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(runner.h2d)
+    for i in range(args.steps):
+        runner.submit(i, [xh], outs[i % 2], before_forward=flush)
+    e1.record(runner.d2h)
+    runner.synchronize()
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    ms_e2e = sum(a.elapsed_time(b) for a, b in ev2) / args.steps
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    oh = outs[0][0]
+    del runner
 
     # ---- per-kernel times and the dominant kernel's roofline
-    ktimes = time_kernels(mod, flush)
     peaks, peak_src = _peaks()
     top = max(mod.launches, key=lambda l: ktimes[l.name])
     work = kernel_work(top, prog, mod)
@@ -357,6 +357,7 @@ def main() -> None:
                          "algorithmic_bytes": work["bytes"], "algorithmic_flops": work["flops"],
                          "launch_ms": ktimes[top.name], "traffic": traffic},
             "e2e": {"value": n * tokens / (ms_e2e / 1e3), "unit": unit, "ms_per_step": ms_e2e,
+                    "entry": "CompileResult.streaming_runner (2 slots, H2D/compute/D2H streams)",
                     "h2d_bytes_per_step": xh.numel() * xh.element_size(),
                     "d2h_bytes_per_step": oh.numel() * oh.element_size()},
             "gpu_launches": mod.n_launches * args.steps,

@@ -127,3 +127,25 @@ def test_cuda_graph_replay_matches_eager(tmp_path):
     res.run(u2)
     again = res.run(u)[0]
     assert torch.equal(eager, again)
+
+
+@pytest.mark.parametrize("cuda_graph", [False, True], ids=["eager", "graph"])
+def test_streaming_runner_matches_run(tmp_path, cuda_graph):
+    """Overlapped serving (two slots, H2D/compute/D2H streams) returns, batch
+    for batch, exactly what the one-shot entry returns."""
+    from workloads import configs
+    from workloads.mamba import MambaConfig
+
+    cfg = MambaConfig(batch=2, seq=256, d_model=128, headdim=32, d_state=64, chunk=128, n_layers=2, mode="chunked",
+                      ngroups=1, use_conv=True, dtype=torch.bfloat16)
+    m = configs.build(cfg)
+    (u,) = m.example_inputs(seed=1)
+    res = _compile(m, (u,), tmp_path)
+    g = torch.Generator().manual_seed(5)
+    batches = [torch.randn(u.shape, generator=g).to(u.dtype).pin_memory() for _ in range(5)]
+    want = [res.run(b)[0].cpu().clone() for b in batches]
+    runner = res.streaming_runner(depth=2, cuda_graph=cuda_graph)
+    outs = [runner.output_buffers() for _ in batches]
+    runner.run([[b] for b in batches], outs)
+    for w, o in zip(want, outs):
+        assert torch.equal(w.reshape(o[0].shape), o[0])

@@ -50,7 +50,8 @@ class CompiledProgram:
     """A Program bound to device memory on one GPU."""
 
     def __init__(self, program: Program, params: dict[str, torch.Tensor], device: str | torch.device = "cuda",
-                 tp_rank: int = 0, tp_world: int = 1, allreduce: Callable[[torch.Tensor], None] | None = None) -> None:
+                 tp_rank: int = 0, tp_world: int = 1, allreduce: Callable[[torch.Tensor], None] | None = None,
+                 shared_params: dict | None = None) -> None:
         if not torch.cuda.is_available():
             raise lib.B200KernelError("CompiledProgram needs a CUDA device (there is no CPU fallback)")
         lib.load()
@@ -60,7 +61,9 @@ class CompiledProgram:
         self.params = params
         self.views: dict[str, torch.Tensor] = {}
         self.launches: list[KernelLaunch] = []
-        self._dev_params: dict[tuple, torch.Tensor] = {}
+        # device copies of the parameters, keyed by layout; a second program of
+        # the same Program (another pipeline slot) passes the first one's dict
+        self._dev_params: dict[tuple, torch.Tensor] = shared_params if shared_params is not None else {}
         self._graph: torch.cuda.CUDAGraph | None = None
         self._ssd_ws: torch.Tensor | None = None
         self.tp_rank, self.tp_world, self.allreduce = tp_rank, tp_world, allreduce
@@ -318,6 +321,79 @@ class CompiledProgram:
         return [l.name for l in self.launches]
 
 
+class StreamingRunner:
+    """Serve a stream of batches from pinned host memory.
+
+    ``depth`` copies of the program (one set of activation buffers each, the
+    weights shared) rotate over three CUDA streams: the host->device copy of
+    batch i+1 (one copy engine) and the device->host copy of batch i-1 (the
+    other) run while the SMs compute batch i.  Events order every reuse of a
+    slot: its inputs are overwritten only after its previous forward, its
+    outputs only after their previous copy-out.  Steady-state time per batch is
+    max(forward, H2D, D2H) instead of their sum.
+    """
+
+    def __init__(self, program: Program, params: dict[str, torch.Tensor], device: str | torch.device = "cuda",
+                 depth: int = 2, cuda_graph: bool = False) -> None:
+        if depth < 1:
+            raise ValueError("depth must be >= 1")
+        first = CompiledProgram(program, params, device)
+        self.slots = [first] + [CompiledProgram(program, params, device, shared_params=first._dev_params)
+                                for _ in range(depth - 1)]
+        self.device = first.device
+        with torch.cuda.device(self.device):
+            if cuda_graph:
+                for s in self.slots:
+                    s.capture_graph()
+            self.h2d, self.compute, self.d2h = (torch.cuda.Stream(self.device) for _ in range(3))
+            ev = lambda: [torch.cuda.Event() for _ in self.slots]
+            self._loaded, self._computed, self._drained = ev(), ev(), ev()
+        self._used = [False] * depth
+
+    def output_buffers(self, pin: bool = True) -> list[torch.Tensor]:
+        """Host tensors shaped like one batch's outputs (pinned)."""
+        return [torch.empty(v.shape, dtype=v.dtype, pin_memory=pin) for v in self.slots[0].output_views()]
+
+    def submit(self, i: int, inputs: Sequence[torch.Tensor], outputs: Sequence[torch.Tensor],
+               before_forward: Callable[[], None] | None = None) -> None:
+        """Enqueue batch ``i`` (host ``inputs`` -> host ``outputs``); returns at once."""
+        k = i % len(self.slots)
+        s = self.slots[k]
+        with torch.cuda.device(self.device):
+            if self._used[k]:
+                self.h2d.wait_event(self._computed[k])
+            with torch.cuda.stream(self.h2d):
+                s.load_inputs(inputs)
+                self._loaded[k].record(self.h2d)
+            self.compute.wait_event(self._loaded[k])
+            if self._used[k]:
+                self.compute.wait_event(self._drained[k])
+            with torch.cuda.stream(self.compute):
+                if before_forward is not None:
+                    before_forward()
+                s.launch_all()
+                self._computed[k].record(self.compute)
+            self.d2h.wait_event(self._computed[k])
+            with torch.cuda.stream(self.d2h):
+                for o, v in zip(outputs, s.output_views()):
+                    o.copy_(v.reshape(o.shape), non_blocking=True)
+                self._drained[k].record(self.d2h)
+        self._used[k] = True
+
+    def run(self, batches: Sequence[Sequence[torch.Tensor]], outputs: Sequence[Sequence[torch.Tensor]]) -> None:
+        """Serve every batch and wait for the last copy-out."""
+        for i, (inp, out) in enumerate(zip(batches, outputs)):
+            self.submit(i, inp, out)
+        self.synchronize()
+
+    def synchronize(self) -> None:
+        self.d2h.synchronize()
+
+    @property
+    def n_launches(self) -> int:
+        return self.slots[0].n_launches
+
+
 def run_program(program: Program, params: dict[str, torch.Tensor], inputs, device="cuda") -> dict[str, torch.Tensor]:
     """Reference-shaped entry (interpret.py:54-65): run all kernels, return
     the produced tensors by name (device tensors)."""
@@ -335,4 +411,4 @@ def program_outputs(program: Program, params: dict[str, torch.Tensor], inputs, d
     return [o.clone() for o in cp(*inputs)]
 
 
-__all__ = ["CompiledProgram", "KernelLaunch", "run_program", "program_outputs", "math"]
+__all__ = ["CompiledProgram", "KernelLaunch", "StreamingRunner", "run_program", "program_outputs", "math"]

@@ -73,6 +73,17 @@ class CompileResult:
             self.module = device_module(self.program, self.graph.params, self.config)
         return self.module(*inputs)
 
+    def streaming_runner(self, depth: int = 2, cuda_graph: bool | None = None):
+        """A :class:`~torch_helion.b200.runtime.StreamingRunner` over this
+        program: host batches in, host outputs out, copies overlapped with
+        the forward (single GPU)."""
+        from .b200.runtime import StreamingRunner
+
+        if self.config.world_size > 1:
+            raise ValueError("streaming_runner serves one GPU; run one runner per rank")
+        cg = self.config.cuda_graph if cuda_graph is None else cuda_graph
+        return StreamingRunner(self.program, self.graph.params, self.config.device, depth=depth, cuda_graph=cg)
+
 
 def device_module(program: Program, params: dict[str, torch.Tensor], config: CompileConfig):
     """The device program for ``config``: one GPU, or this rank's tensor-parallel
