@@ -334,7 +334,7 @@ def main() -> None:
     traffic = None
     tf = REPO / "profiles" / f"traffic_{args.workload}.json"
     if tf.exists():
-        traffic = json.loads(tf.read_text()).get(top.kind)
+        traffic = json.loads(tf.read_text()).get(top.name)
 
     # ---- aggregate over ranks (max time)
     t = torch.tensor([ms, ms_e2e], device=dev, dtype=torch.float64)
