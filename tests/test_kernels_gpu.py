@@ -232,7 +232,11 @@ def _ssd_recurrence(x, dt, A, B, C, D, b, s, h, p, g, n):
                                                (1, 300, 3, 16, 3, 32, 256),
                                                # tcgen05 scan path: head_dim 64, chunk 256 (full and ragged chunks)
                                                (2, 512, 4, 64, 1, 128, 256), (1, 700, 4, 64, 2, 64, 256),
-                                               (3, 300, 2, 64, 1, 128, 256)])
+                                               (3, 300, 2, 64, 1, 128, 256),
+                                               # tcgen05 chunk-state + multi-head scan: state 128; head sets,
+                                               # two groups, a chunk shorter than 128 rows, many chunks
+                                               (2, 1024, 24, 64, 1, 128, 256), (1, 600, 8, 64, 2, 128, 256),
+                                               (1, 100, 4, 64, 1, 128, 256), (1, 4096, 2, 64, 1, 128, 256)])
 def test_ssd_matches_recurrence(L, dtype, b, s, h, p, g, n, chunk):
     torch.manual_seed(8)
     t = b * s
@@ -250,6 +254,28 @@ def test_ssd_matches_recurrence(L, dtype, b, s, h, p, g, n, chunk):
     ref = y * F.silu(z.double())
     assert rel_l2(out.float(), ref) < TOL[dtype]
     assert rel_l2(gss, out.float().pow(2).reshape(t, h, p).sum(-1)) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("gate", [False, True])
+def test_ssd_chunk_path_optional_operands(L, dtype, gate):
+    """The tcgen05 chunk path with and without z, D and gss."""
+    torch.manual_seed(11)
+    b, s, h, p, g, n = 2, 640, 6, 64, 1, 128
+    t = b * s
+    x = torch.randn(t, h * p, device=_dev()).to(dtype)
+    B = torch.randn(t, g * n, device=_dev()).to(dtype)
+    C = torch.randn(t, g * n, device=_dev()).to(dtype)
+    dt = torch.rand(t, h, device=_dev()) * 0.099 + 0.001
+    A = -torch.exp(torch.rand(h, device=_dev()) * math.log(16))
+    D = torch.rand(h, device=_dev()) if gate else None
+    z = torch.randn(t, h * p, device=_dev()).to(dtype) if gate else None
+    out = torch.empty(t, h * p, device=_dev(), dtype=dtype)
+    L.ssd(x, dt, A, B, C, out, batch=b, seq=s, heads=h, head_dim=p, ngroups=g, state_dim=n, chunk=256, D=D, z=z)
+    y = _ssd_recurrence(x, dt, A, B, C, D if gate else torch.zeros(h, device=_dev()), b, s, h, p, g, n)
+    ref = y * F.silu(z.double()) if gate else y
+    assert rel_l2(out.float(), ref) < TOL[dtype]
+    assert L.device_error() == 0
 
 
 # ------------------------------------------------------------ embedding

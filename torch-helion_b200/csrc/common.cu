@@ -62,6 +62,27 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, 
   return TH_OK;
 }
 
+int make_tmap_3d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t rows, uint64_t planes,
+                 uint64_t row_stride_bytes, uint64_t plane_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+                 bool swizzle128) {
+  CUtensorMap probe;  // resolves the driver entry point once
+  int rc = make_tmap_2d(&probe, base, dtype, inner, rows, row_stride_bytes, box_inner, box_rows, swizzle128);
+  if (rc) return rc;
+  if (plane_stride_bytes % 16) return fail(TH_EALIGN, "TMA plane stride %llu B is not a multiple of 16", (unsigned long long)plane_stride_bytes);
+  CUtensorMapDataType dt = dtype == TH_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                           : dtype == TH_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[3] = {inner, rows, planes};
+  cuuint64_t strides[2] = {row_stride_bytes, plane_stride_bytes};
+  cuuint32_t box[3] = {box_inner, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TH_ELAUNCH, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  return TH_OK;
+}
+
 int sm_count() {
   static int cached = 0;  // every GPU of a node is the same part
   if (cached == 0) {

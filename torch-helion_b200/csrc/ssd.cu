@@ -264,6 +264,7 @@ static int ssd_geom(const th_ssd_args* a, SsdGeom* g) {
 }  // namespace th
 
 #include "ssd_mma.cu"  // tensor-core passes for 2-byte dtypes (uses ssd_pass_kernel above)
+#include "ssd_chunk.cu"  // tcgen05 chunk-state recurrence + multi-head scan (head_dim 64, state 128)
 
 namespace th {
 
@@ -273,6 +274,7 @@ static int ssd_launch(const th_ssd_args* a, const SsdGeom& g, cudaStream_t st) {
   float* cum = states + g.states_elems;
   if constexpr (!std::is_same<T, float>::value) {
     int rc = TH_OK;
+    if (ssd_chunk_try<T>(a, st, &rc) == 0) return rc;
     if ((reinterpret_cast<uintptr_t>(a->out) & 3) == 0 && a->ldo % 2 == 0 && ssd_mma_try<T>(a, states, cum, st, &rc) == 0)
       return rc;
   }

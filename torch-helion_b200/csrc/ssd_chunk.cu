@@ -1,0 +1,596 @@
+// Chunked SSD on tcgen05 in two launches (2-byte dtypes, head_dim 64,
+// chunk 256, state_dim 128).  With l, i, j rows of a chunk, n the state
+// index and p the head-dim index:
+//
+// ssd_state_tc -- one CTA per (head, batch) walks the chunks in order and
+//   keeps the running state S[n][p] (fp32) in TMEM:
+//     cum_l = sum_{l' <= l} dt_l' A            (inclusive, per chunk)
+//     w_l   = exp(cum_last - cum_l) dt_l       (<= dt_l)
+//     S    <- exp(cum_last) S + B^T (w . x)     (one M=128 N=64 K=256 MMA per chunk,
+//                                               B^T and x MN-major straight from TMA)
+//   Before a chunk's update it stores the state entering that chunk (bf16
+//   [n][p], the scan's operand) and writes the chunk's scalars for the scan:
+//   cum, dt and colf_l = exp(cum_{l|31} - cum_l) dt_l.  This replaces the
+//   separate chunk-state and inter-chunk passes and their fp32 round trips.
+//
+// ssd_scan_mh -- one CTA per (query half, chunk, set of heads, batch).  The
+//   heads of one B/C group share C.B^T, so the CTA computes it once into TMEM
+//   and then, head by head:
+//     G = C.B^T * exp(cum_i - cum_j) dt_j  (j <= i), plus D on the diagonal
+//         (CUDA cores: TMEM -> bf16 128B-swizzled shared-memory operand)
+//     Y = G . x + exp(cum_i) (C . S_in)     (tcgen05, two TMEM buffers)
+//     y = Y * silu(z) -> shared memory -> TMA store, per-head sum of y^2
+//   D on the diagonal of G makes G . x carry the D x skip, so x can be
+//   released as soon as the MMA has read it.  Rows 128-255 of a chunk see 256
+//   keys, rows 0-127 see 128; the heavy halves are scheduled first.
+//   Below-diagonal 32-column blocks use exp(ci - cj) = exp(ci - c_ref)
+//   exp(c_ref - cj) with c_ref the block's last column (both factors <= 1).
+//
+// Warp roles (scan): warp 0 TMA producer, warp 1 MMA issuer, warps 2-9 build
+// G and run the epilogue (two warps per TMEM lane quadrant, splitting the
+// columns).  Every wait is bounded; on a timeout the roles skip their work
+// but still pass every named barrier, so the CTA always drains and frees TMEM.
+#include "common.cuh"
+
+namespace th {
+
+constexpr int CK_L = 256, CK_P = 64, CK_NS = 128;
+// Per (batch, head, chunk) scalar record written by the state kernel:
+// cum[256] | dt[256] | colf[256] | D, 0, 0, 0   (fp32, 3088 bytes)
+constexpr int CK_SCAL = 3 * CK_L + 4;
+constexpr int CK_SR = 4;  // scalar ring depth of the scan
+
+inline size_t ck_scal_bytes(int batch, int heads, int nc) {
+  return ((size_t)batch * heads * nc * CK_SCAL * 4 + 1023) & ~size_t(1023);
+}
+inline size_t ck_ws_bytes(int batch, int seq, int heads, int ns) {
+  const int nc = (seq + CK_L - 1) / CK_L;
+  return ck_scal_bytes(batch, heads, nc) + (size_t)batch * nc * heads * ns * CK_P * 2;
+}
+
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// ------------------------------------------------------------------ states
+struct StC {
+  static constexpr int B_BYTES = 2 * CK_L * 128;  // two 64-wide state atoms x 256 rows
+  static constexpr int X_BYTES = CK_L * 128;
+  static constexpr int DT_BYTES = CK_L * 16;      // dt of 4 heads x 256 rows (fp32)
+  static constexpr int STAGE = B_BYTES + X_BYTES + DT_BYTES;
+  static constexpr int OFF_SIN = 2 * STAGE;          // state staging [128 n][64 p]
+  static constexpr int OFF_REC = OFF_SIN + 128 * 128;  // scalar record staging
+  static constexpr int OFF_F = OFF_REC + CK_SCAL * 4;  // cum[256], w[256], warp totals[8]
+  static constexpr int OFF_BAR = OFF_F + (2 * CK_L + 8) * 4;
+  static constexpr int SMEM = 1024 + OFF_BAR + 64;
+  static_assert(OFF_SIN % 1024 == 0 && OFF_REC % 16 == 0, "alignment");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+
+template <typename T>
+__global__ void __launch_bounds__(320, 1)
+    ssd_state_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmX,
+                 const __grid_constant__ CUtensorMap tmDT, const __grid_constant__ CUtensorMap tmS, th_ssd_args p,
+                 int nc, float* __restrict__ scal) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* rec = reinterpret_cast<float*>(sm + StC::OFF_REC);
+  float* cums = reinterpret_cast<float*>(sm + StC::OFF_F);
+  float* wsm = cums + CK_L;
+  float* wtot = wsm + CK_L;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + StC::OFF_BAR);
+  uint64_t* empty = full + 2;
+  uint64_t* ready = full + 4;
+  uint64_t* done = full + 5;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 6);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = h / (p.heads / p.ngroups);
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+    mbar_init(ready, 256);
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tslot, 64);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int c = 0; c < nc; ++c) {
+        const int s = c & 1;
+        if (c >= 2 && !mbar_wait(&empty[s], ((c >> 1) - 1) & 1, abort_flag)) break;
+        uint8_t* st = sm + s * StC::STAGE;
+        mbar_arrive_expect_tx(&full[s], StC::STAGE);
+        tma_load_3d(st, &tmB, &full[s], g * CK_NS, c * CK_L, b);
+        tma_load_3d(st + CK_L * 128, &tmB, &full[s], g * CK_NS + 64, c * CK_L, b);
+        tma_load_3d(st + StC::B_BYTES, &tmX, &full[s], h * CK_P, c * CK_L, b);
+        tma_load_3d(st + StC::B_BYTES + StC::X_BYTES, &tmDT, &full[s], h & ~3, c * CK_L, b);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr int fmt = DT<T>::id == TH_BF16 ? 1 : 0;
+      constexpr uint32_t idesc = make_idesc_f16(128, 64, fmt, 1, 1);  // A = B^T and B = x, both MN-major
+      for (int c = 0; c < nc; ++c) {
+        if (!mbar_wait(ready, c & 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(sm + (c & 1) * StC::STAGE);
+        for (int k = 0; k < CK_L / 16; ++k) {
+          const uint64_t ad = make_desc_sw128(st + k * 2048, CK_L * 128, 1024);
+          const uint64_t bd = make_desc_sw128(st + StC::B_BYTES + k * 2048, CK_L * 128, 1024);
+          tc_mma_f16(tmem, ad, bd, idesc, (c > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(done);
+        tc_commit(&empty[c & 1]);
+      }
+    }
+  } else {
+    // 256 math threads: token / x row l = mt; TMEM quadrant q, state columns half*32..+32
+    const int mt = tid - 64;
+    const int wm = warp - 2;  // math warp 0..7
+    const int q = warp & 3, half = wm >> 2;
+    const int n = q * 32 + lane;
+    const float Ah = p.A[h];
+    const float Dh = p.D ? p.D[h] : 0.f;
+    bool ok = true;
+    for (int c = 0; c < nc; ++c) {
+      uint8_t* st = sm + (c & 1) * StC::STAGE;
+      ok = ok && mbar_wait(&full[c & 1], (c >> 1) & 1, abort_flag);
+      // inclusive prefix sum of dt*A over the chunk (rows past the sequence were zero-filled by TMA)
+      const int l = mt;
+      const float* dtv = reinterpret_cast<const float*>(st + StC::B_BYTES + StC::X_BYTES);
+      const float d = ok ? dtv[l * 4 + (h & 3)] : 0.f;
+      float v = d * Ah;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      if (lane == 31) wtot[wm] = v;
+      if (mt == 0) bulk_wait_read0();  // the previous chunk's stores have read their staging
+      named_bar(1, 256);
+      float off = 0.f, total = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const float t = wtot[w];
+        off += w < wm ? t : 0.f;
+        total += t;
+      }
+      const float cl = off + v;
+      cums[l] = cl;
+      const float w_l = __expf(total - cl) * d;
+      named_bar(1, 256);
+      // the chunk's scalar record for the scan
+      rec[l] = cl;
+      rec[CK_L + l] = d;
+      rec[2 * CK_L + l] = __expf(cums[l | 31] - cl) * d;
+      if (mt == 0) *reinterpret_cast<float4*>(rec + 3 * CK_L) = make_float4(Dh, 0.f, 0.f, 0.f);
+      // x row l scaled by w_l, in place (whole row: the swizzle only permutes 16-byte chunks)
+      if (ok) {
+        T* row = reinterpret_cast<T*>(st + StC::B_BYTES + l * 128);
+#pragma unroll
+        for (int i8 = 0; i8 < 8; ++i8) {  // chunks in swizzled order: no bank conflicts across rows
+          const int e8 = (i8 ^ (l & 7)) * 8;
+          float f[8];
+          load8<T>(row + e8, f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] *= w_l;
+          store8<T>(row + e8, f);
+        }
+      }
+      // the state entering chunk c: stage it (bf16 [n][p]), then scale it by exp(total) for the update
+      if (c > 0) {
+        ok = ok && mbar_wait(done, (c - 1) & 1, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+          tc_fence_after();
+          float sv[32];
+          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + half * 32;
+          tmem_ld32(ta, sv);
+          uint8_t* sst = sm + StC::OFF_SIN;
+#pragma unroll
+          for (int e8 = 0; e8 < 32; e8 += 8)
+            store8<T>(reinterpret_cast<T*>(sst + sw128_off(n, half * 32 + e8, 128)), sv + e8);
+          const float f = __expf(total);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) sv[e] *= f;
+          tmem_st32(ta, sv);
+          tc_fence_before();
+        }
+      }
+      fence_proxy_async();  // scaled x (read by the MMA) and the staging tiles (read by the stores)
+      named_bar(1, 256);
+      if (mt == 0 && ok) {
+        bulk_store(scal + (((int64_t)b * p.heads + h) * nc + c) * CK_SCAL, rec, CK_SCAL * 4);
+        if (c > 0) tma_store_2d(&tmS, sm + StC::OFF_SIN, 0, (((b * nc + c) * p.heads) + h) * CK_NS);
+        bulk_commit();
+      }
+      mbar_arrive(ready);
+    }
+    mbar_wait(done, (nc - 1) & 1, abort_flag);  // the last update finishes before TMEM is freed
+    if (mt == 0) bulk_wait0();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 64);
+}
+
+// -------------------------------------------------------------------- scan
+struct ScC {
+  static constexpr int KAT = CK_NS / 64;
+  static constexpr int C_BYTES = KAT * 128 * 128;    // 128 query rows
+  static constexpr int B_BYTES = KAT * CK_L * 128;   // up to 256 keys
+  static constexpr int G_BYTES = 4 * 128 * 128;      // 128 rows x 256 keys
+  static constexpr int BG_BYTES = B_BYTES > G_BYTES ? B_BYTES : G_BYTES;
+  static constexpr int X_BYTES = CK_L * 128;
+  static constexpr int S_BYTES = CK_NS * 128;
+  static constexpr int STAGE = X_BYTES + S_BYTES;
+  static constexpr int OFF_C = 0, OFF_B = C_BYTES, OFF_G = OFF_B;  // G replaces B once C.B^T is in TMEM
+  static constexpr int OFF_X = OFF_B + BG_BYTES;                    // 2 stages of x | S_in
+  static constexpr int OFF_Y = OFF_X + 2 * STAGE;                   // z in, y out: 128 rows x 64
+  static constexpr int OFF_SC = OFF_Y + 128 * 128;                  // scalar ring
+  static constexpr int OFF_R = OFF_SC + CK_SR * CK_SCAL * 4;        // row partials of sum y^2
+  static constexpr int OFF_BAR = OFF_R + 4 * 128 * 4;
+  static constexpr int SMEM = 1024 + OFF_BAR + 192;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+
+struct ScMaps {
+  CUtensorMap C, B256, B128, X256, X128, S, Y, Z;
+};
+
+constexpr int SC_MATH = 512;  // 16 math warps: 4 per TMEM lane quadrant
+
+// silu through one MUFU op: x * sigmoid(x) = 0.5 x (1 + tanh(x / 2))
+__device__ __forceinline__ float silu_tanh(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+  return 0.5f * x * (1.0f + t);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(64 + SC_MATH, 1)
+    ssd_scan_mh(const __grid_constant__ ScMaps mp, th_ssd_args p, int nc, int hs, int nsets,
+                const float* __restrict__ scal) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* red = reinterpret_cast<float*>(sm + ScC::OFF_R);  // [4][128] row partials of sum y^2
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + ScC::OFF_BAR);
+  uint64_t* cb_full = bar + 0;
+  uint64_t* cb_done = bar + 1;
+  uint64_t* full = bar + 2;      // [2]
+  uint64_t* empty = bar + 4;     // [2]
+  uint64_t* g_full = bar + 6;
+  uint64_t* g_free = bar + 7;
+  uint64_t* y_full = bar + 8;    // [2]
+  uint64_t* y_empty = bar + 10;  // [2]
+  uint64_t* sc_full = bar + 12;  // [CK_SR]
+  uint64_t* sc_free = bar + 16;  // [CK_SR]
+  uint64_t* z_full = bar + 20;
+  uint64_t* y_ready = bar + 21;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 22);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  // heavy (rows 128-255) CTAs first
+  const int hpg = p.heads / p.ngroups;
+  const int units = p.batch * nc * p.ngroups * nsets;
+  const int qb = (int)blockIdx.x < units ? 1 : 0;
+  int u = qb ? (int)blockIdx.x : (int)blockIdx.x - units;
+  const int set = u % (p.ngroups * nsets);
+  u /= p.ngroups * nsets;
+  const int c = u % nc, b = u / nc;
+  const int g = set / nsets, h0 = g * hpg + (set % nsets) * hs;
+  const int hcount = min(hs, g * hpg + hpg - h0);
+  const int s0 = c * CK_L, len = min(CK_L, p.seq - s0);
+  if (hcount <= 0 || qb * 128 >= len) return;  // nothing to compute (uniform over the CTA)
+  const int nk = qb ? 256 : 128;
+  const bool has_s = c > 0, has_z = p.z != nullptr;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    mbar_init(cb_full, 1);
+    mbar_init(cb_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+      mbar_init(&y_full[i], 1);
+      mbar_init(&y_empty[i], 1);
+    }
+    mbar_init(g_full, 1);
+    mbar_init(g_free, 1);
+    for (int i = 0; i < CK_SR; ++i) { mbar_init(&sc_full[i], 1); mbar_init(&sc_free[i], 1); }
+    mbar_init(z_full, 1);
+    mbar_init(y_ready, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const float* scal_bc = scal + ((int64_t)b * p.heads * nc + c) * CK_SCAL;  // + head * nc * CK_SCAL
+
+  if (warp == 0) {
+    // TMA producer; it also stores each head's y tile and refills the tile with the next head's z
+    if (lane == 0) {
+      const CUtensorMap* tB = qb ? &mp.B256 : &mp.B128;
+      const CUtensorMap* tX = qb ? &mp.X256 : &mp.X128;
+      auto load_xs = [&](int k) {
+        const int s = k & 1;
+        uint8_t* st = sm + ScC::OFF_X + s * ScC::STAGE;
+        mbar_arrive_expect_tx(&full[s], nk * 128 + (has_s ? ScC::S_BYTES : 0));
+        tma_load_3d(st, tX, &full[s], (h0 + k) * CK_P, s0, b);
+        if (has_s)
+          tma_load_2d(st + ScC::X_BYTES, &mp.S, &full[s], 0, (((b * nc + c) * p.heads) + h0 + k) * CK_NS);
+      };
+      auto load_sc = [&](int k) {
+        const int j = k % CK_SR;
+        mbar_arrive_expect_tx(&sc_full[j], CK_SCAL * 4);
+        bulk_load(sm + ScC::OFF_SC + j * CK_SCAL * 4, scal_bc + (int64_t)(h0 + k) * nc * CK_SCAL, CK_SCAL * 4,
+                  &sc_full[j]);
+      };
+      auto store_y = [&](int k) -> bool {  // y of head k is in the tile
+        if (!mbar_wait(y_ready, k & 1, abort_flag)) return false;
+        tma_store_3d(&mp.Y, sm + ScC::OFF_Y, (h0 + k) * CK_P, s0 + qb * 128, b);
+        bulk_commit();
+        bulk_wait_read0();
+        return true;
+      };
+      mbar_arrive_expect_tx(cb_full, ScC::C_BYTES + ScC::KAT * nk * 128);
+      for (int a = 0; a < ScC::KAT; ++a) {
+        tma_load_3d(sm + ScC::OFF_C + a * 128 * 128, &mp.C, cb_full, g * CK_NS + a * 64, s0 + qb * 128, b);
+        tma_load_3d(sm + ScC::OFF_B + a * nk * 128, tB, cb_full, g * CK_NS + a * 64, s0, b);
+      }
+      for (int k = 0; k < min(CK_SR, hcount); ++k) load_sc(k);
+      load_xs(0);
+      bool ok = true;
+      for (int k = 0; ok && k < hcount; ++k) {
+        // x | S_in of head k+1 once the MMA of head k-1 has read its slot
+        if (k + 1 < hcount) {
+          if (k >= 1 && !(ok = mbar_wait(&empty[(k + 1) & 1], ((k - 1) >> 1) & 1, abort_flag))) break;
+          load_xs(k + 1);
+        }
+        // scalars of head k+4 once G of head k has read them
+        if (k + CK_SR < hcount) {
+          if (!(ok = mbar_wait(&sc_free[k % CK_SR], (k / CK_SR) & 1, abort_flag))) break;
+          load_sc(k + CK_SR);
+        }
+        // y of head k-1 out, z of head k in
+        if (k >= 1 && !(ok = store_y(k - 1))) break;
+        if (has_z) {
+          mbar_arrive_expect_tx(z_full, 128 * 128);
+          tma_load_3d(sm + ScC::OFF_Y, &mp.Z, z_full, (h0 + k) * CK_P, s0 + qb * 128, b);
+        }
+      }
+      if (ok) store_y(hcount - 1);
+      bulk_wait0();
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr int fmt = DT<T>::id == TH_BF16 ? 1 : 0;
+      const uint32_t cA = smem_u32(sm + ScC::OFF_C), bA = smem_u32(sm + ScC::OFF_B), gA = smem_u32(sm + ScC::OFF_G);
+      bool ok = mbar_wait(cb_full, 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t id_cb = make_idesc_f16(128, nk, fmt, 0, 0);
+        for (int kk = 0; kk < CK_NS / 16; ++kk) {
+          const uint64_t ad = make_desc_sw128(cA + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = make_desc_sw128(bA + (kk >> 2) * nk * 128 + (kk & 3) * 32, 16, 1024);
+          tc_mma_f16(tmem, ad, bd, id_cb, kk ? 1u : 0u);
+        }
+        tc_commit(cb_done);
+      }
+      constexpr uint32_t id_y = make_idesc_f16(128, 64, fmt, 0, 1);  // B operand (x, S_in) MN-major
+      for (int k = 0; ok && k < hcount; ++k) {
+        const int s = k & 1;
+        ok = mbar_wait(&full[s], (k >> 1) & 1, abort_flag) && mbar_wait(g_full, k & 1, abort_flag) &&
+             (k < 2 || mbar_wait(&y_empty[s], ((k >> 1) - 1) & 1, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t yd = tmem + 256 + s * 128;
+        const uint32_t xA = smem_u32(sm + ScC::OFF_X + s * ScC::STAGE), sA = xA + ScC::X_BYTES;
+        for (int kk = 0; kk < nk / 16; ++kk) {
+          const uint64_t ad = make_desc_sw128(gA + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = make_desc_sw128(xA + kk * 2048, nk * 128, 1024);
+          tc_mma_f16(yd, ad, bd, id_y, kk ? 1u : 0u);
+        }
+        if (has_s) {
+          for (int kk = 0; kk < CK_NS / 16; ++kk) {
+            const uint64_t ad = make_desc_sw128(cA + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = make_desc_sw128(sA + kk * 2048, CK_NS * 128, 1024);
+            tc_mma_f16(yd + 64, ad, bd, id_y, kk ? 1u : 0u);
+          }
+        }
+        tc_commit(g_free);
+        tc_commit(&empty[s]);
+        tc_commit(&y_full[s]);
+      }
+    }
+  } else {
+    // math threads: quadrant q of TMEM lanes (rows), column quarter cq
+    const int mt = tid - 64;
+    const int q = warp & 3, cq = (warp - 2) >> 2;
+    const int r = q * 32 + lane;      // row within the query half (TMEM lane)
+    const int i = qb * 128 + r;       // row within the chunk
+    const int R = qb * 128 + q * 32;  // first row of this warp
+    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+    const int bpq = nk / 128;         // 32-column blocks of G per quarter
+    const int64_t trow = (int64_t)b * p.seq + s0 + i;
+    bool ok = true;
+    float e_prev = 0.f, e_cur = 0.f;
+    for (int k = 0; k <= hcount; ++k) {
+      // ---------------------------------------------------------- G for head k
+      if (k < hcount) {
+        const int j = k % CK_SR;
+        if (k == 0) ok = ok && mbar_wait(cb_done, 0, abort_flag);
+        else ok = ok && mbar_wait(g_free, (k - 1) & 1, abort_flag);
+        ok = ok && mbar_wait(&sc_full[j], (k / CK_SR) & 1, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+          tc_fence_after();
+          const float* cum = reinterpret_cast<const float*>(sm + ScC::OFF_SC + j * CK_SCAL * 4);
+          const float* dts = cum + CK_L;
+          const float* colf = dts + CK_L;
+          const float Dh = colf[CK_L];
+          const float ci = cum[i];
+          e_cur = __expf(ci);
+          uint8_t* gb = sm + ScC::OFF_G;
+          for (int jb = cq * bpq; jb < (cq + 1) * bpq; ++jb) {
+            const int j0 = jb * 32;
+            if (j0 > R) {  // above the diagonal: zeros
+              float zz[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+              for (int e8 = 0; e8 < 32; e8 += 8) store8<T>(reinterpret_cast<T*>(gb + sw128_off(r, j0 + e8, 128)), zz);
+              continue;
+            }
+            const float dref = ci - cum[j0 + 31];  // <= 0 below the diagonal block
+            const bool fact = dref < 80.f;         // exp(ci - cj) = exp(ci - c_ref) exp(c_ref - cj) cannot overflow
+            const float rf = __expf(fact ? dref : 0.f);
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              const int jc = j0 + hf * 16;
+              float v[16];
+              tmem_ld16(tl + jc, v);
+              if (fact) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] *= rf * colf[jc + e];
+              } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] *= __expf(ci - cum[jc + e]) * dts[jc + e];
+              }
+              if (j0 == R) {  // diagonal block: causal mask and the D skip
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                  const int jj = jc + e;
+                  v[e] = jj < i ? v[e] : (jj == i ? v[e] + Dh : 0.f);
+                }
+              }
+#pragma unroll
+              for (int e8 = 0; e8 < 16; e8 += 8)
+                store8<T>(reinterpret_cast<T*>(gb + sw128_off(r, jc + e8, 128)), v + e8);
+            }
+          }
+          fence_proxy_async();
+          tc_fence_before();
+        }
+        named_bar(1, SC_MATH);
+        if (mt == 0) {
+          mbar_arrive(g_full);
+          mbar_arrive(&sc_free[j]);
+        }
+      }
+      // --------------------------------------------------- epilogue of head k-1
+      if (k >= 1) {
+        const int kh = k - 1, s = kh & 1;
+        const int hh = h0 + kh;
+        if (has_z) ok = ok && mbar_wait(z_full, kh & 1, abort_flag);
+        ok = ok && mbar_wait(&y_full[s], (kh >> 1) & 1, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        float ss = 0.f;
+        if (ok) {
+          float yv[16], yo[16];
+          tc_fence_after();
+          const uint32_t ya = tl + 256 + s * 128 + cq * 16;
+          tmem_ld16(ya, yv);
+          if (has_s) tmem_ld16(ya + 64, yo);
+          tc_fence_before();
+          uint8_t* yb = sm + ScC::OFF_Y;  // holds z of this head (when gated); y is written in place
+#pragma unroll
+          for (int c8 = 0; c8 < 2; ++c8) {
+            T* at = reinterpret_cast<T*>(yb + sw128_off(r, cq * 16 + c8 * 8, 128));
+            float zf[8], o[8];
+            if (has_z) load8<T>(at, zf);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              float y = yv[c8 * 8 + e];
+              if (has_s) y += e_prev * yo[c8 * 8 + e];
+              if (has_z) y *= silu_tanh(zf[e]);
+              o[e] = y;
+              const float qv = round_to<T>(y);
+              ss += qv * qv;
+            }
+            store8<T>(at, o);
+          }
+          fence_proxy_async();
+          red[cq * 128 + r] = ss;
+        }
+        named_bar(1, SC_MATH);
+        if (mt == 0) {
+          mbar_arrive(&y_empty[s]);
+          mbar_arrive(y_ready);
+        }
+        if (ok && cq == 0 && i < len && p.gss)
+          p.gss[trow * p.ldgss + hh] = red[r] + red[128 + r] + red[256 + r] + red[384 + r];
+      }
+      e_prev = e_cur;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// Applies to 2-byte dtypes with head_dim 64, state_dim 128, chunk 256,
+// 16-byte aligned rows, dt rows of a multiple of 4 floats and a large enough
+// workspace; returns 1 (not taken) otherwise.
+template <typename T>
+static int ssd_chunk_try(const th_ssd_args* a, cudaStream_t st, int* rc) {
+  if (a->head_dim != CK_P || a->chunk != CK_L || a->state_dim != CK_NS) return 1;
+  if (!aligned16(a->x) || !aligned16(a->B) || !aligned16(a->C) || !aligned16(a->out) || !aligned16(a->dt) ||
+      a->ldx % 8 || a->ldb % 8 || a->ldc % 8 || a->ldo % 8 || a->lddt % 4)
+    return 1;
+  if (a->z && (!aligned16(a->z) || a->ldz % 8)) return 1;
+  if (!aligned16(a->workspace) || a->workspace_bytes < ck_ws_bytes(a->batch, a->seq, a->heads, CK_NS)) return 1;
+  const int nc = (a->seq + CK_L - 1) / CK_L;
+  float* scal = reinterpret_cast<float*>(a->workspace);
+  void* sin = reinterpret_cast<uint8_t*>(a->workspace) + ck_scal_bytes(a->batch, a->heads, nc);
+  const uint64_t gw = (uint64_t)a->ngroups * CK_NS, xw = (uint64_t)a->heads * CK_P;
+  const uint64_t S = (uint64_t)a->seq, Bt = (uint64_t)a->batch;
+  ScMaps m;
+  CUtensorMap tdt;
+  int r = make_tmap_3d(&m.B256, a->B, a->dtype, gw, S, Bt, a->ldb * 2, S * a->ldb * 2, 64, 256);
+  if (!r) r = make_tmap_3d(&m.B128, a->B, a->dtype, gw, S, Bt, a->ldb * 2, S * a->ldb * 2, 64, 128);
+  if (!r) r = make_tmap_3d(&m.C, a->C, a->dtype, gw, S, Bt, a->ldc * 2, S * a->ldc * 2, 64, 128);
+  if (!r) r = make_tmap_3d(&m.X256, a->x, a->dtype, xw, S, Bt, a->ldx * 2, S * a->ldx * 2, 64, 256);
+  if (!r) r = make_tmap_3d(&m.X128, a->x, a->dtype, xw, S, Bt, a->ldx * 2, S * a->ldx * 2, 64, 128);
+  if (!r) r = make_tmap_3d(&m.Y, a->out, a->dtype, xw, S, Bt, a->ldo * 2, S * a->ldo * 2, 64, 128);
+  m.Z = m.Y;
+  if (!r && a->z) r = make_tmap_3d(&m.Z, a->z, a->dtype, xw, S, Bt, a->ldz * 2, S * a->ldz * 2, 64, 128);
+  if (!r)
+    r = make_tmap_2d(&m.S, sin, a->dtype, CK_P, (uint64_t)a->batch * nc * a->heads * CK_NS, CK_P * 2, 64, CK_NS, true);
+  if (!r)
+    r = make_tmap_3d(&tdt, a->dt, TH_F32, (uint64_t)a->heads, S, Bt, a->lddt * 4, S * a->lddt * 4, 4, 256, false);
+  if (r) { *rc = r; return 0; }
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(ssd_state_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, StC::SMEM);
+    cudaFuncSetAttribute(ssd_scan_mh<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScC::SMEM);
+    set = true;
+  }
+  ssd_state_tc<T><<<dim3((unsigned)a->heads, (unsigned)a->batch), 320, StC::SMEM, st>>>(m.B256, m.X256, tdt, m.S, *a,
+                                                                                          nc, scal);
+  *rc = check_launch("th_ssd(chunk states, tcgen05)");
+  if (*rc) return 0;
+  // head sets: about one heavy CTA per SM
+  const int hpg = a->heads / a->ngroups;
+  const int per = a->batch * nc * a->ngroups;
+  int nsets = per >= sm_count() ? 1 : sm_count() / per;
+  nsets = nsets < 1 ? 1 : (nsets > hpg ? hpg : nsets);
+  const int hs = (hpg + nsets - 1) / nsets;
+  nsets = (hpg + hs - 1) / hs;
+  const int units = per * nsets;
+  ssd_scan_mh<T><<<2 * units, 64 + SC_MATH, ScC::SMEM, st>>>(m, *a, nc, hs, nsets, scal);
+  *rc = check_launch("th_ssd(scan, tcgen05 multi-head)");
+  return 0;
+}
+
+}  // namespace th
