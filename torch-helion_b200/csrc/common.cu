@@ -4,7 +4,10 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <string.h>
+
 #include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 
@@ -36,6 +39,54 @@ int check_launch(const char* what) {
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::once_flag g_encode_once;
 
+// Encoded tensor maps, keyed by everything that goes into the encoding.  A
+// runtime that replays the same launches re-encodes nothing; a reused
+// address with the same geometry yields the same map, so stale entries are
+// harmless.
+struct TmapKey {
+  const void* base;
+  uint64_t dims[3], strides[2];
+  uint32_t box[2];
+  int32_t dtype, rank, swz, pad;
+  bool operator==(const TmapKey& o) const { return memcmp(this, &o, sizeof(TmapKey)) == 0; }
+};
+static_assert(sizeof(TmapKey) % 8 == 0, "hashed as 64-bit words");
+struct TmapKeyHash {
+  size_t operator()(const TmapKey& k) const {
+    uint64_t w[sizeof(TmapKey) / 8];
+    memcpy(w, &k, sizeof(k));
+    uint64_t h = 1469598103934665603ull;
+    for (size_t i = 0; i < sizeof(TmapKey) / 8; ++i) h = (h ^ w[i]) * 1099511628211ull;
+    return (size_t)h;
+  }
+};
+static std::mutex g_tmap_mu;
+static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> g_tmap_cache;
+
+static TmapKey tmap_key(const void* base, int dtype, int rank, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                        uint64_t s2, uint32_t b0, uint32_t b1, bool swz) {
+  TmapKey k;
+  memset(&k, 0, sizeof(k));
+  k.base = base;
+  k.dims[0] = d0; k.dims[1] = d1; k.dims[2] = d2;
+  k.strides[0] = s1; k.strides[1] = s2;
+  k.box[0] = b0; k.box[1] = b1;
+  k.dtype = dtype; k.rank = rank; k.swz = swz ? 1 : 0;
+  return k;
+}
+static bool tmap_lookup(const TmapKey& k, CUtensorMap* out) {
+  std::lock_guard<std::mutex> lock(g_tmap_mu);
+  auto it = g_tmap_cache.find(k);
+  if (it == g_tmap_cache.end()) return false;
+  *out = it->second;
+  return true;
+}
+static void tmap_insert(const TmapKey& k, const CUtensorMap& m) {
+  std::lock_guard<std::mutex> lock(g_tmap_mu);
+  if (g_tmap_cache.size() >= 4096) g_tmap_cache.clear();
+  g_tmap_cache.emplace(k, m);
+}
+
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
   std::call_once(g_encode_once, [] {
@@ -48,6 +99,8 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, 
   if (!g_encode) return fail(TH_ELAUNCH, "cuTensorMapEncodeTiled is not available from the driver");
   if (!aligned16(base)) return fail(TH_EALIGN, "TMA base address %p is not 16-byte aligned", base);
   if (row_stride_bytes % 16) return fail(TH_EALIGN, "TMA row stride %llu B is not a multiple of 16", (unsigned long long)row_stride_bytes);
+  const TmapKey key = tmap_key(base, dtype, 2, inner, outer, 0, row_stride_bytes, 0, box_inner, box_outer, swizzle128);
+  if (tmap_lookup(key, map)) return TH_OK;
   CUtensorMapDataType dt = dtype == TH_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                            : dtype == TH_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -59,13 +112,17 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, 
                         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TH_ELAUNCH, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  tmap_insert(key, *map);
   return TH_OK;
 }
 
 int make_tmap_3d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t rows, uint64_t planes,
                  uint64_t row_stride_bytes, uint64_t plane_stride_bytes, uint32_t box_inner, uint32_t box_rows,
                  bool swizzle128) {
-  CUtensorMap probe;  // resolves the driver entry point once
+  const TmapKey key = tmap_key(base, dtype, 3, inner, rows, planes, row_stride_bytes, plane_stride_bytes, box_inner,
+                               box_rows, swizzle128);
+  if (tmap_lookup(key, map)) return TH_OK;
+  CUtensorMap probe;  // resolves the driver entry point once and checks the 2-D part
   int rc = make_tmap_2d(&probe, base, dtype, inner, rows, row_stride_bytes, box_inner, box_rows, swizzle128);
   if (rc) return rc;
   if (plane_stride_bytes % 16) return fail(TH_EALIGN, "TMA plane stride %llu B is not a multiple of 16", (unsigned long long)plane_stride_bytes);
@@ -80,6 +137,7 @@ int make_tmap_3d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, 
                         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TH_ELAUNCH, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  tmap_insert(key, *map);
   return TH_OK;
 }
 

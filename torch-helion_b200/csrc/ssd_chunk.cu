@@ -443,22 +443,30 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
           const float ci = cum[i];
           e_cur = __expf(ci);
           uint8_t* gb = sm + ScC::OFF_G;
-          for (int jb = cq * bpq; jb < (cq + 1) * bpq; ++jb) {
-            const int j0 = jb * 32;
+          // this quarter's 32-column blocks (2 heavy / 1 light); per block both TMEM loads, one wait
+          const int jb0 = cq * bpq;
+          for (int bb = 0; bb < bpq; ++bb) {
+            const int j0 = (jb0 + bb) * 32;
             if (j0 > R) {  // above the diagonal: zeros
               float zz[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
               for (int e8 = 0; e8 < 32; e8 += 8) store8<T>(reinterpret_cast<T*>(gb + sw128_off(r, j0 + e8, 128)), zz);
               continue;
             }
+            uint32_t raw[2][16];
+            tmem_ld16_issue(tl + j0, raw[0]);
+            tmem_ld16_issue(tl + j0 + 16, raw[1]);
             const float dref = ci - cum[j0 + 31];  // <= 0 below the diagonal block
             const bool fact = dref < 80.f;         // exp(ci - cj) = exp(ci - c_ref) exp(c_ref - cj) cannot overflow
             const float rf = __expf(fact ? dref : 0.f);
+            tmem_wait_ld(raw[0]);
+            tmem_wait_ld(raw[1]);
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
               const int jc = j0 + hf * 16;
               float v[16];
-              tmem_ld16(tl + jc, v);
+#pragma unroll
+              for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(raw[hf][e]);
               if (fact) {
 #pragma unroll
                 for (int e = 0; e < 16; ++e) v[e] *= rf * colf[jc + e];
@@ -482,7 +490,7 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
           tc_fence_before();
         }
         named_bar(1, SC_MATH);
-        if (mt == 0) {
+        if (mt == SC_MATH - 1) {  // a thread that issues no global stores: its arrive releases nothing slow
           mbar_arrive(g_full);
           mbar_arrive(&sc_free[j]);
         }
@@ -496,12 +504,17 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
         ok = __all_sync(0xffffffffu, ok);
         float ss = 0.f;
         if (ok) {
-          float yv[16], yo[16];
+          uint32_t ry[16], ro[16];
           tc_fence_after();
           const uint32_t ya = tl + 256 + s * 128 + cq * 16;
-          tmem_ld16(ya, yv);
-          if (has_s) tmem_ld16(ya + 64, yo);
+          tmem_ld16_issue(ya, ry);
+          if (has_s) tmem_ld16_issue(ya + 64, ro);
+          tmem_wait_ld(ry);
+          tmem_wait_ld(ro);
           tc_fence_before();
+          float yv[16], yo[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) { yv[e] = __uint_as_float(ry[e]); yo[e] = __uint_as_float(ro[e]); }
           uint8_t* yb = sm + ScC::OFF_Y;  // holds z of this head (when gated); y is written in place
 #pragma unroll
           for (int c8 = 0; c8 < 2; ++c8) {
@@ -523,7 +536,7 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
           red[cq * 128 + r] = ss;
         }
         named_bar(1, SC_MATH);
-        if (mt == 0) {
+        if (mt == SC_MATH - 1) {
           mbar_arrive(&y_empty[s]);
           mbar_arrive(y_ready);
         }
