@@ -193,11 +193,84 @@ __device__ __forceinline__ float finish_chunk(float* v, int row, int oc, int n_o
   return ss;
 }
 
-// Epilogue of one accumulator row (this thread) of a 128 x BN tile.
+// Epilogue variants compiled as separate kernels (smaller code per kernel).
+constexpr int EPI_ROPE = 1, EPI_SWIGLU = 2, EPI_RES = 4;
+
+// Residual of one 32-column chunk of this thread's row, as raw 16-byte loads.
+template <typename T>
+__device__ __forceinline__ void res_issue(uint4 (&r)[4], int row, bool row_ok, int col, const EpiParams& ep) {
+  const T* res = reinterpret_cast<const T*>(ep.residual) + (int64_t)row * ep.ld_res;
+#pragma unroll
+  for (int e8 = 0; e8 < 4; ++e8) {
+    const int c = col + e8 * 8;
+    r[e8] = (row_ok && c < ep.tail_begin && c < ep.n) ? *reinterpret_cast<const uint4*>(res + c) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Residual epilogue (plain GEMM + residual, optional row scale / activation):
+// the residual of chunk c+2 is in flight while chunk c is stored, and the
+// first two chunks were issued before the accumulator was ready.
 template <typename T, int BN>
+__device__ __forceinline__ void epilogue_row_res(uint32_t tbase, int row, bool row_ok, float rs, int n0,
+                                                 const EpiParams& ep, uint4 (&rb)[3][4]) {
+  const int n_out = ep.n;
+  T* d = reinterpret_cast<T*>(ep.d);
+  float ss = 0.f;
+#pragma unroll
+  for (int ci = 0; ci < BN / 32; ++ci) {
+    const int c = ci * 32, col = n0 + c;
+    if (ci + 2 < BN / 32) res_issue<T>(rb[(ci + 2) % 3], row, row_ok, col + 64, ep);
+    float v[32];
+    tmem_ld32(tbase + c, v);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] *= rs;
+    if (ep.act != TH_ACT_NONE && col < ep.act_end && col + 32 > ep.act_begin) {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int cc = col + e;
+        if (cc >= ep.act_begin && cc < ep.act_end) {
+          float x = v[e] + (ep.bias ? ep.bias[cc - ep.act_begin] : 0.f);
+          v[e] = ep.act == TH_ACT_SILU ? silu_f(x) : softplus_f(x);
+        }
+      }
+    }
+    if (row_ok) {
+#pragma unroll
+      for (int e8 = 0; e8 < 4; ++e8) {
+        const int cc = col + e8 * 8;
+        if (cc >= n_out) break;
+        if (cc >= ep.tail_begin) {
+          float* o2 = ep.out2 + (int64_t)row * ep.ld_out2 + (cc - ep.tail_begin);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (cc + e < n_out) o2[e] = v[e8 * 8 + e];
+          continue;
+        }
+        const uint4 u = rb[ci % 3][e8];
+        const T* rh = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e8 * 8 + e] += to_f32(rh[e]);
+        store8<T>(d + (int64_t)row * ep.ldd + cc, v + e8 * 8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float q = round_to<T>(v[e8 * 8 + e]);
+          ss += q * q;
+        }
+      }
+    }
+    if ((ci & 1) == 1) {
+      const int g0 = col - 32;  // first column of this 64-column group
+      if (ep.ss_out && row_ok && g0 < n_out && g0 < ep.tail_begin) ep.ss_out[(int64_t)row * ep.ss_ld + (g0 >> 6)] = ss;
+      ss = 0.f;
+    }
+  }
+}
+
+// Epilogue of one accumulator row (this thread) of a 128 x BN tile.
+template <typename T, int BN, int EPI>
 __device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_ok, float rs, int n0,
                                              const EpiParams& ep) {
-  if (ep.swiglu) {
+  if constexpr ((EPI & EPI_SWIGLU) != 0) {
     const int n_out = ep.n / 2;
     for (int g = 0; g < BN / 128; ++g) {
       float ss = 0.f;
@@ -233,7 +306,8 @@ __device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_o
         }
       }
     }
-    if (ep.rope_cos && col < ep.rope_end && col + 32 > ep.rope_begin) {
+    if constexpr ((EPI & EPI_ROPE) == 0) {
+    } else if (col < ep.rope_end && col + 32 > ep.rope_begin) {
       const int hd = ep.rope_hd, half = hd >> 1;
       const int64_t pos = row_ok ? (int64_t)(row % ep.rope_seq) * hd : 0;
       if (half >= 32) {  // the partner 32 columns are a whole chunk away
@@ -268,7 +342,7 @@ __device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_o
   }
 }
 
-template <typename T, int BN>
+template <typename T, int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiParams ep,
                    int K, int tiles_m, int tiles_n) {
@@ -328,11 +402,15 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---- MMA issuer
-      constexpr uint32_t idesc = make_idesc_f16(128, BN, DT<T>::id == TH_BF16 ? 1 : 0, 0, 0);
+      constexpr int fmt = DT<T>::id == TH_BF16 ? 1 : 0;
       int it = 0, i = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++i) {
         const int acc = i & 1, use = i >> 1;
+        // the last column tile multiplies only its live columns (N rounded up to 16)
+        const int nlive = ep.n - (tile % tiles_n) * BN;
+        const int ntile = nlive >= BN ? BN : ((nlive + 15) & ~15);
+        const uint32_t idesc = make_idesc_f16(128, ntile, fmt, 0, 0);
         if (!mbar_wait(&tempty[acc], (use & 1) ^ 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * BN);
@@ -362,11 +440,9 @@ __global__ void __launch_bounds__(192, 1)
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++i) {
       const int acc = i & 1, use = i >> 1;
       const int m0 = (tile / tiles_n) * C::BM, n0 = (tile % tiles_n) * BN;
-      if (!mbar_wait(&tfull[acc], use & 1, abort_flag)) break;
-      __syncwarp();
-      tc_fence_after();
       const int row = m0 + rl;
       const bool row_ok = row < ep.m;
+      // row scale and the first residual chunks are fetched while the accumulator fills
       float rs = 1.f;
       if (ep.rs_parts && row_ok) {
         const float* pp = ep.rs_parts + (int64_t)row * ep.rs_nparts;
@@ -374,8 +450,17 @@ __global__ void __launch_bounds__(192, 1)
         for (int k = 0; k < ep.rs_nparts; ++k) sacc += pp[k];
         rs = rsqrtf(sacc * ep.rs_inv_k + ep.rs_eps);
       }
+      uint4 rb[3][4];
+      if constexpr ((EPI & EPI_RES) != 0) {
+        res_issue<T>(rb[0], row, row_ok, n0, ep);
+        res_issue<T>(rb[1], row, row_ok, n0 + 32, ep);
+      }
+      if (!mbar_wait(&tfull[acc], use & 1, abort_flag)) break;
       __syncwarp();
-      epilogue_row<T, BN>(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN), row, row_ok, rs, n0, ep);
+      tc_fence_after();
+      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      if constexpr ((EPI & EPI_RES) != 0) epilogue_row_res<T, BN>(tb, row, row_ok, rs, n0, ep, rb);
+      else epilogue_row<T, BN, EPI>(tb, row, row_ok, rs, n0, ep);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -440,7 +525,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
 }
 
 // ------------------------------------------------------------------- host
-template <typename T, int BN>
+template <typename T, int BN, int EPI>
 static int launch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st) {
   using C = TcCfg<BN>;
   CUtensorMap ta, tb;
@@ -450,17 +535,26 @@ static int launch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st
   if (rc) return rc;
   static bool attr_set = false;  // once per instantiation (keeps it out of CUDA-graph captures)
   if (!attr_set) {
-    cudaFuncSetAttribute(gemm_tc_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_tc_kernel<T, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     attr_set = true;
   }
   const int tiles_m = (int)((a->m + C::BM - 1) / C::BM), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n;
   const int grid = ntiles < sm_count() ? ntiles : sm_count();
-  gemm_tc_kernel<T, BN><<<grid, 192, C::SMEM_BYTES, st>>>(ta, tb, ep, (int)a->k, tiles_m, tiles_n);
+  gemm_tc_kernel<T, BN, EPI><<<grid, 192, C::SMEM_BYTES, st>>>(ta, tb, ep, (int)a->k, tiles_m, tiles_n);
   return check_launch("th_gemm(tcgen05)");
 }
 
 static bool is_al16(const void* p) { return p == nullptr || aligned16(p); }
+
+template <typename T>
+static int dispatch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st, bool wide) {
+  if (a->swiglu)
+    return wide ? launch_tc<T, 256, EPI_SWIGLU>(a, ep, st) : launch_tc<T, 128, EPI_SWIGLU>(a, ep, st);
+  if (a->rope_cos) return wide ? launch_tc<T, 256, EPI_ROPE>(a, ep, st) : launch_tc<T, 128, EPI_ROPE>(a, ep, st);
+  if (a->residual) return wide ? launch_tc<T, 256, EPI_RES>(a, ep, st) : launch_tc<T, 128, EPI_RES>(a, ep, st);
+  return wide ? launch_tc<T, 256, 0>(a, ep, st) : launch_tc<T, 128, 0>(a, ep, st);
+}
 
 }  // namespace th
 
@@ -510,8 +604,12 @@ extern "C" int th_gemm(const th_gemm_args* a, void* stream) {
   // tcgen05 path: TMA wants 16-B aligned bases and row strides
   if (!aligned16(a->a) || !aligned16(a->w) || a->lda % 8 || a->ldw % 8)
     return fail(TH_EALIGN, "th_gemm: a/w must be 16-B aligned with lda, ldw multiples of 8");
-  const bool wide = a->n >= 256 && (!a->rope_cos || 256 % a->rope_head_dim == 0);
-  if (a->dtype == TH_BF16)
-    return wide ? launch_tc<__nv_bfloat16, 256>(a, ep, st) : launch_tc<__nv_bfloat16, 128>(a, ep, st);
-  return wide ? launch_tc<__half, 256>(a, ep, st) : launch_tc<__half, 128>(a, ep, st);
+  bool wide = a->n >= 256 && (!a->rope_cos || 256 % a->rope_head_dim == 0);
+  if (wide) {  // narrow tiles when they cut the wave-quantised work by a fifth or more
+    const int64_t tm = (a->m + 127) / 128, sms = sm_count();
+    const int64_t r256 = (tm * ((a->n + 255) / 256) + sms - 1) / sms, r128 = (tm * ((a->n + 127) / 128) + sms - 1) / sms;
+    if (r128 * 128 * 5 <= r256 * 256 * 4) wide = false;
+  }
+  if (a->dtype == TH_BF16) return dispatch_tc<__nv_bfloat16>(a, ep, st, wide);
+  return dispatch_tc<__half>(a, ep, st, wide);
 }
