@@ -86,7 +86,16 @@ template <> __device__ __forceinline__ void store8<__half>(__half* p, const floa
 // Value as it will be stored (rounded to T), back in fp32.
 template <typename T> __device__ __forceinline__ float round_to(float v) { return to_f32(from_f32<T>(v)); }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// x * sigmoid(x); the fast divide is exact to 2 ulp and gives -0 when exp(-x) overflows
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+// x * sigmoid(x) with one MUFU op: 0.5 x (1 + tanh(x / 2)).  tanh.approx is
+// accurate to about 2^-11, below the rounding of a 2-byte output; used only
+// where the result is stored in bf16/fp16.
+__device__ __forceinline__ float silu_tanh(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+  return 0.5f * x * (1.0f + t);
+}
 // torch.nn.functional.softplus(beta=1, threshold=20)
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(__expf(x)); }
 

@@ -76,67 +76,213 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, i
 }
 
 // ------------------------------------------------------ causal conv1d
-// One thread = CONV_TPT consecutive tokens x 8 consecutive channels.  A 32x8
-// block covers 256 channels x (8*CONV_TPT) tokens: a warp reads 512
-// contiguous bytes of a row, the weights (8 channels x width taps) are read
-// once per thread as float4s, and the CONV_TPT+width-1 input rows a thread
-// needs are independent loads.
-constexpr int CONV_TPT = 4;
+// One thread = CONV_TPT consecutive tokens x 8 consecutive channels; a
+// 32 x CONV_TY block covers 256 channels x (CONV_TY*CONV_TPT) tokens.  A warp reads 512
+// contiguous bytes of a row; a thread keeps its CONV_TPT+width-1 input rows
+// packed (16 bytes each) in registers, all issued before the first use, so
+// the halo is re-read only width-1 times per CONV_TPT tokens and the weights
+// (8 channels x width taps, float4 loads) once per CONV_TPT tokens.
+constexpr int CONV_TPT = 8, CONV_TY = 4;  // tokens per thread, token groups per block
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& u, float* v) {
+  if constexpr (sizeof(T) == 2) {
+    const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = to_f32(h[e]);
+  }
+}
+
 template <typename T, int W>
-__global__ void __launch_bounds__(256) conv1d_kernel(const T* __restrict__ x, int64_t ldx, const float* __restrict__ w,
+__global__ void __launch_bounds__(128) conv1d_kernel(const T* __restrict__ x, int64_t ldx, const float* __restrict__ w,
                                                      const float* __restrict__ bias, T* __restrict__ y, int64_t ldy,
                                                      int batch, int seq, int channels, int act) {
   const int c0 = (blockIdx.x * 32 + threadIdx.x) * 8;
-  const int64_t t0 = ((int64_t)blockIdx.y * 8 + threadIdx.y) * CONV_TPT;  // first token (global row)
+  const int64_t t0 = ((int64_t)blockIdx.y * CONV_TY + threadIdx.y) * CONV_TPT;  // first token (global row)
   const int64_t T_ = (int64_t)batch * seq;
+  // the block's 256 x W weights, tap-major in shared memory (coalesced global
+  // reads; a thread then reads its 8 channels of one tap as two float4)
+  __shared__ __align__(16) float wsm[W][256];
+  {
+    const int cb = blockIdx.x * 256;
+    for (int i = threadIdx.y * 32 + threadIdx.x; i < 256 * W; i += 32 * CONV_TY) {
+      const int cl = i / W, j = i % W;
+      wsm[j][cl] = cb + cl < channels ? w[(int64_t)(cb + cl) * W + j] : 0.f;
+    }
+  }
+  __syncthreads();
   if (c0 >= channels || t0 >= T_) return;
+  // global rows t0-(W-1) .. t0+CONV_TPT-1 (a thread's tokens may straddle two
+  // sequences; taps that would reach into the previous sequence are masked)
+  constexpr int R = CONV_TPT + W - 1;
   float wt[8][W];
-  if constexpr (W == 4) {
+  float bi[8];
+  if constexpr (sizeof(T) == 2) {
+    uint4 raw[R];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float4 q = *reinterpret_cast<const float4*>(w + (int64_t)(c0 + e) * 4);
-      wt[e][0] = q.x; wt[e][1] = q.y; wt[e][2] = q.z; wt[e][3] = q.w;
+    for (int r = 0; r < R; ++r) {
+      const int64_t tr = t0 - (W - 1) + r;
+      raw[r] = (tr >= 0 && tr < T_) ? *reinterpret_cast<const uint4*>(x + tr * ldx + c0) : make_uint4(0, 0, 0, 0);
+    }
+    const int cl = threadIdx.x * 8;
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      const float4 a = *reinterpret_cast<const float4*>(&wsm[j][cl]);
+      const float4 b = *reinterpret_cast<const float4*>(&wsm[j][cl + 4]);
+      wt[0][j] = a.x; wt[1][j] = a.y; wt[2][j] = a.z; wt[3][j] = a.w;
+      wt[4][j] = b.x; wt[5][j] = b.y; wt[6][j] = b.z; wt[7][j] = b.w;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) bi[e] = bias ? bias[c0 + e] : 0.f;
+    float in[R][8];
+#pragma unroll
+    for (int r = 0; r < R; ++r) unpack8<T>(raw[r], in[r]);
+    int sk = (int)(t0 % seq);  // position of token t0 in its sequence
+#pragma unroll
+    for (int k = 0; k < CONV_TPT; ++k, ++sk) {
+      if (sk == seq) sk = 0;
+      const int64_t t = t0 + k;
+      if (t >= T_) break;
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = bi[e];
+      if (sk >= W - 1) {
+#pragma unroll
+        for (int j = 0; j < W; ++j)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] = fmaf(wt[e][j], in[k + j][e], o[e]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          if (sk - (W - 1) + j < 0) continue;  // zero left padding of the causal conv
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] = fmaf(wt[e][j], in[k + j][e], o[e]);
+        }
+      }
+      if (act == TH_ACT_SILU) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = silu_f(o[e]);
+      }
+      store8<T>(y + t * ldy + c0, o);
     }
   } else {
 #pragma unroll
     for (int e = 0; e < 8; ++e)
 #pragma unroll
       for (int j = 0; j < W; ++j) wt[e][j] = w[(int64_t)(c0 + e) * W + j];
-  }
-  float bi[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) bi[e] = bias ? bias[c0 + e] : 0.f;
-  // global rows t0-(W-1) .. t0+CONV_TPT-1 (a thread's tokens may straddle two
-  // sequences; taps that would reach into the previous sequence are masked)
-  constexpr int R = CONV_TPT + W - 1;
-  float in[R][8];
+    for (int e = 0; e < 8; ++e) bi[e] = bias ? bias[c0 + e] : 0.f;
+    for (int k = 0; k < CONV_TPT; ++k) {
+      const int64_t t = t0 + k;
+      if (t >= T_) break;
+      const int sk = (int)(t % seq);
+      float o[8];
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int64_t tr = t0 - (W - 1) + r;
-    if (tr >= 0 && tr < T_) {
-      load8<T>(x + tr * ldx + c0, in[r]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) in[r][e] = 0.f;
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < CONV_TPT; ++k) {
-    const int64_t t = t0 + k;
-    if (t >= T_) break;
-    const int sk = (int)(t % seq);  // position of this token in its sequence
-    float o[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float acc = bi[e];
-#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = bi[e];
       for (int j = 0; j < W; ++j) {
-        const bool in_seq = sk - (W - 1) + j >= 0;  // zero left padding of the causal conv
-        acc = in_seq ? fmaf(wt[e][j], in[k + j][e], acc) : acc;
+        const int64_t tr = t - (W - 1) + j;
+        if (sk - (W - 1) + j < 0) continue;
+        float in[8];
+        load8<T>(x + tr * ldx + c0, in);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = fmaf(wt[e][j], in[e], o[e]);
       }
-      o[e] = act == TH_ACT_SILU ? silu_f(acc) : acc;
+      if (act == TH_ACT_SILU) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = silu_f(o[e]);
+      }
+      store8<T>(y + t * ldy + c0, o);
     }
-    store8<T>(y + t * ldy + c0, o);
+  }
+}
+
+// TMA-staged causal conv (2-byte dtypes): a persistent block streams tiles
+// of 64 tokens x 256 channels through a 3-stage shared-memory ring.  Each
+// tile is one TMA box of (64 + width - 1) rows starting width-1 rows before
+// the tile; the 3-D map [batch][seq][channels] zero-fills rows before the
+// sequence start, which is exactly the causal left padding, and rows past
+// its end.  Thread = 8 channels x 8 tokens, read from shared memory
+// conflict-free (a warp reads one 512-byte row), written with coalesced
+// 16-byte stores.
+constexpr int CT_TOK = 64, CT_CH = 256, CT_STAGES = 3;
+
+template <int W>
+struct CtCfg {
+  static constexpr int ROWS = CT_TOK + W - 1;
+  static constexpr int TILE = ((ROWS * CT_CH * 2 + 127) / 128) * 128;
+  static constexpr int SMEM = 128 + CT_STAGES * TILE + 64;
+};
+
+template <typename T, int W>
+__global__ void __launch_bounds__(256, 2) conv1d_tma(const __grid_constant__ CUtensorMap tmX, const float* __restrict__ w,
+                                                     const float* __restrict__ bias, T* __restrict__ y, int64_t ldy,
+                                                     int seq, int channels, int act, int ncb, int nsb, int ntiles) {
+  using Cf = CtCfg<W>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + CT_STAGES * Cf::TILE);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + CT_STAGES);
+  const int tid = threadIdx.x, tx = tid & 31, ty = tid >> 5;
+  // gridDim.x is a multiple of ncb, so every tile of this block has the same channel block
+  const int cb = blockIdx.x % ncb;
+  auto issue = [&](int k) {  // k-th tile of this block into stage k % CT_STAGES
+    const int tile = blockIdx.x + k * gridDim.x;
+    if (tile >= ntiles) return;
+    const int rest = tile / ncb, sb = rest % nsb, b = rest / nsb;
+    uint64_t* br = &bar[k % CT_STAGES];
+    mbar_arrive_expect_tx(br, Cf::ROWS * CT_CH * 2);
+    tma_load_3d(sm + (k % CT_STAGES) * Cf::TILE, &tmX, br, cb * CT_CH, sb * CT_TOK - (W - 1), b);
+  };
+  if (tid == 0) {
+    for (int i = 0; i < CT_STAGES; ++i) mbar_init(&bar[i], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    for (int k = 0; k < CT_STAGES; ++k) issue(k);
+  }
+  const int c0 = cb * CT_CH + tx * 8;
+  const bool live = c0 < channels;
+  float wt[8][W], bi[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+#pragma unroll
+    for (int j = 0; j < W; ++j) wt[e][j] = live ? w[(int64_t)(c0 + e) * W + j] : 0.f;
+    bi[e] = (live && bias) ? bias[c0 + e] : 0.f;
+  }
+  __syncthreads();
+  bool ok = true;
+  for (int k = 0;; ++k) {
+    const int tile = blockIdx.x + k * gridDim.x;
+    if (tile >= ntiles) break;
+    const int rest = tile / ncb, sb = rest % nsb, b = rest / nsb;
+    ok = ok && mbar_wait(&bar[k % CT_STAGES], (k / CT_STAGES) & 1, abort_flag);
+    if (ok && live) {
+      const uint8_t* st = sm + (k % CT_STAGES) * Cf::TILE;
+      T* yb = y + ((int64_t)b * seq) * ldy + c0;
+#pragma unroll
+      for (int hv = 0; hv < 2; ++hv) {  // 4 tokens at a time keeps the rows in registers
+        const int r0 = ty * 8 + hv * 4;
+        float in[4 + W - 1][8];
+#pragma unroll
+        for (int r = 0; r < 4 + W - 1; ++r)
+          load8<T>(reinterpret_cast<const T*>(st + (size_t)(r0 + r) * (CT_CH * 2) + tx * 16), in[r]);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const int sp = sb * CT_TOK + r0 + kk;
+          if (sp >= seq) break;
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            float acc = bi[e];
+#pragma unroll
+            for (int j = 0; j < W; ++j) acc = fmaf(wt[e][j], in[kk + j][e], acc);
+            o[e] = act == TH_ACT_SILU ? silu_tanh(acc) : acc;
+          }
+          store8<T>(yb + (int64_t)sp * ldy, o);
+        }
+      }
+    }
+    __syncthreads();  // everyone is done with this stage
+    if (tid == 0 && ok) issue(k + CT_STAGES);
   }
 }
 
@@ -205,13 +351,46 @@ extern "C" int th_rmsnorm(const th_rmsnorm_args* a, void* stream) {
 template <typename T, int W>
 static void launch_conv(const th_conv1d_args* a, cudaStream_t st) {
   const int64_t T_ = (int64_t)a->batch * a->seq;
-  dim3 grid((unsigned)((a->channels + 255) / 256), (unsigned)((T_ + 8 * th::CONV_TPT - 1) / (8 * th::CONV_TPT)));
-  th::conv1d_kernel<T, W><<<grid, dim3(32, 8), 0, st>>>((const T*)a->x, a->ldx, a->w, a->bias, (T*)a->y, a->ldy,
+  constexpr int tok = th::CONV_TY * th::CONV_TPT;
+  dim3 grid((unsigned)((a->channels + 255) / 256), (unsigned)((T_ + tok - 1) / tok));
+  th::conv1d_kernel<T, W><<<grid, dim3(32, th::CONV_TY), 0, st>>>((const T*)a->x, a->ldx, a->w, a->bias, (T*)a->y, a->ldy,
                                                         a->batch, a->seq, a->channels, a->act);
+}
+
+template <typename T, int W>
+static int launch_conv_tma(const th_conv1d_args* a, cudaStream_t st) {
+  using Cf = th::CtCfg<W>;
+  CUtensorMap tm;
+  const uint64_t S = (uint64_t)a->seq;
+  int rc = th::make_tmap_3d(&tm, a->x, a->dtype, (uint64_t)a->channels, S, (uint64_t)a->batch, (uint64_t)a->ldx * 2,
+                            S * a->ldx * 2, th::CT_CH, Cf::ROWS, false);
+  if (rc) return rc;
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(th::conv1d_tma<T, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+    set = true;
+  }
+  const int ncb = (a->channels + th::CT_CH - 1) / th::CT_CH, nsb = (a->seq + th::CT_TOK - 1) / th::CT_TOK;
+  const int ntiles = ncb * nsb * a->batch;
+  // a multiple of ncb blocks (each block keeps one channel block and its weights), two per SM
+  int grid = (2 * th::sm_count() / ncb) * ncb;
+  if (grid < ncb) grid = ncb;
+  if (grid > ntiles) grid = ntiles;
+  th::conv1d_tma<T, W><<<grid, 256, Cf::SMEM, st>>>(tm, a->w, a->bias, (T*)a->y, a->ldy, a->seq, a->channels, a->act,
+                                                    ncb, nsb, ntiles);
+  return th::check_launch("th_conv1d(tma)");
 }
 
 template <typename T>
 static int conv_dispatch(const th_conv1d_args* a, cudaStream_t st) {
+  if constexpr (sizeof(T) == 2) {
+    switch (a->width) {
+      case 2: return launch_conv_tma<T, 2>(a, st);
+      case 3: return launch_conv_tma<T, 3>(a, st);
+      case 4: return launch_conv_tma<T, 4>(a, st);
+      default: break;
+    }
+  }
   switch (a->width) {
     case 2: launch_conv<T, 2>(a, st); break;
     case 3: launch_conv<T, 3>(a, st); break;

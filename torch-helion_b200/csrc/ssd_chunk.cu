@@ -248,12 +248,6 @@ struct ScMaps {
 
 constexpr int SC_MATH = 512;  // 16 math warps: 4 per TMEM lane quadrant
 
-// silu through one MUFU op: x * sigmoid(x) = 0.5 x (1 + tanh(x / 2))
-__device__ __forceinline__ float silu_tanh(float x) {
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
-  return 0.5f * x * (1.0f + t);
-}
 
 template <typename T>
 __global__ void __launch_bounds__(64 + SC_MATH, 1)
