@@ -7,7 +7,10 @@
 namespace th {
 
 // ------------------------------------------------------------- rowstat
-template <typename T>
+// Rows of up to 32*8*RV elements (multiples of 8) are held in registers:
+// every 16-byte load of a row is issued before the first one is used.  RV
+// (16-byte vectors per lane) is 4 for rows up to 1024 elements, else 16.
+template <typename T, int RV>
 __global__ void __launch_bounds__(256) rowstat_kernel(const T* __restrict__ x, int64_t ldx, float* __restrict__ out,
                                                       int64_t rows, int cols) {
   const int lane = threadIdx.x & 31;
@@ -16,7 +19,25 @@ __global__ void __launch_bounds__(256) rowstat_kernel(const T* __restrict__ x, i
   for (int64_t r = wid; r < rows; r += nw) {
     const T* p = x + r * ldx;
     float s = 0.f;
-    if ((cols & 7) == 0) {
+    if ((cols & 7) == 0 && cols <= 256 * RV) {
+      uint4 u[RV];
+#pragma unroll
+      for (int k = 0; k < RV; ++k) {
+        const int c = (k * 32 + lane) * 8;
+        if (c < cols) u[k] = *reinterpret_cast<const uint4*>(p + c);
+      }
+#pragma unroll
+      for (int k = 0; k < RV; ++k) {
+        if ((k * 32 + lane) * 8 >= cols) break;
+        const T* h = reinterpret_cast<const T*>(&u[k]);
+#pragma unroll
+        for (int e = 0; e < 16 / (int)sizeof(T); ++e) { const float v = to_f32(h[e]); s = fmaf(v, v, s); }
+        if constexpr (sizeof(T) == 4) {  // fp32: the second half of the 8 elements
+          const float4 b = *reinterpret_cast<const float4*>(p + (k * 32 + lane) * 8 + 4);
+          s = fmaf(b.x, b.x, s); s = fmaf(b.y, b.y, s); s = fmaf(b.z, b.z, s); s = fmaf(b.w, b.w, s);
+        }
+      }
+    } else if ((cols & 7) == 0) {
       for (int c = lane * 8; c < cols; c += 256) {
         float v[8];
         load8<T>(p + c, v);
@@ -35,7 +56,7 @@ __global__ void __launch_bounds__(256) rowstat_kernel(const T* __restrict__ x, i
 }
 
 // ------------------------------------------------------------- rmsnorm
-template <typename T>
+template <typename T, int RV>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, int64_t ldx, const float* __restrict__ g,
                                                       T* __restrict__ y, int64_t ldy, int64_t rows, int cols, float eps) {
   const int lane = threadIdx.x & 31;
@@ -45,6 +66,36 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, i
     const T* p = x + r * ldx;
     T* q = y + r * ldy;
     float s = 0.f;
+    if constexpr (sizeof(T) == 2) {
+      if ((cols & 7) == 0 && cols <= 256 * RV) {  // one pass: the row stays in registers
+        uint4 u[RV];
+#pragma unroll
+        for (int k = 0; k < RV; ++k) {
+          const int c = (k * 32 + lane) * 8;
+          if (c < cols) u[k] = *reinterpret_cast<const uint4*>(p + c);
+        }
+#pragma unroll
+        for (int k = 0; k < RV; ++k) {
+          if ((k * 32 + lane) * 8 >= cols) break;
+          const T* h = reinterpret_cast<const T*>(&u[k]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) { const float v = to_f32(h[e]); s = fmaf(v, v, s); }
+        }
+        s = warp_sum(s);
+        const float rs = rsqrtf(s / (float)cols + eps);
+#pragma unroll
+        for (int k = 0; k < RV; ++k) {
+          const int c = (k * 32 + lane) * 8;
+          if (c >= cols) break;
+          const T* h = reinterpret_cast<const T*>(&u[k]);
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = to_f32(h[e]) * rs * (g ? g[c + e] : 1.f);
+          store8<T>(q + c, v);
+        }
+        continue;
+      }
+    }
     const bool vec = (cols & 7) == 0;
     if (vec) {
       for (int c = lane * 8; c < cols; c += 256) {
@@ -322,10 +373,11 @@ extern "C" int th_rowstat(const th_rowstat_args* a, void* stream) {
   if ((a->cols % 8 == 0) && (!aligned16(a->x) || a->ldx % 8)) return fail(TH_EALIGN, "th_rowstat: x must be 16-B aligned with ldx %% 8 == 0");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const unsigned g = row_grid(a->rows);
+  const bool small = a->cols <= 1024;
   switch (a->dtype) {
-    case TH_F32: rowstat_kernel<float><<<g, 256, 0, st>>>((const float*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols); break;
-    case TH_BF16: rowstat_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols); break;
-    case TH_F16: rowstat_kernel<__half><<<g, 256, 0, st>>>((const __half*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols); break;
+    case TH_F32: (small ? rowstat_kernel<float, 4> : rowstat_kernel<float, 16>)<<<g, 256, 0, st>>>((const float*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols); break;
+    case TH_BF16: (small ? rowstat_kernel<__nv_bfloat16, 4> : rowstat_kernel<__nv_bfloat16, 16>)<<<g, 256, 0, st>>>((const __nv_bfloat16*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols); break;
+    case TH_F16: (small ? rowstat_kernel<__half, 4> : rowstat_kernel<__half, 16>)<<<g, 256, 0, st>>>((const __half*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols); break;
     default: return fail(TH_EDTYPE, "th_rowstat: bad dtype %d", a->dtype);
   }
   return check_launch("th_rowstat");
@@ -339,10 +391,11 @@ extern "C" int th_rmsnorm(const th_rmsnorm_args* a, void* stream) {
     return fail(TH_EALIGN, "th_rmsnorm: x/y must be 16-B aligned with ld %% 8 == 0");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const unsigned g = row_grid(a->rows);
+  const bool small = a->cols <= 1024;
   switch (a->dtype) {
-    case TH_F32: rmsnorm_kernel<float><<<g, 256, 0, st>>>((const float*)a->x, a->ldx, a->gain, (float*)a->y, a->ldy, a->rows, (int)a->cols, a->eps); break;
-    case TH_BF16: rmsnorm_kernel<__nv_bfloat16><<<g, 256, 0, st>>>((const __nv_bfloat16*)a->x, a->ldx, a->gain, (__nv_bfloat16*)a->y, a->ldy, a->rows, (int)a->cols, a->eps); break;
-    case TH_F16: rmsnorm_kernel<__half><<<g, 256, 0, st>>>((const __half*)a->x, a->ldx, a->gain, (__half*)a->y, a->ldy, a->rows, (int)a->cols, a->eps); break;
+    case TH_F32: (small ? rmsnorm_kernel<float, 4> : rmsnorm_kernel<float, 16>)<<<g, 256, 0, st>>>((const float*)a->x, a->ldx, a->gain, (float*)a->y, a->ldy, a->rows, (int)a->cols, a->eps); break;
+    case TH_BF16: (small ? rmsnorm_kernel<__nv_bfloat16, 4> : rmsnorm_kernel<__nv_bfloat16, 16>)<<<g, 256, 0, st>>>((const __nv_bfloat16*)a->x, a->ldx, a->gain, (__nv_bfloat16*)a->y, a->ldy, a->rows, (int)a->cols, a->eps); break;
+    case TH_F16: (small ? rmsnorm_kernel<__half, 4> : rmsnorm_kernel<__half, 16>)<<<g, 256, 0, st>>>((const __half*)a->x, a->ldx, a->gain, (__half*)a->y, a->ldy, a->rows, (int)a->cols, a->eps); break;
     default: return fail(TH_EDTYPE, "th_rmsnorm: bad dtype %d", a->dtype);
   }
   return check_launch("th_rmsnorm");

@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(320, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tslot, 64);
+  if (warp == 1) tmem_alloc(tslot, 128);  // two chunk-state buffers
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(320, 1)
         for (int k = 0; k < CK_L / 16; ++k) {
           const uint64_t ad = make_desc_sw128(st + k * 2048, CK_L * 128, 1024);
           const uint64_t bd = make_desc_sw128(st + StC::B_BYTES + k * 2048, CK_L * 128, 1024);
-          tc_mma_f16(tmem, ad, bd, idesc, (c > 0 || k > 0) ? 1u : 0u);
+          tc_mma_f16(tmem + (c & 1) * 64, ad, bd, idesc, k > 0 ? 1u : 0u);  // the chunk's own state, fresh
         }
         tc_commit(done);
         tc_commit(&empty[c & 1]);
@@ -139,6 +139,10 @@ __global__ void __launch_bounds__(320, 1)
     const float Ah = p.A[h];
     const float Dh = p.D ? p.D[h] : 0.f;
     bool ok = true;
+    float srun[32];  // running state S_in, rows n, columns half*32.. (fp32)
+#pragma unroll
+    for (int e = 0; e < 32; ++e) srun[e] = 0.f;
+    float prev_total = 0.f;
     for (int c = 0; c < nc; ++c) {
       uint8_t* st = sm + (c & 1) * StC::STAGE;
       ok = ok && mbar_wait(&full[c & 1], (c >> 1) & 1, abort_flag);
@@ -184,34 +188,36 @@ __global__ void __launch_bounds__(320, 1)
           store8<T>(row + e8, f);
         }
       }
-      // the state entering chunk c: stage it (bf16 [n][p]), then scale it by exp(total) for the update
+      fence_proxy_async();  // scaled x (read by the MMA) and the record staging (read by its store)
+      tc_fence_before();
+      mbar_arrive(ready);   // the MMA of chunk c may start
+      // the state entering chunk c (c >= 1): S_in(c) = exp(total(c-1)) S_in(c-1) + S(c-1), with S(c-1)
+      // the previous chunk's own state from its MMA; kept in fp32 registers, staged in bf16 for the scan
       if (c > 0) {
         ok = ok && mbar_wait(done, (c - 1) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
           tc_fence_after();
           float sv[32];
-          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + half * 32;
-          tmem_ld32(ta, sv);
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + ((c - 1) & 1) * 64 + half * 32, sv);
+          tc_fence_before();
+          const float f = __expf(prev_total);
           uint8_t* sst = sm + StC::OFF_SIN;
 #pragma unroll
-          for (int e8 = 0; e8 < 32; e8 += 8)
-            store8<T>(reinterpret_cast<T*>(sst + sw128_off(n, half * 32 + e8, 128)), sv + e8);
-          const float f = __expf(total);
+          for (int e = 0; e < 32; ++e) srun[e] = fmaf(f, srun[e], sv[e]);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) sv[e] *= f;
-          tmem_st32(ta, sv);
-          tc_fence_before();
+          for (int e8 = 0; e8 < 32; e8 += 8)
+            store8<T>(reinterpret_cast<T*>(sst + sw128_off(n, half * 32 + e8, 128)), srun + e8);
         }
       }
-      fence_proxy_async();  // scaled x (read by the MMA) and the staging tiles (read by the stores)
+      fence_proxy_async();  // the state staging (read by its store)
       named_bar(1, 256);
       if (mt == 0 && ok) {
         bulk_store(scal + (((int64_t)b * p.heads + h) * nc + c) * CK_SCAL, rec, CK_SCAL * 4);
         if (c > 0) tma_store_2d(&tmS, sm + StC::OFF_SIN, 0, (((b * nc + c) * p.heads) + h) * CK_NS);
         bulk_commit();
       }
-      mbar_arrive(ready);
+      prev_total = total;
     }
     mbar_wait(done, (nc - 1) & 1, abort_flag);  // the last update finishes before TMEM is freed
     if (mt == 0) bulk_wait0();
@@ -219,7 +225,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, 64);
+  if (warp == 1) tmem_dealloc(tmem, 128);
 }
 
 // -------------------------------------------------------------------- scan
