@@ -51,26 +51,35 @@ def _peaks() -> tuple[dict, str]:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
-def _workload(name: str, rank: int):
+def _workload(name: str, rank: int, world: int = 1):
+    """(cfg, model, this rank's input, description, scaling).  C2 runs one full
+    C2 batch per GPU (weak scaling); C4 splits the batch of 16 across the GPUs
+    and C3 runs the whole B8 S4096 block tensor-parallel (strong scaling)."""
     from workloads import configs
 
+    scaling, seed = "weak", 1 + rank
     if name == "c2":
         cfg = configs.c2_mamba_block_bf16()
         desc = "C2 Mamba-2 block bf16: B4 S2048 d768 expand2 headdim64 (24 heads) d_state128 ngroups1 conv4 chunk256"
     elif name == "c4":
-        cfg = configs.c4_mamba24_bf16(batch=2)
-        desc = "C4 Mamba-2 24-layer backbone bf16 (per-GPU batch 2 of 16) S2048 d1024 vocab 50280 tied"
+        if 16 % world:
+            raise SystemExit("c4 splits batch 16: use 1, 2, 4 or 8 GPUs")
+        cfg = configs.c4_mamba24_bf16(batch=16 // world)
+        desc = f"C4 Mamba-2 24-layer backbone bf16 B16 (per-GPU batch {16 // world}) S2048 d1024 vocab 50280 tied"
+        scaling = "strong"
     elif name == "c1":
         cfg = configs.c1_llama_fp32()
         desc = "C1 Llama block fp32: B1 S128 D512 H8 KV8 d64 F1408 causal"
     elif name == "c3":
-        cfg = configs.c3_llama8b_bf16(batch=1, seq=4096)
-        desc = "C3 Llama-3-8B-geometry block bf16 (per-GPU batch 1) S4096 D4096 Hq32 Hkv8 F14336 causal"
+        cfg = configs.c3_llama8b_bf16(batch=8, seq=4096)
+        desc = ("C3 Llama-3-8B-geometry block bf16 B8 S4096 D4096 Hq32 Hkv8 F14336 causal"
+                + (f", tensor-parallel over {world} GPUs" if world > 1 else ""))
+        scaling, seed = "strong", 1  # every rank holds the same batch
     else:
         raise SystemExit(f"unknown workload {name}")
     model = configs.build(cfg, seed=0)
-    (x,) = model.example_inputs(seed=1 + rank)
-    return cfg, model, x, desc
+    (x,) = model.example_inputs(seed=seed)
+    return cfg, model, x, desc, scaling
 
 
 class ClockSampler:
@@ -214,7 +223,7 @@ def main() -> None:
     if args.impl == "reference":
         if rank != 0:
             return
-        cfg, model, x, desc = _workload(args.workload, 0)
+        cfg, model, x, desc, _ = _workload(args.workload, 0)
         torch.set_num_threads(os.cpu_count() or 1)
         cb = None
         vals = []
@@ -244,19 +253,24 @@ def main() -> None:
 
     from torch_helion import CompileConfig, compile_model
 
-    cfg, model, x, desc = _workload(args.workload, rank)
+    cfg, model, x, desc, scaling = _workload(args.workload, rank, world)
+    tp = args.workload == "c3" and world > 1
     res = compile_model(model, (x,), CompileConfig(run_name=f"bench_{args.workload}_r{rank}", device=str(dev),
                                                    verify_passes=False, reference_check=False,
-                                                   results_dir=REPO / "results"))
+                                                   results_dir=REPO / "results", world_size=world if tp else 1,
+                                                   tp_mode="heads" if tp else None))
     mod, prog = res.module, res.program
     tokens = x.shape[0] * x.shape[1]
+    # tokens the whole job processes per step
+    job_tokens = tokens if tp else world * tokens
     flushbuf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     flush = lambda: flushbuf.fill_(1.0)
     xd = x.to(dev)
     mod.load_inputs([xd])
     # the forward is replayed as one CUDA graph (the per-kernel timing pass
     # below launches the same kernels one by one)
-    mod.capture_graph()
+    if not tp:  # graphs holding NCCL calls are left out; TP forwards launch eagerly
+        mod.capture_graph()
     st = torch.cuda.current_stream()
 
     def barrier():
@@ -301,31 +315,51 @@ def main() -> None:
     # every step copies its input from pinned host memory and its output back;
     # step i's copies overlap the forward of its neighbours (two slots, three
     # streams).  The L2 flush runs on the compute stream before each forward.
-    runner = res.streaming_runner(depth=2, cuda_graph=True)
     xh = x.pin_memory()
-    outs = [runner.output_buffers() for _ in range(2)]
-    for i in range(max(3, args.warmup)):
-        runner.submit(i, [xh], outs[i % 2], before_forward=flush)
-    runner.synchronize()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(runner.h2d)
-    for i in range(args.steps):
-        runner.submit(i, [xh], outs[i % 2], before_forward=flush)
-    e1.record(runner.d2h)
-    runner.synchronize()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    ms_e2e = e0.elapsed_time(e1) / args.steps
-    oh = outs[0][0]
-    del runner
+    if not tp:
+        runner = res.streaming_runner(depth=2, cuda_graph=True)
+        outs = [runner.output_buffers() for _ in range(2)]
+        for i in range(max(3, args.warmup)):
+            runner.submit(i, [xh], outs[i % 2], before_forward=flush)
+        runner.synchronize()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(runner.h2d)
+        for i in range(args.steps):
+            runner.submit(i, [xh], outs[i % 2], before_forward=flush)
+        e1.record(runner.d2h)
+        runner.synchronize()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        ms_e2e = e0.elapsed_time(e1) / args.steps
+        oh = outs[0][0]
+        del runner
+    else:
+        # tensor parallel: every rank copies the batch in, runs its shard (two all-reduces) and copies the
+        # block output back, one step after another on its stream
+        oh = torch.empty(mod.output_views()[0].shape, dtype=mod.dtype, pin_memory=True)
+        for _ in range(max(3, args.warmup)):
+            oh.copy_(mod(xh)[0], non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(args.steps):
+            flush()
+            oh.copy_(mod(xh)[0], non_blocking=True)
+        e1.record(st)
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        ms_e2e = e0.elapsed_time(e1) / args.steps
 
     # ---- per-kernel times and the dominant kernel's roofline
     peaks, peak_src = _peaks()
-    top = max(mod.launches, key=lambda l: ktimes[l.name])
+    top = max((l for l in mod.launches if l.kind != "nccl"), key=lambda l: ktimes[l.name])
     work = kernel_work(top, prog, mod)
     ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
     t_top = ktimes[top.name] / 1e3
@@ -348,20 +382,22 @@ def main() -> None:
     if rank == 0:
         cb = None if args.no_cpu_baseline else cpu_baseline(cfg, model, x)
         line = {
-            "metric": metric, "value": n * tokens / (ms / 1e3), "unit": unit, "n_gpus": n, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "metric": metric, "value": job_tokens / (ms / 1e3), "unit": unit, "n_gpus": n, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
             "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[mod.dtype],
             "data": "synthetic",
-            "config": {"workload": desc, "global_batch": n * x.shape[0], "seq_len": x.shape[1],
-                       "parallelism": f"dp{n} (batch-sharded, no communication)" if n > 1 else "single GPU",
+            "config": {"workload": desc, "global_batch": x.shape[0] if tp else n * x.shape[0], "seq_len": x.shape[1],
+                       "parallelism": (f"tp{n} (heads / FFN columns, NCCL all-reduce after o_proj and down_proj)" if tp
+                                       else f"dp{n} (batch-sharded, no communication)" if n > 1 else "single GPU"),
                        "l2": "flushed between steps (256 MiB write, untimed)", "kernels_per_forward": mod.n_launches,
-                       "launch": "one CUDA graph per forward"},
+                       "launch": "eager launches (NCCL inside)" if tp else "one CUDA graph per forward"},
             "roofline": {"bound": bound, "kernel": f"{top.name} ({top.kind})", "achieved": achieved, "peak": peak,
                          "unit": ru, "frac": achieved / peak, "peak_source": peak_src,
                          "algorithmic_bytes": work["bytes"], "algorithmic_flops": work["flops"],
                          "launch_ms": ktimes[top.name], "traffic": traffic},
-            "e2e": {"value": n * tokens / (ms_e2e / 1e3), "unit": unit, "ms_per_step": ms_e2e,
-                    "entry": "CompileResult.streaming_runner (2 slots, CUDA-graph forward, H2D/compute/D2H streams)",
+            "e2e": {"value": job_tokens / (ms_e2e / 1e3), "unit": unit, "ms_per_step": ms_e2e,
+                    "entry": ("CompileResult.module(host batch) per rank" if tp else
+                              "CompileResult.streaming_runner (2 slots, CUDA-graph forward, H2D/compute/D2H streams)"),
                     "h2d_bytes_per_step": xh.numel() * xh.element_size(),
                     "d2h_bytes_per_step": oh.numel() * oh.element_size()},
             "gpu_launches": mod.n_launches * args.steps,

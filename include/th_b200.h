@@ -138,7 +138,8 @@ typedef struct {
   /* 6. fp32 tail */
   float* out2;
   int64_t ld_out2;
-  int32_t tail_begin; /* <= 0 or >= n: no tail */
+  int32_t tail_begin; /* with out2: output columns >= tail_begin (>= 0) go to out2;
+                         0 = all of them (d may then be NULL); >= n or no out2: no tail */
   /* 7. sum-of-squares partials of the stored output, one per 64 columns */
   float* ss_out;
   int64_t ss_ld;

@@ -114,6 +114,23 @@ def test_gemm_softplus_tail(L, dtype):
     assert rel_l2(dt, F.softplus(acc[:, nmain:] + bias)) < (1e-5 if dtype == torch.float32 else 1e-3)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gemm_all_tail(L, dtype):
+    """A GEMM whose whole output is the fp32 tail (tail_begin 0): the planner
+    may give the scan's dt projection a kernel of its own."""
+    torch.manual_seed(4)
+    m, k, n = 300, 256, 32
+    x = torch.randn(m, k, device=_dev()).to(dtype)
+    w = (torch.randn(n, k, device=_dev()) * 0.1).to(dtype)
+    bias = torch.randn(n, device=_dev())
+    dummy = torch.zeros(m, 8, device=_dev(), dtype=dtype)
+    dt = torch.empty(m, n, device=_dev())
+    L.gemm(x, w, dummy, act=L.ACT_SOFTPLUS, act_begin=0, act_end=n, bias=bias, out2=dt, tail_begin=0)
+    acc = _gemm_ref(x, w)
+    assert rel_l2(dt, F.softplus(acc + bias)) < (1e-5 if dtype == torch.float32 else 1e-3)
+    assert torch.count_nonzero(dummy) == 0  # nothing written to the main output
+
+
 def _rope_ref(x, cos, sin, hd, seq):
     t = x.shape[0]
     pos = torch.arange(t, device=x.device) % seq

@@ -561,7 +561,7 @@ static int dispatch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t 
 extern "C" int th_gemm(const th_gemm_args* a, void* stream) {
   using namespace th;
   if (!a) return fail(TH_EINVAL, "th_gemm: args is NULL");
-  if (!a->a || !a->w || !a->d) return fail(TH_EINVAL, "th_gemm: a/w/d must be non-NULL");
+  if (!a->a || !a->w) return fail(TH_EINVAL, "th_gemm: a/w must be non-NULL");
   if (a->m <= 0 || a->n <= 0 || a->k <= 0) return fail(TH_EINVAL, "th_gemm: bad shape m=%lld n=%lld k=%lld", (long long)a->m, (long long)a->n, (long long)a->k);
   if (a->m > INT32_MAX || a->n > INT32_MAX || a->k > INT32_MAX) return fail(TH_EINVAL, "th_gemm: extent exceeds int32");
   if (a->dtype != TH_F32 && a->dtype != TH_BF16 && a->dtype != TH_F16) return fail(TH_EDTYPE, "th_gemm: unknown dtype %d", a->dtype);
@@ -569,10 +569,12 @@ extern "C" int th_gemm(const th_gemm_args* a, void* stream) {
   const int64_t n_out = a->swiglu ? a->n / 2 : a->n;
   if (a->swiglu && a->n % 128) return fail(TH_EINVAL, "th_gemm: swiglu needs n %% 128 == 0 (64 gate | 64 up blocks)");
   if (n_out % 8) return fail(TH_EALIGN, "th_gemm: output width %lld must be a multiple of 8", (long long)n_out);
-  const int tail = (a->tail_begin > 0 && a->tail_begin < n_out) ? a->tail_begin : (int)n_out;
+  // with out2, columns >= tail_begin are the fp32 tail (tail_begin 0: the whole output, d unused)
+  const int tail = (a->out2 && a->tail_begin >= 0 && a->tail_begin < n_out) ? a->tail_begin : (int)n_out;
   if (tail % 8) return fail(TH_EALIGN, "th_gemm: tail_begin must be a multiple of 8");
-  if (tail < n_out && !a->out2) return fail(TH_EINVAL, "th_gemm: tail requested without out2");
-  if (a->ldd < tail || a->ldd % 8 || !is_al16(a->d)) return fail(TH_EALIGN, "th_gemm: d must be 16-B aligned with ldd %% 8 == 0 and ldd >= width");
+  if (tail > 0 && !a->d) return fail(TH_EINVAL, "th_gemm: d must be non-NULL");
+  if (tail > 0 && (a->ldd < tail || a->ldd % 8 || !is_al16(a->d)))
+    return fail(TH_EALIGN, "th_gemm: d must be 16-B aligned with ldd %% 8 == 0 and ldd >= width");
   if (a->residual && (a->ld_res % 8 || !is_al16(a->residual))) return fail(TH_EALIGN, "th_gemm: residual must be 16-B aligned with ld_res %% 8 == 0");
   if (a->rope_cos) {
     const int hd = a->rope_head_dim;

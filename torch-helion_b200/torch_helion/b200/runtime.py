@@ -214,7 +214,7 @@ class CompiledProgram:
                 parts = self._empty(T, (n_main_pad + 63) // 64, torch.float32)
                 self._ss_parts[tname] = parts
                 kw["ss_out"] = parts
-        d = out if n_tail == 0 else out[:, :n_main_pad]
+        d = out if n_tail == 0 or n_main_pad == 0 else out[:, :n_main_pad]  # all-tail GEMMs write no main output
         self.launches.append(KernelLaunch(kname, "gemm", lambda lhs=lhs, W=W, d=d, kw=kw: lib.gemm(lhs, W, d, **kw)))
         if self._allreduced(spec):
             buf = out  # the whole (contiguous) buffer; zero-weight pad columns sum to zero

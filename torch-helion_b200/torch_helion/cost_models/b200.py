@@ -128,8 +128,10 @@ def gemm_cost(spec: KernelSpec, tensors: dict[str, TensorType], hw: B200Spec, bn
     else:
         if bn not in hw.eff_tc:
             raise CostModelError(f"tile width {bn} not built")
+        # the last column tile multiplies only its live width (rounded to 16)
         tiles = math.ceil(T / 128) * math.ceil(N / bn)
-        waves = math.ceil(tiles / hw.sm_count)
+        n_eff = (N // bn) * bn + (math.ceil((N % bn) / 16) * 16 if N % bn else 0)
+        waves = math.ceil(math.ceil(T / 128) * n_eff / bn / hw.sm_count)
         per_tile = 128 * bn * K * 2 / (hw.bf16_tflops * 1e12 / hw.sm_count * hw.eff_tc[bn])
         t_c = waves * per_tile * 1e6
     t_m = byts / (hw.hbm_gbs * 1e9) * 1e6
