@@ -170,18 +170,35 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t sb = tmem + lane_off + s * 128;
       const int k0 = j * C::BN;
       const bool diag = p.causal && (k0 + C::BN - 1 > q0);
-      // pass 1: row max of the masked, scaled scores
-      float mx = -INFINITY;
-      for (int c = 0; c < C::BN; c += 32) {
-        float v[32];
-        tmem_ld32(sb + c, v);
+      // the whole score row into registers with one wait; the S buffer is free right after
+      float v[C::BN];
+      {
+        uint32_t raw[C::BN / 32][32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int kj = k0 + c + e;
-          const bool masked = kj >= p.seq || (diag && kj > qi);
-          mx = masked ? mx : fmaxf(mx, v[e] * sl2);
+        for (int c = 0; c < C::BN / 32; ++c) tmem_ld32_issue(sb + c * 32, raw[c]);
+#pragma unroll
+        for (int c = 0; c < C::BN / 32; ++c) {
+          tmem_wait_ld32(raw[c]);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[c * 32 + e] = __uint_as_float(raw[c][e]);
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[s]);
+      // masking only in the diagonal block and past the sequence end
+      if (diag || k0 + C::BN > p.seq) {
+#pragma unroll
+        for (int e = 0; e < C::BN; ++e) {
+          const int kj = k0 + e;
+          if (kj >= p.seq || (diag && kj > qi)) v[e] = -INFINITY;
+        }
+      }
+      // row max of the raw scores (the scale is positive)
+      float mx = v[0];
+#pragma unroll
+      for (int e = 1; e < C::BN; ++e) mx = fmaxf(mx, v[e]);
+      mx *= sl2;
       float m_new = fmaxf(m_ref, mx);
       const bool rescale = j > 0 && m_new > m_ref + 8.0f;
       const bool any_rescale = __any_sync(0xffffffffu, rescale);
@@ -194,7 +211,7 @@ __global__ void __launch_bounds__(192, 1)
       if (j == 0) {
         m_ref = m_new;
       } else if (any_rescale) {
-        const float f = rescale ? exp2f(m_ref - m_new) : 1.f;
+        const float f = rescale ? ex2_fast(m_ref - m_new) : 1.f;
         for (int c = 0; c < D; c += 32) {
           float o[32];
           tmem_ld32(tO + lane_off + c, o);
@@ -208,29 +225,22 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       const float mref = (m_ref == -INFINITY) ? 0.f : m_ref;  // fully masked row: P = 0
-      // pass 2: P = exp2(s*scale - m_ref) -> bf16 operand tile, running sum
+      // P = exp2(s*scale - m_ref) -> bf16 operand tile, running sum (ex2(-inf) = 0 for masked scores)
       uint8_t* pt = sm + C::OFF_P;
-      for (int c = 0; c < C::BN; c += 32) {
-        float v[32];
-        tmem_ld32(sb + c, v);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int kj = k0 + c + e;
-          const bool masked = kj >= p.seq || (diag && kj > qi);
-          const float pe = masked ? 0.f : exp2f(v[e] * sl2 - mref);
-          v[e] = pe;
-          l += pe;
+      for (int c = 0; c < C::BN; c += 8) {
+        float pe[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          pe[e] = ex2_fast(fmaf(v[c + e], sl2, -mref));
+          l += pe[e];
         }
-#pragma unroll
-        for (int e8 = 0; e8 < 32; e8 += 8) store8<T>(reinterpret_cast<T*>(pt + at_sw128(r, c + e8, C::BM)), v + e8);
+        store8<T>(reinterpret_cast<T*>(pt + at_sw128(r, c, C::BM)), pe);
       }
-      tc_fence_before();
       fence_proxy_async();  // P (generic writes) -> visible to the tensor cores
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s_free[s]);
-        mbar_arrive(p_full);
-      }
+      if (lane == 0) mbar_arrive(p_full);
     }
     // epilogue: O / l
     if (ok && nkv > 0) {
