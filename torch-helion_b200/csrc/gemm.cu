@@ -138,10 +138,11 @@ __device__ void epilogue_tile(const float* tile, int ldt, float* rscale, const E
 }
 
 // ------------------------------------------------------------ tcgen05 path
-// Persistent, warp-specialised kernel (192 threads, one CTA per SM):
+// Persistent, warp-specialised kernel (320 threads, one CTA per SM):
 //   warp 0  TMA producer: A/B tiles (128-byte swizzle) into a STAGES-deep ring
 //   warp 1  MMA issuer:   tcgen05.mma 128xBNx16 into one of two TMEM accumulators
-//   warps 2-5 epilogue:   thread = accumulator row; tcgen05.ld 32 columns at a
+//   warps 2-9 epilogue:   thread = accumulator row, two warps per TMEM lane
+//           quarter splitting the tile's columns; tcgen05.ld 32 columns at a
 //           time, all fused stages in registers, direct stores
 // The two accumulators (2*BN TMEM columns) let the epilogue of tile i overlap
 // the mainloop of tile i+1.  Every wait is bounded (mbar_wait): a stuck
@@ -210,16 +211,16 @@ __device__ __forceinline__ void res_issue(uint4 (&r)[4], int row, bool row_ok, i
 // Residual epilogue (plain GEMM + residual, optional row scale / activation):
 // the residual of chunk c+2 is in flight while chunk c is stored, and the
 // first two chunks were issued before the accumulator was ready.
-template <typename T, int BN>
-__device__ __forceinline__ void epilogue_row_res(uint32_t tbase, int row, bool row_ok, float rs, int n0,
+template <typename T, int NC>
+__device__ __forceinline__ void epilogue_row_res(uint32_t tbase, int row, bool row_ok, float rs, int n0, int cb,
                                                  const EpiParams& ep, uint4 (&rb)[3][4]) {
   const int n_out = ep.n;
   T* d = reinterpret_cast<T*>(ep.d);
   float ss = 0.f;
 #pragma unroll
-  for (int ci = 0; ci < BN / 32; ++ci) {
-    const int c = ci * 32, col = n0 + c;
-    if (ci + 2 < BN / 32) res_issue<T>(rb[(ci + 2) % 3], row, row_ok, col + 64, ep);
+  for (int ci = 0; ci < NC; ++ci) {
+    const int c = cb + ci * 32, col = n0 + c;
+    if (ci + 2 < NC) res_issue<T>(rb[(ci + 2) % 3], row, row_ok, col + 64, ep);
     float v[32];
     tmem_ld32(tbase + c, v);
 #pragma unroll
@@ -268,11 +269,11 @@ __device__ __forceinline__ void epilogue_row_res(uint32_t tbase, int row, bool r
 
 // Epilogue of one accumulator row (this thread) of a 128 x BN tile.
 template <typename T, int BN, int EPI>
-__device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_ok, float rs, int n0,
+__device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_ok, float rs, int n0, int cb, int ce,
                                              const EpiParams& ep) {
   if constexpr ((EPI & EPI_SWIGLU) != 0) {
     const int n_out = ep.n / 2;
-    for (int g = 0; g < BN / 128; ++g) {
+    for (int g = cb / 128; g < ce / 128; ++g) {
       float ss = 0.f;
       for (int q = 0; q < 2; ++q) {
         float gv[32], uv[32];
@@ -290,7 +291,7 @@ __device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_o
   }
   const int n_out = ep.n;
   float ss = 0.f;
-  for (int c = 0; c < BN; c += 32) {
+  for (int c = cb; c < ce; c += 32) {
     float v[32];
     tmem_ld32(tbase + c, v);
     const int col = n0 + c;
@@ -343,7 +344,7 @@ __device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_o
 }
 
 template <typename T, int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiParams ep,
                    int K, int tiles_m, int tiles_n) {
   using C = TcCfg<BN>;
@@ -368,7 +369,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);  // one arrive per epilogue warp
+      mbar_init(&tempty[a], 8);  // one arrive per epilogue warp
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -433,9 +434,15 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_commit(done);  // tracks every MMA this thread issued
     }
-  } else {  // ---- epilogue warps 2..5
+  } else {  // ---- epilogue warps 2..9: two per TMEM lane quarter, each one half of the tile's columns
     const int q = warp & 3;  // TMEM lane quarter this warp may read
+    const int hh = (warp - 2) >> 2;
     const int rl = q * 32 + lane;
+    // a head of RoPE or a 128-column gate|up block must not straddle the halves
+    constexpr bool split = !((EPI & EPI_SWIGLU) != 0 && BN < 256);
+    const bool rope_whole = (EPI & EPI_ROPE) != 0 && ep.rope_hd > BN / 2;
+    const bool halves = split && !rope_whole;
+    const int cb = halves ? hh * (BN / 2) : 0, ce = halves ? cb + BN / 2 : (hh ? 0 : BN);
     int i = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++i) {
       const int acc = i & 1, use = i >> 1;
@@ -444,7 +451,7 @@ __global__ void __launch_bounds__(192, 1)
       const bool row_ok = row < ep.m;
       // row scale and the first residual chunks are fetched while the accumulator fills
       float rs = 1.f;
-      if (ep.rs_parts && row_ok) {
+      if (ep.rs_parts && row_ok && ce > cb) {
         const float* pp = ep.rs_parts + (int64_t)row * ep.rs_nparts;
         float sacc = 0.f;
         for (int k = 0; k < ep.rs_nparts; ++k) sacc += pp[k];
@@ -452,15 +459,15 @@ __global__ void __launch_bounds__(192, 1)
       }
       uint4 rb[3][4];
       if constexpr ((EPI & EPI_RES) != 0) {
-        res_issue<T>(rb[0], row, row_ok, n0, ep);
-        res_issue<T>(rb[1], row, row_ok, n0 + 32, ep);
+        res_issue<T>(rb[0], row, row_ok, n0 + cb, ep);
+        res_issue<T>(rb[1], row, row_ok, n0 + cb + 32, ep);
       }
       if (!mbar_wait(&tfull[acc], use & 1, abort_flag)) break;
       __syncwarp();
       tc_fence_after();
       const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      if constexpr ((EPI & EPI_RES) != 0) epilogue_row_res<T, BN>(tb, row, row_ok, rs, n0, ep, rb);
-      else epilogue_row<T, BN, EPI>(tb, row, row_ok, rs, n0, ep);
+      if constexpr ((EPI & EPI_RES) != 0) epilogue_row_res<T, BN / 64>(tb, row, row_ok, rs, n0, cb, ep, rb);
+      else if (ce > cb) epilogue_row<T, BN, EPI>(tb, row, row_ok, rs, n0, cb, ce, ep);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -541,7 +548,7 @@ static int launch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st
   const int tiles_m = (int)((a->m + C::BM - 1) / C::BM), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n;
   const int grid = ntiles < sm_count() ? ntiles : sm_count();
-  gemm_tc_kernel<T, BN, EPI><<<grid, 192, C::SMEM_BYTES, st>>>(ta, tb, ep, (int)a->k, tiles_m, tiles_n);
+  gemm_tc_kernel<T, BN, EPI><<<grid, 320, C::SMEM_BYTES, st>>>(ta, tb, ep, (int)a->k, tiles_m, tiles_n);
   return check_launch("th_gemm(tcgen05)");
 }
 
