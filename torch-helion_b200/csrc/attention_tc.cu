@@ -1,13 +1,14 @@
 // tcgen05 flash attention (forward) for bf16/fp16, head_dim 64 or 128.
 //
 // One CTA = 128 query rows of one (batch, query head); KV blocks of 128 rows.
-// 192 threads, warp-specialised:
+// 320 threads, warp-specialised:
 //   warp 0    TMA: the Q tile once, K/V tiles of each KV block into a 2-stage ring
 //   warp 1    MMA: S_j = Q K_j^T into one of two TMEM S buffers (so S_{j+1} is
 //             computed while the softmax warps work on S_j), then O += P_j V_j
 //             (V is an MN-major operand: head_dim is its contiguous axis)
-//   warps 2-5 softmax, one thread per query row: read S_j from TMEM, masked
-//             online softmax in the log2 domain, P_j (bf16) written to shared
+//   warps 2-9 softmax, two threads per query row (each half of the columns,
+//             row maxima exchanged through shared memory): read S_j from TMEM,
+//             masked online softmax in the log2 domain, P_j (bf16) written to shared
 //             memory in the 128-byte-swizzled K-major operand layout.  O is
 //             rescaled in TMEM only when the running max grows by more than
 //             2^8 (a lazy rescale: P stays <= 256, the final O/l is exact).
@@ -31,7 +32,8 @@ struct AtCfg {
   static constexpr int OFF_K = Q_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
   static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int OFF_RED = OFF_P + P_BYTES;   // row-max / row-sum exchange between the halves
+  static constexpr int OFF_BAR = OFF_RED + 4 * 128 * 4;
   static constexpr int SMEM = 1024 + OFF_BAR + 256;
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
@@ -42,7 +44,7 @@ __device__ __forceinline__ uint32_t at_sw128(int row, int col, int rows) {
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, th_attention_args p) {
   using C = AtCfg<D>;
@@ -76,9 +78,9 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 4);
+      mbar_init(&s_free[s], 8);
     }
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(pv_done, 1);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -154,103 +156,109 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_commit(mma_done);
     }
-  } else {  // ------------------------------------------- softmax warps 2..5
+  } else {  // ------------------------------------- softmax warps 2..9, two per TMEM lane quarter
     const int q4 = warp & 3;
+    const int hh = (warp - 2) >> 2;        // column half of S (and of O) this warp owns
     const int r = q4 * 32 + lane;          // row within the tile (TMEM lane)
     const int qi = q0 + r;                 // query position
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const float sl2 = p.scale * 1.4426950408889634f;
+    constexpr int HB = C::BN / 2, HD = D / 2;
+    float* red = reinterpret_cast<float*>(sm + C::OFF_RED);  // [2 parities][2 halves][128 rows]
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
+      // no early exit: both halves must pass the same named barriers
       const int s = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[s], (j >> 1) & 1, abort_flag));
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t sb = tmem + lane_off + s * 128;
-      const int k0 = j * C::BN;
-      const bool diag = p.causal && (k0 + C::BN - 1 > q0);
-      // the whole score row into registers with one wait; the S buffer is free right after
-      float v[C::BN];
-      {
-        uint32_t raw[C::BN / 32][32];
+      ok = __all_sync(0xffffffffu, ok && mbar_wait(&s_full[s], (j >> 1) & 1, abort_flag));
+      const int k0 = j * C::BN + hh * HB;  // first key of this warp's columns
+      const bool diag = p.causal && (j * C::BN + C::BN - 1 > q0);
+      float v[HB];
+      float mx = -INFINITY;
+      if (ok) {
+        tc_fence_after();
+        const uint32_t sb = tmem + lane_off + s * 128 + hh * HB;
+        uint32_t raw[HB / 32][32];
 #pragma unroll
-        for (int c = 0; c < C::BN / 32; ++c) tmem_ld32_issue(sb + c * 32, raw[c]);
+        for (int c = 0; c < HB / 32; ++c) tmem_ld32_issue(sb + c * 32, raw[c]);
 #pragma unroll
-        for (int c = 0; c < C::BN / 32; ++c) {
+        for (int c = 0; c < HB / 32; ++c) {
           tmem_wait_ld32(raw[c]);
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[c * 32 + e] = __uint_as_float(raw[c][e]);
         }
+        tc_fence_before();
+        if (diag || k0 + HB > p.seq) {  // masking only in the diagonal block and past the sequence end
+#pragma unroll
+          for (int e = 0; e < HB; ++e) {
+            const int kj = k0 + e;
+            if (kj >= p.seq || (diag && kj > qi)) v[e] = -INFINITY;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < HB; ++e) mx = fmaxf(mx, v[e]);
       }
-      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[s]);
-      // masking only in the diagonal block and past the sequence end
-      if (diag || k0 + C::BN > p.seq) {
-#pragma unroll
-        for (int e = 0; e < C::BN; ++e) {
-          const int kj = k0 + e;
-          if (kj >= p.seq || (diag && kj > qi)) v[e] = -INFINITY;
-        }
-      }
-      // row max of the raw scores (the scale is positive)
-      float mx = v[0];
-#pragma unroll
-      for (int e = 1; e < C::BN; ++e) mx = fmaxf(mx, v[e]);
-      mx *= sl2;
-      float m_new = fmaxf(m_ref, mx);
+      // row max over both halves (the scale is positive)
+      red[(s * 2 + hh) * 128 + r] = mx;
+      named_bar(1, 256);
+      mx = fmaxf(red[(s * 2) * 128 + r], red[(s * 2 + 1) * 128 + r]) * sl2;
+      const float m_new = fmaxf(m_ref, mx);
       const bool rescale = j > 0 && m_new > m_ref + 8.0f;
       const bool any_rescale = __any_sync(0xffffffffu, rescale);
       // P_{j-1} must be consumed (and O complete) before P_j / O are touched
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, abort_flag));
-        if (!ok) break;
+      if (j > 0) ok = __all_sync(0xffffffffu, ok && mbar_wait(pv_done, (j - 1) & 1, abort_flag));
+      if (ok) {
         tc_fence_after();
-      }
-      if (j == 0) {
-        m_ref = m_new;
-      } else if (any_rescale) {
-        const float f = rescale ? ex2_fast(m_ref - m_new) : 1.f;
-        for (int c = 0; c < D; c += 32) {
-          float o[32];
-          tmem_ld32(tO + lane_off + c, o);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] *= f;
-          tmem_st32(tO + lane_off + c, o);
-        }
-        if (rescale) {
-          l *= f;
+        if (j == 0) {
           m_ref = m_new;
-        }
-      }
-      const float mref = (m_ref == -INFINITY) ? 0.f : m_ref;  // fully masked row: P = 0
-      // P = exp2(s*scale - m_ref) -> bf16 operand tile, running sum (ex2(-inf) = 0 for masked scores)
-      uint8_t* pt = sm + C::OFF_P;
+        } else if (any_rescale) {
+          const float f = rescale ? ex2_fast(m_ref - m_new) : 1.f;
+          for (int c = hh * HD; c < hh * HD + HD; c += 32) {
+            float o[32];
+            tmem_ld32(tO + lane_off + c, o);
 #pragma unroll
-      for (int c = 0; c < C::BN; c += 8) {
-        float pe[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pe[e] = ex2_fast(fmaf(v[c + e], sl2, -mref));
-          l += pe[e];
+            for (int e = 0; e < 32; ++e) o[e] *= f;
+            tmem_st32(tO + lane_off + c, o);
+          }
+          if (rescale) {
+            l *= f;
+            m_ref = m_new;
+          }
         }
-        store8<T>(reinterpret_cast<T*>(pt + at_sw128(r, c, C::BM)), pe);
+        const float mref = (m_ref == -INFINITY) ? 0.f : m_ref;  // fully masked row: P = 0
+        // P = exp2(s*scale - m_ref) -> bf16 operand tile, running sum (2^-inf = 0 for masked scores)
+        uint8_t* pt = sm + C::OFF_P;
+#pragma unroll
+        for (int c = 0; c < HB; c += 8) {
+          float pe[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            pe[e] = ex2_fast(fmaf(v[c + e], sl2, -mref));
+            l += pe[e];
+          }
+          store8<T>(reinterpret_cast<T*>(pt + at_sw128(r, hh * HB + c, C::BM)), pe);
+        }
       }
       fence_proxy_async();  // P (generic writes) -> visible to the tensor cores
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    // epilogue: O / l
+    // epilogue: O / l, l summed over both halves
     if (ok && nkv > 0) {
       ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (nkv - 1) & 1, abort_flag));
       tc_fence_after();
     }
+    named_bar(1, 256);  // the last block's maxima have been read
+    red[hh * 128 + r] = l;
+    named_bar(1, 256);
+    const float lt = red[r] + red[128 + r];
     if (ok) {
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
       T* orow = reinterpret_cast<T*>(p.o) + (row0 + qi) * p.ldo + (int64_t)h * D;
-      for (int c = 0; c < D; c += 32) {
+      for (int c = hh * HD; c < hh * HD + HD; c += 32) {
         float o[32];
         tmem_ld32(tO + lane_off + c, o);
 #pragma unroll
@@ -292,11 +300,11 @@ static int attention_tc_try(const th_attention_args* a, cudaStream_t st, int* rc
   if (D == 128) {
     static bool set = false;
     if (!set) { cudaFuncSetAttribute(attention_tc_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, AtCfg<128>::SMEM); set = true; }
-    attention_tc_kernel<T, 128><<<grid, 192, AtCfg<128>::SMEM, st>>>(tq, tk, tv, *a);
+    attention_tc_kernel<T, 128><<<grid, 320, AtCfg<128>::SMEM, st>>>(tq, tk, tv, *a);
   } else {
     static bool set = false;
     if (!set) { cudaFuncSetAttribute(attention_tc_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AtCfg<64>::SMEM); set = true; }
-    attention_tc_kernel<T, 64><<<grid, 192, AtCfg<64>::SMEM, st>>>(tq, tk, tv, *a);
+    attention_tc_kernel<T, 64><<<grid, 320, AtCfg<64>::SMEM, st>>>(tq, tk, tv, *a);
   }
   *rc = check_launch("th_attention(tcgen05)");
   return 0;
