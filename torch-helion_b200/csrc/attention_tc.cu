@@ -32,8 +32,8 @@ struct AtCfg {
   static constexpr int OFF_K = Q_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
   static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
-  static constexpr int OFF_RED = OFF_P + P_BYTES;   // row-max / row-sum exchange between the halves
-  static constexpr int OFF_BAR = OFF_RED + 4 * 128 * 4;
+  static constexpr int OFF_RED = OFF_P + 2 * P_BYTES;  // P double-buffered; then the row-max / row-sum
+  static constexpr int OFF_BAR = OFF_RED + 2 * 128 * 4;  // exchange between the two column halves
   static constexpr int SMEM = 1024 + OFF_BAR + 256;
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
@@ -57,9 +57,9 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* s_full = bars + 5;         // [2]
   uint64_t* s_free = bars + 7;         // [2]
   uint64_t* p_full = bars + 9;
-  uint64_t* pv_done = bars + 10;
-  uint64_t* mma_done = bars + 11;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* pv_done = bars + 10;       // [2], one per P buffer
+  uint64_t* mma_done = bars + 12;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 13);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -81,7 +81,8 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&s_free[s], 8);
     }
     mbar_init(p_full, 8);
-    mbar_init(pv_done, 1);
+    mbar_init(&pv_done[0], 1);
+    mbar_init(&pv_done[1], 1);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -144,14 +145,15 @@ __global__ void __launch_bounds__(320, 1)
         tc_fence_after();
         const int s = j & 1;
         const uint32_t va = smem_u32(sm + C::OFF_V + s * C::KV_BYTES);
+        const uint32_t pb = pa + s * C::P_BYTES;
 #pragma unroll
         for (int k = 0; k < C::BN / 16; ++k) {
           // A = P rows x kv (K-major, 2 atoms of 128 rows); B = V kv x D (MN-major, atoms 128 rows apart)
           const uint32_t poff = (uint32_t)((k >> 2) * C::BM * 128 + (k & 3) * 32);
-          tc_mma_f16(tO, make_desc_sw128(pa + poff, 16, 1024),
+          tc_mma_f16(tO, make_desc_sw128(pb + poff, 16, 1024),
                      make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o, (j | k) ? 1u : 0u);
         }
-        tc_commit(pv_done);
+        tc_commit(&pv_done[s]);
         tc_commit(&kv_empty[s]);
       }
       tc_commit(mma_done);
@@ -164,7 +166,7 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const float sl2 = p.scale * 1.4426950408889634f;
     constexpr int HB = C::BN / 2, HD = D / 2;
-    float* red = reinterpret_cast<float*>(sm + C::OFF_RED);  // [2 parities][2 halves][128 rows]
+    float* red = reinterpret_cast<float*>(sm + C::OFF_RED);  // [2 halves][128 rows]
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
@@ -201,14 +203,18 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[s]);
       // row max over both halves (the scale is positive)
-      red[(s * 2 + hh) * 128 + r] = mx;
+      red[hh * 128 + r] = mx;
       named_bar(1, 256);
-      mx = fmaxf(red[(s * 2) * 128 + r], red[(s * 2 + 1) * 128 + r]) * sl2;
+      mx = fmaxf(red[r], red[128 + r]) * sl2;
+      named_bar(1, 256);  // both halves have read before the next block's maxima are written
       const float m_new = fmaxf(m_ref, mx);
       const bool rescale = j > 0 && m_new > m_ref + 8.0f;
       const bool any_rescale = __any_sync(0xffffffffu, rescale);
-      // P_{j-1} must be consumed (and O complete) before P_j / O are touched
-      if (j > 0) ok = __all_sync(0xffffffffu, ok && mbar_wait(pv_done, (j - 1) & 1, abort_flag));
+      // O is rescaled only once O += P_{j-1} V_{j-1} is complete; P_j's buffer is free once
+      // P_{j-2} V_{j-2} is (the other buffer lets P_j be written while P_{j-1} V_{j-1} runs)
+      if (j > 0 && any_rescale)
+        ok = __all_sync(0xffffffffu, ok && mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag));
+      if (j > 1) ok = __all_sync(0xffffffffu, ok && mbar_wait(&pv_done[s], ((j - 2) >> 1) & 1, abort_flag));
       if (ok) {
         tc_fence_after();
         if (j == 0) {
@@ -229,7 +235,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         const float mref = (m_ref == -INFINITY) ? 0.f : m_ref;  // fully masked row: P = 0
         // P = exp2(s*scale - m_ref) -> bf16 operand tile, running sum (2^-inf = 0 for masked scores)
-        uint8_t* pt = sm + C::OFF_P;
+        uint8_t* pt = sm + C::OFF_P + s * C::P_BYTES;
 #pragma unroll
         for (int c = 0; c < HB; c += 8) {
           float pe[8];
@@ -248,10 +254,9 @@ __global__ void __launch_bounds__(320, 1)
     }
     // epilogue: O / l, l summed over both halves
     if (ok && nkv > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (nkv - 1) & 1, abort_flag));
+      ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, abort_flag));
       tc_fence_after();
     }
-    named_bar(1, 256);  // the last block's maxima have been read
     red[hh * 128 + r] = l;
     named_bar(1, 256);
     const float lt = red[r] + red[128 + r];
