@@ -1,0 +1,108 @@
+"""Time one C-ABI kernel on seeded synthetic operands.
+
+    python -m torch_helion.b200.microbench attention --batch 1 --seq 4096 --hq 32 --hkv 8 --head-dim 128 --causal
+    python -m torch_helion.b200.microbench ssd --batch 4 --seq 2048 --heads 24 --state 128
+    python -m torch_helion.b200.microbench gemm --m 8192 --n 3328 --k 768
+    python -m torch_helion.b200.microbench conv --batch 4 --seq 2048 --channels 1792
+
+Each mode runs 3 warm-up launches and times ``--iters`` launches with CUDA
+events (L2 flushed before each when ``--flush``), printing one JSON line with
+the median time and the kernel's algorithmic throughput.  This is the
+command behind the single-kernel ncu captures.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+from . import lib
+
+
+def _time(fn, iters: int, flush: bool) -> float:
+    buf = torch.empty(64 << 20, dtype=torch.float32, device="cuda") if flush else None
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        if buf is not None:
+            buf.fill_(1.0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    ts.sort()
+    return ts[len(ts) // 2] / 1e3  # seconds
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("kernel", choices=["attention", "ssd", "gemm", "conv"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--hq", type=int, default=32)
+    ap.add_argument("--hkv", type=int, default=8)
+    ap.add_argument("--head-dim", type=int, default=128)
+    ap.add_argument("--causal", action="store_true")
+    ap.add_argument("--heads", type=int, default=24)
+    ap.add_argument("--state", type=int, default=128)
+    ap.add_argument("--m", type=int, default=8192)
+    ap.add_argument("--n", type=int, default=3328)
+    ap.add_argument("--k", type=int, default=768)
+    ap.add_argument("--channels", type=int, default=1792)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--flush", action="store_true")
+    a = ap.parse_args(argv)
+    torch.manual_seed(0)
+    dev, bf = "cuda", torch.bfloat16
+    if a.kernel == "attention":
+        t = a.batch * a.seq
+        q = torch.randn(t, a.hq * a.head_dim, device=dev).to(bf)
+        k = torch.randn(t, a.hkv * a.head_dim, device=dev).to(bf)
+        v = torch.randn(t, a.hkv * a.head_dim, device=dev).to(bf)
+        o = torch.empty_like(q)
+        fn = lambda: lib.attention(q, k, v, o, batch=a.batch, seq=a.seq, hq=a.hq, hkv=a.hkv, head_dim=a.head_dim,
+                                   scale=a.head_dim ** -0.5, causal=a.causal)
+        work, unit = 4.0 * a.batch * a.hq * a.seq * a.seq * a.head_dim * (0.5 if a.causal else 1.0), "TFLOP/s"
+    elif a.kernel == "ssd":
+        t, h, p, n = a.batch * a.seq, a.heads, 64, a.state
+        x = torch.randn(t, h * p, device=dev).to(bf)
+        B = torch.randn(t, n, device=dev).to(bf)
+        C = torch.randn(t, n, device=dev).to(bf)
+        dt = torch.exp(torch.rand(t, h, device=dev) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3))
+        A = -torch.exp(torch.rand(h, device=dev) * math.log(16.0))
+        D = torch.ones(h, device=dev)
+        z = torch.randn(t, h * p, device=dev).to(bf)
+        out = torch.empty(t, h * p, device=dev, dtype=bf)
+        gss = torch.empty(t, h, device=dev)
+        ws = torch.empty(lib.ssd_workspace_size(a.batch, a.seq, h, p, n, 256), dtype=torch.uint8, device=dev)
+        fn = lambda: lib.ssd(x, dt, A, B, C, out, batch=a.batch, seq=a.seq, heads=h, head_dim=p, ngroups=1,
+                             state_dim=n, chunk=256, D=D, z=z, gss=gss, workspace=ws)
+        work, unit = t * (4 * h * p * 2 + 2 * n * 2 + 4 * h + 4 * h), "GB/s"  # x, z in; y out; B, C; dt; gss
+    elif a.kernel == "gemm":
+        x = torch.randn(a.m, a.k, device=dev).to(bf)
+        w = (torch.randn(a.n, a.k, device=dev) * 0.02).to(bf)
+        d = torch.empty(a.m, a.n, device=dev, dtype=bf)
+        fn = lambda: lib.gemm(x, w, d)
+        work, unit = 2.0 * a.m * a.n * a.k, "TFLOP/s"
+    else:
+        t = a.batch * a.seq
+        x = torch.randn(t, a.channels, device=dev).to(bf)
+        w = torch.randn(a.channels, 4, device=dev)
+        y = torch.empty_like(x)
+        fn = lambda: lib.conv1d(x, w, y, batch=a.batch, seq=a.seq, act=lib.ACT_SILU)
+        work, unit = 2.0 * t * a.channels * 2, "GB/s"
+    sec = _time(fn, a.iters, a.flush)
+    rate = work / sec / (1e12 if unit == "TFLOP/s" else 1e9)
+    print(json.dumps({"kernel": a.kernel, "args": vars(a), "us": sec * 1e6, "rate": rate, "unit": unit,
+                      "device_error": lib.device_error()}))
+
+
+if __name__ == "__main__":
+    main()
