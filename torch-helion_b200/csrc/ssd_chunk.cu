@@ -13,16 +13,16 @@
 //   cum, dt and colf_l = exp(cum_{l|31} - cum_l) dt_l.  This replaces the
 //   separate chunk-state and inter-chunk passes and their fp32 round trips.
 //
-// ssd_scan_mh -- one CTA per (query half, chunk, set of heads, batch).  The
-//   heads of one B/C group share C.B^T, so the CTA computes it once into TMEM
-//   and then, head by head:
+// ssd_scan_mh -- one CTA per (chunk, set of heads, batch), in two passes:
+//   query rows 128-255 (256 keys), then rows 0-127 (128 keys), so every CTA
+//   carries the same work.  The heads of one B/C group share C.B^T, so each
+//   pass computes it once into TMEM and then, head by head:
 //     G = C.B^T * exp(cum_i - cum_j) dt_j  (j <= i), plus D on the diagonal
 //         (CUDA cores: TMEM -> bf16 128B-swizzled shared-memory operand)
 //     Y = G . x + exp(cum_i) (C . S_in)     (tcgen05, two TMEM buffers)
 //     y = Y * silu(z) -> shared memory -> TMA store, per-head sum of y^2
 //   D on the diagonal of G makes G . x carry the D x skip, so x can be
-//   released as soon as the MMA has read it.  Rows 128-255 of a chunk see 256
-//   keys, rows 0-127 see 128; the heavy halves are scheduled first.
+//   released as soon as the MMA has read it.
 //   Below-diagonal 32-column blocks use exp(ci - cj) = exp(ci - c_ref)
 //   exp(c_ref - cj) with c_ref the block's last column (both factors <= 1).
 //
@@ -278,23 +278,34 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
-  // heavy (rows 128-255) CTAs first
+  // one CTA per (chunk, head set, batch) does the rows 128-255 (256 keys) and then the rows 0-127
+  // (128 keys) of its heads, so every CTA carries the same work
   const int hpg = p.heads / p.ngroups;
-  const int units = p.batch * nc * p.ngroups * nsets;
-  const int qb = (int)blockIdx.x < units ? 1 : 0;
-  int u = qb ? (int)blockIdx.x : (int)blockIdx.x - units;
+  int u = (int)blockIdx.x;
   const int set = u % (p.ngroups * nsets);
   u /= p.ngroups * nsets;
   const int c = u % nc, b = u / nc;
   const int g = set / nsets, h0 = g * hpg + (set % nsets) * hs;
   const int hcount = min(hs, g * hpg + hpg - h0);
   const int s0 = c * CK_L, len = min(CK_L, p.seq - s0);
-  if (hcount <= 0 || qb * 128 >= len) return;  // nothing to compute (uniform over the CTA)
-  const int nk = qb ? 256 : 128;
+  if (hcount <= 0) return;  // nothing to compute (uniform over the CTA)
   const bool has_s = c > 0, has_z = p.z != nullptr;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) {
+  if (tid == 0) *abort_flag = 0;
+  if (warp == 1) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  for (int pass = 0; pass < 2; ++pass) {
+  const int qb = 1 - pass;
+  if (qb * 128 >= len) continue;  // a chunk of at most 128 rows has no second half (uniform)
+  const int nk = qb ? 256 : 128;
+  if (tid == 0) {  // fresh barriers for each pass (the previous pass has fully drained)
+    uint64_t* all = bar;
+    if (pass > 0)
+      for (int i = 0; i < 22; ++i) mbar_inval(&all[i]);  // bar[0..21]; bar[22] holds the TMEM address
     mbar_init(cb_full, 1);
     mbar_init(cb_done, 1);
     for (int i = 0; i < 2; ++i) {
@@ -308,14 +319,9 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
     for (int i = 0; i < CK_SR; ++i) { mbar_init(&sc_full[i], 1); mbar_init(&sc_free[i], 1); }
     mbar_init(z_full, 1);
     mbar_init(y_ready, 1);
-    *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tslot, 512);
-  tc_fence_before();
   __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tslot;
   const float* scal_bc = scal + ((int64_t)b * p.heads * nc + c) * CK_SCAL;  // + head * nc * CK_SCAL
 
   if (warp == 0) {
@@ -547,8 +553,9 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
     }
   }
   tc_fence_before();
-  __syncthreads();
+  __syncthreads();  // this pass has drained: every store, load and MMA is complete
   tc_fence_after();
+  }  // pass
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
@@ -593,7 +600,7 @@ static int ssd_chunk_try(const th_ssd_args* a, cudaStream_t st, int* rc) {
                                                                                           nc, scal);
   *rc = check_launch("th_ssd(chunk states, tcgen05)");
   if (*rc) return 0;
-  // head sets: about one heavy CTA per SM
+  // head sets: about one CTA per SM
   const int hpg = a->heads / a->ngroups;
   const int per = a->batch * nc * a->ngroups;
   int nsets = per >= sm_count() ? 1 : sm_count() / per;
@@ -601,7 +608,7 @@ static int ssd_chunk_try(const th_ssd_args* a, cudaStream_t st, int* rc) {
   const int hs = (hpg + nsets - 1) / nsets;
   nsets = (hpg + hs - 1) / hs;
   const int units = per * nsets;
-  ssd_scan_mh<T><<<2 * units, 64 + SC_MATH, ScC::SMEM, st>>>(m, *a, nc, hs, nsets, scal);
+  ssd_scan_mh<T><<<units, 64 + SC_MATH, ScC::SMEM, st>>>(m, *a, nc, hs, nsets, scal);
   *rc = check_launch("th_ssd(scan, tcgen05 multi-head)");
   return 0;
 }
