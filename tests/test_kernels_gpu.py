@@ -176,6 +176,63 @@ def test_gemm_swiglu(L, dtype):
     assert rel_l2(out.float(), ref) < TOL[dtype]
 
 
+@pytest.mark.parametrize("case", ["plain", "residual", "tail", "swiglu", "rope"])
+@pytest.mark.parametrize("m", [4000, 8192])
+def test_gemm_pair_tiles(L, case, m):
+    """Shapes that take the CTA-pair kernel at its 128-, 192- and 256-column
+    widths (on 148 SMs), with a ragged last row tile (m = 4000) that leaves
+    the odd CTA of the last pair partly or wholly past the end."""
+    torch.manual_seed(6)
+    dt = torch.bfloat16
+    k = 512
+    if case == "swiglu":
+        f = 2048
+        x = torch.randn(m, k, device=_dev()).to(dt)
+        wg, wu = torch.randn(f, k, device=_dev()) * 0.05, torch.randn(f, k, device=_dev()) * 0.05
+        w = torch.stack((wg.reshape(f // 64, 64, k), wu.reshape(f // 64, 64, k)), 1).reshape(2 * f, k).to(dt)
+        out = torch.empty(m, f, device=_dev(), dtype=dt)
+        L.gemm(x, w, out, swiglu=True)
+        ref = F.silu(x.float() @ wg.to(dt).float().t()) * (x.float() @ wu.to(dt).float().t())
+        assert rel_l2(out.float(), ref) < TOL[dt]
+        return
+    n = {"plain": 640, "residual": 768, "tail": 3352, "rope": 6144}[case]
+    x = torch.randn(m, k, device=_dev()).to(dt)
+    w = (torch.randn(n, k, device=_dev()) * 0.05).to(dt)
+    acc = _gemm_ref(x, w)
+    if case == "plain":
+        out = torch.empty(m, n, device=_dev(), dtype=dt)
+        L.gemm(x, w, out)
+        ref = acc
+    elif case == "residual":
+        res = torch.randn(m, n, device=_dev()).to(dt)
+        parts = L.rowstat(x).reshape(m, 1)
+        out = torch.empty(m, n, device=_dev(), dtype=dt)
+        L.gemm(x, w, out, rs_parts=parts, rs_inv_k=1.0 / k, rs_eps=1e-6, residual=res)
+        r = torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6)
+        ref = acc * r + res.float()
+    elif case == "tail":
+        nmain = n - 24
+        bias = torch.randn(24, device=_dev())
+        out = torch.empty(m, nmain, device=_dev(), dtype=dt)
+        dtail = torch.empty(m, 24, device=_dev())
+        L.gemm(x, w, out, act=L.ACT_SOFTPLUS, act_begin=nmain, act_end=n, bias=bias, out2=dtail, tail_begin=nmain)
+        assert rel_l2(dtail, F.softplus(acc[:, nmain:] + bias)) < 1e-3
+        ref = acc[:, :nmain]
+    else:
+        hd, seq = 128, m // 2
+        inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=_dev()).float() / hd))
+        fr = torch.outer(torch.arange(seq, device=_dev()).float(), inv)
+        emb = torch.cat((fr, fr), -1)
+        cos, sin = emb.cos().contiguous(), emb.sin().contiguous()
+        out = torch.empty(m, n, device=_dev(), dtype=dt)
+        rope_end = n - 1024
+        L.gemm(x, w, out, rope_cos=cos, rope_sin=sin, rope_begin=0, rope_end=rope_end, rope_head_dim=hd)
+        ref = torch.cat((_rope_ref(acc[:, :rope_end], cos, sin, hd, seq), acc[:, rope_end:]), -1)
+    torch.cuda.synchronize()
+    assert L.device_error() == 0
+    assert rel_l2(out.float(), ref) < TOL[dt]
+
+
 def test_gemm_rejects_bad_alignment(L):
     a = torch.randn(64, 100, device=_dev(), dtype=torch.bfloat16)  # lda=100: 200 B rows, not 16-B multiple
     w = torch.randn(64, 100, device=_dev(), dtype=torch.bfloat16)

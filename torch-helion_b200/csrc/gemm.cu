@@ -10,6 +10,8 @@
 // Both stage the accumulator tile in shared memory and run the same
 // epilogue (row scale, activation segment, RoPE, SwiGLU, residual, stores,
 // sum-of-squares partials), so the two paths have identical semantics.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace th {
@@ -118,12 +120,7 @@ __device__ void epilogue_tile(const float* tile, int ldt, float* rscale, const E
 #pragma unroll
             for (int e = 0; e < 8; ++e) v[e] += r8[e];
           }
-          store8<T>(d + (int64_t)row * ep.ldd + oc, v);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float q = round_to<T>(v[e]);
-            ss += q * q;
-          }
+          ss = store8_ss<T>(d + (int64_t)row * ep.ldd + oc, v);
         }
       }
       if (ep.ss_out) {
@@ -147,6 +144,19 @@ __device__ void epilogue_tile(const float* tile, int ldt, float* rscale, const E
 // The two accumulators (2*BN TMEM columns) let the epilogue of tile i overlap
 // the mainloop of tile i+1.  Every wait is bounded (mbar_wait): a stuck
 // pipeline sets the device error word and the kernel drains and exits.
+// Tile order of the persistent kernels: groups of 8 row tiles walked column
+// by column, so the tiles in flight (one per CTA or CTA pair) share a few row
+// tiles of A and one band of B rows, both L2-resident even when B alone is
+// larger than L2 (a 28672 x 4096 gate|up weight is 235 MB).
+__device__ __forceinline__ int2 tile_coords(int tile, int tiles_m, int tiles_n) {
+  constexpr int GM = 8;
+  const int per_group = GM * tiles_n;
+  const int g = tile / per_group, r = tile - g * per_group;
+  const int rows_left = tiles_m - g * GM;
+  const int gm = rows_left < GM ? rows_left : GM;
+  return make_int2(g * GM + r % gm, r / gm);  // (row tile, column tile)
+}
+
 template <int BN>
 struct TcCfg {
   static constexpr int BM = 128, BK = 64;
@@ -161,11 +171,13 @@ struct TcCfg {
 
 // Residual add, store, fp32 tail and sum-of-squares partials of a 32-value
 // row chunk whose first element is output column `oc`.  Returns the chunk's
-// sum of squares of the stored (rounded) values.
+// sum of squares of the stored (rounded) values (0 when the GEMM has no
+// sum-of-squares output).
 template <typename T>
 __device__ __forceinline__ float finish_chunk(float* v, int row, int oc, int n_out, const EpiParams& ep) {
   T* d = reinterpret_cast<T*>(ep.d);
   const T* res = reinterpret_cast<const T*>(ep.residual);
+  const bool want_ss = ep.ss_out != nullptr;
   float ss = 0.f;
 #pragma unroll
   for (int e8 = 0; e8 < 32; e8 += 8) {
@@ -184,12 +196,8 @@ __device__ __forceinline__ float finish_chunk(float* v, int row, int oc, int n_o
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[e8 + e] += r8[e];
     }
-    store8<T>(d + (int64_t)row * ep.ldd + c, v + e8);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float q = round_to<T>(v[e8 + e]);
-      ss += q * q;
-    }
+    if (want_ss) ss += store8_ss<T>(d + (int64_t)row * ep.ldd + c, v + e8);
+    else store8<T>(d + (int64_t)row * ep.ldd + c, v + e8);
   }
   return ss;
 }
@@ -216,6 +224,7 @@ __device__ __forceinline__ void epilogue_row_res(uint32_t tbase, int row, bool r
                                                  const EpiParams& ep, uint4 (&rb)[3][4]) {
   const int n_out = ep.n;
   T* d = reinterpret_cast<T*>(ep.d);
+  const bool want_ss = ep.ss_out != nullptr;
   float ss = 0.f;
 #pragma unroll
   for (int ci = 0; ci < NC; ++ci) {
@@ -251,12 +260,8 @@ __device__ __forceinline__ void epilogue_row_res(uint32_t tbase, int row, bool r
         const T* rh = reinterpret_cast<const T*>(&u);
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e8 * 8 + e] += to_f32(rh[e]);
-        store8<T>(d + (int64_t)row * ep.ldd + cc, v + e8 * 8);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float q = round_to<T>(v[e8 * 8 + e]);
-          ss += q * q;
-        }
+        if (want_ss) ss += store8_ss<T>(d + (int64_t)row * ep.ldd + cc, v + e8 * 8);
+        else store8<T>(d + (int64_t)row * ep.ldd + cc, v + e8 * 8);
       }
     }
     if ((ci & 1) == 1) {
@@ -343,6 +348,47 @@ __device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_o
   }
 }
 
+// One epilogue warp's share (warps 2..9: two per TMEM lane quarter, each one
+// half of the columns) of the 128 x BN accumulator tile at TMEM column
+// `tacc` whose first output row is m0: the row scale and the first residual
+// chunks are fetched while the accumulator fills, then the rows are finished.
+// Returns false when the wait for the accumulator gave up.
+template <typename T, int BN, int EPI>
+__device__ __forceinline__ bool epilogue_tmem_tile(uint32_t tacc, int warp, int lane, int m0, int n0, uint64_t* tfull,
+                                              uint32_t parity, volatile int* abort_flag, const EpiParams& ep) {
+  const int q = warp & 3;  // TMEM lane quarter this warp may read
+  const int hh = (warp - 2) >> 2;
+  const int rl = q * 32 + lane;
+  // a head of RoPE or a 128-column gate|up block must not straddle the halves
+  constexpr bool split = !((EPI & EPI_SWIGLU) != 0 && BN < 256);
+  const bool rope_whole = (EPI & EPI_ROPE) != 0 && ep.rope_hd > BN / 2;
+  const bool halves = split && !rope_whole;
+  const int cb = halves ? hh * (BN / 2) : 0, ce = halves ? cb + BN / 2 : (hh ? 0 : BN);
+  const int row = m0 + rl;
+  const bool row_ok = row < ep.m;
+  float rs = 1.f;
+  if (ep.rs_parts && row_ok && ce > cb) {
+    const float* pp = ep.rs_parts + (int64_t)row * ep.rs_nparts;
+    float sacc = 0.f;
+    for (int k = 0; k < ep.rs_nparts; ++k) sacc += pp[k];
+    rs = rsqrtf(sacc * ep.rs_inv_k + ep.rs_eps);
+  }
+  uint4 rb[3][4];
+  if constexpr ((EPI & EPI_RES) != 0) {
+    res_issue<T>(rb[0], row, row_ok, n0 + cb, ep);
+    res_issue<T>(rb[1], row, row_ok, n0 + cb + 32, ep);
+  }
+  if (!mbar_wait(tfull, parity, abort_flag)) return false;
+  __syncwarp();
+  tc_fence_after();
+  const uint32_t tb = tacc + ((uint32_t)(q * 32) << 16);
+  if constexpr ((EPI & EPI_RES) != 0) epilogue_row_res<T, BN / 64>(tb, row, row_ok, rs, n0, cb, ep, rb);
+  else if (ce > cb) epilogue_row<T, BN, EPI>(tb, row, row_ok, rs, n0, cb, ce, ep);
+  tc_fence_before();
+  __syncwarp();
+  return true;
+}
+
 template <typename T, int BN, int EPI>
 __global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiParams ep,
@@ -389,7 +435,8 @@ __global__ void __launch_bounds__(320, 1)
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-        const int m0 = (tile / tiles_n) * C::BM, n0 = (tile % tiles_n) * BN;
+        const int2 tc = tile_coords(tile, tiles_m, tiles_n);
+        const int m0 = tc.x * C::BM, n0 = tc.y * BN;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
@@ -409,7 +456,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++i) {
         const int acc = i & 1, use = i >> 1;
         // the last column tile multiplies only its live columns (N rounded up to 16)
-        const int nlive = ep.n - (tile % tiles_n) * BN;
+        const int nlive = ep.n - tile_coords(tile, tiles_m, tiles_n).y * BN;
         const int ntile = nlive >= BN ? BN : ((nlive + 15) & ~15);
         const uint32_t idesc = make_idesc_f16(128, ntile, fmt, 0, 0);
         if (!mbar_wait(&tempty[acc], (use & 1) ^ 1, abort_flag)) break;
@@ -435,41 +482,14 @@ __global__ void __launch_bounds__(320, 1)
       tc_commit(done);  // tracks every MMA this thread issued
     }
   } else {  // ---- epilogue warps 2..9: two per TMEM lane quarter, each one half of the tile's columns
-    const int q = warp & 3;  // TMEM lane quarter this warp may read
-    const int hh = (warp - 2) >> 2;
-    const int rl = q * 32 + lane;
-    // a head of RoPE or a 128-column gate|up block must not straddle the halves
-    constexpr bool split = !((EPI & EPI_SWIGLU) != 0 && BN < 256);
-    const bool rope_whole = (EPI & EPI_ROPE) != 0 && ep.rope_hd > BN / 2;
-    const bool halves = split && !rope_whole;
-    const int cb = halves ? hh * (BN / 2) : 0, ce = halves ? cb + BN / 2 : (hh ? 0 : BN);
     int i = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++i) {
       const int acc = i & 1, use = i >> 1;
-      const int m0 = (tile / tiles_n) * C::BM, n0 = (tile % tiles_n) * BN;
-      const int row = m0 + rl;
-      const bool row_ok = row < ep.m;
-      // row scale and the first residual chunks are fetched while the accumulator fills
-      float rs = 1.f;
-      if (ep.rs_parts && row_ok && ce > cb) {
-        const float* pp = ep.rs_parts + (int64_t)row * ep.rs_nparts;
-        float sacc = 0.f;
-        for (int k = 0; k < ep.rs_nparts; ++k) sacc += pp[k];
-        rs = rsqrtf(sacc * ep.rs_inv_k + ep.rs_eps);
-      }
-      uint4 rb[3][4];
-      if constexpr ((EPI & EPI_RES) != 0) {
-        res_issue<T>(rb[0], row, row_ok, n0 + cb, ep);
-        res_issue<T>(rb[1], row, row_ok, n0 + cb + 32, ep);
-      }
-      if (!mbar_wait(&tfull[acc], use & 1, abort_flag)) break;
-      __syncwarp();
-      tc_fence_after();
-      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      if constexpr ((EPI & EPI_RES) != 0) epilogue_row_res<T, BN / 64>(tb, row, row_ok, rs, n0, cb, ep, rb);
-      else if (ce > cb) epilogue_row<T, BN, EPI>(tb, row, row_ok, rs, n0, cb, ce, ep);
-      tc_fence_before();
-      __syncwarp();
+      const int2 tc = tile_coords(tile, tiles_m, tiles_n);
+      const int m0 = tc.x * C::BM, n0 = tc.y * BN;
+      if (!epilogue_tmem_tile<T, BN, EPI>(tmem + (uint32_t)(acc * BN), warp, lane, m0, n0, &tfull[acc], use & 1,
+                                          abort_flag, ep))
+        break;
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
   }
@@ -482,6 +502,160 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// ------------------------------------------------- tcgen05 CTA-pair path
+// Cluster of two CTAs on an SM pair computing 256 x BN tiles with
+// tcgen05.mma.cta_group::2: each CTA stages its own 128 rows of A and one half
+// (BN/2 rows) of B per k-block, so a CTA moves (128 + BN/2) x 64 operands for
+// a 128 x BN x 64 product, against (128 + BN) x 64 in the single-CTA kernel.
+//   warp 0 (both CTAs)  TMA: its A rows and B half into its own ring; the bytes
+//                       are counted on the even CTA's `full` barrier
+//   warp 1 (even CTA)   MMA issuer; each ring-slot / accumulator commit arrives
+//                       on the barrier of both CTAs
+//   warps 2-9 (both)    epilogue of the CTA's 128 rows (its TMEM lanes); the
+//                       odd CTA's warps release the accumulator on the even
+//                       CTA's `tempty` barrier
+// No TMA load multicasts: each CTA loads only its own operands.
+template <int BN>
+struct Tc2Cfg {
+  static constexpr int BM = 128, BK = 64;  // per CTA; the pair's tile is 256 x BN
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (196 * 1024) / STAGE_BYTES > 8 ? 8 : (196 * 1024) / STAGE_BYTES;
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;  // a power of two
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + RING_BYTES + 256 /*barriers*/;
+};
+
+template <typename T, int BN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiParams ep,
+                    int K, int tiles_m, int tiles_n) {
+  using C = Tc2Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int ntiles = tiles_m * tiles_n;
+  const int nk = (K + C::BK - 1) / C::BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 16);  // one arrive per epilogue warp of both CTAs
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  __syncwarp();
+  if (warp == 0) tmem_alloc_pair(tmem_slot, C::TMEM_COLS);  // the same warp in both CTAs
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // columns the pair multiplies on a tile (the last column tile: its live
+  // columns rounded up to 16); CTA r holds B rows [r * nt / 2, (r + 1) * nt / 2)
+  auto tile_cols = [&](int tile) {
+    const int nlive = ep.n - tile_coords(tile, tiles_m, tiles_n).y * BN;
+    return nlive >= BN ? BN : ((nlive + 15) & ~15);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer (both CTAs)
+      const uint32_t full0 = cluster_addr(full, 0);
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < ntiles; tile += npairs) {
+        const int2 tc = tile_coords(tile, tiles_m, tiles_n);
+        const int m0 = tc.x * 2 * C::BM + (int)rank * C::BM;
+        const int nb = tc.y * BN + (int)rank * (tile_cols(tile) / 2);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+          uint8_t* sa = smem + s * C::STAGE_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
+          const uint32_t fb = full0 + (uint32_t)(s * 8);
+          tma_load_2d_pair(sa, &tmA, fb, kb * C::BK, m0);
+          tma_load_2d_pair(sa + C::A_BYTES, &tmB, fb, kb * C::BK, nb);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {  // ---- MMA issuer (even CTA)
+      constexpr int fmt = DT<T>::id == TH_BF16 ? 1 : 0;
+      int it = 0, i = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < ntiles; tile += npairs, ++i) {
+        const int acc = i & 1, use = i >> 1;
+        const uint32_t idesc = make_idesc_f16(256, tile_cols(tile), fmt, 0, 0);
+        if (!mbar_wait(&tempty[acc], (use & 1) ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < C::BK / 16; ++k) {
+            const uint64_t ad = make_desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = make_desc_sw128(sb + k * 32, 16, 1024);
+            tc_mma_f16_pair(d, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit_pair_both(&empty[s]);
+        }
+        if (ok) tc_commit_pair_both(&tfull[acc]);
+      }
+      tc_commit_pair(done);  // tracks every MMA this thread issued
+    }
+  } else {  // ---- epilogue warps 2..9 (both CTAs): this CTA's 128 rows of the pair's tile
+    const uint32_t tempty0 = cluster_addr(tempty, 0);
+    int i = 0;
+    for (int tile = pair; tile < ntiles; tile += npairs, ++i) {
+      const int acc = i & 1, use = i >> 1;
+      const int2 tc = tile_coords(tile, tiles_m, tiles_n);
+      const int m0 = tc.x * 2 * C::BM + (int)rank * C::BM, n0 = tc.y * BN;
+      if (!epilogue_tmem_tile<T, BN, EPI>(tmem + (uint32_t)(acc * BN), warp, lane, m0, n0, &tfull[acc], use & 1,
+                                          abort_flag, ep))
+        break;
+      if (lane == 0) mbar_arrive_cluster(tempty0 + (uint32_t)(acc * 8));
+    }
+  }
+  __syncwarp();
+  // teardown: the even CTA waits (bounded) for its MMAs to retire; then neither
+  // CTA frees TMEM or exits while the other may still touch its barriers
+  if (leader && threadIdx.x == 64) {
+    volatile int dummy = 0;
+    mbar_wait(done, 0, &dummy);
+  }
+  __syncwarp();  // the cluster barrier is .aligned: warps arrive converged
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc_pair(tmem, C::TMEM_COLS);
 }
 
 // --------------------------------------------------------------- FFMA path
@@ -552,6 +726,71 @@ static int launch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st
   return check_launch("th_gemm(tcgen05)");
 }
 
+template <typename T, int BN, int EPI>
+static int launch_tc2(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st) {
+  using C = Tc2Cfg<BN>;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, a->a, a->dtype, (uint64_t)a->k, (uint64_t)a->m, (uint64_t)a->lda * 2, 64, C::BM, true);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tb, a->w, a->dtype, (uint64_t)a->k, (uint64_t)a->n, (uint64_t)a->ldw * 2, 64, BN / 2, true);
+  if (rc) return rc;
+  static bool attr_set = false;  // once per instantiation (keeps it out of CUDA-graph captures)
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemm_tc2_kernel<T, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    attr_set = true;
+  }
+  const int tiles_m = (int)((a->m + 2 * C::BM - 1) / (2 * C::BM)), tiles_n = (int)((a->n + BN - 1) / BN);
+  const int ntiles = tiles_m * tiles_n, pairs = sm_count() / 2;
+  const int grid = 2 * (ntiles < pairs ? ntiles : pairs);
+  gemm_tc2_kernel<T, BN, EPI><<<grid, 320, C::SMEM_BYTES, st>>>(ta, tb, ep, (int)a->k, tiles_m, tiles_n);
+  return check_launch("th_gemm(tcgen05 pair)");
+}
+
+// Tile width of the pair kernel: the one with the least wave-quantised work,
+// rounds x (BN + 32) (the 32 stands for a tile's fixed cost).  192 is offered
+// only where no 64-column group (SwiGLU block, RoPE head, sum-of-squares
+// group) may straddle the epilogue's column halves.
+static int pair_mode() {  // TH_GEMM_PAIR: 0 single-CTA kernel, 1 (default) pair kernel, 128/192/256 its width
+  static const int env = [] {
+    const char* e = getenv("TH_GEMM_PAIR");
+    return e ? atoi(e) : 1;
+  }();
+  return env;
+}
+
+static int pair_width(const th_gemm_args* a) {
+  const int64_t tm = (a->m + 255) / 256, pairs = sm_count() / 2;
+  const bool no192 = a->swiglu || a->rope_cos || a->ss_out;
+  const int forced = pair_mode();
+  if (forced == 256 || forced == 128 || (forced == 192 && !no192)) return forced;
+  int best = 256;
+  int64_t best_cost = INT64_MAX;
+  for (int bn : {256, 192, 128}) {
+    if (bn == 192 && no192) continue;
+    const int64_t rounds = (tm * ((a->n + bn - 1) / bn) + pairs - 1) / pairs;
+    const int64_t cost = rounds * (bn + 32);
+    if (cost < best_cost) best_cost = cost, best = bn;
+  }
+  return best;
+}
+
+template <typename T>
+static int dispatch_tc2(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st) {
+  const int bn = pair_width(a);
+  if (a->swiglu) return bn == 256 ? launch_tc2<T, 256, EPI_SWIGLU>(a, ep, st) : launch_tc2<T, 128, EPI_SWIGLU>(a, ep, st);
+  if (a->rope_cos) return bn == 256 ? launch_tc2<T, 256, EPI_ROPE>(a, ep, st) : launch_tc2<T, 128, EPI_ROPE>(a, ep, st);
+  if (a->residual) {
+    if (bn == 256) return launch_tc2<T, 256, EPI_RES>(a, ep, st);
+    return bn == 192 ? launch_tc2<T, 192, EPI_RES>(a, ep, st) : launch_tc2<T, 128, EPI_RES>(a, ep, st);
+  }
+  if (bn == 256) return launch_tc2<T, 256, 0>(a, ep, st);
+  return bn == 192 ? launch_tc2<T, 192, 0>(a, ep, st) : launch_tc2<T, 128, 0>(a, ep, st);
+}
+
+// The pair kernel serves every 2-byte GEMM with more than one 128-row tile
+// (TH_GEMM_PAIR=0 in the environment selects the single-CTA kernel instead).
+static bool use_pair(const th_gemm_args* a) { return pair_mode() != 0 && a->m > 128 && sm_count() >= 2; }
+
 static bool is_al16(const void* p) { return p == nullptr || aligned16(p); }
 
 template <typename T>
@@ -618,6 +857,10 @@ extern "C" int th_gemm(const th_gemm_args* a, void* stream) {
     const int64_t tm = (a->m + 127) / 128, sms = sm_count();
     const int64_t r256 = (tm * ((a->n + 255) / 256) + sms - 1) / sms, r128 = (tm * ((a->n + 127) / 128) + sms - 1) / sms;
     if (r128 * 128 * 5 <= r256 * 256 * 4) wide = false;
+  }
+  if (use_pair(a)) {
+    if (a->dtype == TH_BF16) return dispatch_tc2<__nv_bfloat16>(a, ep, st);
+    return dispatch_tc2<__half>(a, ep, st);
   }
   if (a->dtype == TH_BF16) return dispatch_tc<__nv_bfloat16>(a, ep, st, wide);
   return dispatch_tc<__half>(a, ep, st, wide);

@@ -2,13 +2,22 @@
 
     python -m torch_helion.b200.microbench attention --batch 1 --seq 4096 --hq 32 --hkv 8 --head-dim 128 --causal
     python -m torch_helion.b200.microbench ssd --batch 4 --seq 2048 --heads 24 --state 128
-    python -m torch_helion.b200.microbench gemm --m 8192 --n 3328 --k 768
+    python -m torch_helion.b200.microbench ssd-sweep --flush
+    python -m torch_helion.b200.microbench gemm --m 8192 --n 3328 --k 768 --vs-torch
     python -m torch_helion.b200.microbench conv --batch 4 --seq 2048 --channels 1792
+    python -m torch_helion.b200.microbench rmsnorm --m 8192 --k 768
 
 Each mode runs 3 warm-up launches and times ``--iters`` launches with CUDA
 events (L2 flushed before each when ``--flush``), printing one JSON line with
 the median time and the kernel's algorithmic throughput.  This is the
 command behind the single-kernel ncu captures.
+
+``ssd-sweep`` is the standalone chunked-scan sweep: batch 8, 64 heads of 64,
+one B/C group, chunk 256, d_state in {64, 128, 256} x seqlen in {512, 2048,
+8192, 16384}, no gate and no D skip; one JSON line per point.  Its bytes per
+token are x in + y out (bf16), B and C (bf16) and dt (fp32, the ABI's dt
+type), and the line carries the fraction of the measured HBM copy bandwidth
+and of the measured bf16 tensor peak.
 """
 
 from __future__ import annotations
@@ -16,6 +25,7 @@ from __future__ import annotations
 import argparse
 import json
 import math
+from pathlib import Path
 
 import torch
 
@@ -41,9 +51,54 @@ def _time(fn, iters: int, flush: bool) -> float:
     return ts[len(ts) // 2] / 1e3  # seconds
 
 
+def _ssd_case(batch: int, seq: int, h: int, n: int, gate: bool, p: int = 64):
+    """th_ssd on seeded operands: x, B, C ~ N(0, 1) bf16, dt log-uniform in
+    [1e-3, 0.1], A = -exp(U[0, log 16]).  Returns (launch, algorithmic bytes)."""
+    dev, bf = "cuda", torch.bfloat16
+    t = batch * seq
+    x = torch.randn(t, h * p, device=dev).to(bf)
+    B = torch.randn(t, n, device=dev).to(bf)
+    C = torch.randn(t, n, device=dev).to(bf)
+    dt = torch.exp(torch.rand(t, h, device=dev) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3))
+    A = -torch.exp(torch.rand(h, device=dev) * math.log(16.0))
+    D = torch.ones(h, device=dev) if gate else None
+    z = torch.randn(t, h * p, device=dev).to(bf) if gate else None
+    out = torch.empty(t, h * p, device=dev, dtype=bf)
+    gss = torch.empty(t, h, device=dev) if gate else None
+    ws = torch.empty(lib.ssd_workspace_size(batch, seq, h, p, n, 256), dtype=torch.uint8, device=dev)
+    fn = lambda: lib.ssd(x, dt, A, B, C, out, batch=batch, seq=seq, heads=h, head_dim=p, ngroups=1,
+                         state_dim=n, chunk=256, D=D, z=z, gss=gss, workspace=ws)
+    per_tok = 2 * h * p * 2 + 2 * n * 2 + 4 * h          # x in, y out, B, C, dt
+    per_tok += (h * p * 2 + 4 * h) if gate else 0         # z in, per-head sum of squares out
+    return fn, t * per_tok
+
+
+def _ssd_sweep(a) -> None:
+    peaks_file = Path(__file__).resolve().parents[3] / "MEASURED_PEAKS.json"
+    peaks = json.loads(peaks_file.read_text()) if peaks_file.exists() else {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+    src = "measured" if peaks_file.exists() else "fallback"
+    h, p, batch, L = 64, 64, 8, 256
+    for n in (64, 128, 256):
+        for seq in (512, 2048, 8192, 16384):
+            fn, nbytes = _ssd_case(batch, seq, h, n, gate=False)
+            sec = _time(fn, a.iters, a.flush)
+            t = batch * seq
+            flops = t * h * (2 * L * p + 4 * p * n + 2 * L * n / h)
+            gbs, tfs = nbytes / sec / 1e9, flops / sec / 1e12
+            ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+            print(json.dumps({"kernel": "ssd", "batch": batch, "heads": h, "head_dim": p, "state": n, "seq": seq,
+                              "us": sec * 1e6, "bytes": nbytes, "flops": flops, "GB/s": gbs,
+                              "hbm_frac": gbs / peaks["hbm_gbs"], "TFLOP/s": tfs,
+                              "tensor_frac": tfs / peaks["bf16_tflops"],
+                              "bound": "hbm" if flops / nbytes < ridge else "tensor", "peaks": src,
+                              "device_error": lib.device_error()}), flush=True)
+            del fn
+            torch.cuda.empty_cache()
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("kernel", choices=["attention", "ssd", "gemm", "conv"])
+    ap.add_argument("kernel", choices=["attention", "ssd", "ssd-sweep", "gemm", "conv", "rmsnorm", "rowstat"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--hq", type=int, default=32)
@@ -58,9 +113,15 @@ def main(argv=None) -> None:
     ap.add_argument("--channels", type=int, default=1792)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--flush", action="store_true")
+    ap.add_argument("--no-gate", action="store_true", help="ssd: no silu(z) gate, no D skip, no row sums")
+    ap.add_argument("--vs-torch", action="store_true", help="gemm: also time torch.matmul (cuBLAS)")
     a = ap.parse_args(argv)
     torch.manual_seed(0)
     dev, bf = "cuda", torch.bfloat16
+    extra: dict = {}
+    if a.kernel == "ssd-sweep":
+        _ssd_sweep(a)
+        return
     if a.kernel == "attention":
         t = a.batch * a.seq
         q = torch.randn(t, a.hq * a.head_dim, device=dev).to(bf)
@@ -71,26 +132,28 @@ def main(argv=None) -> None:
                                    scale=a.head_dim ** -0.5, causal=a.causal)
         work, unit = 4.0 * a.batch * a.hq * a.seq * a.seq * a.head_dim * (0.5 if a.causal else 1.0), "TFLOP/s"
     elif a.kernel == "ssd":
-        t, h, p, n = a.batch * a.seq, a.heads, 64, a.state
-        x = torch.randn(t, h * p, device=dev).to(bf)
-        B = torch.randn(t, n, device=dev).to(bf)
-        C = torch.randn(t, n, device=dev).to(bf)
-        dt = torch.exp(torch.rand(t, h, device=dev) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3))
-        A = -torch.exp(torch.rand(h, device=dev) * math.log(16.0))
-        D = torch.ones(h, device=dev)
-        z = torch.randn(t, h * p, device=dev).to(bf)
-        out = torch.empty(t, h * p, device=dev, dtype=bf)
-        gss = torch.empty(t, h, device=dev)
-        ws = torch.empty(lib.ssd_workspace_size(a.batch, a.seq, h, p, n, 256), dtype=torch.uint8, device=dev)
-        fn = lambda: lib.ssd(x, dt, A, B, C, out, batch=a.batch, seq=a.seq, heads=h, head_dim=p, ngroups=1,
-                             state_dim=n, chunk=256, D=D, z=z, gss=gss, workspace=ws)
-        work, unit = t * (4 * h * p * 2 + 2 * n * 2 + 4 * h + 4 * h), "GB/s"  # x, z in; y out; B, C; dt; gss
+        fn, work = _ssd_case(a.batch, a.seq, a.heads, a.state, gate=not a.no_gate)
+        unit = "GB/s"
     elif a.kernel == "gemm":
         x = torch.randn(a.m, a.k, device=dev).to(bf)
         w = (torch.randn(a.n, a.k, device=dev) * 0.02).to(bf)
         d = torch.empty(a.m, a.n, device=dev, dtype=bf)
         fn = lambda: lib.gemm(x, w, d)
         work, unit = 2.0 * a.m * a.n * a.k, "TFLOP/s"
+        if a.vs_torch:  # cuBLAS through torch on the same operands, for comparison
+            extra["torch_us"] = _time(lambda: torch.matmul(x, w.t()), a.iters, a.flush) * 1e6
+    elif a.kernel in ("rmsnorm", "rowstat"):  # --m rows x --k columns
+        x = torch.randn(a.m, a.k, device=dev).to(bf)
+        if a.kernel == "rmsnorm":
+            g = torch.rand(a.k, device=dev) + 0.5
+            y = torch.empty_like(x)
+            fn = lambda: lib.rmsnorm(x, g, 1e-5, out=y)
+            work = 2.0 * a.m * a.k * 2
+        else:
+            s_out = torch.empty(a.m, device=dev)
+            fn = lambda: lib.rowstat(x, out=s_out)
+            work = a.m * a.k * 2 + a.m * 4.0
+        unit = "GB/s"
     else:
         t = a.batch * a.seq
         x = torch.randn(t, a.channels, device=dev).to(bf)
@@ -100,7 +163,7 @@ def main(argv=None) -> None:
         work, unit = 2.0 * t * a.channels * 2, "GB/s"
     sec = _time(fn, a.iters, a.flush)
     rate = work / sec / (1e12 if unit == "TFLOP/s" else 1e9)
-    print(json.dumps({"kernel": a.kernel, "args": vars(a), "us": sec * 1e6, "rate": rate, "unit": unit,
+    print(json.dumps({"kernel": a.kernel, "args": vars(a), "us": sec * 1e6, "rate": rate, "unit": unit, **extra,
                       "device_error": lib.device_error()}))
 
 
