@@ -126,6 +126,95 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, i
   }
 }
 
+// ------------------------------------------- 2-byte rows held in registers
+// Rows of up to 256*RV elements (multiples of 8) of a 2-byte type: a warp
+// issues every 16-byte load of ROWS rows before the first is used, so each
+// warp keeps ROWS * cols * 2 bytes in flight.  The RMSNorm gain is staged in
+// shared memory once per block (16-byte reads, no per-element global loads).
+template <typename T, int RV, int ROWS>
+__global__ void __launch_bounds__(256) rowstat_rows(const T* __restrict__ x, int64_t ldx, float* __restrict__ out,
+                                                    int64_t rows, int cols) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r0 = wid * ROWS; r0 < rows; r0 += nw * ROWS) {
+    uint4 u[ROWS][RV];
+#pragma unroll
+    for (int k = 0; k < RV; ++k) {
+      const int c = (k * 32 + lane) * 8;
+#pragma unroll
+      for (int j = 0; j < ROWS; ++j)
+        if (c < cols && r0 + j < rows) u[j][k] = *reinterpret_cast<const uint4*>(x + (r0 + j) * ldx + c);
+    }
+    float s[ROWS];
+#pragma unroll
+    for (int j = 0; j < ROWS; ++j) {
+      s[j] = 0.f;
+#pragma unroll
+      for (int k = 0; k < RV; ++k) {
+        if ((k * 32 + lane) * 8 >= cols) break;
+        const T* h = reinterpret_cast<const T*>(&u[j][k]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { const float v = to_f32(h[e]); s[j] = fmaf(v, v, s[j]); }
+      }
+      s[j] = warp_sum(s[j]);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int j = 0; j < ROWS; ++j)
+        if (r0 + j < rows) out[r0 + j] = s[j];
+    }
+  }
+}
+
+template <typename T, int RV, int ROWS>
+__global__ void __launch_bounds__(256) rmsnorm_rows(const T* __restrict__ x, int64_t ldx, const float* __restrict__ g,
+                                                    T* __restrict__ y, int64_t ldy, int64_t rows, int cols, float eps) {
+  extern __shared__ float4 gain4[];  // cols / 4
+  float* gain = reinterpret_cast<float*>(gain4);
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) gain[c] = g ? g[c] : 1.f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r0 = wid * ROWS; r0 < rows; r0 += nw * ROWS) {
+    uint4 u[ROWS][RV];
+#pragma unroll
+    for (int k = 0; k < RV; ++k) {
+      const int c = (k * 32 + lane) * 8;
+#pragma unroll
+      for (int j = 0; j < ROWS; ++j)
+        if (c < cols && r0 + j < rows) u[j][k] = *reinterpret_cast<const uint4*>(x + (r0 + j) * ldx + c);
+    }
+#pragma unroll
+    for (int j = 0; j < ROWS; ++j) {
+      if (r0 + j >= rows) break;
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < RV; ++k) {
+        if ((k * 32 + lane) * 8 >= cols) break;
+        const T* h = reinterpret_cast<const T*>(&u[j][k]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { const float v = to_f32(h[e]); s = fmaf(v, v, s); }
+      }
+      s = warp_sum(s);
+      const float rs = rsqrtf(s / (float)cols + eps);
+#pragma unroll
+      for (int k = 0; k < RV; ++k) {
+        const int c = (k * 32 + lane) * 8;
+        if (c >= cols) break;
+        const T* h = reinterpret_cast<const T*>(&u[j][k]);
+        const float4 ga = gain4[c / 4], gb = gain4[c / 4 + 1];
+        const float gv[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = to_f32(h[e]) * rs * gv[e];
+        store8<T>(y + (r0 + j) * ldy + c, v);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------ causal conv1d
 // One thread = CONV_TPT consecutive tokens x 8 consecutive channels; a
 // 32 x CONV_TY block covers 256 channels x (CONV_TY*CONV_TPT) tokens.  A warp reads 512
@@ -357,6 +446,13 @@ __global__ void __launch_bounds__(256) embedding_kernel(const int64_t* __restric
   }
 }
 
+// Blocks of 8 warps for `rows` rows at `per_warp` rows per warp (one pass,
+// at most 8 blocks per SM; larger inputs loop).
+static unsigned rows_grid(int64_t rows, int per_warp) {
+  const int64_t want = (rows + 8 * per_warp - 1) / (8 * per_warp), cap = (int64_t)sm_count() * 8;
+  return (unsigned)(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
 static unsigned row_grid(int64_t rows) {
   const int64_t per_block = 8;  // warps per 256-thread block
   int64_t want = (rows + per_block - 1) / per_block;
@@ -372,8 +468,19 @@ extern "C" int th_rowstat(const th_rowstat_args* a, void* stream) {
   if (a->rows <= 0 || a->cols <= 0 || a->ldx < a->cols || a->cols > INT32_MAX) return fail(TH_EINVAL, "th_rowstat: bad shape");
   if ((a->cols % 8 == 0) && (!aligned16(a->x) || a->ldx % 8)) return fail(TH_EALIGN, "th_rowstat: x must be 16-B aligned with ldx %% 8 == 0");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const unsigned g = row_grid(a->rows);
   const bool small = a->cols <= 1024;
+  if (a->dtype != TH_F32 && a->cols % 8 == 0 && a->cols <= 4096) {  // rows in registers, two at a time when short
+    const unsigned g = small ? rows_grid(a->rows, 2) : rows_grid(a->rows, 1);
+    if (a->dtype == TH_BF16) {
+      auto k = small ? rowstat_rows<__nv_bfloat16, 4, 2> : rowstat_rows<__nv_bfloat16, 16, 1>;
+      k<<<g, 256, 0, st>>>((const __nv_bfloat16*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols);
+    } else {
+      auto k = small ? rowstat_rows<__half, 4, 2> : rowstat_rows<__half, 16, 1>;
+      k<<<g, 256, 0, st>>>((const __half*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols);
+    }
+    return check_launch("th_rowstat");
+  }
+  const unsigned g = row_grid(a->rows);
   switch (a->dtype) {
     case TH_F32: (small ? rowstat_kernel<float, 4> : rowstat_kernel<float, 16>)<<<g, 256, 0, st>>>((const float*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols); break;
     case TH_BF16: (small ? rowstat_kernel<__nv_bfloat16, 4> : rowstat_kernel<__nv_bfloat16, 16>)<<<g, 256, 0, st>>>((const __nv_bfloat16*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols); break;
@@ -390,8 +497,22 @@ extern "C" int th_rmsnorm(const th_rmsnorm_args* a, void* stream) {
   if ((a->cols % 8 == 0) && (!aligned16(a->x) || !aligned16(a->y) || a->ldx % 8 || a->ldy % 8))
     return fail(TH_EALIGN, "th_rmsnorm: x/y must be 16-B aligned with ld %% 8 == 0");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const unsigned g = row_grid(a->rows);
   const bool small = a->cols <= 1024;
+  if (a->dtype != TH_F32 && a->cols % 8 == 0 && a->cols <= 4096) {  // rows in registers, gain in shared memory
+    const unsigned g = small ? rows_grid(a->rows, 2) : rows_grid(a->rows, 1);
+    const size_t sm = (size_t)a->cols * 4;
+    if (a->dtype == TH_BF16) {
+      auto k = small ? rmsnorm_rows<__nv_bfloat16, 4, 2> : rmsnorm_rows<__nv_bfloat16, 16, 1>;
+      k<<<g, 256, sm, st>>>((const __nv_bfloat16*)a->x, a->ldx, a->gain, (__nv_bfloat16*)a->y, a->ldy, a->rows,
+                            (int)a->cols, a->eps);
+    } else {
+      auto k = small ? rmsnorm_rows<__half, 4, 2> : rmsnorm_rows<__half, 16, 1>;
+      k<<<g, 256, sm, st>>>((const __half*)a->x, a->ldx, a->gain, (__half*)a->y, a->ldy, a->rows, (int)a->cols,
+                            a->eps);
+    }
+    return check_launch("th_rmsnorm");
+  }
+  const unsigned g = row_grid(a->rows);
   switch (a->dtype) {
     case TH_F32: (small ? rmsnorm_kernel<float, 4> : rmsnorm_kernel<float, 16>)<<<g, 256, 0, st>>>((const float*)a->x, a->ldx, a->gain, (float*)a->y, a->ldy, a->rows, (int)a->cols, a->eps); break;
     case TH_BF16: (small ? rmsnorm_kernel<__nv_bfloat16, 4> : rmsnorm_kernel<__nv_bfloat16, 16>)<<<g, 256, 0, st>>>((const __nv_bfloat16*)a->x, a->ldx, a->gain, (__nv_bfloat16*)a->y, a->ldy, a->rows, (int)a->cols, a->eps); break;

@@ -41,6 +41,7 @@ def _time(fn, iters: int, flush: bool) -> float:
     for _ in range(iters):
         if buf is not None:
             buf.fill_(1.0)
+        torch.cuda._sleep(200_000)  # keeps the GPU busy while the host enqueues the timed launch
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         fn()
