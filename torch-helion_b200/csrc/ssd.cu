@@ -301,7 +301,10 @@ extern "C" size_t th_ssd_workspace_size(int32_t batch, int32_t seq, int32_t head
   const int64_t nch = (seq + chunk - 1) / chunk;
   const int64_t states = (int64_t)batch * nch * heads * head_dim * state_dim;
   const int64_t cum = (int64_t)batch * heads * nch * chunk;
-  return (size_t)(states + cum) * sizeof(float);
+  const size_t general = (size_t)(states + cum) * sizeof(float);
+  // the chunk-256 tcgen05 path: scalar records and two bf16 state sets
+  const size_t chunked = th::ck_ws_bytes(batch, seq, heads, state_dim, head_dim);
+  return general > chunked ? general : chunked;
 }
 
 extern "C" int th_ssd(const th_ssd_args* a, void* stream) {

@@ -43,9 +43,13 @@ constexpr int CK_SR = 4;  // scalar ring depth of the scan
 inline size_t ck_scal_bytes(int batch, int heads, int nc) {
   return ((size_t)batch * heads * nc * CK_SCAL * 4 + 1023) & ~size_t(1023);
 }
-inline size_t ck_ws_bytes(int batch, int seq, int heads, int ns) {
+// scalar records | S_in (bf16, one slot per chunk; slot 0 unused) | S_c (bf16; last slot unused)
+inline size_t ck_state_bytes(int batch, int nc, int heads, int ns, int p) {
+  return (size_t)batch * nc * heads * ns * p * 2;
+}
+inline size_t ck_ws_bytes(int batch, int seq, int heads, int ns, int p = CK_P) {
   const int nc = (seq + CK_L - 1) / CK_L;
-  return ck_scal_bytes(batch, heads, nc) + (size_t)batch * nc * heads * ns * CK_P * 2;
+  return ck_scal_bytes(batch, heads, nc) + 2 * ck_state_bytes(batch, nc, heads, ns, p);
 }
 
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
@@ -226,6 +230,243 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, 128);
+}
+
+// ------------------------------------------------- chunk states, parallel
+// ssd_chunk_states -- a persistent kernel over units (batch, chunk, head,
+//   128-row half of the state), consecutive units sharing the chunk's B: per
+//   unit it computes the chunk's scalars (cum, dt, colf and D, written when
+//   the unit is the state's first half), scales x rows by w_l and forms the
+//   chunk's own state S_c = B^T (w . x) with one M=128 N=64 K=256 MMA, stored
+//   bf16.  Two shared-memory stages and two TMEM buffers overlap the loads of
+//   unit j+1, the MMA of unit j and the state store of unit j-1.  The last
+//   chunk's state is not needed and is not formed.
+// ssd_state_pass -- the inter-chunk recurrence in fp32, elementwise over the
+//   state: S_in(c+1) = exp(cum_last(c)) S_in(c) + S_c(c), stored bf16 for
+//   the scan.
+struct SpC {
+  static constexpr int B_BYTES = 2 * CK_L * 128;  // two 64-wide state atoms x 256 rows
+  static constexpr int X_BYTES = CK_L * 128;
+  static constexpr int DT_BYTES = CK_L * 16;      // dt of 4 heads x 256 rows (fp32)
+  static constexpr int STAGE = B_BYTES + X_BYTES + DT_BYTES;
+  static constexpr int OFF_F = 2 * STAGE;         // warp totals, two sets of 8
+  static constexpr int OFF_BAR = OFF_F + 64;
+  static constexpr int SMEM = 1024 + OFF_BAR + 128;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+
+template <typename T>
+__global__ void __launch_bounds__(320, 1)
+    ssd_chunk_states(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmX,
+                     const __grid_constant__ CUtensorMap tmDT, th_ssd_args p, int nc, float* __restrict__ scal,
+                     T* __restrict__ sc) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* wtot = reinterpret_cast<float*>(sm + SpC::OFF_F);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + SpC::OFF_BAR);
+  uint64_t* empty = full + 2;
+  uint64_t* ready = full + 4;
+  uint64_t* tdone = full + 6;
+  uint64_t* tfree = full + 8;
+  uint64_t* fin = full + 10;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 11);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int H = p.heads, NS = p.state_dim;
+  const int nhalf = (NS + 127) / 128;  // 128-row halves of the state (one for d_state 64)
+  const int units = p.batch * nc * H * nhalf;
+  const int hpg = H / p.ngroups;
+  auto need = [&](int u) { return (u / (H * nhalf)) % nc < nc - 1; };  // the chunk's state is used
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+      mbar_init(&ready[i], 256);
+      mbar_init(&tdone[i], 1);
+      mbar_init(&tfree[i], 8);
+    }
+    mbar_init(fin, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tslot, 128);  // two unit-state buffers of 64 columns
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer
+      int j = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&empty[s], ((j >> 1) - 1) & 1, abort_flag)) break;
+        const int nh = u % nhalf, h = (u / nhalf) % H, c = (u / (nhalf * H)) % nc, b = u / (nhalf * H * nc);
+        const int g = h / hpg;
+        uint8_t* st = sm + s * SpC::STAGE;
+        const bool nd = need(u);
+        mbar_arrive_expect_tx(&full[s], nd ? (NS >= 128 ? SpC::STAGE : SpC::STAGE - CK_L * 128) : SpC::DT_BYTES);
+        if (nd) {
+          tma_load_3d(st, &tmB, &full[s], g * NS + nh * 128, c * CK_L, b);
+          if (NS >= 128) tma_load_3d(st + CK_L * 128, &tmB, &full[s], g * NS + nh * 128 + 64, c * CK_L, b);
+          tma_load_3d(st + SpC::B_BYTES, &tmX, &full[s], h * CK_P, c * CK_L, b);
+        }
+        tma_load_3d(st + SpC::B_BYTES + SpC::X_BYTES, &tmDT, &full[s], h & ~3, c * CK_L, b);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      constexpr int fmt = DT<T>::id == TH_BF16 ? 1 : 0;
+      constexpr uint32_t idesc = make_idesc_f16(128, 64, fmt, 1, 1);  // A = B^T and B = x, both MN-major
+      int j = 0, k = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&ready[s], (j >> 1) & 1, abort_flag)) break;
+        if (!need(u)) {  // scalars only: hand the stage back
+          mbar_arrive(&empty[s]);
+          continue;
+        }
+        if (k >= 2 && !mbar_wait(&tfree[k & 1], ((k >> 1) - 1) & 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(sm + s * SpC::STAGE);
+        for (int kk = 0; kk < CK_L / 16; ++kk) {
+          const uint64_t ad = make_desc_sw128(st + kk * 2048, CK_L * 128, 1024);
+          const uint64_t bd = make_desc_sw128(st + SpC::B_BYTES + kk * 2048, CK_L * 128, 1024);
+          tc_mma_f16(tmem + (k & 1) * 64, ad, bd, idesc, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&tdone[k & 1]);
+        tc_commit(&empty[s]);
+        ++k;
+      }
+      tc_commit(fin);  // tracks every MMA this thread issued
+    }
+  } else {
+    // 256 math threads: token row l = mt for the scalars and x; for a state
+    // store, row n = q*32 + lane of TMEM quadrant q, columns half*32..+32
+    const int mt = tid - 64, wm = warp - 2;
+    const int q = warp & 3, half = wm >> 2;
+    const int n = q * 32 + lane;
+    bool ok = true;
+    int j = 0, k = 0;
+    int pu = -1;  // the previous unit whose state waits to be stored
+    auto store_state = [&](int u, int kb) {  // TMEM buffer kb & 1 -> S_c of unit u
+      ok = ok && mbar_wait(&tdone[kb & 1], (kb >> 1) & 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        float sv[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (kb & 1) * 64 + half * 32, sv);
+        tc_fence_before();
+        const int nh = u % nhalf, h = (u / nhalf) % H, c = (u / (nhalf * H)) % nc, b = u / (nhalf * H * nc);
+        const int row = nh * 128 + n;
+        if (row < NS) {
+          T* dst = sc + ((((int64_t)b * nc + c) * H + h) * NS + row) * CK_P + half * 32;
+#pragma unroll
+          for (int e8 = 0; e8 < 32; e8 += 8) store8<T>(dst + e8, sv + e8);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tfree[kb & 1]);
+    };
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+      const int s = j & 1;
+      const int nh = u % nhalf, h = (u / nhalf) % H, c = (u / (nhalf * H)) % nc, b = u / (nhalf * H * nc);
+      const bool nd = need(u);
+      uint8_t* st = sm + s * SpC::STAGE;
+      ok = ok && mbar_wait(&full[s], (j >> 1) & 1, abort_flag);
+      // inclusive prefix sum of dt*A over the chunk (rows past the sequence were zero-filled by TMA)
+      const int l = mt;
+      const float* dtv = reinterpret_cast<const float*>(st + SpC::B_BYTES + SpC::X_BYTES);
+      const float d = ok ? dtv[l * 4 + (h & 3)] : 0.f;
+      float v = d * p.A[h];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      float* wt = wtot + (j & 1) * 8;  // two sets: a warp is at most one unit ahead of the others
+      if (lane == 31) wt[wm] = v;
+      named_bar(1, 256);
+      float off = 0.f, total = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const float t = wt[w];
+        off += w < wm ? t : 0.f;
+        total += t;
+      }
+      const float cl = off + v;
+      const float c_last31 = __shfl_sync(0xffffffffu, cl, 31);  // cum of row l | 31
+      if (nh == 0) {  // the chunk's scalar record for the scan
+        float* rec = scal + (((int64_t)b * H + h) * nc + c) * CK_SCAL;
+        rec[l] = cl;
+        rec[CK_L + l] = d;
+        rec[2 * CK_L + l] = __expf(c_last31 - cl) * d;
+        if (mt == 0) *reinterpret_cast<float4*>(rec + 3 * CK_L) = make_float4(p.D ? p.D[h] : 0.f, 0.f, 0.f, 0.f);
+      }
+      if (nd && ok) {  // x row l scaled by w_l = exp(total - cum_l) dt_l, in place, chunks in swizzled order
+        const float w_l = __expf(total - cl) * d;
+        T* xr = reinterpret_cast<T*>(st + SpC::B_BYTES + l * 128);
+#pragma unroll
+        for (int i8 = 0; i8 < 8; ++i8) {
+          const int e8 = (i8 ^ (l & 7)) * 8;
+          float f[8];
+          load8<T>(xr + e8, f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] *= w_l;
+          store8<T>(xr + e8, f);
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(&ready[s]);
+      // the previous unit's state leaves while this unit's MMA runs
+      if (pu >= 0) {
+        store_state(pu, k - 1);
+        pu = -1;
+      }
+      if (nd) {
+        pu = u;
+        ++k;
+      }
+    }
+    if (pu >= 0) store_state(pu, k - 1);
+    if (tid == 64) {  // bounded: the MMAs retire before TMEM is freed, also after an abort
+      volatile int dummy = 0;
+      mbar_wait(fin, 0, &dummy);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 128);
+}
+
+// S_in(0) = 0; S_in(c+1) = exp(cum_last(c)) S_in(c) + S_c(c), four state
+// elements per thread, fp32 running state; S_in(c) stored for c >= 1.
+template <typename T>
+__global__ void __launch_bounds__(256) ssd_state_pass(th_ssd_args p, int nc, const float* __restrict__ scal,
+                                                      const T* __restrict__ sc, T* __restrict__ sin) {
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int64_t per = (int64_t)p.state_dim * CK_P;  // elements of one state
+  const int64_t e = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (e >= per) return;
+  float sv[4] = {0.f, 0.f, 0.f, 0.f};
+  const float* rec = scal + ((int64_t)b * p.heads + h) * nc * CK_SCAL;
+  for (int c = 0; c + 1 < nc; ++c) {
+    const int64_t slot = (((int64_t)b * nc + c) * p.heads + h) * per + e;
+    const uint2 raw = *reinterpret_cast<const uint2*>(sc + slot);
+    const T* hv = reinterpret_cast<const T*>(&raw);
+    const float f = __expf(rec[(int64_t)c * CK_SCAL + CK_L - 1]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sv[i] = fmaf(f, sv[i], to_f32(hv[i]));
+    uint2 o;
+    T* ov = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ov[i] = from_f32<T>(sv[i]);
+    *reinterpret_cast<uint2*>(sin + slot + per * p.heads) = o;  // slot of chunk c + 1
+  }
 }
 
 // -------------------------------------------------------------------- scan
@@ -474,8 +715,15 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
 #pragma unroll
               for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(raw[hf][e]);
               if (fact) {
+                const float4* cf4 = reinterpret_cast<const float4*>(colf + jc);  // 16-byte aligned: jc % 16 == 0
 #pragma unroll
-                for (int e = 0; e < 16; ++e) v[e] *= rf * colf[jc + e];
+                for (int e4 = 0; e4 < 4; ++e4) {
+                  const float4 cf = cf4[e4];
+                  v[4 * e4 + 0] *= rf * cf.x;
+                  v[4 * e4 + 1] *= rf * cf.y;
+                  v[4 * e4 + 2] *= rf * cf.z;
+                  v[4 * e4 + 3] *= rf * cf.w;
+                }
               } else {
 #pragma unroll
                 for (int e = 0; e < 16; ++e) v[e] *= __expf(ci - cum[jc + e]) * dts[jc + e];
@@ -533,10 +781,8 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
               if (has_s) y += e_prev * yo[c8 * 8 + e];
               if (has_z) y *= silu_tanh(zf[e]);
               o[e] = y;
-              const float qv = round_to<T>(y);
-              ss += qv * qv;
             }
-            store8<T>(at, o);
+            ss += store8_ss<T>(at, o);  // sum of squares of the stored (rounded) values
           }
           fence_proxy_async();
           red[cq * 128 + r] = ss;
@@ -572,7 +818,8 @@ static int ssd_chunk_try(const th_ssd_args* a, cudaStream_t st, int* rc) {
   if (!aligned16(a->workspace) || a->workspace_bytes < ck_ws_bytes(a->batch, a->seq, a->heads, CK_NS)) return 1;
   const int nc = (a->seq + CK_L - 1) / CK_L;
   float* scal = reinterpret_cast<float*>(a->workspace);
-  void* sin = reinterpret_cast<uint8_t*>(a->workspace) + ck_scal_bytes(a->batch, a->heads, nc);
+  T* sin = reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(a->workspace) + ck_scal_bytes(a->batch, a->heads, nc));
+  T* sc = reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(sin) + ck_state_bytes(a->batch, nc, a->heads, CK_NS, CK_P));
   const uint64_t gw = (uint64_t)a->ngroups * CK_NS, xw = (uint64_t)a->heads * CK_P;
   const uint64_t S = (uint64_t)a->seq, Bt = (uint64_t)a->batch;
   ScMaps m;
@@ -593,13 +840,33 @@ static int ssd_chunk_try(const th_ssd_args* a, cudaStream_t st, int* rc) {
   static bool set = false;
   if (!set) {
     cudaFuncSetAttribute(ssd_state_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, StC::SMEM);
+    cudaFuncSetAttribute(ssd_chunk_states<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SpC::SMEM);
     cudaFuncSetAttribute(ssd_scan_mh<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScC::SMEM);
     set = true;
   }
-  ssd_state_tc<T><<<dim3((unsigned)a->heads, (unsigned)a->batch), 320, StC::SMEM, st>>>(m.B256, m.X256, tdt, m.S, *a,
-                                                                                          nc, scal);
-  *rc = check_launch("th_ssd(chunk states, tcgen05)");
-  if (*rc) return 0;
+  static const bool serial = [] {  // TH_SSD_STATES=p selects the parallel chunk states + pass
+    const char* e = getenv("TH_SSD_STATES");
+    return !(e && e[0] == 'p');
+  }();
+  if (serial) {
+    ssd_state_tc<T><<<dim3((unsigned)a->heads, (unsigned)a->batch), 320, StC::SMEM, st>>>(m.B256, m.X256, tdt, m.S,
+                                                                                            *a, nc, scal);
+    *rc = check_launch("th_ssd(chunk states, tcgen05)");
+    if (*rc) return 0;
+  } else {
+    const int units = a->batch * nc * a->heads * ((CK_NS + 127) / 128);
+    const int grid = units < sm_count() ? units : sm_count();
+    ssd_chunk_states<T><<<grid, 320, SpC::SMEM, st>>>(m.B256, m.X256, tdt, *a, nc, scal, sc);
+    *rc = check_launch("th_ssd(chunk states, parallel)");
+    if (*rc) return 0;
+    if (nc > 1) {
+      const int per = CK_NS * CK_P / 4;
+      ssd_state_pass<T><<<dim3((unsigned)((per + 255) / 256), (unsigned)a->heads, (unsigned)a->batch), 256, 0, st>>>(
+          *a, nc, scal, sc, sin);
+      *rc = check_launch("th_ssd(state pass)");
+      if (*rc) return 0;
+    }
+  }
   // head sets: about one CTA per SM
   const int hpg = a->heads / a->ngroups;
   const int per = a->batch * nc * a->ngroups;
