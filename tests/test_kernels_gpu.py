@@ -310,7 +310,12 @@ def _ssd_recurrence(x, dt, A, B, C, D, b, s, h, p, g, n):
                                                # tcgen05 chunk-state + multi-head scan: state 128; head sets,
                                                # two groups, a chunk shorter than 128 rows, many chunks
                                                (2, 1024, 24, 64, 1, 128, 256), (1, 600, 8, 64, 2, 128, 256),
-                                               (1, 100, 4, 64, 1, 128, 256), (1, 4096, 2, 64, 1, 128, 256)])
+                                               (1, 100, 4, 64, 1, 128, 256), (1, 4096, 2, 64, 1, 128, 256),
+                                               # the same path at state 64 and 256 (chunk-parallel states + pass;
+                                               # 256: B in two halves, single-buffered x | S_in)
+                                               (2, 1024, 24, 64, 1, 64, 256), (2, 512, 6, 64, 3, 64, 256),
+                                               (1, 600, 8, 64, 2, 256, 256), (1, 100, 4, 64, 1, 256, 256),
+                                               (1, 2048, 4, 64, 1, 256, 256)])
 def test_ssd_matches_recurrence(L, dtype, b, s, h, p, g, n, chunk):
     torch.manual_seed(8)
     t = b * s
@@ -332,10 +337,11 @@ def test_ssd_matches_recurrence(L, dtype, b, s, h, p, g, n, chunk):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("gate", [False, True])
-def test_ssd_chunk_path_optional_operands(L, dtype, gate):
+@pytest.mark.parametrize("n", [64, 128, 256])
+def test_ssd_chunk_path_optional_operands(L, dtype, gate, n):
     """The tcgen05 chunk path with and without z, D and gss."""
     torch.manual_seed(11)
-    b, s, h, p, g, n = 2, 640, 6, 64, 1, 128
+    b, s, h, p, g = 2, 640, 6, 64, 1
     t = b * s
     x = torch.randn(t, h * p, device=_dev()).to(dtype)
     B = torch.randn(t, g * n, device=_dev()).to(dtype)

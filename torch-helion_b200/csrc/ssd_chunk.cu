@@ -470,23 +470,31 @@ __global__ void __launch_bounds__(256) ssd_state_pass(th_ssd_args p, int nc, con
 }
 
 // -------------------------------------------------------------------- scan
-struct ScC {
-  static constexpr int KAT = CK_NS / 64;
-  static constexpr int C_BYTES = KAT * 128 * 128;    // 128 query rows
-  static constexpr int B_BYTES = KAT * CK_L * 128;   // up to 256 keys
-  static constexpr int G_BYTES = 4 * 128 * 128;      // 128 rows x 256 keys
+// Shared-memory plan of the scan for d_state NS (64, 128 or 256).  B (up to
+// 256 keys) occupies the G region only until C.B^T is in TMEM; with NS = 256
+// it arrives in two 128-state halves through that region, and x | S_in of a
+// head (64 KB) is single-buffered.
+template <int NS>
+struct ScCfg {
+  static constexpr int KAT = NS / 64;                  // 64-wide state atoms
+  static constexpr int KB = KAT < 2 ? KAT : 2;         // B atoms resident at a time
+  static constexpr int C_BYTES = KAT * 128 * 128;      // 128 query rows
+  static constexpr int B_BYTES = KB * CK_L * 128;      // up to 256 keys
+  static constexpr int G_BYTES = 4 * 128 * 128;        // 128 rows x 256 keys
   static constexpr int BG_BYTES = B_BYTES > G_BYTES ? B_BYTES : G_BYTES;
   static constexpr int X_BYTES = CK_L * 128;
-  static constexpr int S_BYTES = CK_NS * 128;
+  static constexpr int S_BYTES = NS * 128;
+  static constexpr int STAGES = NS > 128 ? 1 : 2;
   static constexpr int STAGE = X_BYTES + S_BYTES;
   static constexpr int OFF_C = 0, OFF_B = C_BYTES, OFF_G = OFF_B;  // G replaces B once C.B^T is in TMEM
-  static constexpr int OFF_X = OFF_B + BG_BYTES;                    // 2 stages of x | S_in
-  static constexpr int OFF_Y = OFF_X + 2 * STAGE;                   // z in, y out: 128 rows x 64
+  static constexpr int OFF_X = OFF_B + BG_BYTES;                    // stages of x | S_in
+  static constexpr int OFF_Y = OFF_X + STAGES * STAGE;              // z in, y out: 128 rows x 64
   static constexpr int OFF_SC = OFF_Y + 128 * 128;                  // scalar ring
   static constexpr int OFF_R = OFF_SC + CK_SR * CK_SCAL * 4;        // row partials of sum y^2
   static constexpr int OFF_BAR = OFF_R + 4 * 128 * 4;
-  static constexpr int SMEM = 1024 + OFF_BAR + 192;
+  static constexpr int SMEM = 1024 + OFF_BAR + 200;
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(OFF_X % 1024 == 0 && OFF_Y % 1024 == 0, "128-byte swizzle atoms");
 };
 
 struct ScMaps {
@@ -496,10 +504,11 @@ struct ScMaps {
 constexpr int SC_MATH = 512;  // 16 math warps: 4 per TMEM lane quadrant
 
 
-template <typename T>
+template <typename T, int NS>
 __global__ void __launch_bounds__(64 + SC_MATH, 1)
     ssd_scan_mh(const __grid_constant__ ScMaps mp, th_ssd_args p, int nc, int hs, int nsets,
                 const float* __restrict__ scal) {
+  using ScC = ScCfg<NS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* red = reinterpret_cast<float*>(sm + ScC::OFF_R);  // [4][128] row partials of sum y^2
@@ -516,7 +525,8 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
   uint64_t* sc_free = bar + 16;  // [CK_SR]
   uint64_t* z_full = bar + 20;
   uint64_t* y_ready = bar + 21;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 22);
+  uint64_t* b_free = bar + 22;  // d_state 256: the first half of B has been read by the C.B^T MMA
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 23);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   // one CTA per (chunk, head set, batch) does the rows 128-255 (256 keys) and then the rows 0-127
@@ -546,7 +556,7 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
   if (tid == 0) {  // fresh barriers for each pass (the previous pass has fully drained)
     uint64_t* all = bar;
     if (pass > 0)
-      for (int i = 0; i < 22; ++i) mbar_inval(&all[i]);  // bar[0..21]; bar[22] holds the TMEM address
+      for (int i = 0; i < 23; ++i) mbar_inval(&all[i]);  // bar[0..22]; bar[23] holds the TMEM address
     mbar_init(cb_full, 1);
     mbar_init(cb_done, 1);
     for (int i = 0; i < 2; ++i) {
@@ -560,6 +570,7 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
     for (int i = 0; i < CK_SR; ++i) { mbar_init(&sc_full[i], 1); mbar_init(&sc_free[i], 1); }
     mbar_init(z_full, 1);
     mbar_init(y_ready, 1);
+    mbar_init(b_free, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -571,12 +582,11 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
       const CUtensorMap* tB = qb ? &mp.B256 : &mp.B128;
       const CUtensorMap* tX = qb ? &mp.X256 : &mp.X128;
       auto load_xs = [&](int k) {
-        const int s = k & 1;
+        const int s = ScC::STAGES == 2 ? (k & 1) : 0;
         uint8_t* st = sm + ScC::OFF_X + s * ScC::STAGE;
         mbar_arrive_expect_tx(&full[s], nk * 128 + (has_s ? ScC::S_BYTES : 0));
         tma_load_3d(st, tX, &full[s], (h0 + k) * CK_P, s0, b);
-        if (has_s)
-          tma_load_2d(st + ScC::X_BYTES, &mp.S, &full[s], 0, (((b * nc + c) * p.heads) + h0 + k) * CK_NS);
+        if (has_s) tma_load_2d(st + ScC::X_BYTES, &mp.S, &full[s], 0, (((b * nc + c) * p.heads) + h0 + k) * NS);
       };
       auto load_sc = [&](int k) {
         const int j = k % CK_SR;
@@ -591,18 +601,28 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
         bulk_wait_read0();
         return true;
       };
-      mbar_arrive_expect_tx(cb_full, ScC::C_BYTES + ScC::KAT * nk * 128);
+      mbar_arrive_expect_tx(cb_full, ScC::C_BYTES + ScC::KB * nk * 128);
       for (int a = 0; a < ScC::KAT; ++a) {
-        tma_load_3d(sm + ScC::OFF_C + a * 128 * 128, &mp.C, cb_full, g * CK_NS + a * 64, s0 + qb * 128, b);
-        tma_load_3d(sm + ScC::OFF_B + a * nk * 128, tB, cb_full, g * CK_NS + a * 64, s0, b);
+        tma_load_3d(sm + ScC::OFF_C + a * 128 * 128, &mp.C, cb_full, g * NS + a * 64, s0 + qb * 128, b);
+        if (a < ScC::KB) tma_load_3d(sm + ScC::OFF_B + a * nk * 128, tB, cb_full, g * NS + a * 64, s0, b);
+      }
+      bool ok = true;
+      if constexpr (ScC::KAT > ScC::KB) {  // the second half of B once the MMA has read the first
+        ok = mbar_wait(b_free, 0, abort_flag);
+        if (ok) {
+          mbar_arrive_expect_tx(cb_full, (ScC::KAT - ScC::KB) * nk * 128);
+          for (int a = ScC::KB; a < ScC::KAT; ++a)
+            tma_load_3d(sm + ScC::OFF_B + (a - ScC::KB) * nk * 128, tB, cb_full, g * NS + a * 64, s0, b);
+        }
       }
       for (int k = 0; k < min(CK_SR, hcount); ++k) load_sc(k);
       load_xs(0);
-      bool ok = true;
       for (int k = 0; ok && k < hcount; ++k) {
-        // x | S_in of head k+1 once the MMA of head k-1 has read its slot
+        // x | S_in of head k+1 once the MMA of head k+1-STAGES has read its slot
         if (k + 1 < hcount) {
-          if (k >= 1 && !(ok = mbar_wait(&empty[(k + 1) & 1], ((k - 1) >> 1) & 1, abort_flag))) break;
+          const int prev = k + 1 - ScC::STAGES;  // the head that last used the slot
+          const int ps = ScC::STAGES == 2 ? (prev & 1) : 0, pph = ScC::STAGES == 2 ? ((prev >> 1) & 1) : (prev & 1);
+          if (prev >= 0 && !(ok = mbar_wait(&empty[ps], pph, abort_flag))) break;
           load_xs(k + 1);
         }
         // scalars of head k+4 once G of head k has read them
@@ -628,36 +648,45 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
       if (ok) {
         tc_fence_after();
         const uint32_t id_cb = make_idesc_f16(128, nk, fmt, 0, 0);
-        for (int kk = 0; kk < CK_NS / 16; ++kk) {
+        for (int kk = 0; kk < NS / 16; ++kk) {
+          if constexpr (ScC::KAT > ScC::KB) {
+            if (kk == ScC::KB * 4) {  // d_state 256: the second half of B replaces the first
+              tc_commit(b_free);
+              if (!(ok = mbar_wait(cb_full, 1, abort_flag))) break;
+              tc_fence_after();
+            }
+          }
+          const int ba = (kk >> 2) & (ScC::KB - 1);  // B atom slot (KB is 1 or 2)
           const uint64_t ad = make_desc_sw128(cA + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = make_desc_sw128(bA + (kk >> 2) * nk * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = make_desc_sw128(bA + ba * nk * 128 + (kk & 3) * 32, 16, 1024);
           tc_mma_f16(tmem, ad, bd, id_cb, kk ? 1u : 0u);
         }
         tc_commit(cb_done);
       }
       constexpr uint32_t id_y = make_idesc_f16(128, 64, fmt, 0, 1);  // B operand (x, S_in) MN-major
       for (int k = 0; ok && k < hcount; ++k) {
-        const int s = k & 1;
-        ok = mbar_wait(&full[s], (k >> 1) & 1, abort_flag) && mbar_wait(g_full, k & 1, abort_flag) &&
+        const int s = k & 1, xs = ScC::STAGES == 2 ? s : 0;  // TMEM Y buffer, x | S_in stage
+        const int xph = ScC::STAGES == 2 ? ((k >> 1) & 1) : (k & 1);
+        ok = mbar_wait(&full[xs], xph, abort_flag) && mbar_wait(g_full, k & 1, abort_flag) &&
              (k < 2 || mbar_wait(&y_empty[s], ((k >> 1) - 1) & 1, abort_flag));
         if (!ok) break;
         tc_fence_after();
         const uint32_t yd = tmem + 256 + s * 128;
-        const uint32_t xA = smem_u32(sm + ScC::OFF_X + s * ScC::STAGE), sA = xA + ScC::X_BYTES;
+        const uint32_t xA = smem_u32(sm + ScC::OFF_X + xs * ScC::STAGE), sA = xA + ScC::X_BYTES;
         for (int kk = 0; kk < nk / 16; ++kk) {
           const uint64_t ad = make_desc_sw128(gA + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = make_desc_sw128(xA + kk * 2048, nk * 128, 1024);
           tc_mma_f16(yd, ad, bd, id_y, kk ? 1u : 0u);
         }
         if (has_s) {
-          for (int kk = 0; kk < CK_NS / 16; ++kk) {
+          for (int kk = 0; kk < NS / 16; ++kk) {
             const uint64_t ad = make_desc_sw128(cA + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = make_desc_sw128(sA + kk * 2048, CK_NS * 128, 1024);
+            const uint64_t bd = make_desc_sw128(sA + kk * 2048, NS * 128, 1024);
             tc_mma_f16(yd + 64, ad, bd, id_y, kk ? 1u : 0u);
           }
         }
         tc_commit(g_free);
-        tc_commit(&empty[s]);
+        tc_commit(&empty[xs]);
         tc_commit(&y_full[s]);
       }
     }
@@ -805,22 +834,44 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-// Applies to 2-byte dtypes with head_dim 64, state_dim 128, chunk 256,
-// 16-byte aligned rows, dt rows of a multiple of 4 floats and a large enough
-// workspace; returns 1 (not taken) otherwise.
+template <typename T, int NS>
+static void ssd_scan_launch(const ScMaps& m, const th_ssd_args* a, int nc, cudaStream_t st) {
+  using Cf = ScCfg<NS>;
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(ssd_scan_mh<T, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+    set = true;
+  }
+  // head sets: about one CTA per SM
+  const int hpg = a->heads / a->ngroups;
+  const int per = a->batch * nc * a->ngroups;
+  int nsets = per >= sm_count() ? 1 : sm_count() / per;
+  nsets = nsets < 1 ? 1 : (nsets > hpg ? hpg : nsets);
+  const int hs = (hpg + nsets - 1) / nsets;
+  nsets = (hpg + hs - 1) / hs;
+  const int units = per * nsets;
+  ssd_scan_mh<T, NS><<<units, 64 + SC_MATH, Cf::SMEM, st>>>(m, *a, nc, hs, nsets, reinterpret_cast<const float*>(a->workspace));
+}
+
+// Applies to 2-byte dtypes with head_dim 64, state_dim 64, 128 or 256, chunk
+// 256, 16-byte aligned rows, dt rows of a multiple of 4 floats and a large
+// enough workspace; returns 1 (not taken) otherwise.  d_state 128 runs the
+// chunk states as one serial walk per (batch, head); 64 and 256 run them
+// chunk-parallel followed by the state pass.
 template <typename T>
 static int ssd_chunk_try(const th_ssd_args* a, cudaStream_t st, int* rc) {
-  if (a->head_dim != CK_P || a->chunk != CK_L || a->state_dim != CK_NS) return 1;
+  const int NS = a->state_dim;
+  if (a->head_dim != CK_P || a->chunk != CK_L || (NS != 64 && NS != 128 && NS != 256)) return 1;
   if (!aligned16(a->x) || !aligned16(a->B) || !aligned16(a->C) || !aligned16(a->out) || !aligned16(a->dt) ||
       a->ldx % 8 || a->ldb % 8 || a->ldc % 8 || a->ldo % 8 || a->lddt % 4)
     return 1;
   if (a->z && (!aligned16(a->z) || a->ldz % 8)) return 1;
-  if (!aligned16(a->workspace) || a->workspace_bytes < ck_ws_bytes(a->batch, a->seq, a->heads, CK_NS)) return 1;
+  if (!aligned16(a->workspace) || a->workspace_bytes < ck_ws_bytes(a->batch, a->seq, a->heads, NS)) return 1;
   const int nc = (a->seq + CK_L - 1) / CK_L;
   float* scal = reinterpret_cast<float*>(a->workspace);
   T* sin = reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(a->workspace) + ck_scal_bytes(a->batch, a->heads, nc));
-  T* sc = reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(sin) + ck_state_bytes(a->batch, nc, a->heads, CK_NS, CK_P));
-  const uint64_t gw = (uint64_t)a->ngroups * CK_NS, xw = (uint64_t)a->heads * CK_P;
+  T* sc = reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(sin) + ck_state_bytes(a->batch, nc, a->heads, NS, CK_P));
+  const uint64_t gw = (uint64_t)a->ngroups * NS, xw = (uint64_t)a->heads * CK_P;
   const uint64_t S = (uint64_t)a->seq, Bt = (uint64_t)a->batch;
   ScMaps m;
   CUtensorMap tdt;
@@ -833,7 +884,7 @@ static int ssd_chunk_try(const th_ssd_args* a, cudaStream_t st, int* rc) {
   m.Z = m.Y;
   if (!r && a->z) r = make_tmap_3d(&m.Z, a->z, a->dtype, xw, S, Bt, a->ldz * 2, S * a->ldz * 2, 64, 128);
   if (!r)
-    r = make_tmap_2d(&m.S, sin, a->dtype, CK_P, (uint64_t)a->batch * nc * a->heads * CK_NS, CK_P * 2, 64, CK_NS, true);
+    r = make_tmap_2d(&m.S, sin, a->dtype, CK_P, (uint64_t)a->batch * nc * a->heads * NS, CK_P * 2, 64, NS, true);
   if (!r)
     r = make_tmap_3d(&tdt, a->dt, TH_F32, (uint64_t)a->heads, S, Bt, a->lddt * 4, S * a->lddt * 4, 4, 256, false);
   if (r) { *rc = r; return 0; }
@@ -841,41 +892,34 @@ static int ssd_chunk_try(const th_ssd_args* a, cudaStream_t st, int* rc) {
   if (!set) {
     cudaFuncSetAttribute(ssd_state_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, StC::SMEM);
     cudaFuncSetAttribute(ssd_chunk_states<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SpC::SMEM);
-    cudaFuncSetAttribute(ssd_scan_mh<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScC::SMEM);
     set = true;
   }
-  static const bool serial = [] {  // TH_SSD_STATES=p selects the parallel chunk states + pass
+  static const bool serial128 = [] {  // TH_SSD_STATES=p selects the parallel states for d_state 128 too
     const char* e = getenv("TH_SSD_STATES");
     return !(e && e[0] == 'p');
   }();
-  if (serial) {
+  if (NS == CK_NS && serial128) {
     ssd_state_tc<T><<<dim3((unsigned)a->heads, (unsigned)a->batch), 320, StC::SMEM, st>>>(m.B256, m.X256, tdt, m.S,
                                                                                             *a, nc, scal);
     *rc = check_launch("th_ssd(chunk states, tcgen05)");
     if (*rc) return 0;
   } else {
-    const int units = a->batch * nc * a->heads * ((CK_NS + 127) / 128);
+    const int units = a->batch * nc * a->heads * ((NS + 127) / 128);
     const int grid = units < sm_count() ? units : sm_count();
     ssd_chunk_states<T><<<grid, 320, SpC::SMEM, st>>>(m.B256, m.X256, tdt, *a, nc, scal, sc);
     *rc = check_launch("th_ssd(chunk states, parallel)");
     if (*rc) return 0;
     if (nc > 1) {
-      const int per = CK_NS * CK_P / 4;
+      const int per = NS * CK_P / 4;
       ssd_state_pass<T><<<dim3((unsigned)((per + 255) / 256), (unsigned)a->heads, (unsigned)a->batch), 256, 0, st>>>(
           *a, nc, scal, sc, sin);
       *rc = check_launch("th_ssd(state pass)");
       if (*rc) return 0;
     }
   }
-  // head sets: about one CTA per SM
-  const int hpg = a->heads / a->ngroups;
-  const int per = a->batch * nc * a->ngroups;
-  int nsets = per >= sm_count() ? 1 : sm_count() / per;
-  nsets = nsets < 1 ? 1 : (nsets > hpg ? hpg : nsets);
-  const int hs = (hpg + nsets - 1) / nsets;
-  nsets = (hpg + hs - 1) / hs;
-  const int units = per * nsets;
-  ssd_scan_mh<T><<<units, 64 + SC_MATH, ScC::SMEM, st>>>(m, *a, nc, hs, nsets, scal);
+  if (NS == 64) ssd_scan_launch<T, 64>(m, a, nc, st);
+  else if (NS == 128) ssd_scan_launch<T, 128>(m, a, nc, st);
+  else ssd_scan_launch<T, 256>(m, a, nc, st);
   *rc = check_launch("th_ssd(scan, tcgen05 multi-head)");
   return 0;
 }
