@@ -257,7 +257,9 @@ def _attn_ref(q, k, v, b, s, hq, hkv, d, scale, causal):
                                                  (2, 256, 8, 2, 128, True), (1, 70, 2, 1, 32, False),
                                                  # tcgen05 path: several KV blocks, ragged tails, GQA
                                                  (2, 640, 8, 2, 128, True), (1, 1000, 4, 4, 64, False),
-                                                 (3, 333, 4, 1, 128, True), (1, 2048, 2, 2, 64, True)])
+                                                 (3, 333, 4, 1, 128, True), (1, 2048, 2, 2, 64, True),
+                                                 # 256-row CTAs: second tile partly / wholly past the end
+                                                 (1, 300, 4, 2, 128, False), (1, 4096, 4, 1, 128, True)])
 def test_attention(L, dtype, b, s, hq, hkv, d, causal):
     torch.manual_seed(6)
     t = b * s
