@@ -213,6 +213,7 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp-chunks", type=int, default=4, help="c3 tensor parallel: row chunks of the all-reduce overlap")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -258,7 +259,7 @@ def main() -> None:
     res = compile_model(model, (x,), CompileConfig(run_name=f"bench_{args.workload}_r{rank}", device=str(dev),
                                                    verify_passes=False, reference_check=False,
                                                    results_dir=REPO / "results", world_size=world if tp else 1,
-                                                   tp_mode="heads" if tp else None))
+                                                   tp_mode="heads" if tp else None, tp_chunks=args.tp_chunks))
     mod, prog = res.module, res.program
     tokens = x.shape[0] * x.shape[1]
     # tokens the whole job processes per step
@@ -395,7 +396,8 @@ def main() -> None:
             "dtype": {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[mod.dtype],
             "data": "synthetic",
             "config": {"workload": desc, "global_batch": x.shape[0] if tp else n * x.shape[0], "seq_len": x.shape[1],
-                       "parallelism": (f"tp{n} (heads / FFN columns, NCCL all-reduce after o_proj and down_proj)" if tp
+                       "parallelism": (f"tp{n} (heads / FFN columns, NCCL all-reduce after o_proj and down_proj, "
+                                       f"{args.tp_chunks} row chunks overlapping all-reduce and GEMMs)" if tp
                                        else f"dp{n} (batch-sharded, no communication)" if n > 1 else "single GPU"),
                        "l2": "flushed between steps (256 MiB write, untimed)", "kernels_per_forward": mod.n_launches,
                        "launch": "eager launches (NCCL inside)" if tp else "one CUDA graph per forward"},

@@ -156,6 +156,30 @@ def test_gloo_world2(tmp_path):
     assert rel_l2(outs[0], ref) < 1e-6
 
 
+# ------------------------------------------------------- GPU, one device
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_row_chunked_schedule_matches_sequential(tmp_path, dtype):
+    """The row-chunked tensor-parallel schedule (all-reduce of chunk c on a
+    second stream overlapping chunk c+1's GEMMs) computes exactly what the
+    launch-by-launch order computes.  Rank 0 of a 2-way shard runs on one GPU
+    with a stand-in all-reduce (x2: two ranks holding the same partial)."""
+    from torch_helion.b200.runtime import CompiledProgram
+    from torch_helion.b200.tp import shard_program
+
+    prog, params, x, _ = _program(tmp_path, batch=2, seq=256, hidden=512, heads=8, kv_heads=4, intermediate=1024,
+                                  dtype=dtype)
+    sp, spar = shard_program(prog, params, 2, 0)
+    outs = []
+    for chunks in (1, 4):
+        mod = CompiledProgram(sp, spar, "cuda:0", tp_rank=0, tp_world=2, allreduce=lambda t: t.mul_(2.0),
+                              tp_chunks=chunks)
+        assert (mod._pipe is not None) == (chunks > 1)
+        outs.append(mod(x.to("cuda:0"))[0].float().cpu())
+        torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+
+
 # ------------------------------------------------------------------ GPU (NCCL)
 def _nccl_rank(rank, world, port, path, kw):
     import sys

@@ -44,6 +44,9 @@ class KernelLaunch:
     name: str
     kind: str
     fn: Callable[[], None]
+    # the same launch restricted to rows [r0, r1) of every row-indexed operand
+    # (None: the kernel does not decompose by rows, e.g. attention or RoPE)
+    fn_rows: Callable[[int, int], None] | None = None
 
 
 class CompiledProgram:
@@ -51,7 +54,7 @@ class CompiledProgram:
 
     def __init__(self, program: Program, params: dict[str, torch.Tensor], device: str | torch.device = "cuda",
                  tp_rank: int = 0, tp_world: int = 1, allreduce: Callable[[torch.Tensor], None] | None = None,
-                 shared_params: dict | None = None) -> None:
+                 shared_params: dict | None = None, tp_chunks: int = 4) -> None:
         if not torch.cuda.is_available():
             raise lib.B200KernelError("CompiledProgram needs a CUDA device (there is no CPU fallback)")
         lib.load()
@@ -67,8 +70,11 @@ class CompiledProgram:
         self._graph: torch.cuda.CUDAGraph | None = None
         self._ssd_ws: torch.Tensor | None = None
         self.tp_rank, self.tp_world, self.allreduce = tp_rank, tp_world, allreduce
+        self.tp_chunks = tp_chunks
+        self._pipe: tuple | None = None  # chunked tensor-parallel schedule (see _plan_tp_pipeline)
         with torch.cuda.device(self.device):
             self._build()
+            self._plan_tp_pipeline()
 
     # ------------------------------------------------------------ parameters
     def _param(self, name: str, kind: str = "raw", dtype: torch.dtype | None = None) -> torch.Tensor:
@@ -169,7 +175,9 @@ class CompiledProgram:
         # no producer writes it: a th_rowstat launch right before the consumer
         x = self.views[tname]
         parts = self._empty(x.shape[0], 1, torch.float32)
-        self.launches.append(KernelLaunch(f"rowstat({tname})", "rowstat", lambda x=x, parts=parts: lib.rowstat(x, parts.view(-1))))
+        self.launches.append(KernelLaunch(
+            f"rowstat({tname})", "rowstat", lambda x=x, parts=parts: lib.rowstat(x, parts.view(-1)),
+            lambda r0, r1, x=x, parts=parts: lib.rowstat(x[r0:r1], parts.view(-1)[r0:r1])))
         self._ss_parts[tname] = parts
         return parts
 
@@ -215,10 +223,21 @@ class CompiledProgram:
                 self._ss_parts[tname] = parts
                 kw["ss_out"] = parts
         d = out if n_tail == 0 or n_main_pad == 0 else out[:, :n_main_pad]  # all-tail GEMMs write no main output
-        self.launches.append(KernelLaunch(kname, "gemm", lambda lhs=lhs, W=W, d=d, kw=kw: lib.gemm(lhs, W, d, **kw)))
+        fn_rows = None
+        if p.rope is None:  # RoPE positions follow the row index: no row slicing
+            row_kw = [k for k in ("rs_parts", "residual", "out2", "ss_out") if k in kw]
+
+            def fn_rows(r0, r1, lhs=lhs, W=W, d=d, kw=kw, row_kw=row_kw):
+                kr = dict(kw)
+                for k in row_kw:
+                    kr[k] = kw[k][r0:r1]
+                lib.gemm(lhs[r0:r1], W, d[r0:r1], **kr)
+        self.launches.append(KernelLaunch(kname, "gemm", lambda lhs=lhs, W=W, d=d, kw=kw: lib.gemm(lhs, W, d, **kw),
+                                          fn_rows))
         if self._allreduced(spec):
             buf = out  # the whole (contiguous) buffer; zero-weight pad columns sum to zero
-            self.launches.append(KernelLaunch(f"allreduce({kname})", "nccl", lambda buf=buf: self.allreduce(buf)))
+            self.launches.append(KernelLaunch(f"allreduce({kname})", "nccl", lambda buf=buf: self.allreduce(buf),
+                                              lambda r0, r1, buf=buf: self.allreduce(buf[r0:r1])))
 
     def _add_macro(self, kname: str, p: MacroPlan, need_ss, ss_by_producer) -> None:
         prog = self.program
@@ -278,9 +297,80 @@ class CompiledProgram:
             src = x.reshape(dst.shape) if dst.dim() == 1 else x.reshape(dst.shape[0], -1)
             dst.copy_(src, non_blocking=True)
 
+    def _plan_tp_pipeline(self) -> None:
+        """Row-chunked schedule of the tensor-parallel tail of the program.
+
+        From the GEMM whose output is the first all-reduce to the end (o_proj,
+        all-reduce, row statistics, gate|up, down, all-reduce in the Llama
+        block) every launch works row by row, so the rows are cut into chunks:
+        chunk c's all-reduce runs on a communication stream while chunk c+1's
+        GEMMs run on the compute stream, and the part after the first all-reduce
+        of chunk c waits only for that chunk's all-reduce.  The rows of every
+        chunk are a multiple of 128 (whole GEMM row tiles)."""
+        if self.tp_world <= 1 or self.tp_chunks <= 1:
+            return
+        first = next((i for i, l in enumerate(self.launches) if l.kind == "nccl"), None)
+        if first is None or first == 0:
+            return
+        seg = self.launches[first - 1:]
+        if any(l.fn_rows is None for l in seg):
+            return
+        rows = {v.shape[0] for v in self.views.values() if v.dim() == 2}
+        T = max(rows)
+        n = min(self.tp_chunks, T // 128)
+        if n <= 1:
+            return
+        per = (T // n + 127) // 128 * 128
+        bounds = [(r0, min(T, r0 + per)) for r0 in range(0, T, per)]
+        pre = seg[:2]    # the GEMM and its all-reduce
+        post = seg[2:]   # everything after, per chunk
+        self._pipe = (self.launches[:first - 1], pre, post, bounds, torch.cuda.Stream(device=self.device))
+
+    def _launch_pipelined(self) -> None:
+        prefix, pre, post, bounds, comm = self._pipe
+        main = torch.cuda.current_stream()
+        for l in prefix:
+            l.fn()
+
+        def collective(l, r0, r1) -> torch.cuda.Event:
+            ready = torch.cuda.Event()
+            ready.record(main)
+            comm.wait_event(ready)
+            with torch.cuda.stream(comm):
+                l.fn_rows(r0, r1)
+            done = torch.cuda.Event()
+            done.record(comm)
+            return done
+
+        def run(chunk, r0, r1) -> torch.cuda.Event | None:
+            last = None
+            for l in chunk:
+                if l.kind == "nccl":
+                    last = collective(l, r0, r1)
+                else:
+                    if last is not None:  # compute after a collective of the same rows
+                        main.wait_event(last)
+                        last = None
+                    l.fn_rows(r0, r1)
+            return last
+
+        pending = [run(pre, *bounds[0])]
+        tail = None
+        for c, (r0, r1) in enumerate(bounds):
+            if c + 1 < len(bounds):
+                pending.append(run(pre, *bounds[c + 1]))
+            if pending[c] is not None:
+                main.wait_event(pending[c])
+            tail = run(post, r0, r1) or tail
+        if tail is not None:
+            main.wait_event(tail)  # every chunk's last collective precedes it on the comm stream
+
     def launch_all(self) -> None:
         if self._graph is not None:
             self._graph.replay()
+            return
+        if self._pipe is not None:
+            self._launch_pipelined()
             return
         for l in self.launches:
             l.fn()
@@ -315,6 +405,11 @@ class CompiledProgram:
 
     @property
     def n_launches(self) -> int:
+        """Kernels of this library launched per forward (NCCL's own kernels excluded)."""
+        if self._pipe is not None:
+            prefix, pre, post, bounds, _ = self._pipe
+            per_chunk = sum(1 for l in pre + post if l.kind != "nccl")
+            return sum(1 for l in prefix if l.kind != "nccl") + len(bounds) * per_chunk
         return sum(1 for l in self.launches if l.kind != "nccl")
 
     def launch_names(self) -> list[str]:

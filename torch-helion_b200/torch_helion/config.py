@@ -37,6 +37,8 @@ class CompileConfig:
       cuda_graph         replay the forward as one CUDA graph
       kernel_launch_overhead_us  per-kernel launch cost in the planner (us)
       world_size / tp_mode  tensor parallelism ("heads" for the Llama block)
+      tp_chunks          row chunks of the tensor-parallel part after attention:
+                         each chunk's all-reduce overlaps the next chunk's GEMMs
       measure_iters      time the forward on the device (0 = skip)
     """
 
@@ -65,6 +67,7 @@ class CompileConfig:
     kernel_launch_overhead_us: float = 3.0
     world_size: int = 1
     tp_mode: str | None = None
+    tp_chunks: int = 4
     measure_iters: int = 0
 
     @property
