@@ -165,3 +165,24 @@ def test_unknown_backend_raises():
     _, m, args = _llama()
     with pytest.raises(ValueError):
         compile_model(m, args, CompileConfig(backend="loom"))
+
+
+def test_saved_artifact_round_trips(tmp_path):
+    """compile_model(save_params=True) leaves 06_opir.json + params.pt; the
+    Program read back is the same Program (the GPU test runs it)."""
+    import torch
+
+    from torch_helion import CompileConfig, compile_model
+    from torch_helion.optimizer.opir import Program
+    from workloads import configs
+    from workloads.mamba import MambaConfig
+
+    cfg = MambaConfig(batch=1, seq=256, d_model=64, headdim=32, d_state=32, chunk=128, n_layers=1, mode="chunked",
+                      ngroups=1, use_conv=True, dtype=torch.float32)
+    m = configs.build(cfg)
+    (u,) = m.example_inputs(seed=1)
+    res = compile_model(m, (u,), CompileConfig(run_name="a", results_dir=tmp_path, execute=False, save_params=True))
+    prog = Program.from_json(tmp_path / "a" / "06_opir.json")
+    assert prog.to_dict() == res.program.to_dict()
+    params = torch.load(tmp_path / "a" / "params.pt", weights_only=True)
+    assert set(prog.params) <= set(params)

@@ -274,17 +274,26 @@ def test_attention(L, dtype, b, s, hq, hkv, d, causal):
 
 # --------------------------------------------------------------- conv1d
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_conv1d_silu(L, dtype):
+@pytest.mark.parametrize("b,s,ch,wd,with_bias,silu", [(3, 150, 1792, 4, False, True),
+                                                      # C2 shape: many token tiles per block
+                                                      (2, 2048, 1792, 4, False, True),
+                                                      # a partial channel block, width 3, bias
+                                                      (1, 300, 1000, 3, True, True),
+                                                      # width 2, no activation, one row past a tile
+                                                      (2, 129, 512, 2, True, False)])
+def test_conv1d(L, dtype, b, s, ch, wd, with_bias, silu):
     torch.manual_seed(7)
-    b, s, ch, wd = 3, 150, 1792, 4
     src = torch.randn(b * s, ch + 64, device=_dev()).to(dtype)
     x = src[:, 32: 32 + ch]  # strided view, like xBC inside the in_proj output
     w = torch.randn(ch, wd, device=_dev()) * 0.3
+    bias = torch.randn(ch, device=_dev()) * 0.1 if with_bias else None
     y = torch.empty(b * s, ch, device=_dev(), dtype=dtype)
-    L.conv1d(x, w, y, batch=b, seq=s)
+    L.conv1d(x, w, y, batch=b, seq=s, act=L.ACT_SILU if silu else L.ACT_NONE, bias=bias)
     xt = x.float().reshape(b, s, ch).transpose(1, 2)
-    ref = F.silu(F.conv1d(F.pad(xt, (wd - 1, 0)), w.unsqueeze(1), groups=ch)).transpose(1, 2).reshape(b * s, ch)
+    ref = F.conv1d(F.pad(xt, (wd - 1, 0)), w.unsqueeze(1), bias=bias, groups=ch)
+    ref = (F.silu(ref) if silu else ref).transpose(1, 2).reshape(b * s, ch)
     assert rel_l2(y.float(), ref) < TOL[dtype]
+    assert L.device_error() == 0
 
 
 # ------------------------------------------------------------------ ssd

@@ -149,3 +149,22 @@ def test_streaming_runner_matches_run(tmp_path, cuda_graph):
     runner.run([[b] for b in batches], outs)
     for w, o in zip(want, outs):
         assert torch.equal(w.reshape(o[0].shape), o[0])
+
+
+@pytest.mark.parametrize("cuda_graph", [False, True], ids=["eager", "graph"])
+def test_load_compiled_artifact(tmp_path, cuda_graph):
+    """A results directory (06_opir.json + params.pt) runs again on the GPU
+    without re-capture and returns exactly what compile_model's module does."""
+    from torch_helion import load_compiled
+    from workloads import configs
+    from workloads.mamba import MambaConfig
+
+    cfg = MambaConfig(batch=2, seq=512, d_model=128, headdim=64, d_state=128, chunk=256, n_layers=2, mode="chunked",
+                      ngroups=1, use_conv=True, dtype=torch.bfloat16)
+    m = configs.build(cfg)
+    (u,) = m.example_inputs(seed=1)
+    res = _compile(m, (u,), tmp_path, save_params=True)
+    want = res.run(u)[0].cpu().clone()
+    mod = load_compiled(tmp_path / "t", device="cuda:0", cuda_graph=cuda_graph)
+    got = mod(u.to("cuda:0"))[0].cpu()
+    assert torch.equal(want.reshape(got.shape), got)
