@@ -96,6 +96,8 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  pdl_wait();  // the previous kernel's outputs (this kernel's inputs) are complete
+  pdl_trigger();
   const uint32_t tO = tmem + 256;
 
   if (warp == 0) {
@@ -305,11 +307,11 @@ static int attention_tc_try(const th_attention_args* a, cudaStream_t st, int* rc
   if (D == 128) {
     static bool set = false;
     if (!set) { cudaFuncSetAttribute(attention_tc_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, AtCfg<128>::SMEM); set = true; }
-    attention_tc_kernel<T, 128><<<grid, 320, AtCfg<128>::SMEM, st>>>(tq, tk, tv, *a);
+    launch_pdl(attention_tc_kernel<T, 128>, grid, dim3(320), AtCfg<128>::SMEM, st, tq, tk, tv, *a);
   } else {
     static bool set = false;
     if (!set) { cudaFuncSetAttribute(attention_tc_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AtCfg<64>::SMEM); set = true; }
-    attention_tc_kernel<T, 64><<<grid, 320, AtCfg<64>::SMEM, st>>>(tq, tk, tv, *a);
+    launch_pdl(attention_tc_kernel<T, 64>, grid, dim3(320), AtCfg<64>::SMEM, st, tq, tk, tv, *a);
   }
   *rc = check_launch("th_attention(tcgen05)");
   return 0;

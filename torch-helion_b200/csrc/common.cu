@@ -9,6 +9,8 @@
 #include <mutex>
 #include <unordered_map>
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace th {
@@ -139,6 +141,14 @@ int make_tmap_3d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, 
   if (r != CUDA_SUCCESS) return fail(TH_ELAUNCH, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
   tmap_insert(key, *map);
   return TH_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("TH_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 int sm_count() {

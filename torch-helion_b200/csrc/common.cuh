@@ -267,6 +267,15 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---- programmatic dependent launch ----
+// A kernel launched with launch_pdl may start while the previous kernel of
+// the stream is still finishing; it does its set-up (barriers, TMEM,
+// descriptor prefetch) and then pdl_wait() blocks until that kernel has
+// completed and its memory is visible.  pdl_trigger() lets the next kernel's
+// blocks be scheduled once every block of this grid has issued it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- tcgen05 (5th-generation tensor cores, accumulators in TMEM) ----
 // One warp allocates `ncols` TMEM columns (power of two >= 32) and the base
 // address is written to shared memory.
@@ -487,5 +496,23 @@ int make_tmap_3d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, 
 inline int elem_bytes(int dtype) { return dtype == TH_F32 ? 4 : 2; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 int sm_count();
+bool pdl_enabled();  // TH_PDL=0 in the environment turns programmatic dependent launch off
+
+// Launch `kern` on `st` with programmatic stream serialisation: only for
+// kernels that call pdl_wait() before their first access to global memory.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 
 }  // namespace th

@@ -429,6 +429,8 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs (this GEMM's operands) are complete
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {  // ---- TMA producer
@@ -572,6 +574,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
   cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs (this GEMM's operands) are complete
+  pdl_trigger();
 
   // columns the pair multiplies on a tile (the last column tile: its live
   // columns rounded up to 16); CTA r holds B rows [r * nt / 2, (r + 1) * nt / 2)
@@ -722,7 +726,8 @@ static int launch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st
   const int tiles_m = (int)((a->m + C::BM - 1) / C::BM), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n;
   const int grid = ntiles < sm_count() ? ntiles : sm_count();
-  gemm_tc_kernel<T, BN, EPI><<<grid, 320, C::SMEM_BYTES, st>>>(ta, tb, ep, (int)a->k, tiles_m, tiles_n);
+  launch_pdl(gemm_tc_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb, ep, (int)a->k, tiles_m,
+             tiles_n);
   return check_launch("th_gemm(tcgen05)");
 }
 
@@ -742,7 +747,8 @@ static int launch_tc2(const th_gemm_args* a, const EpiParams& ep, cudaStream_t s
   const int tiles_m = (int)((a->m + 2 * C::BM - 1) / (2 * C::BM)), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n, pairs = sm_count() / 2;
   const int grid = 2 * (ntiles < pairs ? ntiles : pairs);
-  gemm_tc2_kernel<T, BN, EPI><<<grid, 320, C::SMEM_BYTES, st>>>(ta, tb, ep, (int)a->k, tiles_m, tiles_n);
+  launch_pdl(gemm_tc2_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb, ep, (int)a->k, tiles_m,
+             tiles_n);
   return check_launch("th_gemm(tcgen05 pair)");
 }
 

@@ -134,6 +134,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, i
 template <typename T, int RV, int ROWS>
 __global__ void __launch_bounds__(256) rowstat_rows(const T* __restrict__ x, int64_t ldx, float* __restrict__ out,
                                                     int64_t rows, int cols) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -172,6 +174,8 @@ __global__ void __launch_bounds__(256) rmsnorm_rows(const T* __restrict__ x, int
                                                     T* __restrict__ y, int64_t ldy, int64_t rows, int cols, float eps) {
   extern __shared__ float4 gain4[];  // cols / 4
   float* gain = reinterpret_cast<float*>(gain4);
+  pdl_wait();
+  pdl_trigger();
   for (int c = threadIdx.x; c < cols; c += blockDim.x) gain[c] = g ? g[c] : 1.f;
   __syncthreads();
   const int lane = threadIdx.x & 31;
@@ -377,8 +381,11 @@ __global__ void __launch_bounds__(256, 2) conv1d_tma(const __grid_constant__ CUt
     for (int i = 0; i < CT_STAGES; ++i) mbar_init(&bar[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
-    for (int k = 0; k < CT_STAGES; ++k) issue(k);
   }
+  pdl_wait();  // the previous kernel's output (this conv's input) is complete
+  pdl_trigger();
+  if (tid == 0)
+    for (int k = 0; k < CT_STAGES; ++k) issue(k);
   const int c0 = cb * CT_CH + tx * 8;
   const bool live = c0 < channels;
   float wt[8][W], bi[8];
@@ -473,10 +480,10 @@ extern "C" int th_rowstat(const th_rowstat_args* a, void* stream) {
     const unsigned g = small ? rows_grid(a->rows, 2) : rows_grid(a->rows, 1);
     if (a->dtype == TH_BF16) {
       auto k = small ? rowstat_rows<__nv_bfloat16, 4, 2> : rowstat_rows<__nv_bfloat16, 16, 1>;
-      k<<<g, 256, 0, st>>>((const __nv_bfloat16*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols);
+      launch_pdl(k, dim3(g), dim3(256), 0, st, (const __nv_bfloat16*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols);
     } else {
       auto k = small ? rowstat_rows<__half, 4, 2> : rowstat_rows<__half, 16, 1>;
-      k<<<g, 256, 0, st>>>((const __half*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols);
+      launch_pdl(k, dim3(g), dim3(256), 0, st, (const __half*)a->x, a->ldx, a->sumsq, a->rows, (int)a->cols);
     }
     return check_launch("th_rowstat");
   }
@@ -503,12 +510,12 @@ extern "C" int th_rmsnorm(const th_rmsnorm_args* a, void* stream) {
     const size_t sm = (size_t)a->cols * 4;
     if (a->dtype == TH_BF16) {
       auto k = small ? rmsnorm_rows<__nv_bfloat16, 4, 2> : rmsnorm_rows<__nv_bfloat16, 16, 1>;
-      k<<<g, 256, sm, st>>>((const __nv_bfloat16*)a->x, a->ldx, a->gain, (__nv_bfloat16*)a->y, a->ldy, a->rows,
-                            (int)a->cols, a->eps);
+      launch_pdl(k, dim3(g), dim3(256), sm, st, (const __nv_bfloat16*)a->x, a->ldx, a->gain, (__nv_bfloat16*)a->y,
+                 a->ldy, a->rows, (int)a->cols, a->eps);
     } else {
       auto k = small ? rmsnorm_rows<__half, 4, 2> : rmsnorm_rows<__half, 16, 1>;
-      k<<<g, 256, sm, st>>>((const __half*)a->x, a->ldx, a->gain, (__half*)a->y, a->ldy, a->rows, (int)a->cols,
-                            a->eps);
+      launch_pdl(k, dim3(g), dim3(256), sm, st, (const __half*)a->x, a->ldx, a->gain, (__half*)a->y, a->ldy, a->rows,
+                 (int)a->cols, a->eps);
     }
     return check_launch("th_rmsnorm");
   }
@@ -550,8 +557,8 @@ static int launch_conv_tma(const th_conv1d_args* a, cudaStream_t st) {
   int grid = (2 * th::sm_count() / ncb) * ncb;
   if (grid < ncb) grid = ncb;
   if (grid > ntiles) grid = ntiles;
-  th::conv1d_tma<T, W><<<grid, 256, Cf::SMEM, st>>>(tm, a->w, a->bias, (T*)a->y, a->ldy, a->seq, a->channels, a->act,
-                                                    ncb, nsb, ntiles);
+  th::launch_pdl(th::conv1d_tma<T, W>, dim3(grid), dim3(256), Cf::SMEM, st, tm, a->w, a->bias, (T*)a->y, a->ldy,
+                 a->seq, a->channels, a->act, ncb, nsb, ntiles);
   return th::check_launch("th_conv1d(tma)");
 }
 

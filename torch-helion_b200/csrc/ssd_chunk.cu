@@ -103,6 +103,8 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  pdl_wait();  // the previous kernel's outputs (this kernel's inputs) are complete
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -296,6 +298,8 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  pdl_wait();  // the previous kernel's outputs (this kernel's inputs) are complete
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {  // ---- TMA producer
@@ -448,6 +452,8 @@ __global__ void __launch_bounds__(320, 1)
 template <typename T>
 __global__ void __launch_bounds__(256) ssd_state_pass(th_ssd_args p, int nc, const float* __restrict__ scal,
                                                       const T* __restrict__ sc, T* __restrict__ sin) {
+  pdl_wait();
+  pdl_trigger();
   const int h = blockIdx.y, b = blockIdx.z;
   const int64_t per = (int64_t)p.state_dim * CK_P;  // elements of one state
   const int64_t e = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
@@ -549,6 +555,8 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  pdl_wait();  // the previous kernel's outputs (this kernel's inputs) are complete
+  pdl_trigger();
   for (int pass = 0; pass < 2; ++pass) {
   const int qb = 1 - pass;
   if (qb * 128 >= len) continue;  // a chunk of at most 128 rows has no second half (uniform)
@@ -850,7 +858,8 @@ static void ssd_scan_launch(const ScMaps& m, const th_ssd_args* a, int nc, cudaS
   const int hs = (hpg + nsets - 1) / nsets;
   nsets = (hpg + hs - 1) / hs;
   const int units = per * nsets;
-  ssd_scan_mh<T, NS><<<units, 64 + SC_MATH, Cf::SMEM, st>>>(m, *a, nc, hs, nsets, reinterpret_cast<const float*>(a->workspace));
+  launch_pdl(ssd_scan_mh<T, NS>, dim3(units), dim3(64 + SC_MATH), Cf::SMEM, st, m, *a, nc, hs, nsets,
+             reinterpret_cast<const float*>(a->workspace));
 }
 
 // Applies to 2-byte dtypes with head_dim 64, state_dim 64, 128 or 256, chunk
@@ -899,20 +908,20 @@ static int ssd_chunk_try(const th_ssd_args* a, cudaStream_t st, int* rc) {
     return !(e && e[0] == 'p');
   }();
   if (NS == CK_NS && serial128) {
-    ssd_state_tc<T><<<dim3((unsigned)a->heads, (unsigned)a->batch), 320, StC::SMEM, st>>>(m.B256, m.X256, tdt, m.S,
-                                                                                            *a, nc, scal);
+    launch_pdl(ssd_state_tc<T>, dim3((unsigned)a->heads, (unsigned)a->batch), dim3(320), StC::SMEM, st, m.B256, m.X256,
+               tdt, m.S, *a, nc, scal);
     *rc = check_launch("th_ssd(chunk states, tcgen05)");
     if (*rc) return 0;
   } else {
     const int units = a->batch * nc * a->heads * ((NS + 127) / 128);
     const int grid = units < sm_count() ? units : sm_count();
-    ssd_chunk_states<T><<<grid, 320, SpC::SMEM, st>>>(m.B256, m.X256, tdt, *a, nc, scal, sc);
+    launch_pdl(ssd_chunk_states<T>, dim3(grid), dim3(320), SpC::SMEM, st, m.B256, m.X256, tdt, *a, nc, scal, sc);
     *rc = check_launch("th_ssd(chunk states, parallel)");
     if (*rc) return 0;
     if (nc > 1) {
       const int per = NS * CK_P / 4;
-      ssd_state_pass<T><<<dim3((unsigned)((per + 255) / 256), (unsigned)a->heads, (unsigned)a->batch), 256, 0, st>>>(
-          *a, nc, scal, sc, sin);
+      launch_pdl(ssd_state_pass<T>, dim3((unsigned)((per + 255) / 256), (unsigned)a->heads, (unsigned)a->batch),
+                 dim3(256), 0, st, *a, nc, (const float*)scal, (const T*)sc, sin);
       *rc = check_launch("th_ssd(state pass)");
       if (*rc) return 0;
     }
