@@ -2,7 +2,10 @@
 //
 // One CTA = 128 query rows of one (batch, query head); KV blocks of 128 rows.
 // 320 threads, warp-specialised:
-//   warp 0    TMA: the Q tile once, K/V tiles of each KV block into a 2-stage ring
+//   warp 0    TMA: the Q tile once, then K and V tiles into separate 2-stage rings, in
+//             the order the MMA warp consumes them (K_{j+2} as soon as S_j has read
+//             its slot, V_{j+1} once P_{j-1} V_{j-1} has), so the load of the next
+//             K block never waits for a P.V product
 //   warp 1    MMA: S_j = Q K_j^T into one of two TMEM S buffers (so S_{j+1} is
 //             computed while the softmax warps work on S_j), then O += P_j V_j
 //             (V is an MN-major operand: head_dim is its contiguous axis)
@@ -52,14 +55,16 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;        // [2]
-  uint64_t* kv_empty = bars + 3;       // [2]
+  uint64_t* k_full = bars + 1;         // [2]
+  uint64_t* k_empty = bars + 3;        // [2]
   uint64_t* s_full = bars + 5;         // [2]
   uint64_t* s_free = bars + 7;         // [2]
   uint64_t* p_full = bars + 9;
   uint64_t* pv_done = bars + 10;       // [2], one per P buffer
   uint64_t* mma_done = bars + 12;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* v_full = bars + 13;        // [2]
+  uint64_t* v_empty = bars + 15;       // [2]
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -75,8 +80,10 @@ __global__ void __launch_bounds__(320, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 8);
     }
@@ -105,16 +112,23 @@ __global__ void __launch_bounds__(320, 1)
       mbar_arrive_expect_tx(q_full, C::Q_BYTES);
       for (int a = 0; a < C::DA; ++a)
         tma_load_2d(sm + C::OFF_Q + a * C::BM * 128, &tmQ, q_full, h * D + a * 64, (int)(row0 + q0));
-      for (int j = 0; j < nkv; ++j) {
+      // one K or V tile of block j into its ring slot once the slot's previous reader is done
+      auto load = [&](const CUtensorMap* tm, int off, uint64_t* full, uint64_t* empty, int j) -> bool {
         const int s = j & 1;
-        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * C::KV_BYTES);
-        for (int a = 0; a < C::DA; ++a) {
-          tma_load_2d(sm + C::OFF_K + s * C::KV_BYTES + a * C::BN * 128, &tmK, &kv_full[s], hk * D + a * 64,
+        if (!mbar_wait(&empty[s], ((j >> 1) & 1) ^ 1, abort_flag)) return false;
+        mbar_arrive_expect_tx(&full[s], C::KV_BYTES);
+        for (int a = 0; a < C::DA; ++a)
+          tma_load_2d(sm + off + s * C::KV_BYTES + a * C::BN * 128, tm, &full[s], hk * D + a * 64,
                       (int)(row0 + j * C::BN));
-          tma_load_2d(sm + C::OFF_V + s * C::KV_BYTES + a * C::BN * 128, &tmV, &kv_full[s], hk * D + a * 64,
-                      (int)(row0 + j * C::BN));
-        }
+        return true;
+      };
+      // consumption order: S_0, S_1, PV_0, S_2, PV_1, ... -> loads K_0, K_1, V_0, K_2, V_1, K_3, V_2, ...
+      bool ok = true;
+      for (int j = 0; ok && j < min(nkv, 2); ++j) ok = load(&tmK, C::OFF_K, k_full, k_empty, j);
+      if (ok && nkv > 0) ok = load(&tmV, C::OFF_V, v_full, v_empty, 0);
+      for (int j = 0; ok && j + 1 < nkv; ++j) {
+        if (j + 2 < nkv && !(ok = load(&tmK, C::OFF_K, k_full, k_empty, j + 2))) break;
+        ok = load(&tmV, C::OFF_V, v_full, v_empty, j + 1);
       }
     }
   } else if (warp == 1) {
@@ -126,7 +140,7 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = mbar_wait(q_full, 0, abort_flag);
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
-        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag)) return false;
+        if (!mbar_wait(&k_full[s], (j >> 1) & 1, abort_flag)) return false;
         if (!mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1, abort_flag)) return false;
         tc_fence_after();
         const uint32_t ka = smem_u32(sm + C::OFF_K + s * C::KV_BYTES);
@@ -138,14 +152,15 @@ __global__ void __launch_bounds__(320, 1)
                      k ? 1u : 0u);
         }
         tc_commit(&s_full[s]);
+        tc_commit(&k_empty[s]);
         return true;
       };
       if (ok && nkv > 0) ok = issue_s(0);
       for (int j = 0; ok && j < nkv; ++j) {
         if (j + 1 < nkv && !issue_s(j + 1)) break;
-        if (!mbar_wait(p_full, j & 1, abort_flag)) break;
-        tc_fence_after();
         const int s = j & 1;
+        if (!mbar_wait(p_full, j & 1, abort_flag) || !mbar_wait(&v_full[s], (j >> 1) & 1, abort_flag)) break;
+        tc_fence_after();
         const uint32_t va = smem_u32(sm + C::OFF_V + s * C::KV_BYTES);
         const uint32_t pb = pa + s * C::P_BYTES;
 #pragma unroll
@@ -156,7 +171,7 @@ __global__ void __launch_bounds__(320, 1)
                      make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o, (j | k) ? 1u : 0u);
         }
         tc_commit(&pv_done[s]);
-        tc_commit(&kv_empty[s]);
+        tc_commit(&v_empty[s]);
       }
       tc_commit(mma_done);
     }
@@ -206,9 +221,10 @@ __global__ void __launch_bounds__(320, 1)
       if (lane == 0) mbar_arrive(&s_free[s]);
       // row max over both halves (the scale is positive)
       red[hh * 128 + r] = mx;
-      named_bar(1, 256);
+      // only the two warps of this TMEM lane quarter share rows: a 64-thread barrier per quarter
+      named_bar(1 + q4, 64);
       mx = fmaxf(red[r], red[128 + r]) * sl2;
-      named_bar(1, 256);  // both halves have read before the next block's maxima are written
+      named_bar(1 + q4, 64);  // both halves have read before the next block's maxima are written
       const float m_new = fmaxf(m_ref, mx);
       const bool rescale = j > 0 && m_new > m_ref + 8.0f;
       const bool any_rescale = __any_sync(0xffffffffu, rescale);
@@ -260,7 +276,7 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
     }
     red[hh * 128 + r] = l;
-    named_bar(1, 256);
+    named_bar(1 + q4, 64);
     const float lt = red[r] + red[128 + r];
     if (ok) {
       const float inv = lt > 0.f ? 1.f / lt : 0.f;
