@@ -9,16 +9,18 @@
 //   warp 1    MMA: S_j = Q K_j^T into one of two TMEM S buffers (so S_{j+1} is
 //             computed while the softmax warps work on S_j), then O += P_j V_j
 //             (V is an MN-major operand: head_dim is its contiguous axis)
-//   warps 2-9 softmax, two threads per query row (each half of the columns,
-//             row maxima exchanged through shared memory): read S_j from TMEM,
-//             masked online softmax in the log2 domain, P_j (bf16) written to shared
-//             memory in the 128-byte-swizzled K-major operand layout.  O is
-//             rescaled in TMEM only when the running max grows by more than
-//             2^8 (a lazy rescale: P stays <= 256, the final O/l is exact).
+//   warps 2-9 softmax, two threads per query row, each owning one half of the key
+//             columns with its own running max, row sum and O accumulator
+//             (O = O_0 + O_1, P_h V_h into O_h), so the halves never exchange
+//             maxima inside the loop: read S_j from TMEM, masked online softmax
+//             in the log2 domain, P_j (bf16) written to shared memory in the
+//             128-byte-swizzled K-major operand layout.  O_h is rescaled in TMEM
+//             only when its running max grows by more than 2^8 (a lazy rescale:
+//             P stays <= 256); the epilogue merges the halves once.
 // Causal masking skips KV blocks above the diagonal and masks the diagonal
 // block; grouped-query heads read K/V head h / (hq/hkv).  Rows of a tile that
 // run past the sequence (into the next batch element) are masked.
-// TMEM: S buffers at columns [0,128) and [128,256), O at [256, 256+D).
+// TMEM: S buffers at columns [0,128) and [128,256), O_0 at [256, 256+D), O_1 after it.
 #include "common.cuh"
 
 namespace th {
@@ -165,10 +167,11 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t pb = pa + s * C::P_BYTES;
 #pragma unroll
         for (int k = 0; k < C::BN / 16; ++k) {
-          // A = P rows x kv (K-major, 2 atoms of 128 rows); B = V kv x D (MN-major, atoms 128 rows apart)
+          // A = P rows x kv (K-major, 2 atoms of 128 rows: atom h = key half h); B = V kv x D
+          // (MN-major, atoms 128 rows apart); key half h accumulates into O_h
           const uint32_t poff = (uint32_t)((k >> 2) * C::BM * 128 + (k & 3) * 32);
-          tc_mma_f16(tO, make_desc_sw128(pb + poff, 16, 1024),
-                     make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o, (j | k) ? 1u : 0u);
+          tc_mma_f16(tO + (uint32_t)((k >> 2) * D), make_desc_sw128(pb + poff, 16, 1024),
+                     make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o, (j | (k & 3)) ? 1u : 0u);
         }
         tc_commit(&pv_done[s]);
         tc_commit(&v_empty[s]);
@@ -177,17 +180,17 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {  // ------------------------------------- softmax warps 2..9, two per TMEM lane quarter
     const int q4 = warp & 3;
-    const int hh = (warp - 2) >> 2;        // column half of S (and of O) this warp owns
+    const int hh = (warp - 2) >> 2;        // key half of S this warp owns (and its accumulator O_hh)
     const int r = q4 * 32 + lane;          // row within the tile (TMEM lane)
     const int qi = q0 + r;                 // query position
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const float sl2 = p.scale * 1.4426950408889634f;
     constexpr int HB = C::BN / 2, HD = D / 2;
-    float* red = reinterpret_cast<float*>(sm + C::OFF_RED);  // [2 halves][128 rows]
+    float* red = reinterpret_cast<float*>(sm + C::OFF_RED);  // [2 halves][128 rows], epilogue only
+    const uint32_t tOh = tO + lane_off + (uint32_t)(hh * D);  // this half's accumulator row
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      // no early exit: both halves must pass the same named barriers
       const int s = j & 1;
       ok = __all_sync(0xffffffffu, ok && mbar_wait(&s_full[s], (j >> 1) & 1, abort_flag));
       const int k0 = j * C::BN + hh * HB;  // first key of this warp's columns
@@ -214,17 +217,13 @@ __global__ void __launch_bounds__(320, 1)
             if (kj >= p.seq || (diag && kj > qi)) v[e] = -INFINITY;
           }
         }
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
 #pragma unroll
-        for (int e = 0; e < HB; ++e) mx = fmaxf(mx, v[e]);
+        for (int e = 0; e < HB; ++e) m4[e & 3] = fmaxf(m4[e & 3], v[e]);
+        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;  // the scale is positive
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[s]);
-      // row max over both halves (the scale is positive)
-      red[hh * 128 + r] = mx;
-      // only the two warps of this TMEM lane quarter share rows: a 64-thread barrier per quarter
-      named_bar(1 + q4, 64);
-      mx = fmaxf(red[r], red[128 + r]) * sl2;
-      named_bar(1 + q4, 64);  // both halves have read before the next block's maxima are written
       const float m_new = fmaxf(m_ref, mx);
       const bool rescale = j > 0 && m_new > m_ref + 8.0f;
       const bool any_rescale = __any_sync(0xffffffffu, rescale);
@@ -239,12 +238,12 @@ __global__ void __launch_bounds__(320, 1)
           m_ref = m_new;
         } else if (any_rescale) {
           const float f = rescale ? ex2_fast(m_ref - m_new) : 1.f;
-          for (int c = hh * HD; c < hh * HD + HD; c += 32) {
+          for (int c = 0; c < D; c += 32) {
             float o[32];
-            tmem_ld32(tO + lane_off + c, o);
+            tmem_ld32(tOh + c, o);
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] *= f;
-            tmem_st32(tO + lane_off + c, o);
+            tmem_st32(tOh + c, o);
           }
           if (rescale) {
             l *= f;
@@ -254,38 +253,52 @@ __global__ void __launch_bounds__(320, 1)
         const float mref = (m_ref == -INFINITY) ? 0.f : m_ref;  // fully masked row: P = 0
         // P = exp2(s*scale - m_ref) -> bf16 operand tile, running sum (2^-inf = 0 for masked scores)
         uint8_t* pt = sm + C::OFF_P + s * C::P_BYTES;
+        float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < HB; c += 8) {
           float pe[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             pe[e] = ex2_fast(fmaf(v[c + e], sl2, -mref));
-            l += pe[e];
+            l4[e & 3] += pe[e];
           }
           store8<T>(reinterpret_cast<T*>(pt + at_sw128(r, hh * HB + c, C::BM)), pe);
         }
+        l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
       }
       fence_proxy_async();  // P (generic writes) -> visible to the tensor cores
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    // epilogue: O / l, l summed over both halves
+    // epilogue: O = (O_0 2^(m_0-m) + O_1 2^(m_1-m)) / (l_0 2^(m_0-m) + l_1 2^(m_1-m)), m = max(m_0, m_1);
+    // the two warps of a TMEM lane quarter swap (m, l) through a 64-thread barrier of their own
     if (ok && nkv > 0) {
       ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, abort_flag));
       tc_fence_after();
     }
+    red[hh * 128 + r] = m_ref;
+    named_bar(1 + q4, 64);
+    const float m_o = red[(1 - hh) * 128 + r];
+    named_bar(1 + q4, 64);
     red[hh * 128 + r] = l;
     named_bar(1 + q4, 64);
-    const float lt = red[r] + red[128 + r];
+    const float l_o = red[(1 - hh) * 128 + r];
+    const float m_all = fmaxf(m_ref, m_o);
+    const float a_s = m_ref == -INFINITY ? 0.f : ex2_fast(m_ref - m_all);  // this half's weight
+    const float a_o = m_o == -INFINITY ? 0.f : ex2_fast(m_o - m_all);      // the other half's
+    const float lt = l * a_s + l_o * a_o;
     if (ok) {
       const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      const float w_s = a_s * inv, w_o = a_o * inv;
+      const uint32_t tOo = tO + lane_off + (uint32_t)((1 - hh) * D);
       T* orow = reinterpret_cast<T*>(p.o) + (row0 + qi) * p.ldo + (int64_t)h * D;
       for (int c = hh * HD; c < hh * HD + HD; c += 32) {
-        float o[32];
-        tmem_ld32(tO + lane_off + c, o);
+        float o[32], o2[32];
+        tmem_ld32(tOh + c, o);
+        tmem_ld32(tOo + c, o2);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] *= inv;
+        for (int e = 0; e < 32; ++e) o[e] = o[e] * w_s + o2[e] * w_o;
         if (qi < p.seq) {
 #pragma unroll
           for (int e8 = 0; e8 < 32; e8 += 8) store8<T>(orow + c + e8, o + e8);
