@@ -2,25 +2,28 @@
 //
 // One CTA = 128 query rows of one (batch, query head); KV blocks of 128 rows.
 // 320 threads, warp-specialised:
-//   warp 0    TMA: the Q tile once, then K and V tiles into separate 2-stage rings, in
-//             the order the MMA warp consumes them (K_{j+2} as soon as S_j has read
-//             its slot, V_{j+1} once P_{j-1} V_{j-1} has), so the load of the next
-//             K block never waits for a P.V product
+//   warp 0    TMA: the Q tile once, then K and V tiles into separate 3-stage rings, in
+//             the order the MMA warp consumes them (K_0, K_1, V_0, K_2, V_1, ...), so
+//             the load of the next K block never waits for a P.V product
 //   warp 1    MMA: S_j = Q K_j^T into one of two TMEM S buffers (so S_{j+1} is
-//             computed while the softmax warps work on S_j), then O += P_j V_j
-//             (V is an MN-major operand: head_dim is its contiguous axis)
+//             computed while the softmax warps work on S_j), then O += P_j V_j with
+//             P_j read from tensor memory (V is an MN-major shared-memory operand:
+//             head_dim is its contiguous axis); S buffer j&1 is reused by S_{j+2}
+//             once P_j V_j, which reads P_j out of it, has completed
 //   warps 2-9 softmax, two threads per query row, each owning one half of the key
 //             columns with its own running max, row sum and O accumulator
 //             (O = O_0 + O_1, P_h V_h into O_h), so the halves never exchange
 //             maxima inside the loop: read S_j from TMEM, masked online softmax
-//             in the log2 domain, P_j (bf16) written to shared memory in the
-//             128-byte-swizzled K-major operand layout.  O_h is rescaled in TMEM
+//             in the log2 domain, P_j (bf16 pairs) stored back into the first 32
+//             columns of the thread's own 64-column part of the S_j buffer, where
+//             the P.V MMA reads it as its A operand.  O_h is rescaled in TMEM
 //             only when its running max grows by more than 2^8 (a lazy rescale:
 //             P stays <= 256); the epilogue merges the halves once.
 // Causal masking skips KV blocks above the diagonal and masks the diagonal
 // block; grouped-query heads read K/V head h / (hq/hkv).  Rows of a tile that
 // run past the sequence (into the next batch element) are masked.
-// TMEM: S buffers at columns [0,128) and [128,256), O_0 at [256, 256+D), O_1 after it.
+// TMEM: S buffers at columns [0,128) and [128,256) (P_j of key half h in columns
+// [h*64, h*64+32) of its buffer), O_0 at [256, 256+D), O_1 after it.
 #include "common.cuh"
 
 namespace th {
@@ -31,22 +34,15 @@ struct AtCfg {
   static constexpr int DA = D / 64;                // 64-column atoms of head_dim
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;      // one K or one V tile
-  static constexpr int P_BYTES = BM * BN * 2;
-  static constexpr int STAGES = 2;
+  static constexpr int STAGES = 3;                 // K ring and V ring depth
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = Q_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
-  static constexpr int OFF_RED = OFF_P + 2 * P_BYTES;  // P double-buffered; then the row-max / row-sum
-  static constexpr int OFF_BAR = OFF_RED + 2 * 128 * 4;  // exchange between the two column halves
+  static constexpr int OFF_RED = OFF_V + STAGES * KV_BYTES;  // epilogue (max, sum) exchange of the halves
+  static constexpr int OFF_BAR = OFF_RED + 2 * 128 * 4;
   static constexpr int SMEM = 1024 + OFF_BAR + 256;
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
-
-__device__ __forceinline__ uint32_t at_sw128(int row, int col, int rows) {
-  const int atom = col >> 6, chunk = (col & 63) >> 3, e = col & 7;
-  return (uint32_t)(atom * rows * 128 + row * 128 + ((chunk ^ (row & 7)) << 4) + e * 2);
-}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(320, 1)
@@ -56,17 +52,18 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
+  constexpr int NS = C::STAGES;
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;         // [2]
-  uint64_t* k_empty = bars + 3;        // [2]
-  uint64_t* s_full = bars + 5;         // [2]
-  uint64_t* s_free = bars + 7;         // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* pv_done = bars + 10;       // [2], one per P buffer
-  uint64_t* mma_done = bars + 12;
-  uint64_t* v_full = bars + 13;        // [2]
-  uint64_t* v_empty = bars + 15;       // [2]
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* k_full = bars + 1;             // [NS]
+  uint64_t* k_empty = k_full + NS;         // [NS]
+  uint64_t* v_full = k_empty + NS;         // [NS]
+  uint64_t* v_empty = v_full + NS;         // [NS]
+  uint64_t* s_full = v_empty + NS;         // [2]
+  uint64_t* s_free = s_full + 2;           // [2] S buffer (and the P in it) consumed by P.V
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_done = p_full + 1;          // [2]
+  uint64_t* mma_done = pv_done + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -81,13 +78,15 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 8);
+      mbar_init(&s_free[s], 1);
     }
     mbar_init(p_full, 8);
     mbar_init(&pv_done[0], 1);
@@ -116,8 +115,8 @@ __global__ void __launch_bounds__(320, 1)
         tma_load_2d(sm + C::OFF_Q + a * C::BM * 128, &tmQ, q_full, h * D + a * 64, (int)(row0 + q0));
       // one K or V tile of block j into its ring slot once the slot's previous reader is done
       auto load = [&](const CUtensorMap* tm, int off, uint64_t* full, uint64_t* empty, int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&empty[s], ((j >> 1) & 1) ^ 1, abort_flag)) return false;
+        const int s = j % NS;
+        if (!mbar_wait(&empty[s], ((j / NS) & 1) ^ 1, abort_flag)) return false;
         mbar_arrive_expect_tx(&full[s], C::KV_BYTES);
         for (int a = 0; a < C::DA; ++a)
           tma_load_2d(sm + off + s * C::KV_BYTES + a * C::BN * 128, tm, &full[s], hk * D + a * 64,
@@ -138,14 +137,14 @@ __global__ void __launch_bounds__(320, 1)
       constexpr int fmt = DT<T>::id == TH_BF16 ? 1 : 0;
       constexpr uint32_t id_s = make_idesc_f16(128, C::BN, fmt, 0, 0);
       constexpr uint32_t id_o = make_idesc_f16(128, D, fmt, 0, 1);  // V: MN-major
-      const uint32_t qa = smem_u32(sm + C::OFF_Q), pa = smem_u32(sm + C::OFF_P);
+      const uint32_t qa = smem_u32(sm + C::OFF_Q);
       bool ok = mbar_wait(q_full, 0, abort_flag);
       auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&k_full[s], (j >> 1) & 1, abort_flag)) return false;
+        const int s = j & 1, ks = j % NS;
+        if (!mbar_wait(&k_full[ks], (j / NS) & 1, abort_flag)) return false;
         if (!mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t ka = smem_u32(sm + C::OFF_K + s * C::KV_BYTES);
+        const uint32_t ka = smem_u32(sm + C::OFF_K + ks * C::KV_BYTES);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const uint32_t off = (uint32_t)((k >> 2) * C::BM * 128 + (k & 3) * 32);
@@ -154,27 +153,27 @@ __global__ void __launch_bounds__(320, 1)
                      k ? 1u : 0u);
         }
         tc_commit(&s_full[s]);
-        tc_commit(&k_empty[s]);
+        tc_commit(&k_empty[ks]);
         return true;
       };
       if (ok && nkv > 0) ok = issue_s(0);
       for (int j = 0; ok && j < nkv; ++j) {
         if (j + 1 < nkv && !issue_s(j + 1)) break;
-        const int s = j & 1;
-        if (!mbar_wait(p_full, j & 1, abort_flag) || !mbar_wait(&v_full[s], (j >> 1) & 1, abort_flag)) break;
+        const int s = j & 1, vs = j % NS;
+        if (!mbar_wait(p_full, j & 1, abort_flag) || !mbar_wait(&v_full[vs], (j / NS) & 1, abort_flag)) break;
         tc_fence_after();
-        const uint32_t va = smem_u32(sm + C::OFF_V + s * C::KV_BYTES);
-        const uint32_t pb = pa + s * C::P_BYTES;
+        const uint32_t va = smem_u32(sm + C::OFF_V + vs * C::KV_BYTES);
 #pragma unroll
         for (int k = 0; k < C::BN / 16; ++k) {
-          // A = P rows x kv (K-major, 2 atoms of 128 rows: atom h = key half h); B = V kv x D
-          // (MN-major, atoms 128 rows apart); key half h accumulates into O_h
-          const uint32_t poff = (uint32_t)((k >> 2) * C::BM * 128 + (k & 3) * 32);
-          tc_mma_f16(tO + (uint32_t)((k >> 2) * D), make_desc_sw128(pb + poff, 16, 1024),
-                     make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o, (j | (k & 3)) ? 1u : 0u);
+          // A = P_j from TMEM: key half h = k / 4 sits in columns [h*64, h*64+32) of S buffer s, eight
+          // columns per 16 keys; B = V kv x D (MN-major, atoms 128 rows apart); half h accumulates into O_h
+          const uint32_t pt = tmem + (uint32_t)(s * 128 + (k >> 2) * 64 + (k & 3) * 8);
+          tc_mma_f16_ts(tO + (uint32_t)((k >> 2) * D), pt, make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024),
+                        id_o, (j | (k & 3)) ? 1u : 0u);
         }
         tc_commit(&pv_done[s]);
-        tc_commit(&v_empty[s]);
+        tc_commit(&s_free[s]);
+        tc_commit(&v_empty[vs]);
       }
       tc_commit(mma_done);
     }
@@ -222,16 +221,13 @@ __global__ void __launch_bounds__(320, 1)
         for (int e = 0; e < HB; ++e) m4[e & 3] = fmaxf(m4[e & 3], v[e]);
         mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;  // the scale is positive
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[s]);
       const float m_new = fmaxf(m_ref, mx);
       const bool rescale = j > 0 && m_new > m_ref + 8.0f;
       const bool any_rescale = __any_sync(0xffffffffu, rescale);
-      // O is rescaled only once O += P_{j-1} V_{j-1} is complete; P_j's buffer is free once
-      // P_{j-2} V_{j-2} is (the other buffer lets P_j be written while P_{j-1} V_{j-1} runs)
+      // O is rescaled only once O += P_{j-1} V_{j-1} is complete (P_j goes into S_j's own buffer,
+      // which nothing else reads before P_j V_j)
       if (j > 0 && any_rescale)
         ok = __all_sync(0xffffffffu, ok && mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag));
-      if (j > 1) ok = __all_sync(0xffffffffu, ok && mbar_wait(&pv_done[s], ((j - 2) >> 1) & 1, abort_flag));
       if (ok) {
         tc_fence_after();
         if (j == 0) {
@@ -251,22 +247,20 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         const float mref = (m_ref == -INFINITY) ? 0.f : m_ref;  // fully masked row: P = 0
-        // P = exp2(s*scale - m_ref) -> bf16 operand tile, running sum (2^-inf = 0 for masked scores)
-        uint8_t* pt = sm + C::OFF_P + s * C::P_BYTES;
+        // P = exp2(s*scale - m_ref) as 16-bit pairs into TMEM, running sum (2^-inf = 0 for masked scores)
+        float pk[HB / 2];
         float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < HB; c += 8) {
-          float pe[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            pe[e] = ex2_fast(fmaf(v[c + e], sl2, -mref));
-            l4[e & 3] += pe[e];
-          }
-          store8<T>(reinterpret_cast<T*>(pt + at_sw128(r, hh * HB + c, C::BM)), pe);
+        for (int c = 0; c < HB / 2; ++c) {
+          const float p0 = ex2_fast(fmaf(v[2 * c], sl2, -mref));
+          const float p1 = ex2_fast(fmaf(v[2 * c + 1], sl2, -mref));
+          l4[(2 * c) & 3] += p0;
+          l4[(2 * c + 1) & 3] += p1;
+          pk[c] = __uint_as_float(pack2<T>(p0, p1));
         }
+        tmem_st32(tmem + lane_off + (uint32_t)(s * 128 + hh * HB), pk);
         l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
       }
-      fence_proxy_async();  // P (generic writes) -> visible to the tensor cores
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
