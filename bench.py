@@ -409,7 +409,12 @@ def main() -> None:
                     "entry": ("CompileResult.module(host batch) per rank" if tp else
                               "CompileResult.streaming_runner (2 slots, CUDA-graph forward, H2D/compute/D2H streams)"),
                     "h2d_bytes_per_step": xh.numel() * xh.element_size(),
-                    "d2h_bytes_per_step": oh.numel() * oh.element_size()},
+                    "d2h_bytes_per_step": oh.numel() * oh.element_size(),
+                    # the larger copy's bytes per e2e step time: the host link rate sustained when
+                    # the copies, not the forward, set the step (e2e step well above the device step)
+                    "copy_gbs": max(xh.numel() * xh.element_size(), oh.numel() * oh.element_size()) / ms_e2e / 1e6,
+                    "bound": ("copies and forward in sequence" if tp else
+                              "host copies" if ms_e2e > 1.2 * ms else "device forward")},
             "gpu_launches": mod.n_launches * args.steps,
             "clocks": clocks.summary(),
             "kernels_ms": ktimes,
