@@ -341,38 +341,55 @@ __global__ void __launch_bounds__(128) conv1d_kernel(const T* __restrict__ x, in
 }
 
 // TMA-staged causal conv (2-byte dtypes): a persistent block streams tiles
-// of 64 tokens x 256 channels through a 3-stage shared-memory ring.  Each
-// tile is one TMA box of (64 + width - 1) rows starting width-1 rows before
+// of 32 tokens x 256 channels through a 3-stage shared-memory ring.  Each
+// tile is one TMA box of (32 + width - 1) rows starting width-1 rows before
 // the tile; the 3-D map [batch][seq][channels] zero-fills rows before the
 // sequence start, which is exactly the causal left padding, and rows past
-// its end.  Thread = 8 channels x 8 tokens, read from shared memory
-// conflict-free (a warp reads one 512-byte row), written with coalesced
-// 16-byte stores.
-constexpr int CT_TOK = 64, CT_CH = 256, CT_STAGES = 3;
+// its end.  Thread = 8 channels x 4 tokens, read from shared memory
+// conflict-free (a warp reads one 512-byte row).  The outputs go to one of two
+// shared-memory output tiles and leave by TMA store, which clips rows past the
+// sequence end and channels past the last one, so the threads issue no global
+// stores (per-thread 16-byte stores of every output stalled on the LSU queue).
+constexpr int CT_TOK = 32, CT_CH = 256, CT_STAGES = 3;
 
 template <int W>
 struct CtCfg {
   static constexpr int ROWS = CT_TOK + W - 1;
   static constexpr int TILE = ((ROWS * CT_CH * 2 + 127) / 128) * 128;
-  static constexpr int SMEM = 128 + CT_STAGES * TILE + 64;
+  static constexpr int OUT = CT_TOK * CT_CH * 2;  // one output tile
+  static constexpr int OFF_OUT = CT_STAGES * TILE;
+  static constexpr int OFF_W = OFF_OUT + 2 * OUT;        // taps of the block's channels, [W][CT_CH] fp32
+  static constexpr int OFF_B = OFF_W + W * CT_CH * 4;    // bias, [CT_CH] fp32
+  static constexpr int OFF_BAR = OFF_B + CT_CH * 4;
+  static constexpr int SMEM = 128 + OFF_BAR + 64;
 };
 
 template <typename T, int W>
-__global__ void __launch_bounds__(256, 2) conv1d_tma(const __grid_constant__ CUtensorMap tmX, const float* __restrict__ w,
-                                                     const float* __restrict__ bias, T* __restrict__ y, int64_t ldy,
-                                                     int seq, int channels, int act, int ncb, int nsb, int ntiles) {
+__global__ void __launch_bounds__(256, 2) conv1d_tma(const __grid_constant__ CUtensorMap tmX,
+                                                     const __grid_constant__ CUtensorMap tmY, const float* __restrict__ w,
+                                                     const float* __restrict__ bias, int channels, int act, int ncb,
+                                                     int nsb, int ntiles) {
   using Cf = CtCfg<W>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + CT_STAGES * Cf::TILE);
+  uint8_t* outs = sm + Cf::OFF_OUT;  // [2] output tiles
+  float* wsm = reinterpret_cast<float*>(sm + Cf::OFF_W);
+  float* bsm = reinterpret_cast<float*>(sm + Cf::OFF_B);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cf::OFF_BAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar + CT_STAGES);
   const int tid = threadIdx.x, tx = tid & 31, ty = tid >> 5;
   // gridDim.x is a multiple of ncb, so every tile of this block has the same channel block
   const int cb = blockIdx.x % ncb;
+  auto coords = [&](int tile, int& sb, int& b) {
+    const int rest = tile / ncb;
+    sb = rest % nsb;
+    b = rest / nsb;
+  };
   auto issue = [&](int k) {  // k-th tile of this block into stage k % CT_STAGES
     const int tile = blockIdx.x + k * gridDim.x;
     if (tile >= ntiles) return;
-    const int rest = tile / ncb, sb = rest % nsb, b = rest / nsb;
+    int sb, b;
+    coords(tile, sb, b);
     uint64_t* br = &bar[k % CT_STAGES];
     mbar_arrive_expect_tx(br, Cf::ROWS * CT_CH * 2);
     tma_load_3d(sm + (k % CT_STAGES) * Cf::TILE, &tmX, br, cb * CT_CH, sb * CT_TOK - (W - 1), b);
@@ -386,51 +403,70 @@ __global__ void __launch_bounds__(256, 2) conv1d_tma(const __grid_constant__ CUt
   pdl_trigger();
   if (tid == 0)
     for (int k = 0; k < CT_STAGES; ++k) issue(k);
-  const int c0 = cb * CT_CH + tx * 8;
-  const bool live = c0 < channels;
-  float wt[8][W], bi[8];
+  {
+    // the block's taps and bias through shared memory: thread i reads channel i's W taps (a warp
+    // reads one contiguous span) and stores them tap-major; per-thread reads of eight channels'
+    // taps straight from global memory touched 32 cache lines per warp load and dominated the kernel
+    const int ci = cb * CT_CH + tid;
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-#pragma unroll
-    for (int j = 0; j < W; ++j) wt[e][j] = live ? w[(int64_t)(c0 + e) * W + j] : 0.f;
-    bi[e] = (live && bias) ? bias[c0 + e] : 0.f;
+    for (int j = 0; j < W; ++j) wsm[j * CT_CH + tid] = ci < channels ? w[(int64_t)ci * W + j] : 0.f;
+    bsm[tid] = (ci < channels && bias) ? bias[ci] : 0.f;
   }
   __syncthreads();
+  float wt[8][W], bi[8];
+#pragma unroll
+  for (int j = 0; j < W; ++j) {
+    const float4 a = *reinterpret_cast<const float4*>(wsm + j * CT_CH + tx * 8);
+    const float4 c = *reinterpret_cast<const float4*>(wsm + j * CT_CH + tx * 8 + 4);
+    wt[0][j] = a.x; wt[1][j] = a.y; wt[2][j] = a.z; wt[3][j] = a.w;
+    wt[4][j] = c.x; wt[5][j] = c.y; wt[6][j] = c.z; wt[7][j] = c.w;
+  }
+  {
+    const float4 a = *reinterpret_cast<const float4*>(bsm + tx * 8);
+    const float4 c = *reinterpret_cast<const float4*>(bsm + tx * 8 + 4);
+    bi[0] = a.x; bi[1] = a.y; bi[2] = a.z; bi[3] = a.w;
+    bi[4] = c.x; bi[5] = c.y; bi[6] = c.z; bi[7] = c.w;
+  }
   bool ok = true;
   for (int k = 0;; ++k) {
     const int tile = blockIdx.x + k * gridDim.x;
     if (tile >= ntiles) break;
-    const int rest = tile / ncb, sb = rest % nsb, b = rest / nsb;
     ok = ok && mbar_wait(&bar[k % CT_STAGES], (k / CT_STAGES) & 1, abort_flag);
-    if (ok && live) {
+    if (ok) {
+      // rows past the sequence end and channels past the last read as zero; the store clips them
       const uint8_t* st = sm + (k % CT_STAGES) * Cf::TILE;
-      T* yb = y + ((int64_t)b * seq) * ldy + c0;
+      uint8_t* ob = outs + (k & 1) * Cf::OUT;
+      const int r0 = ty * 4;
+      float in[4 + W - 1][8];
 #pragma unroll
-      for (int hv = 0; hv < 2; ++hv) {  // 4 tokens at a time keeps the rows in registers
-        const int r0 = ty * 8 + hv * 4;
-        float in[4 + W - 1][8];
+      for (int r = 0; r < 4 + W - 1; ++r)
+        load8<T>(reinterpret_cast<const T*>(st + (size_t)(r0 + r) * (CT_CH * 2) + tx * 16), in[r]);
 #pragma unroll
-        for (int r = 0; r < 4 + W - 1; ++r)
-          load8<T>(reinterpret_cast<const T*>(st + (size_t)(r0 + r) * (CT_CH * 2) + tx * 16), in[r]);
+      for (int kk = 0; kk < 4; ++kk) {
+        float o[8];
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const int sp = sb * CT_TOK + r0 + kk;
-          if (sp >= seq) break;
-          float o[8];
+        for (int e = 0; e < 8; ++e) {
+          float acc = bi[e];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            float acc = bi[e];
-#pragma unroll
-            for (int j = 0; j < W; ++j) acc = fmaf(wt[e][j], in[kk + j][e], acc);
-            o[e] = act == TH_ACT_SILU ? silu_tanh(acc) : acc;
-          }
-          store8<T>(yb + (int64_t)sp * ldy, o);
+          for (int j = 0; j < W; ++j) acc = fmaf(wt[e][j], in[kk + j][e], acc);
+          o[e] = act == TH_ACT_SILU ? silu_tanh(acc) : acc;
         }
+        store8<T>(reinterpret_cast<T*>(ob + (size_t)(r0 + kk) * (CT_CH * 2) + tx * 16), o);
       }
     }
-    __syncthreads();  // everyone is done with this stage
-    if (tid == 0 && ok) issue(k + CT_STAGES);
+    fence_proxy_async();  // the output tile (generic writes) -> visible to the TMA store
+    // the store of the previous tile has read its buffer, which the next tile writes
+    if (tid == 0) bulk_wait_read0();
+    __syncthreads();  // everyone is done with this input stage and this output tile
+    if (tid == 0 && ok) {
+      int sb, b;
+      coords(tile, sb, b);
+      tma_store_3d(&tmY, outs + (k & 1) * Cf::OUT, cb * CT_CH, sb * CT_TOK, b);
+      bulk_commit();
+      issue(k + CT_STAGES);
+    }
   }
+  if (tid == 0) bulk_wait0();  // the output stores are complete before the block exits
 }
 
 // ------------------------------------------------------------ embedding
@@ -541,10 +577,13 @@ static void launch_conv(const th_conv1d_args* a, cudaStream_t st) {
 template <typename T, int W>
 static int launch_conv_tma(const th_conv1d_args* a, cudaStream_t st) {
   using Cf = th::CtCfg<W>;
-  CUtensorMap tm;
+  CUtensorMap tm, ty;
   const uint64_t S = (uint64_t)a->seq;
   int rc = th::make_tmap_3d(&tm, a->x, a->dtype, (uint64_t)a->channels, S, (uint64_t)a->batch, (uint64_t)a->ldx * 2,
                             S * a->ldx * 2, th::CT_CH, Cf::ROWS, false);
+  if (!rc)
+    rc = th::make_tmap_3d(&ty, a->y, a->dtype, (uint64_t)a->channels, S, (uint64_t)a->batch, (uint64_t)a->ldy * 2,
+                          S * a->ldy * 2, th::CT_CH, th::CT_TOK, false);
   if (rc) return rc;
   static bool set = false;
   if (!set) {
@@ -557,8 +596,8 @@ static int launch_conv_tma(const th_conv1d_args* a, cudaStream_t st) {
   int grid = (2 * th::sm_count() / ncb) * ncb;
   if (grid < ncb) grid = ncb;
   if (grid > ntiles) grid = ntiles;
-  th::launch_pdl(th::conv1d_tma<T, W>, dim3(grid), dim3(256), Cf::SMEM, st, tm, a->w, a->bias, (T*)a->y, a->ldy,
-                 a->seq, a->channels, a->act, ncb, nsb, ntiles);
+  th::launch_pdl(th::conv1d_tma<T, W>, dim3(grid), dim3(256), Cf::SMEM, st, tm, ty, a->w, a->bias, a->channels, a->act,
+                 ncb, nsb, ntiles);
   return th::check_launch("th_conv1d(tma)");
 }
 
