@@ -28,6 +28,8 @@ struct EpiParams {
   const float* rope_cos;
   const float* rope_sin;
   int rope_begin, rope_end, rope_hd, rope_seq;
+  int rope_vec;  // tables 16-byte aligned and head_dim % 4 == 0: 16-byte table loads
+  int rs_vec;    // row-scale parts 16-byte aligned with a multiple of 4 per row: 16-byte loads
   int swiglu;
   const void* residual;
   int64_t ld_res;
@@ -321,10 +323,28 @@ __device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_o
         const bool first = within0 < half;
         float pv[32];
         tmem_ld32(tbase + (first ? c + half : c - half), pv);
+        if (ep.rope_vec) {
+          // each lane (row) reads its own table row: 16-byte loads cut the cache lines a warp
+          // touches per table element fourfold, which bounded the QKV GEMM's epilogue
+          const float4* c4 = reinterpret_cast<const float4*>(ep.rope_cos + pos + within0);
+          const float4* s4 = reinterpret_cast<const float4*>(ep.rope_sin + pos + within0);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float rot = first ? -pv[e] * rs : pv[e] * rs;
-          v[e] = v[e] * ep.rope_cos[pos + within0 + e] + rot * ep.rope_sin[pos + within0 + e];
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 cq = __ldg(c4 + q4), sq = __ldg(s4 + q4);
+            const float cv[4] = {cq.x, cq.y, cq.z, cq.w}, sv[4] = {sq.x, sq.y, sq.z, sq.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int k = q4 * 4 + e;
+              const float rot = first ? -pv[k] * rs : pv[k] * rs;
+              v[k] = v[k] * cv[e] + rot * sv[e];
+            }
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float rot = first ? -pv[e] * rs : pv[e] * rs;
+            v[e] = v[e] * ep.rope_cos[pos + within0 + e] + rot * ep.rope_sin[pos + within0 + e];
+          }
         }
       } else {  // heads of <= 32 columns: partner inside this chunk
         float t[32];
@@ -370,7 +390,19 @@ __device__ __forceinline__ bool epilogue_tmem_tile(uint32_t tacc, int warp, int 
   if (ep.rs_parts && row_ok && ce > cb) {
     const float* pp = ep.rs_parts + (int64_t)row * ep.rs_nparts;
     float sacc = 0.f;
-    for (int k = 0; k < ep.rs_nparts; ++k) sacc += pp[k];
+    if (ep.rs_vec) {  // each lane reads its own row: 16-byte loads touch a quarter of the lines
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int k = 0; k < ep.rs_nparts; k += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(pp + k));
+        s4[0] += v.x;
+        s4[1] += v.y;
+        s4[2] += v.z;
+        s4[3] += v.w;
+      }
+      sacc = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+    } else {
+      for (int k = 0; k < ep.rs_nparts; ++k) sacc += pp[k];
+    }
     rs = rsqrtf(sacc * ep.rs_inv_k + ep.rs_eps);
   }
   uint4 rb[3][4];
@@ -843,6 +875,8 @@ extern "C" int th_gemm(const th_gemm_args* a, void* stream) {
   ep.act = a->act; ep.act_begin = a->act_begin; ep.act_end = a->act_end; ep.bias = a->bias;
   ep.rope_cos = a->rope_cos; ep.rope_sin = a->rope_sin; ep.rope_begin = a->rope_begin; ep.rope_end = a->rope_end;
   ep.rope_hd = a->rope_head_dim; ep.rope_seq = a->rope_seq;
+  ep.rope_vec = a->rope_cos && is_al16(a->rope_cos) && is_al16(a->rope_sin) && a->rope_head_dim % 4 == 0;
+  ep.rs_vec = a->rs_parts && is_al16(a->rs_parts) && a->rs_nparts % 4 == 0;
   ep.swiglu = a->swiglu; ep.residual = a->residual; ep.ld_res = a->ld_res;
   ep.out2 = a->out2; ep.ld_out2 = a->ld_out2; ep.tail_begin = tail;
   ep.ss_out = a->ss_out; ep.ss_ld = a->ss_ld;
