@@ -18,9 +18,14 @@
  *     ELEMENTS (`ld*`).  Activations are token-major [T, features],
  *     T = batch * seq, exactly the 2-D form the reference optimizer gives
  *     every activation (src/torch_helion/optimizer/passes.py:719-762).
- *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy stream).
- *     Calls are re-entrant: the only global mutable state is a thread-local
- *     error string and one device-side error word (th_device_error).
+ *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy stream)
+ *     on the CURRENT device.  Calls may come from several threads and for
+ *     several devices in one process.  Process-wide state: a thread-local
+ *     error string; one device-side error word per device (th_device_error);
+ *     host caches guarded by mutexes -- encoded TMA descriptors (keyed by
+ *     address and geometry), each kernel's raised shared-memory limit and the
+ *     SM count (both per device ordinal), and th_ssd_noalloc's scratch
+ *     address (per CUDA context).  None of it changes a call's result.
  *   - Return value: TH_OK (0) or a negative TH_E* code; the message is in
  *     th_last_error_string().
  */
@@ -61,6 +66,15 @@ const char* th_version(void);
 /* Reads (and with clear!=0 resets) the device error word that kernels set
  * when a bounded wait gives up.  Synchronises the current device. */
 int th_device_error(int* out_code, int clear);
+
+/* Diagnostic -- no counterpart in the reference (its kernels never run on a
+ * device).  Launches one CTA whose thread 0 waits on an mbarrier through the
+ * same bounded wait every pipelined kernel here uses, but with a limit of
+ * `limit_ns`, while thread 32 arrives after `arrive_ns`.  *completed (device
+ * memory) becomes 1 when the arrival was seen and 0 when the wait gave up,
+ * in which case the device error word reports TH_DEVERR_MBAR_TIMEOUT (1)
+ * through th_device_error.  limit_ns in [1e3, 1e8], arrive_ns in [0, 1e8]. */
+int th_selftest_bounded_wait(int64_t limit_ns, int64_t arrive_ns, int32_t* completed, void* stream);
 
 /* ----------------------------------------------------------------- rowstat
  * sumsq[r] = sum_k x[r,k]^2 (fp32).  Replaces the `row_sumsq` column the
@@ -218,9 +232,12 @@ int th_ssd(const th_ssd_args* a, void* stream);
  * ignored: the chunk-state scratch is a file-scope device array of
  * TH_SSD_NOALLOC_MAX_BYTES that every GPU loading the library keeps until
  * exit; shapes needing more (see th_ssd_workspace_size) are rejected with
- * TH_EINVAL.  Inputs and outputs are still the caller's.  The first call on
- * a device looks up the array's device address with that device current
- * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * TH_EINVAL.  Inputs and outputs are still the caller's.  The first call in
+ * a CUDA context looks up the array's device address with the caller's
+ * device current (cudaGetSymbolAddress) and caches it per context (the
+ * driver's context ID), so a device reset or another context on the same
+ * device gets its own lookup; make that first call before any stream
+ * capture.
  * All calls share the one array and it keeps the previous call's contents
  * (nothing in it needs to start at zero), so calls whose work overlaps on
  * the GPU -- concurrent streams, or threads sharing a device -- race. */

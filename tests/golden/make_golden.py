@@ -2,7 +2,7 @@
 
     PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py [--ref /path/to/torch-helion]
 
-The reference checkout (default: $TH_REFERENCE or /root/reference) is only
+The reference checkout (--ref, or $TH_REFERENCE; required) is only
 needed here, when the fixtures are (re)generated; the tests read the
 committed ``*.pt`` files and never import the reference.  Every fixture is
 produced by the reference's own modules (models/llama_block.py,
@@ -53,8 +53,11 @@ def _baseline_a(model, seed: int = 0) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("TH_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("TH_REFERENCE"),
+                    help="checkout of the reference project (or set $TH_REFERENCE)")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give the reference checkout with --ref or $TH_REFERENCE")
     sys.path.insert(0, a.ref)
     from models.llama_block import LlamaBlockConfig, build_llama_block
     from models.mamba import MambaConfig, build_mamba_model, causal_chunk_masks, ssd_chunked, ssd_quadratic

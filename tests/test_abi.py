@@ -32,7 +32,8 @@ def declared_functions() -> list[str]:
 def test_header_declares_entry_points():
     fns = declared_functions()
     for f in ("th_gemm", "th_attention", "th_ssd", "th_ssd_workspace_size", "th_rmsnorm", "th_rowstat", "th_conv1d",
-              "th_embedding", "th_ssd_noalloc", "th_version", "th_last_error_string", "th_device_error"):
+              "th_embedding", "th_ssd_noalloc", "th_selftest_bounded_wait", "th_version", "th_last_error_string",
+              "th_device_error"):
         assert f in fns, fns
 
 
@@ -42,7 +43,7 @@ def test_library_exports_every_declared_symbol():
     so = lib.load()
     missing = [f for f in declared_functions() if not hasattr(so, f)]
     assert not missing, missing
-    assert set(lib.EXPORTED_SYMBOLS) <= set(declared_functions())
+    assert set(lib.EXPORTED_SYMBOLS) == set(declared_functions())
     assert lib.version()
 
 

@@ -15,7 +15,6 @@ on two calls in a row (the scratch keeps the previous call's contents).
 
 from __future__ import annotations
 
-import ctypes
 import math
 
 import pytest
@@ -26,20 +25,17 @@ from conftest import rel_l2
 pytestmark = pytest.mark.gpu
 
 
-def _noalloc_fn():
+def _lib():
     from torch_helion.b200 import lib
 
-    l = lib.load()
-    fn = l.th_ssd_noalloc
-    fn.restype = ctypes.c_int
-    fn.argtypes = [ctypes.POINTER(lib.SsdArgs), ctypes.c_void_p]
-    return lib, fn
+    lib.load()
+    return lib
 
 
-def _inputs(b, s, h, p, g, n, dtype, seed):
+def _inputs(b, s, h, p, g, n, dtype, seed, device="cuda:0"):
     torch.manual_seed(seed)
     t = b * s
-    dev = torch.device("cuda:0")
+    dev = torch.device(device)
     return dict(
         x=torch.randn(t, h * p, device=dev).to(dtype),
         B=torch.randn(t, g * n, device=dev).to(dtype),
@@ -51,54 +47,69 @@ def _inputs(b, s, h, p, g, n, dtype, seed):
     )
 
 
-def _args(lib, t, out, gss, b, s, h, p, g, n, chunk, dtype_code):
-    a = lib.SsdArgs()
-    a.x, a.ldx = t["x"].data_ptr(), t["x"].stride(0)
-    a.dt, a.lddt = t["dt"].data_ptr(), t["dt"].stride(0)
-    a.A = t["A"].data_ptr()
-    a.B, a.ldb = t["B"].data_ptr(), t["B"].stride(0)
-    a.C, a.ldc = t["C"].data_ptr(), t["C"].stride(0)
-    a.D = t["D"].data_ptr()
-    a.z, a.ldz = t["z"].data_ptr(), t["z"].stride(0)
-    a.out, a.ldo = out.data_ptr(), out.stride(0)
-    a.gss, a.ldgss = gss.data_ptr(), gss.stride(0)
-    a.batch, a.seq, a.heads, a.head_dim, a.ngroups, a.state_dim, a.chunk = b, s, h, p, g, n, chunk
-    a.dtype = dtype_code
-    a.workspace, a.workspace_bytes = None, 0
-    return a
+def _both(lib, t, b, s, h, p, g, n, chunk):
+    """(th_ssd output, gss) and (th_ssd_noalloc output, gss) on the same inputs;
+    the no-alloc outputs start as NaN so nothing stale can pass."""
+    kw = dict(batch=b, seq=s, heads=h, head_dim=p, ngroups=g, state_dim=n, chunk=chunk, D=t["D"], z=t["z"])
+    ref = torch.empty_like(t["x"])
+    ref_gss = torch.empty(b * s, h, device=ref.device)
+    lib.ssd(t["x"], t["dt"], t["A"], t["B"], t["C"], ref, gss=ref_gss, **kw)
+    out = torch.full_like(ref, float("nan"))
+    gss = torch.full_like(ref_gss, float("nan"))
+    lib.ssd_noalloc(t["x"], t["dt"], t["A"], t["B"], t["C"], out, gss=gss, **kw)
+    torch.cuda.synchronize(ref.device)
+    return (ref, ref_gss), (out, gss)
 
 
-@pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 1e-2), (torch.float32, 1e-5)])
-def test_noalloc_matches_th_ssd_on_two_calls(dtype, tol):
-    lib, fn = _noalloc_fn()
-    b, s, h, p, g, n, chunk = 2, 640, 8, 64, 1, 128, 256
-    code = lib.TH_BF16 if dtype == torch.bfloat16 else lib.TH_F32
-    for call in range(2):
+# (b, s, h, p, g, n, chunk): the chunk-256 tcgen05 path at every state size
+# (128: serial chunk walk; 64 and 256: chunk-parallel states + state pass),
+# the mma.sync path (head_dim 32, chunk 128) and, in fp32, the SIMT path
+SHAPES = {
+    "tc_state128": (2, 640, 8, 64, 1, 128, 256),
+    "tc_state64": (2, 640, 8, 64, 1, 64, 256),
+    "tc_state256": (1, 700, 4, 64, 1, 256, 256),
+    "mma_hd32_chunk128": (2, 384, 6, 32, 2, 64, 128),
+}
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.bfloat16, 1e-2), (torch.float16, 1e-2), (torch.float32, 1e-5)],
+                         ids=["bf16", "fp16", "fp32"])
+@pytest.mark.parametrize("shape", list(SHAPES), ids=list(SHAPES))
+def test_noalloc_matches_th_ssd_on_two_calls(shape, dtype, tol):
+    lib = _lib()
+    b, s, h, p, g, n, chunk = SHAPES[shape]
+    for call in range(2):  # the scratch keeps the first call's contents when the second runs
         t = _inputs(b, s, h, p, g, n, dtype, seed=100 + call)
-        ref = torch.empty_like(t["x"])
-        ref_gss = torch.empty(b * s, h, device=ref.device)
-        lib.ssd(t["x"], t["dt"], t["A"], t["B"], t["C"], ref, batch=b, seq=s, heads=h, head_dim=p, ngroups=g,
-                state_dim=n, chunk=chunk, D=t["D"], z=t["z"], gss=ref_gss)
-        out = torch.full_like(ref, float("nan"))
-        gss = torch.full_like(ref_gss, float("nan"))
-        a = _args(lib, t, out, gss, b, s, h, p, g, n, chunk, code)
-        rc = fn(ctypes.byref(a), torch.cuda.current_stream().cuda_stream)
-        assert rc == 0, lib.load().th_last_error_string().decode()
-        torch.cuda.synchronize()
+        (ref, ref_gss), (out, gss) = _both(lib, t, b, s, h, p, g, n, chunk)
         assert rel_l2(out.float(), ref.float()) <= tol
         assert rel_l2(gss, ref_gss) <= 1e-5
     assert lib.device_error() == 0
 
 
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_noalloc_on_a_second_device():
+    """Each GPU that loads the library has its own copy of the scratch array;
+    a call on cuda:1 after cuda:0 (one process) uses cuda:1's copy."""
+    lib = _lib()
+    b, s, h, p, g, n, chunk = SHAPES["tc_state128"]
+    for dev in ("cuda:0", "cuda:1", "cuda:0"):
+        with torch.cuda.device(dev):
+            t = _inputs(b, s, h, p, g, n, torch.bfloat16, seed=7, device=dev)
+            (ref, ref_gss), (out, gss) = _both(lib, t, b, s, h, p, g, n, chunk)
+            assert rel_l2(out.float(), ref.float()) <= 1e-2
+            assert lib.device_error() == 0
+
+
 def test_noalloc_rejects_shapes_beyond_its_scratch():
-    lib, fn = _noalloc_fn()
+    from torch_helion.b200 import lib
+
     b, s, h, p, g, n, chunk = 8, 4096, 64, 64, 1, 128, 256  # needs far more than the built-in scratch
     need = lib.ssd_workspace_size(b, s, h, p, n, chunk)
-    t = {k: torch.empty(1, 1, device="cuda:0") for k in ("x", "B", "C", "z", "dt", "A", "D")}
-    out = torch.empty(1, 1, device="cuda:0")
-    gss = torch.empty(1, 64, device="cuda:0")
-    a = _args(lib, t, out, gss, b, s, h, p, g, n, chunk, lib.TH_BF16)
-    rc = fn(ctypes.byref(a), torch.cuda.current_stream().cuda_stream)
-    msg = lib.load().th_last_error_string().decode()
     assert need > (32 << 20)
-    assert rc == -1 and "scratch" in msg and str(32 << 20) in msg
+    t = {k: torch.empty(1, 1, device="cuda:0") for k in ("x", "B", "C", "z")}
+    with pytest.raises(lib.B200KernelError) as e:
+        lib.ssd_noalloc(t["x"].bfloat16(), torch.empty(1, 1, device="cuda:0"), torch.empty(64, device="cuda:0"),
+                        t["B"].bfloat16(), t["C"].bfloat16(), torch.empty(1, 1, device="cuda:0").bfloat16(),
+                        batch=b, seq=s, heads=h, head_dim=p, ngroups=g, state_dim=n, chunk=chunk)
+    msg = str(e.value)
+    assert "status -1" in msg and "scratch" in msg and str(32 << 20) in msg

@@ -3,13 +3,19 @@
     python torch-helion_b200/build.py [--force] [--verbose]
 
 The library is compiled in-tree with nvcc from ``csrc/th_b200.cu`` (a unity
-translation unit) so it travels with the repository snapshot.  It is rebuilt
-only when a source under ``csrc/`` or ``include/`` is newer than the .so.
+translation unit) so it travels with the repository snapshot.  Beside it,
+``libth_b200.so.sha256`` records a SHA-256 digest of every source under
+``csrc/`` and ``include/`` plus the nvcc flags it was built from.  It is
+rebuilt whenever that digest differs from the current sources' (file
+contents, not modification times), and the loader refuses a library whose
+digest does not match, so a binary in the tree is provably built from the
+sources beside it.
 """
 
 from __future__ import annotations
 
 import argparse
+import hashlib
 import os
 import shutil
 import subprocess
@@ -35,12 +41,25 @@ def _nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
+SHA = LIB.with_name(LIB.name + ".sha256")
+
+
+def source_digest() -> str:
+    """SHA-256 over the sources (path and contents, sorted) and the nvcc flags."""
+    h = hashlib.sha256()
+    srcs = sorted(list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h")))
+    for f in srcs:
+        h.update(f.name.encode() + b"\0" + f.read_bytes() + b"\0")
+    h.update(" ".join(NVCC_FLAGS).encode())
+    return h.hexdigest()
+
+
+def built_digest() -> str | None:
+    return SHA.read_text().strip() if SHA.exists() and LIB.exists() else None
+
+
 def _stale() -> bool:
-    if not LIB.exists():
-        return True
-    t = LIB.stat().st_mtime
-    srcs = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
-    return any(s.stat().st_mtime > t for s in srcs)
+    return built_digest() != source_digest()
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
@@ -56,6 +75,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if verbose:
         sys.stderr.write(res.stderr)
     tmp.replace(LIB)
+    SHA.write_text(source_digest() + "\n")
     return LIB
 
 

@@ -99,11 +99,7 @@ __global__ void __launch_bounds__(256) attention_simt_kernel(th_attention_args p
 template <typename T, int D>
 static int launch_attention(const th_attention_args* a, cudaStream_t st) {
   const size_t smem = sizeof(float) * (AT_BQ * (D + 1) + AT_BK * (D + 1) + AT_BK * D + AT_BQ * (AT_BK + 1));
-  static bool attr_set = false;  // once per instantiation (keeps it out of CUDA-graph captures)
-  if (!attr_set) {
-    cudaFuncSetAttribute(attention_simt_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_set = true;
-  }
+  if (int rc = smem_limit(attention_simt_kernel<T, D>, smem, "th_attention")) return rc;
   dim3 grid((unsigned)((a->seq + AT_BQ - 1) / AT_BQ), (unsigned)a->hq, (unsigned)a->batch);
   attention_simt_kernel<T, D><<<grid, 256, smem, st>>>(*a);
   return check_launch("th_attention");

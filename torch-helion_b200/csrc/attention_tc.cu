@@ -328,12 +328,10 @@ static int attention_tc_try(const th_attention_args* a, cudaStream_t st, int* rc
   if (r) { *rc = r; return 0; }
   dim3 grid((unsigned)((a->seq + 127) / 128), (unsigned)a->hq, (unsigned)a->batch);
   if (D == 128) {
-    static bool set = false;
-    if (!set) { cudaFuncSetAttribute(attention_tc_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, AtCfg<128>::SMEM); set = true; }
+    if ((*rc = smem_limit(attention_tc_kernel<T, 128>, AtCfg<128>::SMEM, "th_attention(tcgen05)"))) return 0;
     launch_pdl(attention_tc_kernel<T, 128>, grid, dim3(320), AtCfg<128>::SMEM, st, tq, tk, tv, *a);
   } else {
-    static bool set = false;
-    if (!set) { cudaFuncSetAttribute(attention_tc_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, AtCfg<64>::SMEM); set = true; }
+    if ((*rc = smem_limit(attention_tc_kernel<T, 64>, AtCfg<64>::SMEM, "th_attention(tcgen05)"))) return 0;
     launch_pdl(attention_tc_kernel<T, 64>, grid, dim3(320), AtCfg<64>::SMEM, st, tq, tk, tv, *a);
   }
   *rc = check_launch("th_attention(tcgen05)");

@@ -6,6 +6,8 @@
 
 #include <string.h>
 
+#include <atomic>
+#include <functional>
 #include <mutex>
 #include <unordered_map>
 
@@ -151,15 +153,52 @@ bool pdl_enabled() {
   return on;
 }
 
+constexpr int kMaxDevices = 64;
+
 int sm_count() {
-  static int cached = 0;  // every GPU of a node is the same part
-  if (cached == 0) {
-    int dev = 0, n = 0;
-    cudaGetDevice(&dev);
+  static std::atomic<int> cached[kMaxDevices];  // zero-initialised (static storage)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) dev = 0;
+  if (dev >= kMaxDevices) {
+    int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached = n > 0 ? n : 148;
+    return n > 0 ? n : 148;
   }
-  return cached;
+  int v = cached[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    v = n > 0 ? n : 148;
+    cached[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
+struct SmemKey {
+  const void* fn;
+  int dev;
+  bool operator==(const SmemKey& o) const { return fn == o.fn && dev == o.dev; }
+};
+struct SmemKeyHash {
+  size_t operator()(const SmemKey& k) const {
+    return std::hash<const void*>()(k.fn) ^ (static_cast<size_t>(k.dev) * 0x9e3779b97f4a7c15ull);
+  }
+};
+static std::mutex g_smem_mu;
+static std::unordered_map<SmemKey, size_t, SmemKeyHash> g_smem_set;
+
+int smem_limit_raw(const void* kernel, size_t bytes, const char* what) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(TH_ELAUNCH, "%s: cudaGetDevice: %s", what, cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(g_smem_mu);
+  size_t& have = g_smem_set[SmemKey{kernel, dev}];
+  if (have >= bytes) return TH_OK;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess)
+    return fail(TH_ELAUNCH, "%s: raising the shared-memory limit to %zu B: %s", what, bytes, cudaGetErrorString(e));
+  have = bytes;
+  return TH_OK;
 }
 
 }  // namespace th

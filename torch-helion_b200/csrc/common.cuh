@@ -206,20 +206,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait for the phase with `parity` to complete.  Returns false (and
-// sets the device error word and *abort) when the limit is hit or another
-// role already gave up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// sets the device error word and *abort) when `limit_ns` of %globaltimer
+// pass first or another role already gave up.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                              unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   unsigned long long t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *abort = 1;
       atomicOr(&g_device_error, TH_DEVERR_MBAR_TIMEOUT);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  return mbar_wait_for(bar, parity, abort, kWaitLimitNs);
 }
 
 // 2-D / 3-D TMA tile loads into shared memory, completion via mbarrier tx count.
@@ -516,8 +520,18 @@ int make_tmap_3d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, 
                  bool swizzle128 = true);
 inline int elem_bytes(int dtype) { return dtype == TH_F32 ? 4 : 2; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-int sm_count();
+int sm_count();  // SMs of the current device (cached per device ordinal)
 bool pdl_enabled();  // TH_PDL=0 in the environment turns programmatic dependent launch off
+
+// Raise `kernel`'s dynamic shared-memory limit to at least `bytes` on the
+// CURRENT device.  cudaFuncSetAttribute acts on one device, so the limit is
+// tracked per (kernel, device ordinal): a process that drives several GPUs
+// sets it on each of them, and concurrent first calls are serialised.
+int smem_limit_raw(const void* kernel, size_t bytes, const char* what);
+template <typename... KArgs>
+inline int smem_limit(void (*kernel)(KArgs...), size_t bytes, const char* what) {
+  return smem_limit_raw(reinterpret_cast<const void*>(kernel), bytes, what);
+}
 
 // Launch `kern` on `st` with programmatic stream serialisation: only for
 // kernels that call pdl_wait() before their first access to global memory.

@@ -750,11 +750,7 @@ static int launch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st
   if (rc) return rc;
   rc = make_tmap_2d(&tb, a->w, a->dtype, (uint64_t)a->k, (uint64_t)a->n, (uint64_t)a->ldw * 2, 64, BN, true);
   if (rc) return rc;
-  static bool attr_set = false;  // once per instantiation (keeps it out of CUDA-graph captures)
-  if (!attr_set) {
-    cudaFuncSetAttribute(gemm_tc_kernel<T, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    attr_set = true;
-  }
+  if ((rc = smem_limit(gemm_tc_kernel<T, BN, EPI>, C::SMEM_BYTES, "th_gemm(tcgen05)"))) return rc;
   const int tiles_m = (int)((a->m + C::BM - 1) / C::BM), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n;
   const int grid = ntiles < sm_count() ? ntiles : sm_count();
@@ -771,11 +767,7 @@ static int launch_tc2(const th_gemm_args* a, const EpiParams& ep, cudaStream_t s
   if (rc) return rc;
   rc = make_tmap_2d(&tb, a->w, a->dtype, (uint64_t)a->k, (uint64_t)a->n, (uint64_t)a->ldw * 2, 64, BN / 2, true);
   if (rc) return rc;
-  static bool attr_set = false;  // once per instantiation (keeps it out of CUDA-graph captures)
-  if (!attr_set) {
-    cudaFuncSetAttribute(gemm_tc2_kernel<T, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    attr_set = true;
-  }
+  if ((rc = smem_limit(gemm_tc2_kernel<T, BN, EPI>, C::SMEM_BYTES, "th_gemm(tcgen05 pair)"))) return rc;
   const int tiles_m = (int)((a->m + 2 * C::BM - 1) / (2 * C::BM)), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n, pairs = sm_count() / 2;
   const int grid = 2 * (ntiles < pairs ? ntiles : pairs);

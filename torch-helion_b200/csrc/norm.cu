@@ -585,11 +585,7 @@ static int launch_conv_tma(const th_conv1d_args* a, cudaStream_t st) {
     rc = th::make_tmap_3d(&ty, a->y, a->dtype, (uint64_t)a->channels, S, (uint64_t)a->batch, (uint64_t)a->ldy * 2,
                           S * a->ldy * 2, th::CT_CH, th::CT_TOK, false);
   if (rc) return rc;
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(th::conv1d_tma<T, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
-    set = true;
-  }
+  if ((rc = th::smem_limit(th::conv1d_tma<T, W>, Cf::SMEM, "th_conv1d(tma)"))) return rc;
   const int ncb = (a->channels + th::CT_CH - 1) / th::CT_CH, nsb = (a->seq + th::CT_TOK - 1) / th::CT_TOK;
   const int ntiles = ncb * nsb * a->batch;
   // a multiple of ncb blocks (each block keeps one channel block and its weights), two per SM

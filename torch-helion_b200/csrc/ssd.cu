@@ -14,8 +14,11 @@
 //      sum of squares that the gated RMSNorm consumes.
 // This file is the fp32 CUDA-core implementation (all dtypes); exponents
 // are always <= 0 inside a chunk, so nothing overflows at any length.
+#include <cudaTypedefs.h>
+
 #include <mutex>
 #include <type_traits>
+#include <unordered_map>
 
 #include "common.cuh"
 
@@ -280,9 +283,8 @@ static int ssd_launch(const th_ssd_args* a, const SsdGeom& g, cudaStream_t st) {
   }
   const size_t sm1 = sizeof(float) * (SSD_MAXL + 32 * g.hd + 32 * g.ns);
   const size_t sm3 = sizeof(float) * (SSD_RB * g.ns + 64 * g.ns + 64 * g.hd + SSD_RB * 65 + SSD_RB + 64 + 64);
-  static size_t set1 = 0, set3 = 0;  // raise the limit only when a larger one is needed
-  if (sm1 > set1) { cudaFuncSetAttribute(ssd_state_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1); set1 = sm1; }
-  if (sm3 > set3) { cudaFuncSetAttribute(ssd_scan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm3); set3 = sm3; }
+  if (int rc = smem_limit(ssd_state_kernel<T>, sm1, "th_ssd(state)")) return rc;
+  if (int rc = smem_limit(ssd_scan_kernel<T>, sm3, "th_ssd(scan)")) return rc;
   ssd_state_kernel<T><<<dim3(g.nchunks, g.heads, g.batch), 256, sm1, st>>>(*a, g, states, cum);
   int rc = check_launch("th_ssd(state)");
   if (rc) return rc;
@@ -338,26 +340,56 @@ namespace th {
 
 static __device__ __align__(256) unsigned char g_ssd_noalloc_scratch[TH_SSD_NOALLOC_MAX_BYTES];
 
-// Device address of the scratch array, looked up once per device.  On the
-// host, the array's name is only a stand-in symbol (not a device address),
-// so the kernels are given the address cudaGetSymbolAddress returns.
+// Device address of the scratch array, looked up once per CUDA context.  On
+// the host, the array's name is only a stand-in symbol (not a device
+// address), so the kernels are given the address cudaGetSymbolAddress
+// returns with the caller's device current.  The cache is keyed by the
+// driver's context ID (unique for the life of the process), so a device
+// reset or a different context on the same device gets a fresh lookup.
 static std::mutex g_noalloc_mu;
-static void* g_noalloc_ptr[64] = {};
+static std::unordered_map<unsigned long long, void*> g_noalloc_ptr;
+static PFN_cuCtxGetCurrent_v4000 g_ctx_current = nullptr;
+static PFN_cuCtxGetId_v12000 g_ctx_id = nullptr;
+static std::once_flag g_ctx_once;
+
+static int current_context_id(unsigned long long* id) {
+  std::call_once(g_ctx_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(fn);
+  });
+  if (!g_ctx_current || !g_ctx_id) return fail(TH_ELAUNCH, "th_ssd_noalloc: driver context queries unavailable");
+  CUcontext ctx = nullptr;
+  if (g_ctx_current(&ctx) != CUDA_SUCCESS || !ctx) return fail(TH_ELAUNCH, "th_ssd_noalloc: no current CUDA context");
+  if (g_ctx_id(ctx, id) != CUDA_SUCCESS) return fail(TH_ELAUNCH, "th_ssd_noalloc: cuCtxGetId failed");
+  return TH_OK;
+}
 
 static int noalloc_scratch(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(TH_ELAUNCH, "th_ssd_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= 64) return fail(TH_EUNSUPPORTED, "th_ssd_noalloc: device ordinal %d >= 64", dev);
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_ssd_noalloc_scratch);  // with `dev` current
-    if (e != cudaSuccess || !p)
-      return fail(TH_ELAUNCH, "th_ssd_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = p;
+  unsigned long long id = 0;
+  void* p = nullptr;
+  if (current_context_id(&id) == TH_OK) {
+    auto it = g_noalloc_ptr.find(id);
+    if (it != g_noalloc_ptr.end()) {
+      *out = it->second;
+      return TH_OK;
+    }
   }
-  *out = g_noalloc_ptr[dev];
+  // first call in this context (this also makes the runtime's primary context current when none is)
+  cudaError_t e = cudaGetSymbolAddress(&p, g_ssd_noalloc_scratch);
+  if (e != cudaSuccess || !p)
+    return fail(TH_ELAUNCH, "th_ssd_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+  int rc = current_context_id(&id);
+  if (rc) return rc;
+  g_noalloc_ptr[id] = p;
+  *out = p;
   return TH_OK;
 }
 

@@ -843,13 +843,9 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
 }
 
 template <typename T, int NS>
-static void ssd_scan_launch(const ScMaps& m, const th_ssd_args* a, int nc, cudaStream_t st) {
+static int ssd_scan_launch(const ScMaps& m, const th_ssd_args* a, int nc, cudaStream_t st) {
   using Cf = ScCfg<NS>;
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(ssd_scan_mh<T, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
-    set = true;
-  }
+  if (int rc = smem_limit(ssd_scan_mh<T, NS>, Cf::SMEM, "th_ssd(scan, tcgen05 multi-head)")) return rc;
   // head sets: about one CTA per SM
   const int hpg = a->heads / a->ngroups;
   const int per = a->batch * nc * a->ngroups;
@@ -860,6 +856,7 @@ static void ssd_scan_launch(const ScMaps& m, const th_ssd_args* a, int nc, cudaS
   const int units = per * nsets;
   launch_pdl(ssd_scan_mh<T, NS>, dim3(units), dim3(64 + SC_MATH), Cf::SMEM, st, m, *a, nc, hs, nsets,
              reinterpret_cast<const float*>(a->workspace));
+  return TH_OK;
 }
 
 // Applies to 2-byte dtypes with head_dim 64, state_dim 64, 128 or 256, chunk
@@ -897,12 +894,8 @@ static int ssd_chunk_try(const th_ssd_args* a, cudaStream_t st, int* rc) {
   if (!r)
     r = make_tmap_3d(&tdt, a->dt, TH_F32, (uint64_t)a->heads, S, Bt, a->lddt * 4, S * a->lddt * 4, 4, 256, false);
   if (r) { *rc = r; return 0; }
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(ssd_state_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, StC::SMEM);
-    cudaFuncSetAttribute(ssd_chunk_states<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SpC::SMEM);
-    set = true;
-  }
+  if ((*rc = smem_limit(ssd_state_tc<T>, StC::SMEM, "th_ssd(chunk states, tcgen05)"))) return 0;
+  if ((*rc = smem_limit(ssd_chunk_states<T>, SpC::SMEM, "th_ssd(chunk states, parallel)"))) return 0;
   static const bool serial128 = [] {  // TH_SSD_STATES=p selects the parallel states for d_state 128 too
     const char* e = getenv("TH_SSD_STATES");
     return !(e && e[0] == 'p');
@@ -926,10 +919,10 @@ static int ssd_chunk_try(const th_ssd_args* a, cudaStream_t st, int* rc) {
       if (*rc) return 0;
     }
   }
-  if (NS == 64) ssd_scan_launch<T, 64>(m, a, nc, st);
-  else if (NS == 128) ssd_scan_launch<T, 128>(m, a, nc, st);
-  else ssd_scan_launch<T, 256>(m, a, nc, st);
-  *rc = check_launch("th_ssd(scan, tcgen05 multi-head)");
+  r = NS == 64 ? ssd_scan_launch<T, 64>(m, a, nc, st)
+      : NS == 128 ? ssd_scan_launch<T, 128>(m, a, nc, st)
+                  : ssd_scan_launch<T, 256>(m, a, nc, st);
+  *rc = r ? r : check_launch("th_ssd(scan, tcgen05 multi-head)");
   return 0;
 }
 

@@ -406,9 +406,8 @@ template <typename T, int P>
 static int ssd_mma_launch(const th_ssd_args* a, const MmaGeom& g, float* states, float* cum, cudaStream_t st) {
   const size_t sm1 = sizeof(float) * MS_L + sizeof(T) * (MS_LH * (P + 8) + MS_LH * (MS_NS + 8));
   const size_t sm3 = sizeof(T) * (3 * MS_RB * (g.ns + 8) + 2 * MS_RB * (P + 8)) + sizeof(float) * (P * (g.ns + 4) + 5 * MS_RB);
-  static size_t set1 = 0, set3 = 0;
-  if (sm1 > set1) { cudaFuncSetAttribute(ssd_state_mma<T, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1); set1 = sm1; }
-  if (sm3 > set3) { cudaFuncSetAttribute(ssd_scan_mma<T, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm3); set3 = sm3; }
+  if (int rc = smem_limit(ssd_state_mma<T, P>, sm1, "th_ssd(state, mma)")) return rc;
+  if (int rc = smem_limit(ssd_scan_mma<T, P>, sm3, "th_ssd(scan, mma)")) return rc;
   ssd_state_mma<T, P><<<dim3(g.nchunks, g.heads, g.batch * g.nsplit), 256, sm1, st>>>(*a, g, states, cum);
   int rc = check_launch("th_ssd(state, mma)");
   if (rc) return rc;

@@ -283,13 +283,11 @@ static int ssd_scan_tc_try(const th_ssd_args* a, int nchunks, const float* state
   dim3 grid((unsigned)nchunks, (unsigned)a->heads, (unsigned)a->batch);
   if (a->state_dim == 128) {
     using Cf = TsCfg<128>;
-    static bool set = false;
-    if (!set) { cudaFuncSetAttribute(ssd_scan_tc<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM); set = true; }
+    if ((*rc = smem_limit(ssd_scan_tc<T, 128>, Cf::SMEM, "th_ssd(scan, tcgen05)"))) return 0;
     ssd_scan_tc<T, 128><<<grid, 256, Cf::SMEM, st>>>(tc_, tb_, tx_, *a, nchunks, states, cum);
   } else {
     using Cf = TsCfg<64>;
-    static bool set = false;
-    if (!set) { cudaFuncSetAttribute(ssd_scan_tc<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM); set = true; }
+    if ((*rc = smem_limit(ssd_scan_tc<T, 64>, Cf::SMEM, "th_ssd(scan, tcgen05)"))) return 0;
     ssd_scan_tc<T, 64><<<grid, 256, Cf::SMEM, st>>>(tc_, tb_, tx_, *a, nchunks, states, cum);
   }
   *rc = check_launch("th_ssd(scan, tcgen05)");

@@ -5,3 +5,4 @@
 #include "gemm.cu"
 #include "attention.cu"
 #include "ssd.cu"
+#include "selftest.cu"

@@ -24,7 +24,8 @@ _DTYPES = {torch.float32: TH_F32, torch.bfloat16: TH_BF16, torch.float16: TH_F16
 
 EXPORTED_SYMBOLS = (
     "th_last_error_string", "th_version", "th_device_error", "th_rowstat", "th_rmsnorm", "th_gemm",
-    "th_attention", "th_conv1d", "th_ssd_workspace_size", "th_ssd", "th_embedding",
+    "th_attention", "th_conv1d", "th_ssd_workspace_size", "th_ssd", "th_embedding", "th_ssd_noalloc",
+    "th_selftest_bounded_wait",
 )
 
 
@@ -87,12 +88,31 @@ class EmbeddingArgs(ctypes.Structure):
 _LIB: ctypes.CDLL | None = None
 
 
+def _check_built_from_sources() -> None:
+    """Refuse a library whose recorded source digest is not the digest of the
+    sources beside it (torch-helion_b200/build.py writes it at build time)."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_th_build", LIB_PATH.parents[1] / "build.py")
+    if spec is None or spec.loader is None:
+        return  # an installed copy without its build script: nothing to compare
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    if not (mod.CSRC.exists()):
+        return
+    have, want = mod.built_digest(), mod.source_digest()
+    if have != want:
+        raise B200KernelError(f"{LIB_PATH} was not built from the current sources (digest {have} != {want}): "
+                              "rebuild with `python torch-helion_b200/build.py`")
+
+
 def load() -> ctypes.CDLL:
     """Load the shared library once (raises if it has not been built)."""
     global _LIB
     if _LIB is None:
         if not LIB_PATH.exists():
             raise B200KernelError(f"{LIB_PATH} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'`")
+        _check_built_from_sources()
         lib = ctypes.CDLL(str(LIB_PATH))
         lib.th_last_error_string.restype = ctypes.c_char_p
         lib.th_version.restype = ctypes.c_char_p
@@ -100,12 +120,14 @@ def load() -> ctypes.CDLL:
         lib.th_ssd_workspace_size.argtypes = [_i32] * 6
         for name, st in (("th_rowstat", RowstatArgs), ("th_rmsnorm", RmsnormArgs), ("th_gemm", GemmArgs),
                          ("th_attention", AttentionArgs), ("th_conv1d", Conv1dArgs), ("th_ssd", SsdArgs),
-                         ("th_embedding", EmbeddingArgs)):
+                         ("th_ssd_noalloc", SsdArgs), ("th_embedding", EmbeddingArgs)):
             fn = getattr(lib, name)
             fn.restype = ctypes.c_int
             fn.argtypes = [ctypes.POINTER(st), _vp]
         lib.th_device_error.restype = ctypes.c_int
         lib.th_device_error.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_int]
+        lib.th_selftest_bounded_wait.restype = ctypes.c_int
+        lib.th_selftest_bounded_wait.argtypes = [_i64, _i64, _vp, _vp]
         _LIB = lib
     return _LIB
 
@@ -241,16 +263,10 @@ def ssd_workspace_size(batch: int, seq: int, heads: int, head_dim: int, state_di
     return int(load().th_ssd_workspace_size(batch, seq, heads, head_dim, state_dim, chunk))
 
 
-def ssd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, out: torch.Tensor, *,
-        batch: int, seq: int, heads: int, head_dim: int, ngroups: int, state_dim: int, chunk: int = 256,
-        D: torch.Tensor | None = None, z: torch.Tensor | None = None, gss: torch.Tensor | None = None,
-        workspace: torch.Tensor | None = None) -> torch.Tensor:
-    need = ssd_workspace_size(batch, seq, heads, head_dim, state_dim, chunk)
-    if workspace is None:
-        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+def _ssd_args(x, dt, A, B, C, out, batch, seq, heads, head_dim, ngroups, state_dim, chunk, D, z, gss) -> SsdArgs:
     if dt.dtype != torch.float32 or A.dtype != torch.float32 or (D is not None and D.dtype != torch.float32):
         raise B200KernelError("ssd: dt, A and D must be fp32")
-    _cuda(x, dt, A, B, C, out, D, z, gss, workspace)
+    _cuda(x, dt, A, B, C, out, D, z, gss)
     a = SsdArgs()
     a.x, a.ldx = x.data_ptr(), _rows(x)[2]
     a.dt, a.lddt = dt.data_ptr(), _rows(dt)[2]
@@ -265,9 +281,44 @@ def ssd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C: 
         a.gss, a.ldgss = gss.data_ptr(), _rows(gss)[2]
     a.batch, a.seq, a.heads, a.head_dim, a.ngroups, a.state_dim, a.chunk = batch, seq, heads, head_dim, ngroups, state_dim, chunk
     a.dtype = _dt(x)
+    return a
+
+
+def ssd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, out: torch.Tensor, *,
+        batch: int, seq: int, heads: int, head_dim: int, ngroups: int, state_dim: int, chunk: int = 256,
+        D: torch.Tensor | None = None, z: torch.Tensor | None = None, gss: torch.Tensor | None = None,
+        workspace: torch.Tensor | None = None) -> torch.Tensor:
+    need = ssd_workspace_size(batch, seq, heads, head_dim, state_dim, chunk)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    _cuda(workspace)
+    a = _ssd_args(x, dt, A, B, C, out, batch, seq, heads, head_dim, ngroups, state_dim, chunk, D, z, gss)
     a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     _check(load().th_ssd(ctypes.byref(a), _stream()), "th_ssd")
     return out
+
+
+def ssd_noalloc(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C: torch.Tensor,
+                out: torch.Tensor, *, batch: int, seq: int, heads: int, head_dim: int, ngroups: int, state_dim: int,
+                chunk: int = 256, D: torch.Tensor | None = None, z: torch.Tensor | None = None,
+                gss: torch.Tensor | None = None) -> torch.Tensor:
+    """th_ssd_noalloc: the same scan with the library's built-in scratch
+    array instead of a caller workspace (no allocation on either side)."""
+    a = _ssd_args(x, dt, A, B, C, out, batch, seq, heads, head_dim, ngroups, state_dim, chunk, D, z, gss)
+    a.workspace, a.workspace_bytes = None, 0
+    _check(load().th_ssd_noalloc(ctypes.byref(a), _stream()), "th_ssd_noalloc")
+    return out
+
+
+def selftest_bounded_wait(limit_ns: int, arrive_ns: int, completed: torch.Tensor) -> None:
+    """Launch the bounded-wait self-test (see th_selftest_bounded_wait):
+    ``completed`` (int32, one element, on the device) becomes 1 when the
+    late arrival was seen within ``limit_ns``, else 0 with the device error
+    word set."""
+    if completed.dtype != torch.int32 or not completed.is_cuda:
+        raise B200KernelError("selftest_bounded_wait: completed must be an int32 CUDA tensor")
+    _check(load().th_selftest_bounded_wait(int(limit_ns), int(arrive_ns), completed.data_ptr(), _stream()),
+           "th_selftest_bounded_wait")
 
 
 def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor) -> torch.Tensor:

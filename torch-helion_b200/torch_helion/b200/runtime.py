@@ -489,6 +489,94 @@ class StreamingRunner:
         return self.slots[0].n_launches
 
 
+class ShardedStreamingRunner:
+    """Serve a stream of batches on a tensor-parallel group (one process per
+    GPU) with the host I/O sharded by rows.
+
+    Every rank owns rows ``[rank*T/world, (rank+1)*T/world)`` of each batch
+    (T = batch * seq tokens): it copies only those rows in from pinned host
+    memory, the ranks all-gather the rows over NVLink (NCCL) into the
+    program's input, every rank runs its head/column shard of the forward
+    (with its all-reduces), and each rank copies only its own rows of the
+    (replicated) output back.  The host link carries 1/world of the batch per
+    GPU instead of all of it.
+
+    Two device staging slots rotate over three streams: the copy-in of batch
+    i+1 and the copy-out of batch i-1 run while batch i computes; events order
+    every reuse of a slot."""
+
+    def __init__(self, module: "CompiledProgram", depth: int = 2) -> None:
+        import torch.distributed as dist
+
+        if module.tp_world <= 1:
+            raise ValueError("ShardedStreamingRunner needs a tensor-parallel module (world_size > 1)")
+        if len(module.program.inputs) != 1 or len(module.outputs) != 1:
+            raise ValueError("ShardedStreamingRunner serves programs with one input and one output")
+        self.m, self.dist = module, dist
+        self.rank, self.world = module.tp_rank, module.tp_world
+        self.device = module.device
+        xin = module.views[module.program.inputs[0]]
+        yout = module.views[module.outputs[0]]
+        T = xin.shape[0]
+        if T % self.world or not xin.is_contiguous() or yout.shape[0] != T:
+            raise ValueError(f"{T} rows do not split evenly over {self.world} ranks (or the input is strided)")
+        self.T, self.rows = T, T // self.world
+        self.r0 = self.rank * self.rows
+        self.xin, self.yout = xin, yout
+        with torch.cuda.device(self.device):
+            self.x_stage = [torch.empty((self.rows,) + tuple(xin.shape[1:]), dtype=xin.dtype, device=self.device)
+                            for _ in range(depth)]
+            self.y_stage = [torch.empty((self.rows,) + tuple(yout.shape[1:]), dtype=yout.dtype, device=self.device)
+                            for _ in range(depth)]
+            self.h2d, self.compute, self.d2h = (torch.cuda.Stream(self.device) for _ in range(3))
+            ev = lambda: [torch.cuda.Event() for _ in range(depth)]
+            self._loaded, self._gathered, self._computed, self._drained = ev(), ev(), ev(), ev()
+        self._used = [False] * depth
+
+    def input_rows(self, batch: torch.Tensor) -> torch.Tensor:
+        """This rank's rows of a full host batch (a view, no copy)."""
+        return batch.reshape(self.T, -1)[self.r0:self.r0 + self.rows]
+
+    def output_buffer(self, pin: bool = True) -> torch.Tensor:
+        """A host tensor for this rank's rows of one batch's output."""
+        return torch.empty(tuple(self.y_stage[0].shape), dtype=self.yout.dtype, pin_memory=pin)
+
+    def submit(self, i: int, rows_in: torch.Tensor, rows_out: torch.Tensor,
+               before_forward: Callable[[], None] | None = None) -> None:
+        """Enqueue batch ``i``: ``rows_in`` (host, this rank's rows) -> ``rows_out`` (host); returns at once.
+        Every rank must submit the same sequence of batches (the all-gather is collective)."""
+        k = i % len(self.x_stage)
+        with torch.cuda.device(self.device):
+            if self._used[k]:
+                self.h2d.wait_event(self._gathered[k])
+            with torch.cuda.stream(self.h2d):
+                self.x_stage[k].copy_(rows_in.reshape(self.x_stage[k].shape), non_blocking=True)
+                self._loaded[k].record(self.h2d)
+            self.compute.wait_event(self._loaded[k])
+            if self._used[k]:
+                self.compute.wait_event(self._drained[k])
+            with torch.cuda.stream(self.compute):
+                self.dist.all_gather_into_tensor(self.xin.view(self.world, *self.x_stage[k].shape), self.x_stage[k])
+                self._gathered[k].record(self.compute)
+                if before_forward is not None:
+                    before_forward()
+                self.m.launch_all()
+                self.y_stage[k].copy_(self.yout[self.r0:self.r0 + self.rows])
+                self._computed[k].record(self.compute)
+            self.d2h.wait_event(self._computed[k])
+            with torch.cuda.stream(self.d2h):
+                rows_out.copy_(self.y_stage[k].reshape(rows_out.shape), non_blocking=True)
+                self._drained[k].record(self.d2h)
+        self._used[k] = True
+
+    def synchronize(self) -> None:
+        self.d2h.synchronize()
+
+    @property
+    def n_launches(self) -> int:
+        return self.m.n_launches
+
+
 def run_program(program: Program, params: dict[str, torch.Tensor], inputs, device="cuda") -> dict[str, torch.Tensor]:
     """Reference-shaped entry (interpret.py:54-65): run all kernels, return
     the produced tensors by name (device tensors)."""
@@ -506,4 +594,4 @@ def program_outputs(program: Program, params: dict[str, torch.Tensor], inputs, d
     return [o.clone() for o in cp(*inputs)]
 
 
-__all__ = ["CompiledProgram", "KernelLaunch", "StreamingRunner", "run_program", "program_outputs", "math"]
+__all__ = ["CompiledProgram", "KernelLaunch", "StreamingRunner", "ShardedStreamingRunner", "run_program", "program_outputs", "math"]

@@ -74,13 +74,18 @@ class CompileResult:
         return self.module(*inputs)
 
     def streaming_runner(self, depth: int = 2, cuda_graph: bool | None = None):
-        """A :class:`~torch_helion.b200.runtime.StreamingRunner` over this
-        program: host batches in, host outputs out, copies overlapped with
-        the forward (single GPU)."""
-        from .b200.runtime import StreamingRunner
+        """Overlapped serving from pinned host memory.  One GPU: a
+        :class:`~torch_helion.b200.runtime.StreamingRunner` (host batches in,
+        host outputs out, copies overlapped with the forward).  Tensor
+        parallel (``world_size > 1``): a
+        :class:`~torch_helion.b200.runtime.ShardedStreamingRunner` on this
+        rank's module, each rank moving only its own rows over the host link."""
+        from .b200.runtime import ShardedStreamingRunner, StreamingRunner
 
         if self.config.world_size > 1:
-            raise ValueError("streaming_runner serves one GPU; run one runner per rank")
+            if self.module is None:
+                self.module = device_module(self.program, self.graph.params, self.config)
+            return ShardedStreamingRunner(self.module, depth=depth)
         cg = self.config.cuda_graph if cuda_graph is None else cuda_graph
         return StreamingRunner(self.program, self.graph.params, self.config.device, depth=depth, cuda_graph=cg)
 
