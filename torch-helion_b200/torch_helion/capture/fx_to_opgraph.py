@@ -1,12 +1,22 @@
 """Core-ATen FX graph -> raw OpGraph.
 
-A literal translation, as in the reference (src/torch_helion/capture/
-fx_to_opgraph.py:80-121): one OpGraph node per ATen node with the same
-shape, layout ops kept as ``layout`` nodes, parameters/buffers/lifted
-constants emitted with their values, and every semantic rewrite left to the
-optimizer.  Handlers added for the B200 workloads: ``constant_pad_nd``,
-``convolution`` (Mamba's depthwise causal conv) and ``embedding``.
-Unsupported ops raise :class:`UnsupportedOpError`.
+The raw graph is a literal image of the exported program, as the reference
+specifies it (src/torch_helion/capture/fx_to_opgraph.py:80-121): one OpGraph
+node per ATen call with the call's static shape, layout calls kept as
+``layout`` nodes, parameters / buffers / lifted constants as value nodes
+carrying their tensors, and every semantic rewrite left to the optimizer.
+Anything without a mapping raises :class:`UnsupportedOpError` (the
+reference's behaviour for unknown ops, fx_to_opgraph.py:107-109).
+
+How it is organised here: the graph signature's input specs bind the
+placeholders; every ``call_function`` is looked up by its overload name
+("add.Tensor", "mean.dim", ...) in one of three tables -- elementwise ops
+(unary, or binary with an optional scalar operand), ops whose attributes are
+read by a small decoder, and expansions that emit more than one node
+(``addmm``, ``linear``) or none (``split_with_sizes``, resolved when its
+``getitem`` users are met).  Beyond the reference's op set it maps
+``constant_pad_nd``, ``convolution`` (Mamba's depthwise causal conv),
+``embedding``, ``erf`` and ``gelu``.
 """
 
 from __future__ import annotations
@@ -14,6 +24,7 @@ from __future__ import annotations
 from typing import Any, Callable
 
 import torch
+from torch.export.graph_signature import InputKind
 from torch.fx import Node
 
 from .fx_capture import CapturedFx
@@ -24,294 +35,320 @@ class UnsupportedOpError(NotImplementedError):
     """An ATen op has no OpGraph mapping."""
 
 
-_HANDLERS: dict[str, Callable[["_Converter", Node], OpNode]] = {}
+def _overload(target: Any) -> str:
+    """'aten.add.Tensor' -> 'add.Tensor'; the getitem builtin -> 'getitem'."""
+    text = str(target)
+    if text.startswith("aten."):
+        return text[len("aten."):]
+    return "getitem" if "getitem" in text else text
 
 
-def _on(*targets: str):
-    def deco(fn):
-        for t in targets:
-            _HANDLERS[t] = fn
-        return fn
-
-    return deco
-
-
-def _tt(node: Node) -> TensorType:
+def _type_of(node: Node) -> TensorType:
     val = node.meta.get("val")
     if not isinstance(val, torch.Tensor):
-        raise UnsupportedOpError(f"{node.name}: non-tensor value {type(val).__name__}")
-    return TensorType(tuple(int(s) for s in val.shape), str(val.dtype).replace("torch.", ""))
+        raise UnsupportedOpError(f"{node.name}: produces {type(val).__name__}, not a tensor")
+    return TensorType.of(val)
 
 
-def _dim(d: int, rank: int) -> int:
-    return d + rank if d < 0 else d
+def _axis(node: Node, axis: int) -> int:
+    """A possibly negative axis of ``node``'s value, made non-negative."""
+    rank = len(_type_of(node).shape)
+    return axis % rank if rank else 0
 
 
-class _Converter:
+def _arg(node: Node, pos: int, key: str, default: Any) -> Any:
+    if len(node.args) > pos and node.args[pos] is not None:
+        return node.args[pos]
+    return node.kwargs.get(key, default)
+
+
+# Elementwise ops: one OpGraph op per overload.
+_UNARY = {
+    "exp.default": "exp", "log.default": "log", "neg.default": "neg", "rsqrt.default": "rsqrt",
+    "sqrt.default": "sqrt", "sigmoid.default": "sigmoid", "silu.default": "silu", "tanh.default": "tanh",
+    "square.default": "square", "log1p.default": "log1p", "erf.default": "erf",
+}
+_BINARY = {
+    "add.Tensor": "add", "sub.Tensor": "sub", "mul.Tensor": "mul", "div.Tensor": "div", "maximum.default": "max",
+    "pow.Tensor_Tensor": "powf",
+}
+_REDUCTIONS = {"mean.dim": "row_mean", "sum.dim_IntList": "row_sum", "amax.default": "row_max"}
+_VIEWS = ("view.default", "reshape.default", "_unsafe_view.default", "unsqueeze.default", "squeeze.dim",
+          "squeeze.default", "squeeze.dims")
+_COPIES = ("clone.default", "contiguous.default", "alias.default", "detach.default")
+
+
+class _Lowering:
     def __init__(self, captured: CapturedFx) -> None:
         self.captured = captured
-        self.ep = captured.exported
-        self.gm = captured.graph_module
+        self.program = captured.exported
         self.graph = OpGraph("model")
-        self.names: dict[str, str] = {}
-        self.splits: dict[str, tuple[str, list[int], int]] = {}
+        self.value_of: dict[str, str] = {}                       # fx node -> OpGraph value
+        self.pending_splits: dict[str, tuple[str, list[int], int]] = {}
 
-    def src(self, arg: Any) -> str:
-        if isinstance(arg, Node):
-            return self.names[arg.name]
-        raise UnsupportedOpError(f"expected a tensor operand, got {arg!r}")
+    # ---------------------------------------------------------------- helpers
+    def operand(self, arg: Any) -> str:
+        if not isinstance(arg, Node):
+            raise UnsupportedOpError(f"expected a tensor operand, got {arg!r}")
+        return self.value_of[arg.name]
 
-    def emit(self, node: Node, op: str, inputs: list[str], attrs: dict | None = None, kind: str = "compute") -> OpNode:
-        out = self.graph.add(op, inputs, _tt(node), attrs=attrs, kind=kind, name=node.name, origin=str(node.target))
-        self.names[node.name] = out.name
+    def node(self, fx: Node, op: str, inputs: list[str], attrs: dict | None = None, kind: str = "compute") -> OpNode:
+        out = self.graph.add(op, inputs, _type_of(fx), attrs=attrs, kind=kind, name=fx.name, origin=str(fx.target))
+        self.value_of[fx.name] = out.name
         return out
 
-    def binary(self, node: Node, op: str) -> OpNode:
-        a, b = node.args[0], node.args[1]
-        if isinstance(a, Node) and isinstance(b, Node):
-            return self.emit(node, op, [self.src(a), self.src(b)])
-        if isinstance(a, Node):
-            return self.emit(node, op, [self.src(a)], {"scalar": float(b)})
-        return self.emit(node, op, [self.src(b)], {"scalar": float(a), "scalar_first": True})
+    def helper(self, fx: Node, suffix: str, op: str, inputs: list[str], t: TensorType, attrs: dict | None = None,
+               kind: str = "compute") -> OpNode:
+        """An extra node of a multi-node expansion (named after the FX node)."""
+        return self.graph.add(op, inputs, t, attrs=attrs, kind=kind, name=f"{fx.name}_{suffix}",
+                              origin=f"aten.{_overload(fx.target).split('.')[0]}")
 
-    def value_node(self, node: Node, kind: str, pname: str, value: torch.Tensor | None, t: TensorType) -> None:
-        name = pname.replace(".", "_")
-        val = value.detach().clone() if value is not None else None
-        out = self.graph.add(kind, [], t, kind=kind, name=name, origin=node.name, value=val)
-        self.names[node.name] = out.name
-
-    def run(self) -> OpGraph:
-        sig = self.ep.graph_signature
-        params = dict(self.ep.state_dict)
-        consts = getattr(self.ep, "constants", {}) or {}
-        lifted = getattr(sig, "inputs_to_lifted_tensor_constants", {}) or {}
-        for node in self.gm.graph.nodes:
-            if node.op == "placeholder":
-                t = _tt(node)
-                if node.name in sig.inputs_to_parameters:
-                    pn = sig.inputs_to_parameters[node.name]
-                    self.value_node(node, "param", pn, params[pn], t)
-                elif node.name in sig.inputs_to_buffers:
-                    bn = sig.inputs_to_buffers[node.name]
-                    self.value_node(node, "param", bn, params.get(bn, consts.get(bn)), t)
-                elif node.name in lifted:
-                    cn = lifted[node.name]
-                    self.value_node(node, "const", cn, consts[cn], t)
-                else:
-                    self.value_node(node, "input", node.name, None, t)
-            elif node.op == "call_function":
-                key = str(node.target)
-                if key == "aten.split_with_sizes.default":
-                    src = node.args[0]
-                    rank = len(_tt(src).shape)
-                    dim = _dim(int(node.args[2]) if len(node.args) > 2 else 0, rank)
-                    self.splits[node.name] = (self.src(src), [int(v) for v in node.args[1]], dim)
-                    continue
-                fn = _HANDLERS.get(key)
-                if fn is None:
-                    raise UnsupportedOpError(f"no OpGraph mapping for {key} (node {node.name})")
-                fn(self, node)
-            elif node.op == "output":
-                outs = node.args[0]
-                outs = outs if isinstance(outs, (tuple, list)) else (outs,)
-                self.graph.outputs = [self.src(o) for o in outs]
+    # ------------------------------------------------------------- placeholders
+    def bind_inputs(self) -> None:
+        ep = self.program
+        state, consts = dict(ep.state_dict), dict(getattr(ep, "constants", {}) or {})
+        placeholders = {n.name: n for n in ep.graph_module.graph.nodes if n.op == "placeholder"}
+        for spec in ep.graph_signature.input_specs:
+            fx = placeholders[spec.arg.name]
+            t = _type_of(fx)
+            if spec.kind == InputKind.USER_INPUT:
+                kind, label, value = "input", fx.name, None
+            elif spec.kind in (InputKind.PARAMETER, InputKind.BUFFER):
+                kind, label = "param", spec.target
+                value = state[label] if label in state else consts.get(label)
+            elif spec.kind == InputKind.CONSTANT_TENSOR:
+                kind, label, value = "const", spec.target, consts[spec.target]
             else:
-                raise UnsupportedOpError(f"unsupported fx node kind {node.op} ({node.target})")
+                raise UnsupportedOpError(f"placeholder {fx.name}: input kind {spec.kind} is not supported")
+            stored = None if value is None else value.detach().clone()
+            out = self.graph.add(kind, [], t, kind=kind, name=label.replace(".", "_"), origin=fx.name, value=stored)
+            self.value_of[fx.name] = out.name
+
+    # ------------------------------------------------------------------ calls
+    def lower(self, fx: Node) -> None:
+        key = _overload(fx.target)
+        if key in _UNARY:
+            self.node(fx, _UNARY[key], [self.operand(fx.args[0])])
+        elif key in _BINARY:
+            self.binary(fx, _BINARY[key])
+        elif key in _REDUCTIONS:
+            self.reduction(fx, _REDUCTIONS[key])
+        elif key in _VIEWS:
+            self.node(fx, "view", [self.operand(fx.args[0])], {"shape": list(_type_of(fx).shape)}, kind="layout")
+        elif key in _COPIES:
+            self.node(fx, "clone", [self.operand(fx.args[0])], kind="layout")
+        elif key in _DECODERS:
+            op, kind, decode = _DECODERS[key]
+            inputs, attrs = decode(self, fx)
+            self.node(fx, op, inputs, attrs, kind=kind)
+        elif key in _EXPANSIONS:
+            _EXPANSIONS[key](self, fx)
+        else:
+            raise UnsupportedOpError(f"no OpGraph mapping for aten.{key} (node {fx.name})")
+
+    def binary(self, fx: Node, op: str) -> None:
+        lhs, rhs = fx.args[0], fx.args[1]
+        tensors = [a for a in (lhs, rhs) if isinstance(a, Node)]
+        if len(tensors) == 2:
+            self.node(fx, op, [self.operand(lhs), self.operand(rhs)])
+        elif isinstance(lhs, Node):
+            self.node(fx, op, [self.operand(lhs)], {"scalar": float(rhs)})
+        else:  # scalar (op) tensor: the order matters for sub/div/pow
+            self.node(fx, op, [self.operand(rhs)], {"scalar": float(lhs), "scalar_first": True})
+
+    def reduction(self, fx: Node, op: str) -> None:
+        src = fx.args[0]
+        rank = len(_type_of(src).shape)
+        raw = _arg(fx, 1, "dim", None)
+        axes = sorted({(int(d) % rank) for d in ([raw] if isinstance(raw, int) else (raw or []))})
+        if axes != [rank - 1]:
+            raise UnsupportedOpError(f"{fx.name}: only last-axis reductions are supported (axes {axes})")
+        self.node(fx, op, [self.operand(src)], {"keepdim": bool(_arg(fx, 2, "keepdim", False))})
+
+    # ------------------------------------------------------------------ driver
+    def run(self) -> OpGraph:
+        self.bind_inputs()
+        for fx in self.program.graph_module.graph.nodes:
+            if fx.op == "placeholder":
+                continue
+            if fx.op == "call_function":
+                if _overload(fx.target) == "split_with_sizes.default":
+                    src = fx.args[0]
+                    axis = _axis(src, int(_arg(fx, 2, "dim", 0)))
+                    self.pending_splits[fx.name] = (self.operand(src), [int(v) for v in fx.args[1]], axis)
+                else:
+                    self.lower(fx)
+            elif fx.op == "output":
+                results = fx.args[0] if isinstance(fx.args[0], (tuple, list)) else (fx.args[0],)
+                self.graph.outputs = [self.operand(r) for r in results]
+            else:
+                raise UnsupportedOpError(f"unsupported fx node kind {fx.op} ({fx.target})")
         self.graph.metadata["fx_op_histogram"] = self.captured.op_histogram()
         return self.graph
 
 
-# ------------------------------------------------------------------ handlers
-for _t, _o in {"aten.add.Tensor": "add", "aten.sub.Tensor": "sub", "aten.mul.Tensor": "mul", "aten.div.Tensor": "div",
-               "aten.maximum.default": "max"}.items():
-    _HANDLERS[_t] = (lambda op: (lambda c, n: c.binary(n, op)))(_o)
+# ------------------------------------------------- decoders: (inputs, attrs)
+def _dec_pow_scalar(lw: _Lowering, fx: Node):
+    return [lw.operand(fx.args[0])], {"scalar": float(fx.args[1])}
 
 
-@_on("aten.pow.Tensor_Scalar")
-def _pow_s(c, n):
-    return c.emit(n, "powf", [c.src(n.args[0])], {"scalar": float(n.args[1])})
+def _dec_softmax(lw: _Lowering, fx: Node):
+    if _axis(fx.args[0], int(fx.args[1])) != len(_type_of(fx.args[0]).shape) - 1:
+        raise UnsupportedOpError(f"{fx.name}: softmax only over the last axis")
+    return [lw.operand(fx.args[0])], {}
 
 
-@_on("aten.pow.Tensor_Tensor")
-def _pow_t(c, n):
-    return c.emit(n, "powf", [c.src(n.args[0]), c.src(n.args[1])])
+def _dec_two(lw: _Lowering, fx: Node):
+    return [lw.operand(fx.args[0]), lw.operand(fx.args[1])], {}
 
 
-for _t, _o in {"aten.exp.default": "exp", "aten.log.default": "log", "aten.neg.default": "neg",
-               "aten.rsqrt.default": "rsqrt", "aten.sqrt.default": "sqrt", "aten.sigmoid.default": "sigmoid",
-               "aten.silu.default": "silu", "aten.tanh.default": "tanh", "aten.square.default": "square",
-               "aten.log1p.default": "log1p"}.items():
-    _HANDLERS[_t] = (lambda op: (lambda c, n: c.emit(n, op, [c.src(n.args[0])])))(_o)
+def _dec_permute(lw: _Lowering, fx: Node):
+    return [lw.operand(fx.args[0])], {"dims": [int(d) for d in fx.args[1]]}
 
 
-@_on("aten.mean.dim", "aten.sum.dim_IntList", "aten.amax.default")
-def _reduce(c, n):
-    x = n.args[0]
-    dims = n.args[1] if len(n.args) > 1 else None
-    keep = bool(n.args[2]) if len(n.args) > 2 else bool(n.kwargs.get("keepdim", False))
-    rank = len(_tt(x).shape)
-    dims = [dims] if isinstance(dims, int) else list(dims or [])
-    dims = [_dim(int(d), rank) for d in dims]
-    if dims != [rank - 1]:
-        raise UnsupportedOpError(f"{n.name}: only last-axis reductions are supported (dims={dims})")
-    op = {"aten.mean.dim": "row_mean", "aten.sum.dim_IntList": "row_sum", "aten.amax.default": "row_max"}[str(n.target)]
-    return c.emit(n, op, [c.src(x)], {"keepdim": keep})
+def _dec_transpose(lw: _Lowering, fx: Node):
+    src = fx.args[0]
+    order = list(range(len(_type_of(src).shape)))
+    a, b = _axis(src, int(fx.args[1])), _axis(src, int(fx.args[2]))
+    order[a], order[b] = order[b], order[a]
+    return [lw.operand(src)], {"dims": order}
 
 
-@_on("aten._softmax.default", "aten.softmax.int")
-def _softmax(c, n):
-    rank = len(_tt(n.args[0]).shape)
-    if _dim(int(n.args[1]), rank) != rank - 1:
-        raise UnsupportedOpError(f"{n.name}: softmax only over the last axis")
-    return c.emit(n, "softmax", [c.src(n.args[0])])
+def _dec_t(lw: _Lowering, fx: Node):
+    return [lw.operand(fx.args[0])], {"dims": [1, 0]}
 
 
-@_on("aten.mm.default")
-def _mm(c, n):
-    return c.emit(n, "matmul", [c.src(n.args[0]), c.src(n.args[1])])
+def _dec_expand(lw: _Lowering, fx: Node):
+    return [lw.operand(fx.args[0])], {"shape": list(_type_of(fx).shape)}
 
 
-@_on("aten.bmm.default")
-def _bmm(c, n):
-    return c.emit(n, "batch_matmul", [c.src(n.args[0]), c.src(n.args[1])])
+def _dec_cast(lw: _Lowering, fx: Node):
+    return [lw.operand(fx.args[0])], {"dtype": _type_of(fx).dtype}
 
 
-@_on("aten.addmm.default")
-def _addmm(c, n):
-    bias, a, b = n.args[:3]
-    mm = c.graph.add("matmul", [c.src(a), c.src(b)], _tt(n), name=n.name + "_mm", origin="aten.addmm")
-    return c.emit(n, "add", [mm.name, c.src(bias)])
+def _dec_slice(lw: _Lowering, fx: Node):
+    src = fx.args[0]
+    axis = _axis(src, int(_arg(fx, 1, "dim", 0)))
+    extent = _type_of(src).shape[axis]
+    if int(_arg(fx, 4, "step", 1)) != 1:
+        raise UnsupportedOpError(f"{fx.name}: strided slice")
+    lo, hi = int(_arg(fx, 2, "start", 0)), int(_arg(fx, 3, "end", extent))
+    lo, hi = (lo + extent if lo < 0 else lo), (hi + extent if hi < 0 else hi)
+    return [lw.operand(src)], {"dim": axis, "start": max(0, lo), "end": min(extent, hi)}
 
 
-@_on("aten.permute.default")
-def _permute(c, n):
-    return c.emit(n, "permute", [c.src(n.args[0])], {"dims": [int(d) for d in n.args[1]]}, kind="layout")
+def _dec_getitem(lw: _Lowering, fx: Node):
+    parent, index = fx.args[0], int(fx.args[1])
+    if not isinstance(parent, Node) or parent.name not in lw.pending_splits:
+        raise UnsupportedOpError(f"{fx.name}: getitem on something other than a tensor split")
+    base, sizes, axis = lw.pending_splits[parent.name]
+    lo = sum(sizes[:index])
+    return [base], {"dim": axis, "start": lo, "end": lo + sizes[index]}
 
 
-@_on("aten.transpose.int")
-def _transpose(c, n):
-    rank = len(_tt(n.args[0]).shape)
-    d0, d1 = _dim(int(n.args[1]), rank), _dim(int(n.args[2]), rank)
-    dims = list(range(rank))
-    dims[d0], dims[d1] = dims[d1], dims[d0]
-    return c.emit(n, "permute", [c.src(n.args[0])], {"dims": dims}, kind="layout")
+def _dec_cumsum(lw: _Lowering, fx: Node):
+    src = fx.args[0]
+    if _axis(src, int(_arg(fx, 1, "dim", -1))) != len(_type_of(src).shape) - 1:
+        raise UnsupportedOpError(f"{fx.name}: only last-axis cumsum")
+    return [lw.operand(src)], {}
 
 
-@_on("aten.t.default")
-def _t(c, n):
-    return c.emit(n, "permute", [c.src(n.args[0])], {"dims": [1, 0]}, kind="layout")
+def _dec_gt(lw: _Lowering, fx: Node):
+    return [lw.operand(fx.args[0])], {"scalar": float(fx.args[1])}
 
 
-@_on("aten.view.default", "aten.reshape.default", "aten._unsafe_view.default", "aten.unsqueeze.default",
-     "aten.squeeze.dim", "aten.squeeze.default", "aten.squeeze.dims")
-def _view(c, n):
-    return c.emit(n, "view", [c.src(n.args[0])], {"shape": list(_tt(n).shape)}, kind="layout")
+def _dec_where(lw: _Lowering, fx: Node):
+    return [lw.operand(a) for a in fx.args[:3]], {}
 
 
-@_on("aten.expand.default")
-def _expand(c, n):
-    return c.emit(n, "expand", [c.src(n.args[0])], {"shape": list(_tt(n).shape)}, kind="layout")
+def _dec_cat(lw: _Lowering, fx: Node):
+    return [lw.operand(p) for p in fx.args[0]], {"dim": _axis(fx, int(_arg(fx, 1, "dim", 0)))}
 
 
-@_on("aten.clone.default", "aten.contiguous.default", "aten.alias.default", "aten.detach.default")
-def _clone(c, n):
-    return c.emit(n, "clone", [c.src(n.args[0])], kind="layout")
+def _dec_pad(lw: _Lowering, fx: Node):
+    return [lw.operand(fx.args[0])], {"pad": [int(p) for p in fx.args[1]], "value": float(_arg(fx, 2, "value", 0.0))}
 
 
-@_on("aten._to_copy.default", "aten.to.dtype")
-def _cast(c, n):
-    return c.emit(n, "cast", [c.src(n.args[0])], {"dtype": _tt(n).dtype}, kind="layout")
+def _dec_conv(lw: _Lowering, fx: Node):
+    x, w, bias, stride, padding, dilation, transposed, _out_pad, groups = fx.args[:9]
+    if transposed or len(_type_of(x).shape) != 3:
+        raise UnsupportedOpError(f"{fx.name}: only non-transposed 1-D convolution")
+    inputs = [lw.operand(x), lw.operand(w)] + ([lw.operand(bias)] if bias is not None else [])
+    return inputs, {"stride": list(map(int, stride)), "padding": list(map(int, padding)),
+                    "dilation": list(map(int, dilation)), "groups": int(groups)}
 
 
-@_on("aten.slice.Tensor")
-def _slice(c, n):
-    x = n.args[0]
-    rank = len(_tt(x).shape)
-    dim = _dim(int(n.args[1]) if len(n.args) > 1 else 0, rank)
-    size = _tt(x).shape[dim]
-    start = int(n.args[2]) if len(n.args) > 2 and n.args[2] is not None else 0
-    end = int(n.args[3]) if len(n.args) > 3 and n.args[3] is not None else size
-    step = int(n.args[4]) if len(n.args) > 4 else 1
-    if step != 1:
-        raise UnsupportedOpError(f"{n.name}: strided slice")
-    start = max(0, start + size if start < 0 else start)
-    end = min(size, end + size if end < 0 else end)
-    return c.emit(n, "slice", [c.src(x)], {"dim": dim, "start": start, "end": end}, kind="layout")
+def _dec_embedding(lw: _Lowering, fx: Node):
+    table, ids = fx.args[0], fx.args[1]
+    return [lw.operand(ids), lw.operand(table)], {}
 
 
-@_on("<built-in function getitem>")
-def _getitem(c, n):
-    src, idx = n.args[0], int(n.args[1])
-    if not isinstance(src, Node) or src.name not in c.splits:
-        raise UnsupportedOpError(f"{n.name}: getitem on something other than a tensor split")
-    base, sizes, dim = c.splits[src.name]
-    start = sum(sizes[:idx])
-    return c.emit(n, "slice", [base], {"dim": dim, "start": start, "end": start + sizes[idx]}, kind="layout")
+def _dec_gelu(lw: _Lowering, fx: Node):
+    approx = str(_arg(fx, 1, "approximate", "none"))
+    if approx not in ("none", "tanh"):
+        raise UnsupportedOpError(f"{fx.name}: gelu approximate={approx!r}")
+    return [lw.operand(fx.args[0])], {"approximate": approx}
 
 
-@_on("aten.cumsum.default")
-def _cumsum(c, n):
-    rank = len(_tt(n.args[0]).shape)
-    if _dim(int(n.args[1]) if len(n.args) > 1 else -1, rank) != rank - 1:
-        raise UnsupportedOpError(f"{n.name}: only last-axis cumsum")
-    return c.emit(n, "row_cumsum", [c.src(n.args[0])])
+# overload -> (OpGraph op, node kind, decoder)
+_DECODERS: dict[str, tuple[str, str, Callable[[_Lowering, Node], tuple[list[str], dict]]]] = {
+    "pow.Tensor_Scalar": ("powf", "compute", _dec_pow_scalar),
+    "_softmax.default": ("softmax", "compute", _dec_softmax),
+    "softmax.int": ("softmax", "compute", _dec_softmax),
+    "mm.default": ("matmul", "compute", _dec_two),
+    "bmm.default": ("batch_matmul", "compute", _dec_two),
+    "permute.default": ("permute", "layout", _dec_permute),
+    "transpose.int": ("permute", "layout", _dec_transpose),
+    "t.default": ("permute", "layout", _dec_t),
+    "expand.default": ("expand", "layout", _dec_expand),
+    "_to_copy.default": ("cast", "layout", _dec_cast),
+    "to.dtype": ("cast", "layout", _dec_cast),
+    "slice.Tensor": ("slice", "layout", _dec_slice),
+    "getitem": ("slice", "layout", _dec_getitem),
+    "cumsum.default": ("row_cumsum", "compute", _dec_cumsum),
+    "gt.Scalar": ("cmp_gt", "compute", _dec_gt),
+    "where.self": ("select", "compute", _dec_where),
+    "cat.default": ("cat", "layout", _dec_cat),
+    "constant_pad_nd.default": ("pad", "compute", _dec_pad),
+    "convolution.default": ("conv1d", "compute", _dec_conv),
+    "embedding.default": ("embedding", "compute", _dec_embedding),
+    "gelu.default": ("gelu", "compute", _dec_gelu),
+}
 
 
-@_on("aten.gt.Scalar")
-def _gt(c, n):
-    return c.emit(n, "cmp_gt", [c.src(n.args[0])], {"scalar": float(n.args[1])})
+# ------------------------------------------- expansions (several nodes each)
+def _exp_addmm(lw: _Lowering, fx: Node) -> None:
+    bias, a, b = fx.args[:3]
+    prod = lw.helper(fx, "mm", "matmul", [lw.operand(a), lw.operand(b)], _type_of(fx))
+    lw.node(fx, "add", [prod.name, lw.operand(bias)])
 
 
-@_on("aten.where.self")
-def _where(c, n):
-    return c.emit(n, "select", [c.src(a) for a in n.args[:3]])
+def _exp_linear(lw: _Lowering, fx: Node) -> None:
+    x, w = fx.args[0], fx.args[1]
+    bias = _arg(fx, 2, "bias", None)
+    if len(_type_of(x).shape) != 2:
+        raise UnsupportedOpError(f"{fx.name}: linear on a rank-{len(_type_of(x).shape)} input")
+    wt = _type_of(w)
+    w_t = lw.helper(fx, "wT", "permute", [lw.operand(w)], TensorType(wt.shape[::-1], wt.dtype), {"dims": [1, 0]},
+                    kind="layout")
+    if bias is None:
+        lw.node(fx, "matmul", [lw.operand(x), w_t.name])
+        return
+    prod = lw.helper(fx, "mm", "matmul", [lw.operand(x), w_t.name], _type_of(fx))
+    lw.node(fx, "add", [prod.name, lw.operand(bias)])
 
 
-@_on("aten.cat.default")
-def _cat(c, n):
-    rank = len(_tt(n).shape)
-    dim = _dim(int(n.args[1]) if len(n.args) > 1 else 0, rank)
-    return c.emit(n, "cat", [c.src(p) for p in n.args[0]], {"dim": dim}, kind="layout")
-
-
-@_on("aten.constant_pad_nd.default")
-def _pad(c, n):
-    pads = [int(p) for p in n.args[1]]
-    value = float(n.args[2]) if len(n.args) > 2 else 0.0
-    return c.emit(n, "pad", [c.src(n.args[0])], {"pad": pads, "value": value})
-
-
-@_on("aten.convolution.default")
-def _conv(c, n):
-    x, w, bias, stride, padding, dilation, transposed, out_pad, groups = n.args[:9]
-    if transposed or len(_tt(x).shape) != 3:
-        raise UnsupportedOpError(f"{n.name}: only non-transposed 1-D convolution")
-    ins = [c.src(x), c.src(w)] + ([c.src(bias)] if bias is not None else [])
-    return c.emit(n, "conv1d", ins, {"stride": [int(s) for s in stride], "padding": [int(p) for p in padding],
-                                     "dilation": [int(d) for d in dilation], "groups": int(groups)})
-
-
-@_on("aten.embedding.default")
-def _embedding(c, n):
-    return c.emit(n, "embedding", [c.src(n.args[1]), c.src(n.args[0])])
-
-
-@_on("aten.linear.default")
-def _linear(c, n):
-    x, w = n.args[0], n.args[1]
-    wt_t = TensorType(tuple(reversed(_tt(w).shape)), _tt(w).dtype)
-    wt = c.graph.add("permute", [c.src(w)], wt_t, {"dims": [1, 0]}, kind="layout", name=n.name + "_wT", origin="aten.linear")
-    if len(_tt(x).shape) != 2:
-        raise UnsupportedOpError(f"{n.name}: linear on a rank-{len(_tt(x).shape)} input")
-    if len(n.args) > 2 and n.args[2] is not None:
-        mm = c.graph.add("matmul", [c.src(x), wt.name], _tt(n), name=n.name + "_mm", origin="aten.linear")
-        return c.emit(n, "add", [mm.name, c.src(n.args[2])])
-    return c.emit(n, "matmul", [c.src(x), wt.name])
+_EXPANSIONS: dict[str, Callable[[_Lowering, Node], None]] = {
+    "addmm.default": _exp_addmm,
+    "linear.default": _exp_linear,
+}
 
 
 def fx_to_opgraph(captured: CapturedFx) -> OpGraph:
-    return _Converter(captured).run()
+    return _Lowering(captured).run()
 
 
 def supported_aten_ops() -> list[str]:
-    return sorted(_HANDLERS)
+    keys = list(_UNARY) + list(_BINARY) + list(_REDUCTIONS) + list(_VIEWS) + list(_COPIES) + list(_DECODERS) \
+        + list(_EXPANSIONS) + ["split_with_sizes.default"]
+    return sorted(k if k == "getitem" else f"aten.{k}" for k in keys)

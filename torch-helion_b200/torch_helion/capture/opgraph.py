@@ -1,17 +1,25 @@
-"""OpGraph: the operator DAG shared by every compiler stage.
+"""OpGraph: the single-output operator DAG every compiler stage works on.
 
-Same data model and JSON layout as the reference OpGraph
-(src/torch_helion/capture/opgraph.py:29-293) so ``02_opgraph_raw.json`` /
-``03_opgraph_canonical.json`` stay interchangeable: one output per node,
-nodes kept in a topological insertion order, a concrete ``TensorType`` on
-every node, and parameter/constant *values* stored beside the graph
-(``graph.params``) so weight transforms can be folded at compile time.
+The data model and its JSON form are the reference's interchange format
+(src/torch_helion/capture/opgraph.py:29-293): ``02_opgraph_raw.json`` and
+``03_opgraph_canonical.json`` written here load in the reference and back.
+The keys of a node (name, op, kind, inputs, shape, dtype, attrs, origin) and
+of a graph (name, inputs, outputs, metadata, nodes) are therefore fixed.
+
+The container itself is this package's: besides the node table it keeps a
+consumer index (for every value, how many times each node reads it), so use
+counts, consumer lists and use replacement cost O(uses) rather than a sweep
+over the graph -- the canonicalisation passes ask those questions for every
+candidate match.  Parameter and constant *values* live beside the graph in
+``params`` so weight transforms fold at compile time.
 """
 
 from __future__ import annotations
 
+import heapq
 import json
 import math
+from collections import Counter, defaultdict
 from dataclasses import dataclass, field
 from pathlib import Path
 from typing import Any, Iterable, Iterator
@@ -35,7 +43,10 @@ class TensorType:
 
     @property
     def numel(self) -> int:
-        return math.prod(self.shape) if self.shape else 1
+        n = 1
+        for s in self.shape:
+            n *= s
+        return n
 
     @property
     def nbytes(self) -> int:
@@ -46,14 +57,14 @@ class TensorType:
         return getattr(torch, self.dtype)
 
     def with_shape(self, shape: Iterable[int]) -> "TensorType":
-        return TensorType(tuple(int(s) for s in shape), self.dtype)
+        return TensorType(tuple(map(int, shape)), self.dtype)
 
-    @staticmethod
-    def of(t: torch.Tensor) -> "TensorType":
-        return TensorType(tuple(int(s) for s in t.shape), str(t.dtype).replace("torch.", ""))
+    @classmethod
+    def of(cls, t: torch.Tensor) -> "TensorType":
+        return cls(tuple(map(int, t.shape)), str(t.dtype).rsplit(".", 1)[-1])
 
     def __str__(self) -> str:
-        return f"{self.dtype}[{', '.join(str(s) for s in self.shape)}]"
+        return self.dtype + "[" + ", ".join(map(str, self.shape)) + "]"
 
 
 @dataclass
@@ -67,21 +78,26 @@ class OpNode:
     origin: str | None = None
 
     def to_dict(self) -> dict[str, Any]:
-        return {"name": self.name, "op": self.op, "kind": self.kind, "inputs": list(self.inputs),
-                "shape": list(self.type.shape), "dtype": self.type.dtype, "attrs": _jsonable(self.attrs),
-                "origin": self.origin}
+        return dict(name=self.name, op=self.op, kind=self.kind, inputs=list(self.inputs),
+                    shape=list(self.type.shape), dtype=self.type.dtype, attrs=_to_json_value(self.attrs),
+                    origin=self.origin)
 
-    @staticmethod
-    def from_dict(d: dict[str, Any]) -> "OpNode":
-        return OpNode(d["name"], d["op"], list(d["inputs"]), TensorType(tuple(d["shape"]), d["dtype"]),
-                      dict(d.get("attrs", {})), d.get("kind", "compute"), d.get("origin"))
+    @classmethod
+    def from_dict(cls, d: dict[str, Any]) -> "OpNode":
+        return cls(name=d["name"], op=d["op"], inputs=list(d["inputs"]),
+                   type=TensorType(tuple(d["shape"]), d["dtype"]), attrs=dict(d.get("attrs") or {}),
+                   kind=d.get("kind", "compute"), origin=d.get("origin"))
 
     def __str__(self) -> str:
-        a = f" {self.attrs}" if self.attrs else ""
-        return f"{self.name}: {self.type} = {self.op}({', '.join(self.inputs)}){a}"
+        args = ", ".join(self.inputs)
+        extra = f" {self.attrs}" if self.attrs else ""
+        return f"{self.name}: {self.type} = {self.op}({args}){extra}"
 
 
 class OpGraph:
+    """Nodes in a topological order (insertion order unless re-sorted), the
+    graph's input and output value names, parameter values and metadata."""
+
     def __init__(self, name: str = "graph") -> None:
         self.name = name
         self.nodes: dict[str, OpNode] = {}
@@ -89,29 +105,44 @@ class OpGraph:
         self.outputs: list[str] = []
         self.params: dict[str, torch.Tensor] = {}
         self.metadata: dict[str, Any] = {}
-        self._counter = 0
+        self._readers: dict[str, Counter] = defaultdict(Counter)  # value -> {consumer node: times read}
+        self._serial: dict[str, int] = defaultdict(int)          # next suffix per name prefix
 
     # ------------------------------------------------------------- building
     def fresh_name(self, prefix: str) -> str:
         while True:
-            self._counter += 1
-            cand = f"{prefix}_{self._counter}"
+            self._serial[prefix] += 1
+            cand = f"{prefix}_{self._serial[prefix]}"
             if cand not in self.nodes:
                 return cand
+
+    def _index(self, node: OpNode) -> None:
+        for i in node.inputs:
+            self._readers[i][node.name] += 1
+
+    def _unindex(self, node: OpNode) -> None:
+        for i in node.inputs:
+            c = self._readers.get(i)
+            if c is None:
+                continue
+            c[node.name] -= 1
+            if c[node.name] <= 0:
+                del c[node.name]
 
     def add(self, op: str, inputs: Iterable[str], type: TensorType, attrs: dict | None = None, kind: str = "compute",
             name: str | None = None, origin: str | None = None, value: torch.Tensor | None = None) -> OpNode:
         inputs = list(inputs)
-        missing = [i for i in inputs if i not in self.nodes]
-        if missing:
-            raise KeyError(f"{op}: unknown input(s) {missing}")
+        unknown = [i for i in inputs if i not in self.nodes]
+        if unknown:
+            raise KeyError(f"{op}: unknown input(s) {unknown}")
         if kind not in NODE_KINDS:
             raise ValueError(f"unknown node kind {kind!r}")
-        name = name or self.fresh_name(op)
+        name = name if name is not None else self.fresh_name(op)
         if name in self.nodes:
             raise KeyError(f"duplicate node name {name!r}")
         node = OpNode(name, op, inputs, type, dict(attrs or {}), kind, origin)
         self.nodes[name] = node
+        self._index(node)
         if kind == "input":
             self.inputs.append(name)
         if value is not None:
@@ -135,17 +166,20 @@ class OpGraph:
         return len(self.nodes)
 
     def users(self, name: str) -> list[OpNode]:
-        return [n for n in self.nodes.values() if name in n.inputs]
+        """Nodes reading ``name`` (each once), in graph order."""
+        readers = self._readers.get(name)
+        if not readers:
+            return []
+        return [n for n in self.nodes.values() if n.name in readers]
 
     def user_map(self) -> dict[str, list[str]]:
-        m: dict[str, list[str]] = {n: [] for n in self.nodes}
-        for n in self.nodes.values():
-            for i in n.inputs:
-                m[i].append(n.name)
-        return m
+        order = {n: k for k, n in enumerate(self.nodes)}
+        return {n: sorted(self._readers.get(n, ()), key=order.__getitem__) for n in self.nodes}
 
     def num_uses(self, name: str) -> int:
-        return sum(n.inputs.count(name) for n in self.nodes.values()) + self.outputs.count(name)
+        """Reads of ``name`` by nodes (counted per operand slot) plus graph outputs."""
+        readers = self._readers.get(name)
+        return (sum(readers.values()) if readers else 0) + self.outputs.count(name)
 
     def value(self, name: str) -> torch.Tensor:
         return self.params[name]
@@ -157,99 +191,123 @@ class OpGraph:
     def replace_all_uses(self, old: str, new: str) -> None:
         if old == new:
             return
-        for n in self.nodes.values():
-            n.inputs = [new if i == old else i for i in n.inputs]
+        for reader in list(self._readers.get(old, ())):
+            node = self.nodes[reader]
+            self._unindex(node)
+            node.inputs = [new if i == old else i for i in node.inputs]
+            self._index(node)
         self.outputs = [new if o == old else o for o in self.outputs]
 
-    def remove(self, name: str) -> None:
-        if self.num_uses(name):
-            raise ValueError(f"cannot remove {name}: still used")
-        del self.nodes[name]
+    def redefine(self, name: str, op: str, inputs: Iterable[str], attrs: dict | None = None, kind: str = "compute",
+                 type: TensorType | None = None) -> OpNode:
+        """Turn node ``name`` into ``op(inputs)`` in place (its readers keep reading it)."""
+        node = self.nodes[name]
+        self._unindex(node)
+        node.op, node.inputs, node.attrs, node.kind = op, list(inputs), dict(attrs or {}), kind
+        if type is not None:
+            node.type = type
+        self._index(node)
+        return node
+
+    def _drop(self, name: str) -> None:
+        node = self.nodes.pop(name)
+        self._unindex(node)
+        self._readers.pop(name, None)
         self.params.pop(name, None)
         if name in self.inputs:
             self.inputs.remove(name)
 
+    def remove(self, name: str) -> None:
+        if self.num_uses(name):
+            raise ValueError(f"cannot remove {name}: still used")
+        self._drop(name)
+
     def dce(self) -> int:
-        live = set(self.outputs)
-        stack = list(self.outputs)
-        while stack:
-            for i in self.nodes[stack.pop()].inputs:
-                if i not in live:
-                    live.add(i)
-                    stack.append(i)
-        dead = [n for n, node in self.nodes.items() if n not in live and node.kind != "input"]
-        for n in dead:
-            del self.nodes[n]
-            self.params.pop(n, None)
-        return len(dead)
+        """Drop every non-input node that no output depends on; returns how
+        many.  Reference counting over the consumer index: a node nobody reads
+        (and that is not an output) goes, which may leave its operands unread
+        in turn.  It does not rely on the node order, which passes may leave
+        non-topological until they re-sort."""
+        dropped = 0
+        work = [n for n, node in self.nodes.items() if node.kind != "input" and self.num_uses(n) == 0]
+        while work:
+            name = work.pop()
+            if name not in self.nodes or self.num_uses(name):
+                continue
+            operands = set(self.nodes[name].inputs)
+            self._drop(name)
+            dropped += 1
+            work.extend(o for o in operands
+                        if o in self.nodes and self.nodes[o].kind != "input" and self.num_uses(o) == 0)
+        return dropped
 
     def toposort(self) -> None:
+        """Stable topological order (Kahn): among the nodes whose inputs are
+        all placed, the one that came first in the current order goes next."""
+        pos = {n: k for k, n in enumerate(self.nodes)}
+        pending = {n: len(set(node.inputs)) for n, node in self.nodes.items()}
+        ready = [(pos[n], n) for n, k in pending.items() if k == 0]
+        heapq.heapify(ready)
         order: list[str] = []
-        state: dict[str, int] = {}
-        for root in list(self.nodes):
-            if root in state:
-                continue
-            stack = [(root, False)]
-            while stack:
-                name, done = stack.pop()
-                if done:
-                    state[name] = 2
-                    order.append(name)
-                    continue
-                if name in state:
-                    continue
-                state[name] = 1
-                stack.append((name, True))
-                for i in reversed(self.nodes[name].inputs):
-                    if i not in state:
-                        stack.append((i, False))
+        while ready:
+            _, n = heapq.heappop(ready)
+            order.append(n)
+            for reader in self._readers.get(n, ()):
+                pending[reader] -= 1
+                if pending[reader] == 0:
+                    heapq.heappush(ready, (pos[reader], reader))
+        if len(order) != len(self.nodes):
+            raise ValueError(f"{self.name}: the graph has a cycle")
         self.nodes = {n: self.nodes[n] for n in order}
 
     # ---------------------------------------------------------------- output
     def summary(self) -> str:
-        lines = [f"OpGraph {self.name}: {len(self.nodes)} nodes, inputs={self.inputs}, outputs={self.outputs}"]
-        for n in self.nodes.values():
-            lines.append(f"  [{n.kind}] {n.name}: {n.type}" if n.kind in ("param", "const") else f"  {n}")
-        return "\n".join(lines)
+        head = f"OpGraph {self.name}: {len(self.nodes)} nodes, inputs={self.inputs}, outputs={self.outputs}"
+        body = [f"  [{n.kind}] {n.name}: {n.type}" if n.kind in ("param", "const") else f"  {n}"
+                for n in self.nodes.values()]
+        return "\n".join([head] + body)
 
     def to_dict(self) -> dict[str, Any]:
-        return {"name": self.name, "inputs": list(self.inputs), "outputs": list(self.outputs),
-                "metadata": _jsonable(self.metadata), "nodes": [n.to_dict() for n in self.nodes.values()]}
+        return dict(name=self.name, inputs=list(self.inputs), outputs=list(self.outputs),
+                    metadata=_to_json_value(self.metadata), nodes=[n.to_dict() for n in self.nodes.values()])
 
     def to_json(self, path: str | Path) -> None:
         Path(path).write_text(json.dumps(self.to_dict(), indent=2))
 
-    @staticmethod
-    def from_dict(d: dict[str, Any]) -> "OpGraph":
-        g = OpGraph(d.get("name", "graph"))
+    @classmethod
+    def from_dict(cls, d: dict[str, Any]) -> "OpGraph":
+        g = cls(d.get("name", "graph"))
         for nd in d["nodes"]:
             node = OpNode.from_dict(nd)
             g.nodes[node.name] = node
+            g._index(node)
         g.inputs = list(d.get("inputs", []))
         g.outputs = list(d.get("outputs", []))
         g.metadata = dict(d.get("metadata", {}))
         return g
 
-    @staticmethod
-    def from_json(path: str | Path) -> "OpGraph":
-        return OpGraph.from_dict(json.loads(Path(path).read_text()))
+    @classmethod
+    def from_json(cls, path: str | Path) -> "OpGraph":
+        return cls.from_dict(json.loads(Path(path).read_text()))
 
     def copy(self) -> "OpGraph":
         g = OpGraph.from_dict(self.to_dict())
         g.params = dict(self.params)
-        g._counter = self._counter
+        g._serial = defaultdict(int, self._serial)
         return g
 
 
-def _jsonable(obj: Any) -> Any:
-    if isinstance(obj, dict):
-        return {str(k): _jsonable(v) for k, v in obj.items()}
-    if isinstance(obj, (list, tuple)):
-        return [_jsonable(v) for v in obj]
-    if isinstance(obj, torch.dtype):
-        return str(obj).replace("torch.", "")
-    if isinstance(obj, float) and (math.isinf(obj) or math.isnan(obj)):
-        return str(obj)
-    if isinstance(obj, (int, float, str, bool)) or obj is None:
+def _to_json_value(obj: Any) -> Any:
+    """Attribute / metadata values as JSON: torch dtypes by name, non-finite
+    floats as strings, anything unknown as its ``str``."""
+    if obj is None or isinstance(obj, (bool, int, str)):
         return obj
+    if isinstance(obj, float):
+        return obj if math.isfinite(obj) else str(obj)
+    if isinstance(obj, dict):
+        return {str(k): _to_json_value(v) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return [_to_json_value(v) for v in obj]
+    if isinstance(obj, torch.dtype):
+        return str(obj).rsplit(".", 1)[-1]
     return str(obj)

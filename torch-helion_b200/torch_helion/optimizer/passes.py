@@ -42,11 +42,9 @@ class PassError(RuntimeError):
 
 
 # ------------------------------------------------------------------ helpers
-def _convert(node: OpNode, op: str, inputs: list[str], attrs: dict | None = None, kind: str = "compute",
+def _convert(g: OpGraph, node: OpNode, op: str, inputs: list[str], attrs: dict | None = None, kind: str = "compute",
              type: TensorType | None = None) -> None:
-    node.op, node.inputs, node.attrs, node.kind = op, list(inputs), dict(attrs or {}), kind
-    if type is not None:
-        node.type = type
+    g.redefine(node.name, op, inputs, attrs, kind, type)
 
 
 def _is_const(g: OpGraph, name: str) -> bool:
@@ -106,13 +104,13 @@ def _rebuild_chain(g: OpGraph, chain: list[str], new_base: str, target: OpNode) 
         prev = g.add("view", [prev], TensorType(orig_base_shape, g[prev].type.dtype), {"shape": list(orig_base_shape)},
                      kind="layout").name
     if not chain:
-        _convert(target, "view", [prev], {"shape": list(target.type.shape)}, kind="layout")
+        _convert(g, target, "view", [prev], {"shape": list(target.type.shape)}, kind="layout")
         return
     for name in chain[:-1]:
         ln = g[name]
         prev = g.add(ln.op, [prev], ln.type, dict(ln.attrs), kind="layout").name
     last = g[chain[-1]]
-    _convert(target, last.op, [prev], dict(last.attrs), kind="layout", type=last.type)
+    _convert(g, target, last.op, [prev], dict(last.attrs), kind="layout", type=last.type)
 
 
 # -------------------------------------------------------------------- passes
@@ -127,7 +125,7 @@ def fold_constants(g: OpGraph) -> int:
             continue
         val = eval_op(node.op, [g.value(i) for i in node.inputs], node.attrs)
         val = val.reshape(node.type.shape).to(node.type.torch_dtype).contiguous()
-        _convert(node, "const", [], {}, kind="const")
+        _convert(g, node, "const", [], {}, kind="const")
         g.params[node.name] = val
         n += 1
     return n
@@ -142,7 +140,7 @@ def match_silu(g: OpGraph) -> int:
         for a, s in (node.inputs, node.inputs[::-1]):
             sn = g[s]
             if sn.op == "sigmoid" and _strip(g, sn.inputs[0]) == _strip(g, a):
-                _convert(node, "silu", [a])
+                _convert(g, node, "silu", [a])
                 n += 1
                 break
     return n
@@ -163,7 +161,7 @@ def match_softplus(g: OpGraph) -> int:
         e = g[small.inputs[0]]
         if e.op != "exp" or _strip(g, e.inputs[0]) != _strip(g, x):
             continue
-        _convert(node, "softplus", [x], {"threshold": float(cond.attrs["scalar"])})
+        _convert(g, node, "softplus", [x], {"threshold": float(cond.attrs["scalar"])})
         n += 1
     return n
 
@@ -185,7 +183,7 @@ def match_rotate_half(g: OpGraph) -> int:
             continue
         if (sa.attrs["start"], sa.attrs["end"], b.attrs["start"], b.attrs["end"]) != (d // 2, d, 0, d // 2):
             continue
-        _convert(node, "rotate_half", [sa.inputs[0]])
+        _convert(g, node, "rotate_half", [sa.inputs[0]])
         n += 1
     return n
 
@@ -211,7 +209,7 @@ def match_rope(g: OpGraph) -> int:
         if found is None:
             continue
         x, cos, sin = found
-        _convert(node, "rope", [x, cos, sin], {"head_dim": g[x].type.shape[-1]})
+        _convert(g, node, "rope", [x, cos, sin], {"head_dim": g[x].type.shape[-1]})
         n += 1
     return n
 
@@ -274,7 +272,7 @@ def match_rmsnorm(g: OpGraph) -> int:
                       or (sq.op == "mul" and len(sq.inputs) == 2 and all(_strip(g, i) == src for i in sq.inputs)))
                 if not ok:
                     continue
-                _convert(node, "rmsnorm", [xn, gain], {"eps": float(add.attrs["scalar"])})
+                _convert(g, node, "rmsnorm", [xn, gain], {"eps": float(add.attrs["scalar"])})
                 n += 1
                 hit = True
                 break
@@ -311,7 +309,7 @@ def push_slice_into_gemm(g: OpGraph) -> int:
             w = _const_through_layout(g, src.inputs[1])
             wfull = _materialize(g, src.inputs[1])
             wc = g.add_const(wfull[:, lo:hi].contiguous().to(g[w].type.torch_dtype), name=g.fresh_name(w + "_cols"))
-            _convert(node, "matmul", [src.inputs[0], wc.name], {}, type=node.type)
+            _convert(g, node, "matmul", [src.inputs[0], wc.name], {}, type=node.type)
             n += 1
             progressed = True
         if not progressed:
@@ -365,12 +363,12 @@ def lower_rmsnorm(g: OpGraph) -> int:
                 new_mm = g.add("matmul", [x2d, wg.name], flat, origin=f"lower_rmsnorm({mm.name})")
                 bc = g.add("broadcast", [r], flat, {"dim": 1, "shape": list(flat.shape)})
                 sc = g.add("mul", [new_mm.name, bc.name], flat)
-                _convert(mm, "view", [sc.name], {"shape": list(mm.type.shape)}, kind="layout")
+                _convert(g, mm, "view", [sc.name], {"shape": list(mm.type.shape)}, kind="layout")
         else:
             gc = g.add_const(gval.float().contiguous(), name=g.fresh_name(gain + "_f32"))
             t2 = TensorType(_twod(node.type.shape), node.type.dtype)
             rn = g.add("rmsnorm", [x2d, gc.name], t2, {"eps": eps, "lowered": True}, origin=f"rmsnorm({node.name})")
-            _convert(node, "view", [rn.name], {"shape": list(node.type.shape)}, kind="layout")
+            _convert(g, node, "view", [rn.name], {"shape": list(node.type.shape)}, kind="layout")
         n += 1
     g.toposort()
     return n
@@ -450,7 +448,7 @@ def match_attention(g: OpGraph) -> int:
             continue
         ins = [_ensure_2d(g, trace_layout(g, bmm1.inputs[0]).base), _ensure_2d(g, trace_layout(g, bmm1.inputs[1]).base),
                _ensure_2d(g, trace_layout(g, bmm2.inputs[1]).base)]
-        _convert(final, "attention", ins, {"batch": b, "seq": sq, "heads": h, "kv_heads": dk["kv_heads"], "head_dim": d,
+        _convert(g, final, "attention", ins, {"batch": b, "seq": sq, "heads": h, "kv_heads": dk["kv_heads"], "head_dim": d,
                                            "scale": scale, "causal": causal},
                  type=TensorType((b * sq, h * d), final.type.dtype))
         n += 1
@@ -652,7 +650,7 @@ def flatten_to_2d(g: OpGraph) -> int:
         cs = column_slice(prov) if node.op in ("slice", "view", "clone", "cast") else None
         if cs is not None:
             base2d = _ensure_2d(g, prov.base)
-            _convert(node, "slice", [base2d], {"dim": 1, "start": cs[0], "end": cs[1]}, kind="layout",
+            _convert(g, node, "slice", [base2d], {"dim": 1, "start": cs[0], "end": cs[1]}, kind="layout",
                      type=TensorType(_twod(node.type.shape), node.type.dtype))
             continue
         raise PassError(f"layout op {node.name} ({node.op}) survived canonicalisation: {node.type} is a "
@@ -703,7 +701,7 @@ def fuse_conv_activation(g: OpGraph) -> int:
             continue
         src = g[node.inputs[0]]
         if src.op == "causal_conv1d" and src.attrs.get("act") is None and g.num_uses(src.name) == 1:
-            _convert(node, "causal_conv1d", list(src.inputs), {**src.attrs, "act": "silu"})
+            _convert(g, node, "causal_conv1d", list(src.inputs), {**src.attrs, "act": "silu"})
             g.dce()
             n += 1
     return n
@@ -718,7 +716,7 @@ def fuse_ssd_gate(g: OpGraph) -> int:
         for a, b in (node.inputs, node.inputs[::-1]):
             s, z = g[a], g[b]
             if s.op == "ssd" and not s.attrs.get("gate") and z.op == "silu" and g.num_uses(s.name) == 1:
-                _convert(node, "ssd", list(s.inputs) + [z.inputs[0]], {**s.attrs, "gate": True})
+                _convert(g, node, "ssd", list(s.inputs) + [z.inputs[0]], {**s.attrs, "gate": True})
                 g.dce()
                 n += 1
                 break

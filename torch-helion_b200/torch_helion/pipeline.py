@@ -35,7 +35,7 @@ from .optimizer.evaluate import max_rel_err, rel_l2
 from .optimizer.opir import Program
 from .optimizer.passes import canonicalize
 from .optimizer.planner import PlanResult, plan
-from .results import ResultsWriter
+from .results import RunDirectory
 
 log = logging.getLogger("torch_helion")
 
@@ -111,26 +111,30 @@ def device_module(program: Program, params: dict[str, torch.Tensor], config: Com
                            allreduce=lambda t: dist.all_reduce(t), tp_chunks=config.tp_chunks)
 
 
-def _stage(timings: dict[str, float], name: str):
-    class _T:
-        def __enter__(self):
-            self.t = time.time()
-            log.info("stage %s", name)
+class _Stage:
+    """Times one pipeline stage and labels the artefacts it writes."""
 
-        def __exit__(self, *a):
-            timings[name] = time.time() - self.t
+    def __init__(self, timings: dict[str, float], name: str, rundir: RunDirectory | None = None) -> None:
+        self.timings, self.name, self.rundir = timings, name, rundir
 
-    return _T()
+    def __enter__(self) -> None:
+        self.t0 = time.perf_counter()
+        if self.rundir is not None:
+            self.rundir.stage = self.name
+        log.info("stage %s", self.name)
+
+    def __exit__(self, *exc) -> None:
+        self.timings[self.name] = time.perf_counter() - self.t0
 
 
 def compile_model(model: torch.nn.Module, example_args: Sequence[Any], config: CompileConfig | None = None) -> CompileResult:
     config = config or CompileConfig()
     if config.backend != "b200":
         raise ValueError(f"unknown backend {config.backend!r} (this package implements 'b200')")
-    rw = ResultsWriter(config.run_dir)
+    rw = RunDirectory(config.run_dir)
     timings: dict[str, float] = {}
 
-    with _stage(timings, "capture"):
+    with _Stage(timings, "capture", rw):
         fx, raw = capture(model, example_args)
         rw.write_text("00_model.txt", f"{model!r}\n\nconfig: {config!r}\n")
         rw.write_text("01_fx_graph.txt", fx.text())
@@ -138,13 +142,13 @@ def compile_model(model: torch.nn.Module, example_args: Sequence[Any], config: C
         raw.to_json(rw.path("02_opgraph_raw.json"))
         rw.write_text("02_opgraph_raw.txt", raw.summary())
 
-    with _stage(timings, "canonicalize"):
+    with _Stage(timings, "canonicalize", rw):
         graph, pass_log = canonicalize(raw, verify_inputs=list(example_args) if config.verify_passes else None)
         graph.to_json(rw.path("03_opgraph_canonical.json"))
         rw.write_text("03_opgraph_canonical.txt", graph.summary())
         rw.write_json("03_pass_log.json", pass_log)
 
-    with _stage(timings, "plan"):
+    with _Stage(timings, "plan", rw):
         hw = B200Spec.load(config.hw_spec)
         rw.write_json("04_hw_spec.json", hw.summary())
         result = plan(graph, hw, config, name=config.run_name)
@@ -154,7 +158,7 @@ def compile_model(model: torch.nn.Module, example_args: Sequence[Any], config: C
         program.to_json(rw.path("06_opir.json"))
         rw.write_text("06_opir.txt", program.summary())
 
-    with _stage(timings, "codegen"):
+    with _Stage(timings, "codegen", rw):
         kernel_files = emit_program(program, config, rw.path("kernels"))
         rw.write_json("07_launch_plan.json", {k: str(v) for k, v in kernel_files.items()})
         if config.save_params:
@@ -163,22 +167,24 @@ def compile_model(model: torch.nn.Module, example_args: Sequence[Any], config: C
     res = CompileResult(config, rw.run_dir, fx, raw, graph, hw, result, program, kernel_files, timings=timings)
 
     if config.execute:
-        with _stage(timings, "build_device_program"):
+        with _Stage(timings, "build_device_program", rw):
             res.module = device_module(program, graph.params, config)
             if config.cuda_graph:
                 res.module.capture_graph()
         if config.reference_check:
-            with _stage(timings, "reference_check"):
+            with _Stage(timings, "reference_check", rw):
                 res.reference_check = reference_check(model, example_args, res, config.tolerance)
                 rw.write_json("08_reference_check.json", res.reference_check)
         if config.measure_iters > 0:
-            with _stage(timings, "measure"):
+            with _Stage(timings, "measure", rw):
                 res.measured = measure(res, example_args, config.measure_iters)
                 rw.write_json("10_measured.json", res.measured)
 
     rw.write_json("09_cost_report.json", cost_report_json(program, hw, config))
     rw.write_text("09_cost_report.md", cost_report_md(program, hw, config, res.measured))
+    rw.stage = "report"
     rw.write_json("timings.json", timings)
+    rw.write_manifest()
     return res
 
 
