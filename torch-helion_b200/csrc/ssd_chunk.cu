@@ -69,6 +69,8 @@ struct StC {
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
+constexpr int ST_PF = 3;  // chunks of L2 prefetch ahead of the two stages
+
 template <typename T>
 __global__ void __launch_bounds__(320, 1)
     ssd_state_tc(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmX,
@@ -108,8 +110,18 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 0) {
     if (lane == 0) {
+      // L2 prefetch of the chunks ahead of the two smem stages (each chunk's loads are ~100 KB and the
+      // walk is serial: without it the loads' latency sets the pace)
+      auto prefetch = [&](int c) {
+        tma_prefetch_3d(&tmB, g * CK_NS, c * CK_L, b);
+        tma_prefetch_3d(&tmB, g * CK_NS + 64, c * CK_L, b);
+        tma_prefetch_3d(&tmX, h * CK_P, c * CK_L, b);
+        tma_prefetch_3d(&tmDT, h & ~3, c * CK_L, b);
+      };
+      for (int c = 2; c < min(2 + ST_PF, nc); ++c) prefetch(c);
       for (int c = 0; c < nc; ++c) {
         const int s = c & 1;
+        if (c + 2 + ST_PF < nc) prefetch(c + 2 + ST_PF);
         if (c >= 2 && !mbar_wait(&empty[s], ((c >> 1) - 1) & 1, abort_flag)) break;
         uint8_t* st = sm + s * StC::STAGE;
         mbar_arrive_expect_tx(&full[s], StC::STAGE);
@@ -842,6 +854,415 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// ------------------------------------------------------- scan, G in TMEM
+// ssd_scan_g -- the scan with the decay-masked operand G held in tensor
+// memory and separate warp groups for building G and for the epilogue, so
+// head k's epilogue runs while head k+1's G is built and head k+1's MMAs
+// run.  Same CTA decomposition as ssd_scan_mh (chunk, head set, batch; query
+// rows 128-255 against 256 keys, then rows 0-127 against 128 keys).
+//
+// TMEM (512 columns): C.B^T fp32 in [0, 256) (one column per key), a ring of
+// two G units in [256, 384) (a unit is 128 keys as 16-bit pairs, 64
+// columns; a head is two units in the 256-key pass, one in the 128-key
+// pass), and Y (64 columns, G.x) | Yo (64 columns, C.S_in) in [384, 512).
+// G is the A operand of the G.x MMA straight from TMEM.
+//
+// Shared memory: C (128 query rows), B (until C.B^T is in TMEM; then the
+// region holds a ring of four z | y tiles), x | S_in stages, the scalar ring
+// and the sum-of-squares partials.
+//
+// Warps: 0 TMA producer (C, B, x | S_in, scalars); 1 MMA issuer; 2-9 build G
+// (two per TMEM lane quadrant, each taking alternate 32-key blocks); 10-17
+// epilogue (two per quadrant, 32 of the 64 head-dim columns each), whose
+// first thread also loads z and stores y by TMA.
+template <int NS>
+struct SgCfg {
+  static constexpr int KAT = NS / 64;                  // 64-wide state atoms
+  static constexpr int KB = KAT < 2 ? KAT : 2;         // B atoms resident at a time
+  static constexpr int C_BYTES = KAT * 128 * 128;      // 128 query rows
+  static constexpr int B_BYTES = KB * CK_L * 128;      // up to 256 keys
+  static constexpr int TILE = 128 * 128;               // one z | y tile: 128 rows x 64 columns
+  static constexpr int ZS = 4;                         // z | y ring depth
+  static constexpr int BZ_BYTES = B_BYTES > ZS * TILE ? B_BYTES : ZS * TILE;
+  static constexpr int X_BYTES = CK_L * 128;
+  static constexpr int S_BYTES = NS * 128;
+  static constexpr int STAGES = NS > 128 ? 1 : 2;
+  static constexpr int STAGE = X_BYTES + S_BYTES;
+  static constexpr int OFF_C = 0, OFF_B = C_BYTES, OFF_ZY = OFF_B;
+  static constexpr int OFF_X = OFF_B + BZ_BYTES;
+  static constexpr int OFF_SC = OFF_X + STAGES * STAGE;
+  static constexpr int OFF_R = OFF_SC + CK_SR * CK_SCAL * 4;  // [2 heads][2 halves][128] partial sums of y^2
+  static constexpr int OFF_BAR = OFF_R + 2 * 2 * 128 * 4;
+  static constexpr int SMEM = 1024 + OFF_BAR + 256;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(OFF_X % 1024 == 0 && OFF_ZY % 1024 == 0, "128-byte swizzle atoms");
+};
+
+constexpr int SG_THREADS = 64 + 256 + 256;
+constexpr int SG_PF = 4;  // heads of L2 prefetch ahead of the loads
+constexpr uint32_t SG_T_G = 256, SG_T_Y = 384;  // TMEM columns of the G ring and of Y | Yo
+
+template <typename T, int NS>
+__global__ void __maxnreg__(96)
+    ssd_scan_g(const __grid_constant__ ScMaps mp, th_ssd_args p, int nc, int hs, int nsets,
+               const float* __restrict__ scal) {
+  using Cf = SgCfg<NS>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* red = reinterpret_cast<float*>(sm + Cf::OFF_R);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cf::OFF_BAR);
+  uint64_t* cb_full = bar + 0;
+  uint64_t* cb_done = bar + 1;
+  uint64_t* b_free = bar + 2;    // d_state 256: the first half of B has been read by the C.B^T MMA
+  uint64_t* x_full = bar + 3;    // [2]
+  uint64_t* x_empty = bar + 5;   // [2]
+  uint64_t* g_full = bar + 7;    // [2] G unit written (8 builder warps)
+  uint64_t* g_free = bar + 9;    // [2] G unit read by its MMAs
+  uint64_t* y_full = bar + 11;   // Y | Yo of a head complete
+  uint64_t* y_empty = bar + 12;  // Y | Yo read by the 8 epilogue warps
+  uint64_t* sc_full = bar + 13;  // [CK_SR]
+  uint64_t* sc_free = bar + 17;  // [CK_SR] read by 8 builder + 8 epilogue warps
+  uint64_t* z_full = bar + 21;   // [4] z tile landed (or the tile is free, without a gate)
+  constexpr int NBAR = 25;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int hpg = p.heads / p.ngroups;
+  int u = (int)blockIdx.x;
+  const int set = u % (p.ngroups * nsets);
+  u /= p.ngroups * nsets;
+  const int c = u % nc, b = u / nc;
+  const int g = set / nsets, h0 = g * hpg + (set % nsets) * hs;
+  const int hcount = min(hs, g * hpg + hpg - h0);
+  const int s0 = c * CK_L, len = min(CK_L, p.seq - s0);
+  if (hcount <= 0) return;  // nothing to compute (uniform over the CTA)
+  const bool has_s = c > 0, has_z = p.z != nullptr;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) *abort_flag = 0;
+  if (warp == 1) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  pdl_wait();  // the previous kernel's outputs (this kernel's inputs) are complete
+  pdl_trigger();
+  for (int pass = 0; pass < 2; ++pass) {
+    const int qb = 1 - pass;
+    if (qb * 128 >= len) continue;  // a chunk of at most 128 rows has no second half (uniform)
+    const int nk = qb ? 256 : 128;
+    const int upk = nk / 128;       // G units per head
+    if (tid == 0) {  // fresh barriers for each pass (the previous pass has fully drained)
+      if (pass > 0)
+        for (int i = 0; i < NBAR; ++i) mbar_inval(&bar[i]);
+      mbar_init(cb_full, 1);
+      mbar_init(cb_done, 1);
+      mbar_init(b_free, 1);
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&x_full[i], 1);
+        mbar_init(&x_empty[i], 1);
+        mbar_init(&g_full[i], 8);
+        mbar_init(&g_free[i], 1);
+      }
+      mbar_init(y_full, 1);
+      mbar_init(y_empty, 8);
+      for (int i = 0; i < CK_SR; ++i) { mbar_init(&sc_full[i], 1); mbar_init(&sc_free[i], 16); }
+      for (int i = 0; i < 4; ++i) mbar_init(&z_full[i], 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    const float* scal_bc = scal + ((int64_t)b * p.heads * nc + c) * CK_SCAL;  // + head * nc * CK_SCAL
+
+    if (warp == 0) {
+      // ------------------------------------------------ TMA producer
+      if (lane == 0) {
+        const CUtensorMap* tB = qb ? &mp.B256 : &mp.B128;
+        const CUtensorMap* tX = qb ? &mp.X256 : &mp.X128;
+        auto load_xs = [&](int k) {
+          const int s = Cf::STAGES == 2 ? (k & 1) : 0;
+          uint8_t* st = sm + Cf::OFF_X + s * Cf::STAGE;
+          mbar_arrive_expect_tx(&x_full[s], nk * 128 + (has_s ? Cf::S_BYTES : 0));
+          tma_load_3d(st, tX, &x_full[s], (h0 + k) * CK_P, s0, b);
+          if (has_s)
+            tma_load_2d(st + Cf::X_BYTES, &mp.S, &x_full[s], 0, (((b * nc + c) * p.heads) + h0 + k) * NS);
+        };
+        auto load_sc = [&](int k) {
+          const int j = k % CK_SR;
+          mbar_arrive_expect_tx(&sc_full[j], CK_SCAL * 4);
+          bulk_load(sm + Cf::OFF_SC + j * CK_SCAL * 4, scal_bc + (int64_t)(h0 + k) * nc * CK_SCAL, CK_SCAL * 4,
+                    &sc_full[j]);
+        };
+        mbar_arrive_expect_tx(cb_full, Cf::C_BYTES + Cf::KB * nk * 128);
+        for (int a = 0; a < Cf::KAT; ++a) {
+          tma_load_3d(sm + Cf::OFF_C + a * 128 * 128, &mp.C, cb_full, g * NS + a * 64, s0 + qb * 128, b);
+          if (a < Cf::KB) tma_load_3d(sm + Cf::OFF_B + a * nk * 128, tB, cb_full, g * NS + a * 64, s0, b);
+        }
+        bool ok = true;
+        if constexpr (Cf::KAT > Cf::KB) {  // the second half of B once the MMA has read the first
+          ok = mbar_wait(b_free, 0, abort_flag);
+          if (ok) {
+            mbar_arrive_expect_tx(cb_full, (Cf::KAT - Cf::KB) * nk * 128);
+            for (int a = Cf::KB; a < Cf::KAT; ++a)
+              tma_load_3d(sm + Cf::OFF_B + (a - Cf::KB) * nk * 128, tB, cb_full, g * NS + a * 64, s0, b);
+          }
+        }
+        // L2 prefetches SG_PF heads ahead of the loads: the stages alone hold too few bytes in flight
+        // per SM to cover the memory latency
+        auto prefetch = [&](int k) {
+          tma_prefetch_3d(tX, (h0 + k) * CK_P, s0, b);
+          if (has_s) tma_prefetch_2d(&mp.S, 0, (((b * nc + c) * p.heads) + h0 + k) * NS);
+          if (has_z) tma_prefetch_3d(&mp.Z, (h0 + k) * CK_P, s0 + qb * 128, b);
+          bulk_prefetch_l2(scal_bc + (int64_t)(h0 + k) * nc * CK_SCAL, CK_SCAL * 4);
+        };
+        for (int k = 1; k < min(SG_PF + 1, hcount); ++k) prefetch(k);
+        for (int k = 0; k < min(CK_SR - 1, hcount); ++k) load_sc(k);
+        load_xs(0);
+        for (int k = 0; ok && k < hcount; ++k) {
+          if (k + SG_PF + 1 < hcount) prefetch(k + SG_PF + 1);
+          // x | S_in of head k+1 once the MMA of head k+1-STAGES has read its stage
+          if (k + 1 < hcount) {
+            const int prev = k + 1 - Cf::STAGES;
+            const int ps = Cf::STAGES == 2 ? (prev & 1) : 0;
+            const int pph = Cf::STAGES == 2 ? ((prev >> 1) & 1) : (prev & 1);
+            if (prev >= 0 && !(ok = mbar_wait(&x_empty[ps], pph, abort_flag))) break;
+            load_xs(k + 1);
+          }
+          // scalars of head k+3 into the slot head k-1 used
+          if (k + CK_SR - 1 < hcount) {
+            if (k >= 1 && !(ok = mbar_wait(&sc_free[(k - 1) % CK_SR], ((k - 1) / CK_SR) & 1, abort_flag))) break;
+            load_sc(k + CK_SR - 1);
+          }
+        }
+      }
+    } else if (warp == 1) {
+      // ------------------------------------------------ MMA issuer
+      if (lane == 0) {
+        constexpr int fmt = DT<T>::id == TH_BF16 ? 1 : 0;
+        const uint32_t cA = smem_u32(sm + Cf::OFF_C), bA = smem_u32(sm + Cf::OFF_B);
+        bool ok = mbar_wait(cb_full, 0, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t id_cb = make_idesc_f16(128, nk, fmt, 0, 0);
+          for (int kk = 0; kk < NS / 16; ++kk) {
+            if constexpr (Cf::KAT > Cf::KB) {
+              if (kk == Cf::KB * 4) {  // d_state 256: the second half of B replaces the first
+                tc_commit(b_free);
+                if (!(ok = mbar_wait(cb_full, 1, abort_flag))) break;
+                tc_fence_after();
+              }
+            }
+            const int ba = (kk >> 2) & (Cf::KB - 1);
+            const uint64_t ad = make_desc_sw128(cA + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = make_desc_sw128(bA + ba * nk * 128 + (kk & 3) * 32, 16, 1024);
+            tc_mma_f16(tmem, ad, bd, id_cb, kk ? 1u : 0u);
+          }
+          tc_commit(cb_done);
+        }
+        constexpr uint32_t id_y = make_idesc_f16(128, 64, fmt, 0, 1);  // B operand (x, S_in) MN-major
+        int gu = 0;  // G units consumed
+        for (int k = 0; ok && k < hcount; ++k) {
+          const int xs = Cf::STAGES == 2 ? (k & 1) : 0;
+          const int xph = Cf::STAGES == 2 ? ((k >> 1) & 1) : (k & 1);
+          ok = mbar_wait(&x_full[xs], xph, abort_flag) && (k == 0 || mbar_wait(y_empty, (k - 1) & 1, abort_flag));
+          if (!ok) break;
+          const uint32_t xA = smem_u32(sm + Cf::OFF_X + xs * Cf::STAGE), sA = xA + Cf::X_BYTES;
+          for (int un = 0; un < upk; ++un, ++gu) {
+            const int slot = gu & 1;
+            if (!(ok = mbar_wait(&g_full[slot], (gu >> 1) & 1, abort_flag))) break;
+            tc_fence_after();
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint32_t at = tmem + SG_T_G + slot * 64 + kk * 8;
+              const uint64_t bd = make_desc_sw128(xA + (un * 8 + kk) * 2048, nk * 128, 1024);
+              tc_mma_f16_ts(tmem + SG_T_Y, at, bd, id_y, (un | kk) ? 1u : 0u);
+            }
+            tc_commit(&g_free[slot]);
+          }
+          if (!ok) break;
+          if (has_s) {
+            for (int kk = 0; kk < NS / 16; ++kk) {
+              const uint64_t ad = make_desc_sw128(cA + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+              const uint64_t bd = make_desc_sw128(sA + kk * 2048, NS * 128, 1024);
+              tc_mma_f16(tmem + SG_T_Y + 64, ad, bd, id_y, kk ? 1u : 0u);
+            }
+          }
+          tc_commit(&x_empty[xs]);
+          tc_commit(y_full);
+        }
+      }
+    } else if (warp < 10) {
+      // ------------------------------------------------ G builders
+      const int q = warp & 3, half = (warp - 2) >> 2;
+      const int r = q * 32 + lane;      // row within the query half (TMEM lane)
+      const int i = qb * 128 + r;       // row within the chunk
+      const int R = qb * 128 + q * 32;  // first row of this warp
+      const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+      bool ok = mbar_wait(cb_done, 0, abort_flag);
+      int gu = 0;
+      for (int k = 0; k < hcount; ++k) {
+        const int j = k % CK_SR;
+        ok = ok && mbar_wait(&sc_full[j], (k / CK_SR) & 1, abort_flag);
+        const float* cum = reinterpret_cast<const float*>(sm + Cf::OFF_SC + j * CK_SCAL * 4);
+        const float* dts = cum + CK_L;
+        const float* colf = dts + CK_L;
+        const float Dh = colf[CK_L];
+        const float ci = cum[i];
+        for (int un = 0; un < upk; ++un, ++gu) {
+          const int slot = gu & 1;
+          if (gu >= 2) ok = ok && mbar_wait(&g_free[slot], ((gu >> 1) - 1) & 1, abort_flag);
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) {
+            tc_fence_after();
+#pragma unroll 1
+            for (int bi = half; bi < 4; bi += 2) {  // this warp's 32-key blocks of the unit
+              const int j0 = (un * 4 + bi) * 32;
+              const uint32_t gaddr = tl + SG_T_G + slot * 64 + bi * 16;
+              uint32_t pk[16];
+              if (j0 > R) {  // above the diagonal: zeros
+#pragma unroll
+                for (int e = 0; e < 16; ++e) pk[e] = 0u;
+                tmem_st16_nowait(gaddr, pk);
+                continue;
+              }
+              uint32_t raw[32];
+              tmem_ld32_issue(tl + j0, raw);
+              const float dref = ci - cum[j0 + 31];  // <= 0 below the diagonal block
+              const bool fact = dref < 80.f;         // exp(ci - cj) = exp(ci - c_ref) exp(c_ref - cj) cannot overflow
+              const float rf = __expf(fact ? dref : 0.f);
+              tmem_wait_ld32(raw);
+              const float4* cf4 = reinterpret_cast<const float4*>(colf + j0);  // 16-byte aligned: j0 % 32 == 0
+#pragma unroll
+              for (int e4 = 0; e4 < 8; ++e4) {
+                float v[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) v[e] = __uint_as_float(raw[4 * e4 + e]);
+                if (fact) {
+                  const float4 cf = cf4[e4];
+                  v[0] *= rf * cf.x;
+                  v[1] *= rf * cf.y;
+                  v[2] *= rf * cf.z;
+                  v[3] *= rf * cf.w;
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const int jj = j0 + 4 * e4 + e;
+                    v[e] *= __expf(ci - cum[jj]) * dts[jj];
+                  }
+                }
+                if (j0 == R) {  // diagonal block: causal mask and the D skip
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const int jj = j0 + 4 * e4 + e;
+                    v[e] = jj < i ? v[e] : (jj == i ? v[e] + Dh : 0.f);
+                  }
+                }
+                pk[2 * e4] = pack2<T>(v[0], v[1]);
+                pk[2 * e4 + 1] = pack2<T>(v[2], v[3]);
+              }
+              tmem_st16_nowait(gaddr, pk);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&g_full[slot]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sc_free[j]);
+      }
+    } else {
+      // ------------------------------------------------ epilogue
+      const int ew = warp - 10;
+      const int q = warp & 3, half = ew >> 2;
+      const int r = q * 32 + lane;
+      const int i = qb * 128 + r;
+      const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+      const int64_t trow = (int64_t)b * p.seq + s0 + i;
+      const bool lead = ew == 0 && lane == 0;  // loads z and stores y
+      auto tile = [&](int k) { return sm + Cf::OFF_ZY + (k & 3) * Cf::TILE; };
+      auto fetch_z = [&](int k) {  // z of head k into its tile (or mark the free tile ready)
+        if (has_z) {
+          mbar_arrive_expect_tx(&z_full[k & 3], Cf::TILE);
+          tma_load_3d(tile(k), &mp.Z, &z_full[k & 3], (h0 + k) * CK_P, s0 + qb * 128, b);
+        } else {
+          mbar_arrive(&z_full[k & 3]);
+        }
+      };
+      bool ok = true;
+      if (lead) {  // the tiles replace B: wait for the C.B^T MMA to have read it
+        ok = mbar_wait(cb_done, 0, abort_flag);
+        if (ok)
+          for (int k = 0; k < min(4, hcount); ++k) fetch_z(k);
+      }
+      for (int k = 0; k < hcount; ++k) {
+        const int j = k % CK_SR;
+        // the tile of head k+2 reuses the one of head k-2 once that y has left (y of head k-1 may still
+        // be in flight)
+        if (lead && ok && k >= 2 && k + 2 < hcount) {
+          bulk_wait_read1();
+          fetch_z(k + 2);
+        }
+        ok = ok && mbar_wait(&sc_full[j], (k / CK_SR) & 1, abort_flag) &&
+             mbar_wait(&z_full[k & 3], (k >> 2) & 1, abort_flag) && mbar_wait(y_full, k & 1, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        float ss = 0.f;
+        if (ok) {
+          // y = (G.x + exp(cum_i) C.S_in) silu(z), 16 columns at a time straight out of TMEM; Y | Yo is
+          // released as soon as the last columns are in registers
+          const float* cum = reinterpret_cast<const float*>(sm + Cf::OFF_SC + j * CK_SCAL * 4);
+          const float e = has_s ? __expf(cum[i]) : 0.f;
+          uint8_t* yb = tile(k);  // holds z of this head (when gated); y is written in place
+          tc_fence_after();
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t ry[16], ro[16];
+            tmem_ld16_issue(tl + SG_T_Y + half * 32 + hh * 16, ry);
+            if (has_s) tmem_ld16_issue(tl + SG_T_Y + 64 + half * 32 + hh * 16, ro);
+            tmem_wait_ld(ry);
+            tmem_wait_ld(ro);
+            if (hh == 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(y_empty);
+            }
+#pragma unroll
+            for (int c8 = 0; c8 < 2; ++c8) {
+              T* at = reinterpret_cast<T*>(yb + sw128_off(r, half * 32 + hh * 16 + c8 * 8, 128));
+              float zf[8], o[8];
+              if (has_z) load8<T>(at, zf);
+#pragma unroll
+              for (int e8 = 0; e8 < 8; ++e8) {
+                float y = __uint_as_float(ry[c8 * 8 + e8]);
+                if (has_s) y = fmaf(e, __uint_as_float(ro[c8 * 8 + e8]), y);
+                o[e8] = has_z ? y * silu_tanh(zf[e8]) : y;
+              }
+              ss += store8_ss<T>(at, o);  // sum of squares of the stored (rounded) values
+            }
+          }
+          fence_proxy_async();
+          red[(k & 1) * 256 + half * 128 + r] = ss;
+        } else {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(y_empty);
+        }
+        named_bar(2, 256);
+        if (lead && ok) {
+          tma_store_3d(&mp.Y, tile(k), (h0 + k) * CK_P, s0 + qb * 128, b);
+          bulk_commit();
+        }
+        if (ok && half == 0 && i < len && p.gss)
+          p.gss[trow * p.ldgss + h0 + k] = red[(k & 1) * 256 + r] + red[(k & 1) * 256 + 128 + r];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sc_free[j]);
+      }
+      if (lead) bulk_wait0();
+    }
+    tc_fence_before();
+    __syncthreads();  // this pass has drained: every store, load and MMA is complete
+    tc_fence_after();
+  }  // pass
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
 template <typename T, int NS>
 static int ssd_scan_launch(const ScMaps& m, const th_ssd_args* a, int nc, cudaStream_t st) {
   using Cf = ScCfg<NS>;
@@ -854,7 +1275,18 @@ static int ssd_scan_launch(const ScMaps& m, const th_ssd_args* a, int nc, cudaSt
   const int hs = (hpg + nsets - 1) / nsets;
   nsets = (hpg + hs - 1) / hs;
   const int units = per * nsets;
-  launch_pdl(ssd_scan_mh<T, NS>, dim3(units), dim3(64 + SC_MATH), Cf::SMEM, st, m, *a, nc, hs, nsets,
+  static const bool old_scan = [] {  // TH_SSD_SCAN=mh selects the earlier scan (G in shared memory)
+    const char* e = getenv("TH_SSD_SCAN");
+    return e && e[0] == 'm';
+  }();
+  if (old_scan) {
+    launch_pdl(ssd_scan_mh<T, NS>, dim3(units), dim3(64 + SC_MATH), Cf::SMEM, st, m, *a, nc, hs, nsets,
+               reinterpret_cast<const float*>(a->workspace));
+    return TH_OK;
+  }
+  using Gf = SgCfg<NS>;
+  if (int rc = smem_limit(ssd_scan_g<T, NS>, Gf::SMEM, "th_ssd(scan, G in TMEM)")) return rc;
+  launch_pdl(ssd_scan_g<T, NS>, dim3(units), dim3(SG_THREADS), Gf::SMEM, st, m, *a, nc, hs, nsets,
              reinterpret_cast<const float*>(a->workspace));
   return TH_OK;
 }

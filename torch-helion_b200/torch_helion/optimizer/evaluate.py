@@ -14,29 +14,12 @@ gate), ``causal_conv1d``, ``rmsnorm``, ``embedding``.
 from __future__ import annotations
 
 import math
-from typing import Any
+from typing import Any, Callable
 
 import torch
 import torch.nn.functional as F
 
 from ..capture.opgraph import OpGraph
-
-
-def _scalar_binary(op: str, a: torch.Tensor, s: float, first: bool) -> torch.Tensor:
-    x, y = (s, a) if first else (a, s)
-    if op == "add":
-        return x + y
-    if op == "sub":
-        return x - y
-    if op == "mul":
-        return x * y
-    if op == "div":
-        return x / y
-    if op == "max":
-        return torch.clamp_min(a, s)
-    if op == "powf":
-        return torch.pow(torch.full_like(a, s), a) if first else torch.pow(a, s)
-    raise ValueError(op)
 
 
 def rope_2d(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, head_dim: int, seq: int) -> torch.Tensor:
@@ -110,87 +93,199 @@ def causal_conv1d_2d(x, w, batch, seq, act):
     return F.silu(y) if act == "silu" else y
 
 
-def eval_op(op: str, args: list[torch.Tensor], attrs: dict[str, Any]) -> torch.Tensor:
-    xs = [a.float() if a.is_floating_point() else a for a in args]
-    if op in ("add", "sub", "mul", "div", "max", "powf"):
-        if "scalar" in attrs:
-            return _scalar_binary(op, xs[0], float(attrs["scalar"]), bool(attrs.get("scalar_first", False)))
-        fn = {"add": torch.add, "sub": torch.sub, "mul": torch.mul, "div": torch.div, "max": torch.maximum,
-              "powf": torch.pow}[op]
-        return fn(xs[0], xs[1])
-    unary = {"exp": torch.exp, "log": torch.log, "neg": torch.neg, "rsqrt": torch.rsqrt, "sqrt": torch.sqrt,
+# ----------------------------------------------------------- op semantics
+# One function per OpGraph op (or family of ops), registered under the op
+# names it defines.  Each takes the operands (floating ones promoted to
+# fp32) and the node's attributes.
+_SEMANTICS: dict[str, Callable[[list[torch.Tensor], dict[str, Any]], torch.Tensor]] = {}
+
+
+def _defines(*ops: str):
+    def register(fn):
+        for op in ops:
+            _SEMANTICS[op] = fn
+        return fn
+
+    return register
+
+
+_BINARY_FN = {"add": torch.add, "sub": torch.sub, "mul": torch.mul, "div": torch.div, "max": torch.maximum,
+              "powf": torch.pow}
+
+
+def _binary(op: str):
+    fn = _BINARY_FN[op]
+
+    def run(xs, attrs):
+        if "scalar" not in attrs:
+            return fn(xs[0], xs[1])
+        scalar = torch.tensor(float(attrs["scalar"]), dtype=xs[0].dtype)
+        # a scalar operand that came first in the source expression keeps its place (sub, div, pow)
+        return fn(scalar, xs[0]) if attrs.get("scalar_first") else fn(xs[0], scalar)
+
+    return run
+
+
+for _op in _BINARY_FN:
+    _SEMANTICS[_op] = _binary(_op)
+
+_UNARY_FN = {"exp": torch.exp, "log": torch.log, "neg": torch.neg, "rsqrt": torch.rsqrt, "sqrt": torch.sqrt,
              "sigmoid": torch.sigmoid, "silu": F.silu, "tanh": torch.tanh, "log1p": torch.log1p,
-             "softplus": F.softplus}
-    if op in unary:
-        return unary[op](xs[0])
-    if op == "square":
-        return xs[0] * xs[0]
-    if op == "row_cumsum":
-        return torch.cumsum(xs[0], -1)
-    if op == "cmp_gt":
-        return xs[0] > float(attrs["scalar"]) if "scalar" in attrs else xs[0] > xs[1]
-    if op == "select":
-        return torch.where(args[0].bool(), xs[1], xs[2])
-    if op == "row_sum":
-        return xs[0].sum(-1, keepdim=attrs.get("keepdim", True))
-    if op == "row_max":
-        return xs[0].amax(-1, keepdim=attrs.get("keepdim", True))
-    if op == "row_mean":
-        return xs[0].mean(-1, keepdim=attrs.get("keepdim", True))
-    if op == "row_sumsq":
-        return (xs[0] * xs[0]).sum(-1, keepdim=True)
-    if op == "softmax":
-        return torch.softmax(xs[0], -1)
-    if op == "matmul":
-        return xs[0] @ xs[1]
-    if op == "batch_matmul":
-        return torch.bmm(xs[0], xs[1])
-    if op in ("broadcast", "expand"):
-        return xs[0].expand(attrs["shape"])
-    if op == "view":
-        return xs[0].reshape(attrs["shape"])
-    if op == "permute":
-        return xs[0].permute(attrs["dims"])
-    if op in ("clone", "cast"):
-        return xs[0].clone()
-    if op == "slice":
-        return xs[0].narrow(attrs["dim"], attrs["start"], attrs["end"] - attrs["start"])
-    if op == "cat":
-        return torch.cat(xs, attrs["dim"])
-    if op == "pad":
-        return F.pad(xs[0], attrs["pad"], value=attrs.get("value", 0.0))
-    if op == "conv1d":
-        bias = xs[2] if len(xs) > 2 else None
-        return F.conv1d(xs[0], xs[1], bias, attrs["stride"], attrs["padding"], attrs["dilation"], attrs["groups"])
-    if op == "embedding":
-        return xs[1][args[0].long()]
-    if op == "rotate_half":
-        h = xs[0].shape[-1] // 2
-        return torch.cat((-xs[0][..., h:], xs[0][..., :h]), -1)
-    if op == "rmsnorm":
-        x, g = xs
-        return x * torch.rsqrt((x * x).mean(-1, keepdim=True) + attrs["eps"]) * g.reshape(-1)
-    if op == "rope":
-        if "seq" not in attrs:  # head-split form: tables broadcast over batch and heads
-            x, c, s_ = xs
-            h = x.shape[-1] // 2
-            return x * c + torch.cat((-x[..., h:], x[..., :h]), -1) * s_
+             "softplus": F.softplus, "erf": torch.erf, "square": torch.square}
+for _op, _fn in _UNARY_FN.items():
+    _SEMANTICS[_op] = (lambda f: (lambda xs, attrs: f(xs[0])))(_fn)
+
+
+@_defines("gelu")
+def _gelu(xs, attrs):
+    return F.gelu(xs[0], approximate=attrs.get("approximate", "none"))
+
+
+def _reduction(name: str):
+    how = {"row_sum": torch.sum, "row_max": torch.amax, "row_mean": torch.mean}[name]
+    return lambda xs, attrs: how(xs[0], dim=-1, keepdim=attrs.get("keepdim", True))
+
+
+for _op in ("row_sum", "row_max", "row_mean"):
+    _SEMANTICS[_op] = _reduction(_op)
+
+
+@_defines("row_sumsq")
+def _row_sumsq(xs, attrs):
+    return xs[0].square().sum(dim=-1, keepdim=True)
+
+
+@_defines("row_cumsum")
+def _row_cumsum(xs, attrs):
+    return xs[0].cumsum(dim=-1)
+
+
+@_defines("cmp_gt")
+def _cmp_gt(xs, attrs):
+    rhs = float(attrs["scalar"]) if "scalar" in attrs else xs[1]
+    return torch.gt(xs[0], rhs)
+
+
+@_defines("select")
+def _select(xs, attrs):
+    return torch.where(xs[0].bool(), xs[1], xs[2])
+
+
+@_defines("softmax")
+def _softmax(xs, attrs):
+    return xs[0].softmax(dim=-1)
+
+
+@_defines("matmul")
+def _matmul(xs, attrs):
+    return torch.matmul(xs[0], xs[1])
+
+
+@_defines("batch_matmul")
+def _bmm(xs, attrs):
+    return torch.bmm(xs[0], xs[1])
+
+
+@_defines("broadcast", "expand")
+def _expand(xs, attrs):
+    return xs[0].expand(*attrs["shape"])
+
+
+@_defines("view")
+def _view(xs, attrs):
+    return xs[0].reshape(*attrs["shape"])
+
+
+@_defines("permute")
+def _permute(xs, attrs):
+    return xs[0].permute(*attrs["dims"])
+
+
+@_defines("clone", "cast")
+def _copy(xs, attrs):
+    return xs[0].clone()
+
+
+@_defines("slice")
+def _slice(xs, attrs):
+    lo, hi = attrs["start"], attrs["end"]
+    return xs[0].narrow(attrs["dim"], lo, hi - lo)
+
+
+@_defines("cat")
+def _cat(xs, attrs):
+    return torch.cat(list(xs), dim=attrs["dim"])
+
+
+@_defines("pad")
+def _pad(xs, attrs):
+    return F.pad(xs[0], list(attrs["pad"]), value=attrs.get("value", 0.0))
+
+
+@_defines("conv1d")
+def _conv1d(xs, attrs):
+    bias = xs[2] if len(xs) > 2 else None
+    return F.conv1d(xs[0], xs[1], bias, stride=attrs["stride"], padding=attrs["padding"],
+                    dilation=attrs["dilation"], groups=attrs["groups"])
+
+
+@_defines("embedding")
+def _embedding(xs, attrs):
+    ids, table = xs
+    return table.index_select(0, ids.long().reshape(-1)).reshape(*ids.shape, table.shape[-1])
+
+
+def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+    lo, hi = x.chunk(2, dim=-1)
+    return torch.cat((hi.neg(), lo), dim=-1)
+
+
+@_defines("rotate_half")
+def _rotate(xs, attrs):
+    return _rotate_half(xs[0])
+
+
+@_defines("rmsnorm")
+def _rmsnorm(xs, attrs):
+    x, gain = xs
+    return x * (x.square().mean(dim=-1, keepdim=True) + attrs["eps"]).rsqrt() * gain.reshape(-1)
+
+
+@_defines("rope")
+def _rope(xs, attrs):
+    if "seq" in attrs:
         return rope_2d(xs[0], xs[1], xs[2], attrs["head_dim"], attrs["seq"])
-    if op == "attention":
-        a = attrs
-        return attention_2d(xs[0], xs[1], xs[2], a["batch"], a["seq"], a["heads"], a.get("kv_heads", a["heads"]),
-                            a["head_dim"], a["scale"], a.get("causal", False))
-    if op == "ssd":
-        a = attrs
-        x, dt, A, B, C = xs[:5]
-        rest = xs[5:]
-        D = rest.pop(0) if a.get("has_D") else None
-        z = rest.pop(0) if a.get("gate") else None
-        return ssd_2d(x, dt, A, B, C, D, z, a["batch"], a["seq"], a["heads"], a["head_dim"], a["ngroups"],
-                      a["state_dim"], a.get("chunk", 256))
-    if op == "causal_conv1d":
-        return causal_conv1d_2d(xs[0], xs[1], attrs["batch"], attrs["seq"], attrs.get("act"))
-    raise NotImplementedError(f"eval_op: {op}")
+    x, cos, sin = xs  # head-split form: tables broadcast over batch and heads
+    return x * cos + _rotate_half(x) * sin
+
+
+@_defines("attention")
+def _attention(xs, a):
+    return attention_2d(xs[0], xs[1], xs[2], a["batch"], a["seq"], a["heads"], a.get("kv_heads", a["heads"]),
+                        a["head_dim"], a["scale"], a.get("causal", False))
+
+
+@_defines("ssd")
+def _ssd(xs, a):
+    x, dt, A, B, C, *extra = xs
+    D = extra.pop(0) if a.get("has_D") else None
+    z = extra.pop(0) if a.get("gate") else None
+    return ssd_2d(x, dt, A, B, C, D, z, a["batch"], a["seq"], a["heads"], a["head_dim"], a["ngroups"],
+                  a["state_dim"], a.get("chunk", 256))
+
+
+@_defines("causal_conv1d")
+def _causal_conv(xs, attrs):
+    return causal_conv1d_2d(xs[0], xs[1], attrs["batch"], attrs["seq"], attrs.get("act"))
+
+
+def eval_op(op: str, args: list[torch.Tensor], attrs: dict[str, Any]) -> torch.Tensor:
+    """The fp32 value of ``op(args)`` (integer and boolean operands pass
+    through unchanged)."""
+    fn = _SEMANTICS.get(op)
+    if fn is None:
+        raise NotImplementedError(f"eval_op: {op}")
+    return fn([t.float() if t.is_floating_point() else t for t in args], attrs)
 
 
 def evaluate_graph(graph: OpGraph, inputs, keep_float32: bool = True, upto: set[str] | None = None) -> dict[str, torch.Tensor]:

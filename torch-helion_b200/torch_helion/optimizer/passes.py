@@ -26,7 +26,10 @@ de-duplication.  Changed for B200:
 
 from __future__ import annotations
 
+import hashlib
 import math
+import time
+from dataclasses import dataclass
 from typing import Callable
 
 import torch
@@ -65,19 +68,21 @@ def _const_through_layout(g: OpGraph, name: str) -> str | None:
     return name if _is_const(g, name) else None
 
 
-def _twod(shape: tuple[int, ...]) -> tuple[int, int]:
-    if len(shape) == 0:
-        return (1, 1)
-    if len(shape) == 1:
-        return (1, shape[0])
-    return (math.prod(shape[:-1]), shape[-1])
+def _matrix_shape(shape: tuple[int, ...]) -> tuple[int, int]:
+    """The token-major 2-D shape of a tensor: every axis but the last folded
+    into rows (a vector is one row, a scalar a 1 x 1 matrix)."""
+    *lead, last = shape or (1,)
+    rows = 1
+    for extent in lead:
+        rows *= extent
+    return rows, last
 
 
 def _ensure_2d(g: OpGraph, name: str) -> str:
     node = g[name]
     if node.type.rank == 2:
         return name
-    shape = _twod(node.type.shape)
+    shape = _matrix_shape(node.type.shape)
     return g.add("view", [name], TensorType(shape, node.type.dtype), {"shape": list(shape)}, kind="layout",
                  origin=f"ensure_2d({name})").name
 
@@ -147,23 +152,25 @@ def match_silu(g: OpGraph) -> int:
 
 
 def match_softplus(g: OpGraph) -> int:
-    """``where(x > t, x, log1p(exp(x)))`` -> ``softplus(x)`` (threshold t)."""
-    n = 0
-    for node in list(g):
-        if node.op != "select" or len(node.inputs) != 3:
+    """torch's thresholded softplus as export decomposes it --
+    ``where(x > t, x, log1p(exp(x)))`` -- becomes ``softplus(x)`` with that
+    threshold.  The match starts at ``log1p(exp(x))`` and checks the select
+    that consumes it."""
+    rewrites = 0
+    for soft in [nd for nd in g if nd.op == "log1p"]:
+        inner = g[soft.inputs[0]]
+        if inner.op != "exp":
             continue
-        cond, big, small = (g[i] for i in node.inputs)
-        if cond.op != "cmp_gt" or "scalar" not in cond.attrs:
-            continue
-        x = cond.inputs[0]
-        if _strip(g, big.name) != _strip(g, x) or small.op != "log1p":
-            continue
-        e = g[small.inputs[0]]
-        if e.op != "exp" or _strip(g, e.inputs[0]) != _strip(g, x):
-            continue
-        _convert(g, node, "softplus", [x], {"threshold": float(cond.attrs["scalar"])})
-        n += 1
-    return n
+        x = _strip(g, inner.inputs[0])
+        for sel in g.users(soft.name):
+            if sel.op != "select" or len(sel.inputs) != 3 or sel.inputs[2] != soft.name:
+                continue
+            test, taken = g[sel.inputs[0]], sel.inputs[1]
+            if test.op == "cmp_gt" and "scalar" in test.attrs and _strip(g, test.inputs[0]) == x \
+                    and _strip(g, taken) == x:
+                _convert(g, sel, "softplus", [test.inputs[0]], {"threshold": float(test.attrs["scalar"])})
+                rewrites += 1
+    return rewrites
 
 
 def match_rotate_half(g: OpGraph) -> int:
@@ -281,16 +288,22 @@ def match_rmsnorm(g: OpGraph) -> int:
     return n
 
 
-def _gemm_through_reshapes(g: OpGraph, name: str) -> OpNode | None:
-    node = g[name]
-    last = node.type.shape[-1]
-    while node.kind == "layout" and node.op in ("view", "clone", "cast") and len(node.inputs) == 1:
-        if node.type.shape[-1] != last or not trace_layout(g, node.name).is_identity_reshape():
+def _producing_gemm(g: OpGraph, name: str) -> OpNode | None:
+    """The constant-RHS matmul whose columns ``name`` shows unchanged: the
+    value may sit behind identity reshapes / copies / casts that keep the
+    column axis, nothing else."""
+    cols = g[name].type.shape[-1]
+    hops = [g[name]]
+    while hops[-1].kind == "layout":
+        node = hops[-1]
+        keeps_cols = (node.op in ("view", "clone", "cast") and len(node.inputs) == 1
+                      and node.type.shape[-1] == cols and trace_layout(g, node.name).is_identity_reshape())
+        if not keeps_cols:
             return None
-        node = g[node.inputs[0]]
-    if node.op == "matmul" and node.type.shape[-1] == last and _const_through_layout(g, node.inputs[1]):
-        return node
-    return None
+        hops.append(g[node.inputs[0]])
+    root = hops[-1]
+    is_gemm = root.op == "matmul" and root.type.shape[-1] == cols
+    return root if is_gemm and _const_through_layout(g, root.inputs[1]) else None
 
 
 def push_slice_into_gemm(g: OpGraph) -> int:
@@ -302,7 +315,7 @@ def push_slice_into_gemm(g: OpGraph) -> int:
         for node in list(g):
             if node.op != "slice" or node.attrs.get("dim") != g[node.inputs[0]].type.rank - 1:
                 continue
-            src = _gemm_through_reshapes(g, node.inputs[0])
+            src = _producing_gemm(g, node.inputs[0])
             if src is None:
                 continue
             lo, hi = node.attrs["start"], node.attrs["end"]
@@ -359,14 +372,14 @@ def lower_rmsnorm(g: OpGraph) -> int:
             for mm, _via in gemm_users:
                 w = _materialize(g, mm.inputs[1])
                 wg = g.add_const(pt.fold_gain_into_weight(gval, w), name=g.fresh_name(mm.inputs[1] + "_norm"))
-                flat = TensorType(_twod(mm.type.shape), mm.type.dtype)
+                flat = TensorType(_matrix_shape(mm.type.shape), mm.type.dtype)
                 new_mm = g.add("matmul", [x2d, wg.name], flat, origin=f"lower_rmsnorm({mm.name})")
                 bc = g.add("broadcast", [r], flat, {"dim": 1, "shape": list(flat.shape)})
                 sc = g.add("mul", [new_mm.name, bc.name], flat)
                 _convert(g, mm, "view", [sc.name], {"shape": list(mm.type.shape)}, kind="layout")
         else:
             gc = g.add_const(gval.float().contiguous(), name=g.fresh_name(gain + "_f32"))
-            t2 = TensorType(_twod(node.type.shape), node.type.dtype)
+            t2 = TensorType(_matrix_shape(node.type.shape), node.type.dtype)
             rn = g.add("rmsnorm", [x2d, gc.name], t2, {"eps": eps, "lowered": True}, origin=f"rmsnorm({node.name})")
             _convert(g, node, "view", [rn.name], {"shape": list(node.type.shape)}, kind="layout")
         n += 1
@@ -651,7 +664,7 @@ def flatten_to_2d(g: OpGraph) -> int:
         if cs is not None:
             base2d = _ensure_2d(g, prov.base)
             _convert(g, node, "slice", [base2d], {"dim": 1, "start": cs[0], "end": cs[1]}, kind="layout",
-                     type=TensorType(_twod(node.type.shape), node.type.dtype))
+                     type=TensorType(_matrix_shape(node.type.shape), node.type.dtype))
             continue
         raise PassError(f"layout op {node.name} ({node.op}) survived canonicalisation: {node.type} is a "
                         f"reshape/permute view of {prov.base} {g[prov.base].type} via {prov.chain}")
@@ -666,11 +679,11 @@ def flatten_to_2d(g: OpGraph) -> int:
         if node.kind == "input":
             shapes[node.name] = list(node.type.shape)
         if node.op == "broadcast":
-            node.attrs["shape"] = list(_twod(tuple(node.attrs["shape"])))
+            node.attrs["shape"] = list(_matrix_shape(tuple(node.attrs["shape"])))
         if node.kind == "input" and node.type.dtype == "int64":
             node.type = TensorType((math.prod(node.type.shape), 1), "int64")
             continue
-        node.type = TensorType(_twod(node.type.shape), node.type.dtype)
+        node.type = TensorType(_matrix_shape(node.type.shape), node.type.dtype)
     floats = [g[i].type.dtype for i in g.inputs if g[i].type.dtype != "int64"]
     if floats:
         act = floats[0]
@@ -725,21 +738,26 @@ def fuse_ssd_gate(g: OpGraph) -> int:
 
 
 def dedupe_constants(g: OpGraph) -> int:
-    seen: dict[tuple, str] = {}
-    n = 0
-    for node in list(g):
-        if node.kind != "const":
+    """Constants with identical type and bytes are merged into the first one
+    (up to 4 Mi elements; larger tables are left alone).  Candidates are
+    bucketed by a BLAKE2 digest of their bytes and confirmed with
+    ``torch.equal``, so dtypes without a numpy view (bf16) work too."""
+    buckets: dict[tuple, list[str]] = {}
+    merged = 0
+    for node in [nd for nd in g if nd.kind == "const"]:
+        value = g.value(node.name)
+        if value.numel() >= (1 << 22):
             continue
-        v = g.value(node.name)
-        if v.numel() >= (1 << 22):
-            continue
-        key = (node.type.shape, node.type.dtype, bytes(v.contiguous().reshape(-1).view(torch.uint8).numpy()))
-        if key in seen:
-            g.replace_all_uses(node.name, seen[key])
-            n += 1
+        raw = value.detach().contiguous().reshape(-1).view(torch.uint8)
+        digest = hashlib.blake2b(raw.numpy().tobytes(), digest_size=16).digest()
+        key = (tuple(node.type.shape), node.type.dtype, digest)
+        twin = next((k for k in buckets.get(key, ()) if torch.equal(g.value(k), value)), None)
+        if twin is None:
+            buckets.setdefault(key, []).append(node.name)
         else:
-            seen[key] = node.name
-    return n
+            g.replace_all_uses(node.name, twin)
+            merged += 1
+    return merged
 
 
 def cleanup(g: OpGraph) -> int:
@@ -748,46 +766,81 @@ def cleanup(g: OpGraph) -> int:
     return n
 
 
-PASSES: list[tuple[str, Callable[[OpGraph], int]]] = [
-    ("fold_constants", fold_constants),
-    ("match_silu", match_silu),
-    ("match_softplus", match_softplus),
-    ("match_rotate_half", match_rotate_half),
-    ("match_rope", match_rope),
-    ("lower_rope", lower_rope),
-    ("match_rmsnorm", match_rmsnorm),
-    ("push_slice_into_gemm", push_slice_into_gemm),
-    ("lower_rmsnorm", lower_rmsnorm),
-    ("match_attention", match_attention),
-    ("match_causal_conv1d", match_causal_conv1d),
-    ("match_ssd", match_ssd),
-    ("fold_constants_2", fold_constants),
-    ("cleanup_1", cleanup),
-    ("flatten_to_2d", flatten_to_2d),
-    ("fuse_conv_activation", fuse_conv_activation),
-    ("fuse_ssd_gate", fuse_ssd_gate),
-    ("dedupe_constants", dedupe_constants),
-    ("cleanup_2", cleanup),
-]
+@dataclass(frozen=True)
+class Pass:
+    """One canonicalisation step: ``run(graph) -> rewrites``.  ``stage`` groups
+    the steps the way the B200 lowering needs them: pattern matches on the raw
+    graph, lowerings to B200 macro ops, the 2-D flattening, and tidy-ups."""
+
+    name: str
+    run: Callable[[OpGraph], int]
+    stage: str
+
+
+PIPELINE: tuple[Pass, ...] = (
+    Pass("fold_constants", fold_constants, "match"),
+    Pass("match_silu", match_silu, "match"),
+    Pass("match_softplus", match_softplus, "match"),
+    Pass("match_rotate_half", match_rotate_half, "match"),
+    Pass("match_rope", match_rope, "match"),
+    Pass("lower_rope", lower_rope, "lower"),
+    Pass("match_rmsnorm", match_rmsnorm, "match"),
+    Pass("push_slice_into_gemm", push_slice_into_gemm, "lower"),
+    Pass("lower_rmsnorm", lower_rmsnorm, "lower"),
+    Pass("match_attention", match_attention, "match"),
+    Pass("match_causal_conv1d", match_causal_conv1d, "match"),
+    Pass("match_ssd", match_ssd, "match"),
+    Pass("fold_constants_2", fold_constants, "tidy"),
+    Pass("cleanup_1", cleanup, "tidy"),
+    Pass("flatten_to_2d", flatten_to_2d, "layout"),
+    Pass("fuse_conv_activation", fuse_conv_activation, "lower"),
+    Pass("fuse_ssd_gate", fuse_ssd_gate, "lower"),
+    Pass("dedupe_constants", dedupe_constants, "tidy"),
+    Pass("cleanup_2", cleanup, "tidy"),
+)
+# the reference's name for the pass list: (name, function) pairs
+PASSES: list[tuple[str, Callable[[OpGraph], int]]] = [(p.name, p.run) for p in PIPELINE]
+
+
+class _Checker:
+    """Evaluates the graph on the verification inputs and compares its outputs
+    with those of the raw graph (the reference's error metric, max |a-b| /
+    max |b|)."""
+
+    def __init__(self, raw: OpGraph, inputs: list[torch.Tensor] | None, tolerance: float) -> None:
+        self.inputs, self.tolerance = inputs, tolerance
+        self.want = graph_outputs(raw, inputs) if inputs is not None else None
+
+    def error(self, g: OpGraph) -> float | None:
+        if self.want is None:
+            return None
+        got = graph_outputs(g, self.inputs)
+        return max(max_rel_err(a.reshape(-1), b.reshape(-1)) for a, b in zip(got, self.want))
 
 
 def canonicalize(graph: OpGraph, verify_inputs: list[torch.Tensor] | None = None,
                  tolerance: float = 2e-2) -> tuple[OpGraph, list[dict]]:
+    """Run :data:`PIPELINE` on a copy of ``graph``.  With ``verify_inputs``
+    every step that rewrote something is checked numerically against the raw
+    graph and a step that moves the outputs by more than ``tolerance`` raises
+    :class:`PassError`.  Returns the canonical graph and the per-step log."""
     g = graph.copy()
-    raw_shapes = [list(g[o].type.shape) for o in g.outputs]
-    g.metadata["output_shapes_raw"] = {o: s for o, s in zip(g.outputs, raw_shapes)}
-    ref = graph_outputs(g, verify_inputs) if verify_inputs is not None else None
+    out_shapes = [list(g[o].type.shape) for o in g.outputs]
+    g.metadata["output_shapes_raw"] = dict(zip(g.outputs, out_shapes))
+    checker = _Checker(g, verify_inputs, tolerance)
     log: list[dict] = []
-    for name, fn in PASSES:
-        count = fn(g)
-        entry = {"pass": name, "rewrites": count, "nodes": len(g)}
-        if ref is not None and count:
-            outs = graph_outputs(g, verify_inputs)
-            err = max(max_rel_err(o.reshape(-1), r.reshape(-1)) for o, r in zip(outs, ref))
-            entry["max_rel_err"] = err
-            if not err <= tolerance:
-                raise PassError(f"pass {name} changed the numerics (max rel err {err:.3e})")
-        log.append(entry)
-    # outputs may have been renamed by the rewrites; their shapes are positional
-    g.metadata["output_shapes"] = {o: s for o, s in zip(g.outputs, raw_shapes)}
+    for step in PIPELINE:
+        t0 = time.perf_counter()
+        rewrites = step.run(g)
+        record = {"pass": step.name, "stage": step.stage, "rewrites": rewrites, "nodes": len(g),
+                  "seconds": round(time.perf_counter() - t0, 4)}
+        if rewrites:
+            err = checker.error(g)
+            if err is not None:
+                record["max_rel_err"] = err
+                if not err <= tolerance:
+                    raise PassError(f"pass {step.name} changed the numerics (max rel err {err:.3e} > {tolerance})")
+        log.append(record)
+    # rewrites may rename the outputs; their shapes are kept by position
+    g.metadata["output_shapes"] = dict(zip(g.outputs, out_shapes))
     return g, log
