@@ -20,6 +20,7 @@ Which siblings share a kernel (the *grouping*) is the planner's choice;
 
 from __future__ import annotations
 
+import itertools
 from dataclasses import dataclass, field
 
 from ..capture.opgraph import OpGraph, OpNode, TensorType
@@ -46,224 +47,246 @@ def _is_const(g: OpGraph, name: str) -> bool:
 
 
 def sibling_sets(g: OpGraph) -> list[list[str]]:
-    """GEMMs sharing the same LHS tensor, in graph order."""
-    by_lhs: dict[str, list[str]] = {}
-    for n in g:
-        if n.op == "matmul":
-            by_lhs.setdefault(n.inputs[0], []).append(n.name)
-    return list(by_lhs.values())
+    """GEMMs reading the same LHS value, one list per LHS, in graph order
+    (taken from the graph's consumer index)."""
+    sets, done = [], set()
+    for node in g:
+        if node.op != "matmul" or node.inputs[0] in done:
+            continue
+        lhs = node.inputs[0]
+        done.add(lhs)
+        sets.append([u.name for u in g.users(lhs) if u.op == "matmul" and u.inputs[0] == lhs])
+    return sets
 
 
 def default_grouping(g: OpGraph, merge_siblings: bool = True) -> Grouping:
+    """Every sibling set in one kernel (or, unmerged, one kernel per GEMM);
+    group ids are unique across sets."""
+    ids = itertools.count()
     grouping: Grouping = {}
-    gid = 0
-    for group in sibling_sets(g):
-        for m in group:
-            grouping[m] = gid
-            if not merge_siblings:
-                gid += 1
-        if merge_siblings:
-            gid += 1
+    for members in sibling_sets(g):
+        shared = next(ids)
+        grouping.update({m: shared if merge_siblings else next(ids) for m in members})
     return grouping
 
 
 def _ssd_roles(attrs: dict) -> tuple[str, ...]:
-    roles = ["x", "dt", "A", "B", "C"]
-    if attrs.get("has_D"):
-        roles.append("D")
-    if attrs.get("gate"):
-        roles.append("z")
-    return tuple(roles)
+    return ("x", "dt", "A", "B", "C") + (("D",) if attrs.get("has_D") else ()) + (("z",) if attrs.get("gate") else ())
 
 
 @dataclass
-class _K:
+class KernelDraft:
+    """A kernel while the program is assembled: its spec, the graph values
+    computed inside it (value -> the name the kernel body uses for it), where
+    it sits in the graph order, and per-kernel caches of bound operands and
+    of the row-statistic columns cloned into its epilogue."""
+
     spec: KernelSpec
-    owned: dict[str, str] = field(default_factory=dict)
-    order_key: int = 0
-    anchor_key: int = 0
-    lhs_node: str | None = None
-    extra: dict[str, str] = field(default_factory=dict)
-    column_cache: dict[str, str] = field(default_factory=dict)
+    anchor_pos: int
+    last_pos: int
+    lhs: str | None = None
+    local: dict[str, str] = field(default_factory=dict)
+    operands: dict[tuple, str] = field(default_factory=dict)
+    columns: dict[str, str] = field(default_factory=dict)
     widths: set[int] = field(default_factory=set)
 
+    def computes(self, value: str) -> bool:
+        return value in self.local
 
-def _is_column_chain(g: OpGraph, name: str, memo: dict[str, str | None]) -> str | None:
-    """``x`` when ``name`` derives only from ``row_sumsq(x)`` and scalars."""
-    if name in memo:
-        return memo[name]
-    node = g[name]
-    res: str | None = None
-    if node.op == "row_sumsq":
-        res = node.inputs[0]
-    elif node.op in BINARY_OPS or node.op in UNARY_OPS:
-        srcs = {_is_column_chain(g, i, memo) for i in node.inputs}
-        if None not in srcs and len(srcs) == 1:
-            res = srcs.pop()
-    memo[name] = res
-    return res
+
+def _row_stat_source(g: OpGraph, name: str, memo: dict[str, str | None]) -> str | None:
+    """``x`` when value ``name`` is built only from ``row_sumsq(x)`` and
+    scalars (a per-row column such as an RMSNorm scale), else None."""
+    if name not in memo:
+        node = g[name]
+        found: str | None = None
+        if node.op == "row_sumsq":
+            found = node.inputs[0]
+        elif node.op in BINARY_OPS or node.op in UNARY_OPS:
+            sources = {_row_stat_source(g, i, memo) for i in node.inputs}
+            if len(sources) == 1 and None not in sources:
+                found = next(iter(sources))
+        memo[name] = found
+    return memo[name]
 
 
 def _bind(g: OpGraph, name: str) -> tuple[str, list[int] | None]:
-    """Tensor + column range a kernel argument reads for graph value ``name``."""
+    """The tensor and column range a kernel operand reads for value ``name``:
+    2-D column slices become a column view of their base tensor."""
     node = g[name]
-    if node.kind == "layout" and node.op == "slice" and node.attrs.get("dim") == 1 and node.type.rank == 2:
-        base, cols = _bind(g, node.inputs[0])
-        lo, hi = node.attrs["start"], node.attrs["end"]
-        if cols:
-            lo, hi = cols[0] + lo, cols[0] + hi
-        return base, [lo, hi]
-    if node.kind == "layout":
-        raise PartitionError(f"{name}: layout op {node.op} reaches a kernel boundary")
-    return name, None
+    if node.kind != "layout":
+        return name, None
+    if node.op == "slice" and node.attrs.get("dim") == 1 and node.type.rank == 2:
+        base, outer = _bind(g, node.inputs[0])
+        off = outer[0] if outer else 0
+        return base, [off + node.attrs["start"], off + node.attrs["end"]]
+    raise PartitionError(f"{name}: layout op {node.op} reaches a kernel boundary")
+
+
+class _ProgramBuilder:
+    """Turns a canonical graph and a grouping into kernels: anchors first
+    (GEMM groups, macro ops), then every remaining compute node into the
+    epilogue of a GEMM kernel that produces one of its operands, then the
+    DRAM outputs, then a dependency order."""
+
+    def __init__(self, g: OpGraph, grouping: Grouping) -> None:
+        self.g, self.grouping = g, grouping
+        self.pos = {n.name: i for i, n in enumerate(g)}
+        self.drafts: dict[tuple, KernelDraft] = {}
+        self.home: dict[str, KernelDraft] = {}     # value -> kernel computing it
+        self.row_stats: dict[str, str | None] = {}
+
+    # ---- anchors
+    def add_gemm(self, n: OpNode) -> None:
+        lhs, rhs = n.inputs
+        if not _is_const(self.g, rhs):
+            raise PartitionError(f"{n.name}: GEMM with a non-constant RHS has no B200 template")
+        key = ("gemm", self.grouping[n.name])
+        draft = self.drafts.get(key)
+        if draft is None:
+            spec = KernelSpec(name="", kind="gemm", lhs="lhs", k_extent=self.g[lhs].type.shape[1],
+                              grid={"rows": n.type.shape[0], "cols": 0})
+            tensor, cols = _bind(self.g, lhs)
+            spec.args.append(KernelArg("lhs", tensor, "lhs", cols=cols))
+            draft = self.drafts[key] = KernelDraft(spec, self.pos[n.name], self.pos[n.name], lhs=lhs)
+        elif draft.lhs != lhs:
+            raise PartitionError(f"{n.name}: grouped with GEMMs of a different LHS")
+        spec = draft.spec
+        weight = f"w{len(spec.gemms)}"
+        spec.args.append(KernelArg(weight, rhs, "rhs"))
+        spec.gemms.append(GemmSpec(f"acc_{n.name}", weight))
+        spec.grid["cols"] += n.type.shape[1]
+        draft.widths.add(n.type.shape[1])
+        draft.local[n.name] = f"acc_{n.name}"
+        self.home[n.name] = draft
+
+    def add_macro(self, n: OpNode) -> None:
+        roles = _ssd_roles(n.attrs) if n.op == "ssd" else MACRO_ANCHORS[n.op]
+        if len(roles) != len(n.inputs):
+            raise PartitionError(f"{n.name}: {n.op} expects inputs {roles}")
+        spec = KernelSpec(name="", kind=n.op, attrs=dict(n.attrs))
+        for role, value in zip(roles, n.inputs):
+            tensor, cols = _bind(self.g, value)
+            spec.args.append(KernelArg(role, tensor, role, cols=cols))
+        draft = self.drafts[("macro", n.name)] = KernelDraft(spec, self.pos[n.name], self.pos[n.name])
+        draft.local[n.name] = "out"
+        self.home[n.name] = draft
+
+    # ---- epilogues
+    def is_row_column(self, name: str) -> bool:
+        node = self.g[name]
+        if _row_stat_source(self.g, name, self.row_stats) is not None:
+            return True
+        return node.op == "broadcast" and _row_stat_source(self.g, node.inputs[0], self.row_stats) is not None
+
+    def place(self, n: OpNode) -> None:
+        fits = [self.home[i] for i in n.inputs
+                if i in self.home and self.home[i].spec.kind == "gemm"
+                and n.type.shape[0] == self.home[i].spec.grid["rows"] and n.type.shape[1] in self.home[i].widths]
+        if not fits:
+            raise PartitionError(f"{n.name} ({n.op}): elementwise op with no GEMM epilogue to live in")
+        draft = max(fits, key=lambda d: d.anchor_pos)  # the latest-anchored producer
+        draft.last_pos = max(draft.last_pos, self.pos[n.name])
+        operands = [self.operand(draft, i) for i in n.inputs]
+        draft.spec.epilogue.append(BodyOp(n.name, n.op, operands, dict(n.attrs)))
+        draft.local[n.name] = n.name
+        self.home[n.name] = draft
+
+    def operand(self, draft: KernelDraft, value: str) -> str:
+        """The epilogue name of ``value`` inside ``draft``: computed there, a
+        row column rebuilt from the kernel's own Σx², or a bound input."""
+        if value in draft.local:
+            return draft.local[value]
+        if _row_stat_source(self.g, value, self.row_stats) is not None:
+            return self.column(draft, value)
+        node = self.g[value]
+        if node.op == "broadcast" and _row_stat_source(self.g, node.inputs[0], self.row_stats) is not None:
+            inner = self.column(draft, node.inputs[0])
+            key = f"bcast:{inner}:{node.attrs.get('shape')}"
+            if key not in draft.columns:
+                local = f"{node.name}__{len(draft.columns)}"
+                draft.spec.epilogue.append(BodyOp(local, "broadcast", [inner], dict(node.attrs)))
+                draft.columns[key] = local
+            draft.local[value] = draft.columns[key]
+            return draft.local[value]
+        tensor, cols = _bind(self.g, value)
+        key = (tensor, tuple(cols) if cols else None)
+        if key not in draft.operands:
+            name = f"in{len(draft.operands)}"
+            draft.spec.args.append(KernelArg(name, tensor, "const" if _is_const(self.g, tensor) else "extra", cols=cols))
+            draft.operands[key] = name
+        return draft.operands[key]
+
+    def column(self, draft: KernelDraft, value: str) -> str:
+        """Rebuild a row-statistic column inside ``draft`` from its LHS Σx²."""
+        if value in draft.columns:
+            return draft.columns[value]
+        node = self.g[value]
+        if node.op == "row_sumsq":
+            if draft.lhs != node.inputs[0]:
+                raise PartitionError(f"needs the row sum of squares of {node.inputs[0]} but the kernel's LHS "
+                                     f"is {draft.lhs}")
+            draft.spec.sumsq = True
+            draft.columns[value] = "sumsq"
+        else:
+            operands = [self.column(draft, i) for i in node.inputs]
+            local = f"{value}__col"
+            draft.spec.epilogue.append(BodyOp(local, node.op, operands, dict(node.attrs)))
+            draft.columns[value] = local
+        return draft.columns[value]
+
+    # ---- outputs and order
+    def assign_outputs(self) -> None:
+        readers: dict[str, set[int]] = {}
+        for d in self.drafts.values():
+            for a in d.spec.args:
+                readers.setdefault(a.tensor, set()).add(id(d))
+        for value, d in list(self.home.items()):
+            if d.spec.kind != "gemm":
+                d.spec.outputs = [KernelOutput(value, "out")]
+                continue
+            leaves = value in self.g.outputs
+            leaves = leaves or any(u.name not in d.local for u in self.g.users(value) if u.kind in ("compute", "layout"))
+            leaves = leaves or any(r != id(d) for r in readers.get(value, ()))
+            if leaves and d.local[value] and value not in d.spec.output_tensors():
+                d.spec.outputs.append(KernelOutput(value, d.local[value]))
+
+    def ordered(self) -> list[KernelDraft]:
+        """Kernels in dependency order, ties broken by graph position."""
+        producer = {o.tensor: d for d in self.drafts.values() for o in d.spec.outputs}
+        pending = sorted(self.drafts.values(), key=lambda d: d.last_pos)
+        placed: list[KernelDraft] = []
+        placed_ids: set[int] = set()
+        while pending:
+            ready = next((d for d in pending
+                          if all(id(producer[a.tensor]) in placed_ids
+                                 for a in d.spec.args if a.tensor in producer and producer[a.tensor] is not d)), None)
+            if ready is None:
+                raise PartitionError("cyclic kernel dependencies")
+            pending.remove(ready)
+            placed.append(ready)
+            placed_ids.add(id(ready))
+        return placed
 
 
 def build_program(g: OpGraph, grouping: Grouping | None = None, name: str = "program") -> Program:
-    grouping = grouping if grouping is not None else default_grouping(g)
-    order = {n.name: i for i, n in enumerate(g)}
-    kernels: dict[object, _K] = {}
-    owner: dict[str, _K] = {}
-    memo: dict[str, str | None] = {}
-    tensors: dict[str, TensorType] = {n.name: n.type for n in g}
-
-    # ---- anchors
+    b = _ProgramBuilder(g, grouping if grouping is not None else default_grouping(g))
     for n in g:
         if n.op == "matmul":
-            lhs, rhs = n.inputs
-            if not _is_const(g, rhs):
-                raise PartitionError(f"{n.name}: GEMM with a non-constant RHS has no B200 template")
-            key = ("gemm", grouping[n.name])
-            if key not in kernels:
-                spec = KernelSpec(name="", kind="gemm", lhs="lhs", k_extent=g[lhs].type.shape[1],
-                                  grid={"rows": n.type.shape[0], "cols": 0})
-                lt, lcols = _bind(g, lhs)
-                spec.args.append(KernelArg("lhs", lt, "lhs", cols=lcols))
-                kernels[key] = _K(spec, lhs_node=lhs, order_key=order[n.name], anchor_key=order[n.name])
-            k = kernels[key]
-            if k.lhs_node != lhs:
-                raise PartitionError(f"{n.name}: grouped with GEMMs of a different LHS")
-            arg = f"w{len(k.spec.gemms)}"
-            k.spec.args.append(KernelArg(arg, rhs, "rhs"))
-            acc = f"acc_{n.name}"
-            k.spec.gemms.append(GemmSpec(acc, arg))
-            k.spec.grid["cols"] += n.type.shape[1]
-            k.widths.add(n.type.shape[1])
-            k.owned[n.name] = acc
-            owner[n.name] = k
+            b.add_gemm(n)
         elif n.op in MACRO_ANCHORS or n.op == "ssd":
-            roles = _ssd_roles(n.attrs) if n.op == "ssd" else MACRO_ANCHORS[n.op]
-            if len(roles) != len(n.inputs):
-                raise PartitionError(f"{n.name}: {n.op} expects inputs {roles}")
-            spec = KernelSpec(name="", kind=n.op, attrs=dict(n.attrs))
-            for role, src in zip(roles, n.inputs):
-                t, cols = _bind(g, src)
-                spec.args.append(KernelArg(role, t, role, cols=cols))
-            k = _K(spec, order_key=order[n.name], anchor_key=order[n.name])
-            k.owned[n.name] = "out"
-            kernels[("macro", n.name)] = k
-            owner[n.name] = k
+            b.add_macro(n)
         elif n.op == "batch_matmul":
             raise PartitionError(f"{n.name}: standalone batch_matmul has no B200 template")
-
-    # ---- epilogue placement
     for n in g:
-        if n.kind != "compute" or n.op in ("matmul", "row_sumsq") or n.op in MACRO_ANCHORS or n.op == "ssd":
-            continue
-        if _is_column_chain(g, n.name, memo) is not None:
-            continue
-        if n.op == "broadcast" and _is_column_chain(g, n.inputs[0], memo) is not None:
-            continue  # a row-scale broadcast is cloned into each consumer on demand
-        homes = [owner[i] for i in n.inputs if i in owner and owner[i].spec.kind == "gemm"
-                 and n.type.shape[0] == owner[i].spec.grid["rows"] and n.type.shape[1] in owner[i].widths]
-        if not homes:
-            raise PartitionError(f"{n.name} ({n.op}): elementwise op with no GEMM epilogue to live in")
-        home = max(homes, key=lambda k: k.anchor_key)
-        home.order_key = max(home.order_key, order[n.name])
-        ins = [_materialize(g, i, home, memo) for i in n.inputs]
-        home.spec.epilogue.append(BodyOp(n.name, n.op, ins, dict(n.attrs)))
-        home.owned[n.name] = n.name
-        owner[n.name] = home
-
-    # ---- outputs
-    consumers: dict[str, set[int]] = {}
-    for k in kernels.values():
-        for a in k.spec.args:
-            consumers.setdefault(a.tensor, set()).add(id(k))
-    for value, k in list(owner.items()):
-        if k.spec.kind != "gemm":
-            k.spec.outputs = [KernelOutput(value, "out")]
-            continue
-        used_outside = value in g.outputs or any(
-            u.name not in k.owned for u in g.users(value) if u.kind == "compute" or u.kind == "layout")
-        used_outside = used_outside or any(c != id(k) for c in consumers.get(value, ()))
-        if used_outside and k.owned[value] and value not in k.spec.output_tensors():
-            k.spec.outputs.append(KernelOutput(value, k.owned[value]))
-
-    ordered = _order_kernels(list(kernels.values()))
-    for i, k in enumerate(ordered):
-        k.spec.name = f"k{i}_{k.spec.kind}"
-    params = sorted({a.tensor for k in ordered for a in k.spec.args if _is_const(g, a.tensor)})
-    prog = Program(name=name, inputs=list(g.inputs), outputs=list(g.outputs), tensors=tensors,
-                   kernels=[k.spec for k in ordered], params=params, metadata=dict(g.metadata))
-    prog.metadata["grouping"] = dict(grouping)
+        if n.kind == "compute" and n.name not in b.home and n.op != "row_sumsq" and not b.is_row_column(n.name):
+            b.place(n)
+    b.assign_outputs()
+    drafts = b.ordered()
+    for i, d in enumerate(drafts):
+        d.spec.name = f"k{i}_{d.spec.kind}"
+    params = sorted({a.tensor for d in drafts for a in d.spec.args if _is_const(g, a.tensor)})
+    prog = Program(name=name, inputs=list(g.inputs), outputs=list(g.outputs), tensors={n.name: n.type for n in g},
+                   kernels=[d.spec for d in drafts], params=params, metadata=dict(g.metadata))
+    prog.metadata["grouping"] = dict(b.grouping)
     return prog
-
-
-def _materialize(g: OpGraph, src: str, home: _K, memo: dict) -> str:
-    if src in home.owned:
-        return home.owned[src]
-    if _is_column_chain(g, src, memo) is not None:
-        return _clone_column(g, src, home, memo)
-    node = g[src]
-    if node.op == "broadcast" and _is_column_chain(g, node.inputs[0], memo) is not None:
-        inner = _clone_column(g, node.inputs[0], home, memo)
-        key = f"bcast:{inner}:{node.attrs.get('shape')}"
-        if key not in home.column_cache:
-            bn = f"{node.name}__{len(home.column_cache)}"
-            home.spec.epilogue.append(BodyOp(bn, "broadcast", [inner], dict(node.attrs)))
-            home.column_cache[key] = bn
-        home.owned[src] = home.column_cache[key]
-        return home.column_cache[key]
-    t, cols = _bind(g, src)
-    key = f"{t}:{cols}"
-    if key in home.extra:
-        return home.extra[key]
-    arg = f"in{len(home.extra)}"
-    role = "const" if _is_const(g, t) else "extra"
-    home.spec.args.append(KernelArg(arg, t, role, cols=cols))
-    home.extra[key] = arg
-    return arg
-
-
-def _clone_column(g: OpGraph, name: str, home: _K, memo: dict) -> str:
-    if name in home.column_cache:
-        return home.column_cache[name]
-    node = g[name]
-    if node.op == "row_sumsq":
-        if home.lhs_node != node.inputs[0]:
-            raise PartitionError(f"needs the row sum of squares of {node.inputs[0]} but the kernel's LHS is {home.lhs_node}")
-        home.spec.sumsq = True
-        home.column_cache[name] = "sumsq"
-        return "sumsq"
-    ins = [_clone_column(g, i, home, memo) for i in node.inputs]
-    local = f"{name}__col"
-    home.spec.epilogue.append(BodyOp(local, node.op, ins, dict(node.attrs)))
-    home.column_cache[name] = local
-    return local
-
-
-def _order_kernels(kernels: list[_K]) -> list[_K]:
-    produced = {o.tensor: k for k in kernels for o in k.spec.outputs}
-    done: list[_K] = []
-    remaining = sorted(kernels, key=lambda k: k.order_key)
-    while remaining:
-        progressed = False
-        for k in list(remaining):
-            deps = [produced[a.tensor] for a in k.spec.args if a.tensor in produced and produced[a.tensor] is not k]
-            if all(d in done for d in deps):
-                done.append(k)
-                remaining.remove(k)
-                progressed = True
-        if not progressed:
-            raise PartitionError("cyclic kernel dependencies")
-    return done
