@@ -378,3 +378,24 @@ def test_embedding(L, dtype):
     out = torch.empty(77, 256, device=_dev(), dtype=dtype)
     L.embedding(ids, table, out)
     assert torch.equal(out, table[ids])
+
+
+@pytest.mark.parametrize("n", [64, 128])
+def test_ssd_steep_decay(L, n):
+    """dt*A down to -8 per step: 32 steps of decay span more than exp(80),
+    so the tensor-core scan takes its per-element exponential path for the
+    G blocks (the factored form would overflow); still the recurrence."""
+    torch.manual_seed(12)
+    b, s, h, p, g = 1, 512, 4, 64, 1
+    t = b * s
+    x = torch.randn(t, h * p, device=_dev()).bfloat16()
+    B = torch.randn(t, g * n, device=_dev()).bfloat16()
+    C = torch.randn(t, g * n, device=_dev()).bfloat16()
+    dt = torch.rand(t, h, device=_dev()) * 0.4 + 0.1
+    A = -torch.full((h,), 16.0, device=_dev())
+    D = torch.rand(h, device=_dev())
+    out = torch.empty(t, h * p, device=_dev(), dtype=torch.bfloat16)
+    L.ssd(x, dt, A, B, C, out, batch=b, seq=s, heads=h, head_dim=p, ngroups=g, state_dim=n, chunk=256, D=D)
+    ref = _ssd_recurrence(x, dt, A, B, C, D, b, s, h, p, g, n)
+    assert rel_l2(out.float(), ref) < 1e-2
+    assert L.device_error() == 0

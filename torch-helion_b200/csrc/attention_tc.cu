@@ -50,7 +50,7 @@ __global__ void __launch_bounds__(320, 1)
                         const __grid_constant__ CUtensorMap tmV, th_attention_args p) {
   using C = AtCfg<D>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = smem_align<1024>(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
   constexpr int NS = C::STAGES;
   uint64_t* q_full = bars;

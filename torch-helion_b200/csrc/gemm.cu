@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(320, 1)
                    int K, int tiles_m, int tiles_n) {
   using C = TcCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = smem_align<1024>(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
@@ -569,7 +569,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
                     int K, int tiles_m, int tiles_n) {
   using C = Tc2Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = smem_align<1024>(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::RING_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;

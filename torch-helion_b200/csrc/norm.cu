@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(256, 2) conv1d_tma(const __grid_constant__ CUt
                                                      int nsb, int ntiles) {
   using Cf = CtCfg<W>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint8_t* sm = smem_align<128>(smem_raw);
   uint8_t* outs = sm + Cf::OFF_OUT;  // [2] output tiles
   float* wsm = reinterpret_cast<float*>(sm + Cf::OFF_W);
   float* bsm = reinterpret_cast<float*>(sm + Cf::OFF_B);

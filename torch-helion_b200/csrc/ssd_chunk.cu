@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(320, 1)
                  const __grid_constant__ CUtensorMap tmDT, const __grid_constant__ CUtensorMap tmS, th_ssd_args p,
                  int nc, float* __restrict__ scal) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = smem_align<1024>(smem_raw);
   float* rec = reinterpret_cast<float*>(sm + StC::OFF_REC);
   float* cums = reinterpret_cast<float*>(sm + StC::OFF_F);
   float* wsm = cums + CK_L;
@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(320, 1)
                      const __grid_constant__ CUtensorMap tmDT, th_ssd_args p, int nc, float* __restrict__ scal,
                      T* __restrict__ sc) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = smem_align<1024>(smem_raw);
   float* wtot = reinterpret_cast<float*>(sm + SpC::OFF_F);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + SpC::OFF_BAR);
   uint64_t* empty = full + 2;
@@ -528,7 +528,7 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
                 const float* __restrict__ scal) {
   using ScC = ScCfg<NS>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = smem_align<1024>(smem_raw);
   float* red = reinterpret_cast<float*>(sm + ScC::OFF_R);  // [4][128] row partials of sum y^2
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + ScC::OFF_BAR);
   uint64_t* cb_full = bar + 0;
@@ -871,10 +871,10 @@ __global__ void __launch_bounds__(64 + SC_MATH, 1)
 // region holds a ring of four z | y tiles), x | S_in stages, the scalar ring
 // and the sum-of-squares partials.
 //
-// Warps: 0 TMA producer (C, B, x | S_in, scalars); 1 MMA issuer; 2-9 build G
-// (two per TMEM lane quadrant, each taking alternate 32-key blocks); 10-17
-// epilogue (two per quadrant, 32 of the 64 head-dim columns each), whose
-// first thread also loads z and stores y by TMA.
+// Warps: 0 TMA producer (C, B, x | S_in, scalars); 1 MMA issuer; 2-17 build G
+// (four per TMEM lane quadrant, each taking two of a unit's eight 16-key
+// sub-blocks); 18-25 epilogue (two per quadrant, 32 of the 64 head-dim
+// columns each), whose first thread also loads z and stores y by TMA.
 template <int NS>
 struct SgCfg {
   static constexpr int KAT = NS / 64;                  // 64-wide state atoms
@@ -898,17 +898,27 @@ struct SgCfg {
   static_assert(OFF_X % 1024 == 0 && OFF_ZY % 1024 == 0, "128-byte swizzle atoms");
 };
 
-constexpr int SG_THREADS = 64 + 256 + 256;
+constexpr int SG_BUILD_WARPS = 16, SG_EPI_WARPS = 8;
+constexpr int SG_THREADS = 64 + 32 * (SG_BUILD_WARPS + SG_EPI_WARPS);
 constexpr int SG_PF = 4;  // heads of L2 prefetch ahead of the loads
 constexpr uint32_t SG_T_G = 256, SG_T_Y = 384;  // TMEM columns of the G ring and of Y | Yo
 
+// The G factors of a 16-key sub-block whose decay span exceeds exp(80) (so the
+// factored exp(ci - c_ref) exp(c_ref - cj) could overflow): one exponential
+// per element, exp(ci - cj) dt_j <= dt_j for the kept j <= i; the masked
+// j > i may overflow and are zeroed by the caller.  Kept out of line so the
+// common path keeps its registers.
+__device__ __noinline__ void ssd_g_decay_slow(uint32_t (&raw)[16], const float* cum, const float* dts, float ci) {
+  for (int e = 0; e < 16; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * (__expf(ci - cum[e]) * dts[e]));
+}
+
 template <typename T, int NS>
-__global__ void __maxnreg__(96)
+__global__ void __maxnreg__(72)
     ssd_scan_g(const __grid_constant__ ScMaps mp, th_ssd_args p, int nc, int hs, int nsets,
                const float* __restrict__ scal) {
   using Cf = SgCfg<NS>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = smem_align<1024>(smem_raw);
   float* red = reinterpret_cast<float*>(sm + Cf::OFF_R);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cf::OFF_BAR);
   uint64_t* cb_full = bar + 0;
@@ -916,12 +926,12 @@ __global__ void __maxnreg__(96)
   uint64_t* b_free = bar + 2;    // d_state 256: the first half of B has been read by the C.B^T MMA
   uint64_t* x_full = bar + 3;    // [2]
   uint64_t* x_empty = bar + 5;   // [2]
-  uint64_t* g_full = bar + 7;    // [2] G unit written (8 builder warps)
+  uint64_t* g_full = bar + 7;    // [2] G unit written (by every builder warp)
   uint64_t* g_free = bar + 9;    // [2] G unit read by its MMAs
   uint64_t* y_full = bar + 11;   // Y | Yo of a head complete
   uint64_t* y_empty = bar + 12;  // Y | Yo read by the 8 epilogue warps
   uint64_t* sc_full = bar + 13;  // [CK_SR]
-  uint64_t* sc_free = bar + 17;  // [CK_SR] read by 8 builder + 8 epilogue warps
+  uint64_t* sc_free = bar + 17;  // [CK_SR] read by every builder and epilogue warp
   uint64_t* z_full = bar + 21;   // [4] z tile landed (or the tile is free, without a gate)
   constexpr int NBAR = 25;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + NBAR);
@@ -961,12 +971,12 @@ __global__ void __maxnreg__(96)
       for (int i = 0; i < 2; ++i) {
         mbar_init(&x_full[i], 1);
         mbar_init(&x_empty[i], 1);
-        mbar_init(&g_full[i], 8);
+        mbar_init(&g_full[i], SG_BUILD_WARPS);
         mbar_init(&g_free[i], 1);
       }
       mbar_init(y_full, 1);
       mbar_init(y_empty, 8);
-      for (int i = 0; i < CK_SR; ++i) { mbar_init(&sc_full[i], 1); mbar_init(&sc_free[i], 16); }
+      for (int i = 0; i < CK_SR; ++i) { mbar_init(&sc_full[i], 1); mbar_init(&sc_free[i], SG_BUILD_WARPS + SG_EPI_WARPS); }
       for (int i = 0; i < 4; ++i) mbar_init(&z_full[i], 1);
       fence_mbar_init();
     }
@@ -1089,9 +1099,11 @@ __global__ void __maxnreg__(96)
           tc_commit(y_full);
         }
       }
-    } else if (warp < 10) {
-      // ------------------------------------------------ G builders
-      const int q = warp & 3, half = (warp - 2) >> 2;
+    } else if (warp < 2 + SG_BUILD_WARPS) {
+      // ------------------------------------------------ G builders: four warps per TMEM lane quadrant,
+      // each taking two of a unit's eight 16-key sub-blocks
+      const int bw = warp - 2;
+      const int q = warp & 3, part = bw >> 2;
       const int r = q * 32 + lane;      // row within the query half (TMEM lane)
       const int i = qb * 128 + r;       // row within the chunk
       const int R = qb * 128 + q * 32;  // first row of this warp
@@ -1112,53 +1124,64 @@ __global__ void __maxnreg__(96)
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
             tc_fence_after();
-#pragma unroll 1
-            for (int bi = half; bi < 4; bi += 2) {  // this warp's 32-key blocks of the unit
-              const int j0 = (un * 4 + bi) * 32;
-              const uint32_t gaddr = tl + SG_T_G + slot * 64 + bi * 16;
-              uint32_t pk[16];
-              if (j0 > R) {  // above the diagonal: zeros
 #pragma unroll
-                for (int e = 0; e < 16; ++e) pk[e] = 0u;
-                tmem_st16_nowait(gaddr, pk);
+            for (int sb = 0; sb < 2; ++sb) {
+              const int sub = part + 4 * sb;           // 16-key sub-block of the unit
+              const int j0 = un * 128 + sub * 16;      // its first key
+              const uint32_t gaddr = tl + SG_T_G + slot * 64 + sub * 8;
+              uint32_t pk[8];
+              if (j0 >= R + 32) {  // above every row of this warp: zeros
+#pragma unroll
+                for (int e = 0; e < 8; ++e) pk[e] = 0u;
+                tmem_st8_nowait(gaddr, pk);
                 continue;
               }
-              uint32_t raw[32];
-              tmem_ld32_issue(tl + j0, raw);
-              const float dref = ci - cum[j0 + 31];  // <= 0 below the diagonal block
-              const bool fact = dref < 80.f;         // exp(ci - cj) = exp(ci - c_ref) exp(c_ref - cj) cannot overflow
+              uint32_t raw[16];
+              tmem_ld16_issue(tl + j0, raw);
+              // factors against the containing 32-key block's last column (the scalar record's colf):
+              // exp(ci - cj) = exp(ci - c_ref) exp(c_ref - cj), neither of which can overflow below 80
+              const float dref = ci - cum[j0 | 31];
+              const bool fact = __all_sync(0xffffffffu, dref < 80.f);
               const float rf = __expf(fact ? dref : 0.f);
-              tmem_wait_ld32(raw);
-              const float4* cf4 = reinterpret_cast<const float4*>(colf + j0);  // 16-byte aligned: j0 % 32 == 0
+              tmem_wait_ld(raw);
+              if (fact) {
+                const uint64_t rf2 = f2_pack(rf, rf);
+                const ulonglong2* cf = reinterpret_cast<const ulonglong2*>(colf + j0);  // 16-byte aligned
 #pragma unroll
-              for (int e4 = 0; e4 < 8; ++e4) {
-                float v[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) v[e] = __uint_as_float(raw[4 * e4 + e]);
-                if (fact) {
-                  const float4 cf = cf4[e4];
-                  v[0] *= rf * cf.x;
-                  v[1] *= rf * cf.y;
-                  v[2] *= rf * cf.z;
-                  v[3] *= rf * cf.w;
-                } else {
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) {
-                    const int jj = j0 + 4 * e4 + e;
-                    v[e] *= __expf(ci - cum[jj]) * dts[jj];
-                  }
+                for (int e4 = 0; e4 < 4; ++e4) {
+                  const ulonglong2 c4 = cf[e4];
+                  const uint64_t v01 =
+                      f2_mul(f2_mul(rf2, c4.x), f2_pack(__uint_as_float(raw[4 * e4]), __uint_as_float(raw[4 * e4 + 1])));
+                  const uint64_t v23 = f2_mul(f2_mul(rf2, c4.y),
+                                              f2_pack(__uint_as_float(raw[4 * e4 + 2]), __uint_as_float(raw[4 * e4 + 3])));
+                  float a0, a1, a2, a3;
+                  f2_unpack(v01, a0, a1);
+                  f2_unpack(v23, a2, a3);
+                  raw[4 * e4] = __float_as_uint(a0);
+                  raw[4 * e4 + 1] = __float_as_uint(a1);
+                  raw[4 * e4 + 2] = __float_as_uint(a2);
+                  raw[4 * e4 + 3] = __float_as_uint(a3);
                 }
-                if (j0 == R) {  // diagonal block: causal mask and the D skip
+              } else {
+                uint32_t tmp[16];  // the out-of-line call takes a copy: `raw` itself stays in registers
 #pragma unroll
-                  for (int e = 0; e < 4; ++e) {
-                    const int jj = j0 + 4 * e4 + e;
-                    v[e] = jj < i ? v[e] : (jj == i ? v[e] + Dh : 0.f);
-                  }
-                }
-                pk[2 * e4] = pack2<T>(v[0], v[1]);
-                pk[2 * e4 + 1] = pack2<T>(v[2], v[3]);
+                for (int e = 0; e < 16; ++e) tmp[e] = raw[e];
+                ssd_g_decay_slow(tmp, cum + j0, dts + j0, ci);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) raw[e] = tmp[e];
               }
-              tmem_st16_nowait(gaddr, pk);
+              if (j0 + 15 > R) {  // keys that may lie on or above the diagonal: causal mask and the D skip
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                  const int jj = j0 + e;
+                  const float v = __uint_as_float(raw[e]);
+                  raw[e] = __float_as_uint(jj < i ? v : (jj == i ? v + Dh : 0.f));
+                }
+              }
+#pragma unroll
+              for (int e2 = 0; e2 < 8; ++e2)
+                pk[e2] = pack2<T>(__uint_as_float(raw[2 * e2]), __uint_as_float(raw[2 * e2 + 1]));
+              tmem_st8_nowait(gaddr, pk);
             }
             tmem_wait_st();
             tc_fence_before();
@@ -1171,7 +1194,7 @@ __global__ void __maxnreg__(96)
       }
     } else {
       // ------------------------------------------------ epilogue
-      const int ew = warp - 10;
+      const int ew = warp - 2 - SG_BUILD_WARPS;
       const int q = warp & 3, half = ew >> 2;
       const int r = q * 32 + lane;
       const int i = qb * 128 + r;

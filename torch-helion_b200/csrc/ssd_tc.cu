@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(256, 1)
                 const float* __restrict__ cum) {
   using C = TsCfg<NS>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = smem_align<1024>(smem_raw);
   float* cs = reinterpret_cast<float*>(sm + C::OFF_F);  // cumA [256]
   float* dts = cs + TS_L;                                // dt [256]
   float* colf = dts + TS_L;                              // exp(c_ref(j) - c_j) dt_j [256]
