@@ -232,3 +232,23 @@ def test_nccl_world2(tmp_path, kw):
     tol = 1e-5 if cfg.dtype == torch.float32 else 2e-2
     for o in outs:
         assert rel_l2(o, ref) < tol
+
+
+def test_rejects_qkv_from_one_accumulator(tmp_path):
+    """A program whose q and k are both outputs of ONE accumulator (one wide
+    GEMM split by columns, as a reference-built OpIR may have it) cannot be
+    sharded by contiguous column blocks: shard_program refuses it."""
+    import copy
+
+    from torch_helion.b200.tp import TPError, shard_program
+
+    prog, params, _, _ = _program(tmp_path)
+    prog = copy.deepcopy(prog)
+    att = next(k for k in prog.kernels if k.kind == "attention")
+    q_t, k_t = next(a.tensor for a in att.args if a.role == "q"), next(a.tensor for a in att.args if a.role == "k")
+    qkv = next(k for k in prog.kernels if any(o.tensor == q_t for o in k.outputs))
+    q_out = next(o for o in qkv.outputs if o.tensor == q_t)
+    k_out = next(o for o in qkv.outputs if o.tensor == k_t)
+    k_out.value = q_out.value  # k now reads q's accumulator
+    with pytest.raises(TPError, match="one accumulator"):
+        shard_program(prog, params, 2, 0)

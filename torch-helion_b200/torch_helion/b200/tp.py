@@ -58,9 +58,17 @@ def shard_program(program: Program, params: dict[str, torch.Tensor], world: int,
     producer = {o.tensor: k for k in prog.kernels for o in k.outputs}
     sharded: set[str] = set()
 
+    attention_operands = {a.tensor for k in prog.kernels if k.kind == "attention" for a in k.args}
+
     def shard_cols(kspec, out_tensor: str):
         """Column-parallel: keep this rank's 1/world of the GEMM feeding out_tensor."""
         accs = _acc_of_output(kspec, next(o.value for o in kspec.outputs if o.tensor == out_tensor))
+        # one accumulator behind two of q / k / v (a single wide GEMM split by columns): a contiguous
+        # 1/world of its columns would hand this rank a mixed block of q, k and v heads
+        for o in kspec.outputs:
+            if o.tensor != out_tensor and o.tensor in attention_operands and _acc_of_output(kspec, o.value) & accs:
+                raise TPError(f"{kspec.name}: {out_tensor} and {o.tensor} come from one accumulator; "
+                              "compile q, k and v as separate GEMMs to shard them by heads")
         for g in kspec.gemms:
             if g.acc not in accs:
                 continue
