@@ -186,3 +186,22 @@ def test_saved_artifact_round_trips(tmp_path):
     assert prog.to_dict() == res.program.to_dict()
     params = torch.load(tmp_path / "a" / "params.pt", weights_only=True)
     assert set(prog.params) <= set(params)
+
+
+def test_cost_model_calibration_recovers_known_terms():
+    """The calibration fit recovers the efficiency and fixed cost that
+    generated synthetic GEMM and elementwise timings."""
+    from torch_helion.cost_models.b200 import B200Spec
+    from torch_helion.cost_models.calibrate import fit
+
+    hw = B200Spec()
+    recs = []
+    for waves, bn, k in ((1, 256, 768), (7, 256, 768), (3, 128, 1536), (194, 256, 4096), (40, 256, 14336)):
+        work_us = waves * 128 * bn * k * 2 / (hw.sm_tflops * 1e12) * 1e6
+        recs.append(dict(kind="gemm", dtype="bfloat16", waves=waves, tile_n=bn, K=k, measured_us=12.0 + work_us / 0.7))
+    for nbytes in (1e7, 6e7, 3e8):
+        recs.append(dict(kind="rmsnorm", dtype="bfloat16", bytes=nbytes,
+                         measured_us=4.0 + nbytes / (hw.hbm_gbs * 1e9) * 1e6 / 0.5))
+    got = fit(recs, hw)
+    assert abs(got["eff_mma"] - 0.7) < 1e-6 and abs(got["gemm_fixed_us"] - 12.0) < 1e-6
+    assert abs(got["eff_elem"] - 0.5) < 1e-6 and abs(got["elem_fixed_us"] - 4.0) < 1e-6

@@ -3,16 +3,21 @@
 The reference estimates Loom cycles per kernel from per-tile load/compute
 terms on an 8x8 mesh (src/torch_helion/cost_models/analytic.py:109-256)
 and searches 32-aligned tiles that fit L1 (tile_search.py:56-71).  Here a
-kernel's time is a roofline on the B200 --
+kernel's time is a calibrated roofline of the kernel this build launches
+for it:
 
-    t = max(flops / (tensor or FFMA peak),  bytes / HBM bandwidth) + launch
+* GEMM (tcgen05):  fixed + waves x (128 x BN x K MMA work / (SM peak x e_mma)),
+                   tiles = ceil(T/128) x ceil(N/BN) over the SMs, BN searched
+                   in {128, 256}; never below the HBM time of its bytes;
+* GEMM (fp32):     the same over FFMA tiles of 32 x 128 (e_simt);
+* attention:       fixed + flops / (bf16 peak x e_attn) (half the flops when causal);
+* SSD scan:        fixed + max(flops / (bf16 peak x e_ssd_tc), bytes / (HBM x e_ssd_mem));
+* conv / norms / row statistics / embedding: fixed + bytes / (HBM x e_elem).
 
-with GEMMs costed per tile so wave quantisation over the 148 SMs shows
-up: tiles = ceil(T/128) x ceil(N/BN), time = ceil(tiles/148) waves x the
-per-tile MMA time, and the tile width BN in {128, 256} (what th_gemm
-builds, TMEM columns <= 512, shared-memory ring <= 227 KB) is searched.
-Peaks come from ``MEASURED_PEAKS.json`` when present (driver-measured on
-this pool) and fall back to nominal B200 figures otherwise.
+The peaks come from ``MEASURED_PEAKS.json`` (driver-measured on this pool;
+nominal B200 figures otherwise) and the efficiencies and fixed costs from
+``b200_calibration.json`` beside this file, fitted to event-timed kernels
+of this build by :mod:`torch_helion.cost_models.calibrate`.
 """
 
 from __future__ import annotations
@@ -48,10 +53,20 @@ class B200Spec:
     source: str = "nominal"
     path: Path | None = None
 
-    # efficiencies of this build's kernels relative to the peaks (calibrated
-    # against measured runs; the planner only compares candidates)
-    eff_tc: dict[int, float] = field(default_factory=lambda: {128: 0.45, 256: 0.7})
+    # efficiencies of this build's kernels against the peaks and fixed costs
+    # per launch (us), fitted to measured kernel times (b200_calibration.json)
+    eff_mma: float = 0.8
+    gemm_fixed_us: float = 5.0
     eff_simt: float = 0.35
+    eff_attn: float = 0.35
+    attn_fixed_us: float = 5.0
+    eff_ssd_tc: float = 0.2
+    eff_ssd_mem: float = 0.2
+    ssd_fixed_us: float = 5.0
+    eff_elem: float = 0.6
+    elem_fixed_us: float = 5.0
+    calibration: dict[str, Any] = field(default_factory=dict)
+    tile_widths: tuple[int, ...] = (128, 256)
 
     @staticmethod
     def load(path: str | Path | None = None) -> "B200Spec":
@@ -60,19 +75,34 @@ class B200Spec:
         if env:
             cands.append(Path(env))
         cands.append(Path(__file__).resolve().parents[3] / "MEASURED_PEAKS.json")
+        spec = B200Spec()
         for p in cands:
             if p and p.is_file() and p.suffix == ".json":
                 d = json.loads(p.read_text())
                 spec = B200Spec(hbm_gbs=float(d.get("hbm_gbs", 8000.0)), bf16_tflops=float(d.get("bf16_tflops", 2250.0)),
                                 source="measured", path=p)
-                return spec
-        return B200Spec()
+                break
+        spec.apply_calibration(load_calibration())
+        return spec
+
+    def apply_calibration(self, cal: dict[str, Any] | None) -> "B200Spec":
+        """Take the fitted efficiencies / fixed costs of a calibration record."""
+        if cal:
+            for k, v in cal.get("values", {}).items():
+                if hasattr(self, k):
+                    setattr(self, k, float(v))
+            self.calibration = {k: v for k, v in cal.items() if k != "values"}
+        return self
+
+    @property
+    def sm_tflops(self) -> float:
+        return self.bf16_tflops / self.sm_count
 
     @property
     def ridge(self) -> float:
         return self.bf16_tflops * 1e12 / (self.hbm_gbs * 1e9)
 
-    def summary(self) -> dict[str, Any]:
+    def summary(self) -> dict[str, Any]:  # noqa: D401 - artefact 04_hw_spec.json
         d = asdict(self)
         d["path"] = str(self.path) if self.path else None
         d["ridge_flop_per_byte"] = self.ridge
@@ -118,22 +148,20 @@ def gemm_cost(spec: KernelSpec, tensors: dict[str, TensorType], hw: B200Spec, bn
     out_bytes = sum(tensors[o.tensor].numel * eb for o in spec.outputs)
     byts = T * K * eb + N * K * eb + out_bytes + _arg_bytes(spec, tensors, ("extra",))
     if dt == "float32":
-        # 32x128 tiles, several resident per SM; an SM's share of the tiles
-        # runs at its share of the SIMT throughput
-        tiles_m, bn_eff = math.ceil(T / 32), 128
-        tiles = tiles_m * math.ceil(N / bn_eff)
-        waves = math.ceil(tiles / (hw.sm_count * 4))
-        per_tile = 32 * bn_eff * K * 2 / (hw.fp32_tflops * 1e12 / hw.sm_count * hw.eff_simt)
-        t_c = math.ceil(tiles / hw.sm_count) * per_tile * 1e6
+        # 32x128 FFMA tiles, several resident per SM
+        tiles = math.ceil(T / 32) * math.ceil(N / 128)
+        waves = math.ceil(tiles / hw.sm_count)
+        per_tile = 32 * 128 * K * 2 / (hw.fp32_tflops * 1e12 / hw.sm_count * hw.eff_simt)
+        t_c = waves * per_tile * 1e6 + hw.gemm_fixed_us
     else:
-        if bn not in hw.eff_tc:
+        if bn not in hw.tile_widths:
             raise CostModelError(f"tile width {bn} not built")
         # the last column tile multiplies only its live width (rounded to 16)
         tiles = math.ceil(T / 128) * math.ceil(N / bn)
         n_eff = (N // bn) * bn + (math.ceil((N % bn) / 16) * 16 if N % bn else 0)
         waves = math.ceil(math.ceil(T / 128) * n_eff / bn / hw.sm_count)
-        per_tile = 128 * bn * K * 2 / (hw.bf16_tflops * 1e12 / hw.sm_count * hw.eff_tc[bn])
-        t_c = waves * per_tile * 1e6
+        per_tile = 128 * bn * K * 2 / (hw.sm_tflops * 1e12 * hw.eff_mma)
+        t_c = waves * per_tile * 1e6 + hw.gemm_fixed_us
     t_m = byts / (hw.hbm_gbs * 1e9) * 1e6
     us = max(t_c, t_m)
     return CostBreakdown(us, {"tile_m": 128 if dt != "float32" else 32, "tile_n": bn, "tile_k": 64}, flops, byts, t_c,
@@ -145,21 +173,25 @@ def macro_cost(spec: KernelSpec, tensors: dict[str, TensorType], hw: B200Spec) -
     out = tensors[spec.outputs[0].tensor]
     eb = _eb(out)
     byts = _arg_bytes(spec, tensors) + out.numel * eb
-    flops = 0.0
-    simt = hw.fp32_tflops * 1e12 * hw.eff_simt
+    flops, t_c, t_m = 0.0, 0.0, 0.0
+    peak = hw.bf16_tflops * 1e12
     if spec.kind == "attention":
         b, s, h, d = a["batch"], a["seq"], a["heads"], a["head_dim"]
         flops = 4.0 * b * h * s * s * d * (0.5 if a.get("causal") else 1.0)
-        t_c = flops / simt * 1e6
+        if eb == 4:  # fp32 models run the SIMT flash kernel
+            t_c = flops / (hw.fp32_tflops * 1e12 * hw.eff_simt) * 1e6 + hw.attn_fixed_us
+        else:
+            t_c = flops / (peak * hw.eff_attn) * 1e6 + hw.attn_fixed_us
+        t_m = byts / (hw.hbm_gbs * 1e9) * 1e6
     elif spec.kind == "ssd":
         b, s, h, p, n = a["batch"], a["seq"], a["heads"], a["head_dim"], a["state_dim"]
         L = min(256, s)
         flops = b * s * h * (2 * L * p + 4 * p * n + 2 * L * n / max(1, h // a["ngroups"]))
-        t_c = flops / simt * 1e6
-        byts += 2 * b * math.ceil(s / L) * h * p * n * 4  # fp32 chunk states, written and read
+        byts += 2 * b * math.ceil(s / L) * h * p * n * 2  # chunk states (2-byte), written and read
+        t_c = flops / (peak * hw.eff_ssd_tc) * 1e6 + hw.ssd_fixed_us
+        t_m = byts / (hw.hbm_gbs * 1e9 * hw.eff_ssd_mem) * 1e6 + hw.ssd_fixed_us
     else:
-        t_c = 0.0
-    t_m = byts / (hw.hbm_gbs * 1e9) * 1e6
+        t_m = byts / (hw.hbm_gbs * 1e9 * hw.eff_elem) * 1e6 + hw.elem_fixed_us
     return CostBreakdown(max(t_c, t_m), {}, flops, byts, t_c, t_m, "compute" if t_c >= t_m else "hbm")
 
 
@@ -177,7 +209,7 @@ def search_tiles(spec: KernelSpec, tensors: dict[str, TensorType], hw: B200Spec)
         c = macro_cost(spec, tensors, hw)
         return TileSearchResult(c, 1, 1, [c])
     res = []
-    for bn in (128, 256):
+    for bn in hw.tile_widths:
         if bn == 256 and spec.grid["cols"] < 256:
             continue
         res.append(gemm_cost(spec, tensors, hw, bn))
@@ -187,3 +219,12 @@ def search_tiles(spec: KernelSpec, tensors: dict[str, TensorType], hw: B200Spec)
 
 def kernel_cost(spec: KernelSpec, tensors: dict[str, TensorType], hw: B200Spec) -> CostBreakdown:
     return search_tiles(spec, tensors, hw).best
+
+
+CALIBRATION_FILE = Path(__file__).with_name("b200_calibration.json")
+
+
+def load_calibration(path: str | Path | None = None) -> dict[str, Any] | None:
+    """The committed fit (or the file ``$TORCH_HELION_B200_CALIBRATION`` / ``path`` names)."""
+    p = Path(path or os.environ.get("TORCH_HELION_B200_CALIBRATION", CALIBRATION_FILE))
+    return json.loads(p.read_text()) if p.is_file() else None

@@ -214,6 +214,10 @@ def reference_check(model, example_args, res: CompileResult, tolerance: float) -
 
 
 def measure(res: CompileResult, example_args, iters: int) -> dict[str, Any]:
+    """Device time of the forward (CUDA events over ``iters`` forwards) and of
+    every launch on its own (events around each launch, a short device sleep
+    ahead of it so host launch cost stays out), the numbers the cost report
+    sets against the model."""
     mod = res.module
     dev_args = [a.to(res.config.device) for a in example_args]
     for _ in range(3):
@@ -226,9 +230,26 @@ def measure(res: CompileResult, example_args, iters: int) -> dict[str, Any]:
     e.record()
     torch.cuda.synchronize()
     ms = s.elapsed_time(e) / iters
+    per_launch: dict[str, list[float]] = {}
+    mk = lambda: torch.cuda.Event(enable_timing=True)
+    with torch.cuda.device(mod.device):
+        stream = torch.cuda.current_stream()
+        for _ in range(max(1, min(iters, 10))):
+            marks = []
+            for launch in mod.launches:
+                torch.cuda._sleep(100_000)
+                a, b = mk(), mk()
+                a.record(stream)
+                launch.fn()
+                b.record(stream)
+                marks.append((launch.name, a, b))
+            torch.cuda.synchronize()
+            for name, a, b in marks:
+                per_launch.setdefault(name, []).append(a.elapsed_time(b) * 1e3)
+    kernel_us = {k: sorted(v)[len(v) // 2] for k, v in per_launch.items()}
     tokens = res.program.tensors[res.program.inputs[0]].shape[0]
     return {"ms_per_forward": ms, "tokens": tokens, "tokens_per_s": tokens / (ms / 1e3), "iters": iters,
-            "kernels": mod.n_launches, "cuda_graph": mod._graph is not None}
+            "kernels": mod.n_launches, "cuda_graph": mod._graph is not None, "kernel_us": kernel_us}
 
 
 # ---------------------------------------------------------------- reports
@@ -264,11 +285,24 @@ def cost_report_md(program: Program, hw: B200Spec, config: CompileConfig, measur
     if measured:
         lines += [f"Measured on the device: **{measured['ms_per_forward'] * 1e3:,.1f} us** per forward "
                   f"({measured['tokens_per_s']:,.0f} tokens/s).", ""]
-    lines += ["| kernel | kind | tiles | est. us | bound | flops | bytes |", "|---|---|---|---|---|---|---|"]
+    timed = (measured or {}).get("kernel_us", {})
+    lines += ["| kernel | kind | tiles | est. us | measured us | measured / est. | bound | flops | bytes |",
+              "|---|---|---|---|---|---|---|---|---|"]
     for k in program.kernels:
         b = k.cost.get("breakdown", {})
-        lines.append(f"| {k.name} | {k.kind} | {k.tiles} | {k.cost.get('us', 0):,.2f} | {b.get('bound', '-')} | "
+        est = k.cost.get("us", 0.0)
+        got = timed.get(k.name)
+        got_s = f"{got:,.2f}" if got is not None else "-"
+        ratio = f"{got / est:.2f}" if got is not None and est else "-"
+        lines.append(f"| {k.name} | {k.kind} | {k.tiles} | {est:,.2f} | {got_s} | {ratio} | {b.get('bound', '-')} | "
                      f"{b.get('flops', 0):.3g} | {b.get('bytes', 0):.3g} |")
+    extra = {n: v for n, v in timed.items() if n not in {k.name for k in program.kernels}}
+    for n, v in extra.items():  # launches the runtime adds (row statistics, collectives)
+        lines.append(f"| {n} | runtime | - | - | {v:,.2f} | - | - | - | - |")
+    cal = hw.calibration
+    if cal:
+        lines += ["", f"Model terms fitted on {cal.get('when', '?')} to event-timed kernels of "
+                      f"{', '.join(sorted(cal.get('sources', {})))} (torch_helion.cost_models.calibrate)."]
     inter = program.intermediates()
     lines += ["", f"Kernel-to-kernel links: {len(inter)} tensors, "
                   f"{sum(program.tensors[t].nbytes for t in inter):,} bytes through HBM."]
