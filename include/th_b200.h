@@ -59,6 +59,8 @@ extern "C" {
 #define TH_ACT_NONE 0
 #define TH_ACT_SILU 1
 #define TH_ACT_SOFTPLUS 2 /* log(1+exp(x)), identity above 20 as torch */
+#define TH_ACT_GELU 3     /* 0.5 x (1 + erf(x / sqrt 2)), torch gelu(approximate='none') */
+#define TH_ACT_GELU_TANH 4 /* torch gelu(approximate='tanh') */
 
 /* ------------------------------------------------------------ housekeeping */
 const char* th_last_error_string(void);
@@ -114,6 +116,7 @@ int th_rmsnorm(const th_rmsnorm_args* a, void* stream);
  * Epilogue stages, applied per element in this order:
  *   1. row scale:  acc *= rsqrt(sum_p rs_parts[r*rs_nparts+p]*rs_inv_k + rs_eps)
  *   2. column activation on [act_begin, act_end): acc = act(acc + bias[c-act_begin])
+ *      (act TH_ACT_NONE with a bias: the bias alone)
  *   3. RoPE on [rope_begin, rope_end) (head_dim aligned): x*cos + rotate_half(x)*sin
  *      with position = row % rope_seq and fp32 tables [rope_seq, rope_head_dim]
  *   4. SwiGLU: W rows come in blocks of 128 = [64 gate | 64 up]; the output

@@ -60,6 +60,10 @@ def _epilogue_op(op, args, attrs):
         return F.silu(args[0])
     if op == "softplus":
         return F.softplus(args[0])
+    if op == "gelu":  # torch.nn.functional.gelu, erf or tanh form
+        return F.gelu(args[0], approximate=attrs.get("approximate", "none"))
+    if op == "erf":
+        return torch.erf(args[0])
     if op == "exp":
         return torch.exp(args[0])
     if op == "rope":

@@ -399,3 +399,34 @@ def test_ssd_steep_decay(L, n):
     ref = _ssd_recurrence(x, dt, A, B, C, D, b, s, h, p, g, n)
     assert rel_l2(out.float(), ref) < 1e-2
     assert L.device_error() == 0
+
+
+@pytest.mark.parametrize("approx", ["none", "tanh"])
+@pytest.mark.parametrize("dtype,m", [(torch.bfloat16, 300), (torch.bfloat16, 100), (torch.float32, 100)])
+def test_gemm_gelu(L, dtype, m, approx):
+    """GELU activation segment with a bias (an MLP's first projection), both
+    forms of torch's gelu, on the pair kernel (m > 128), the single-CTA kernel
+    and the fp32 path."""
+    torch.manual_seed(4)
+    k, n = 256, 512
+    x = torch.randn(m, k, device=_dev()).to(dtype)
+    w = (torch.randn(n, k, device=_dev()) * 0.1).to(dtype)
+    bias = torch.randn(n, device=_dev()) * 0.1
+    out = torch.empty(m, n, device=_dev(), dtype=dtype)
+    code = L.ACT_GELU if approx == "none" else L.ACT_GELU_TANH
+    L.gemm(x, w, out, act=code, act_begin=0, act_end=n, bias=bias)
+    ref = F.gelu(_gemm_ref(x, w) + bias, approximate=approx)
+    assert rel_l2(out.float(), ref) < TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype,m", [(torch.bfloat16, 300), (torch.float32, 100)])
+def test_gemm_bias_only(L, dtype, m):
+    """A Linear's bias without an activation (act NONE with a bias on a column range)."""
+    torch.manual_seed(5)
+    k, n = 192, 256
+    x = torch.randn(m, k, device=_dev()).to(dtype)
+    w = (torch.randn(n, k, device=_dev()) * 0.1).to(dtype)
+    bias = torch.randn(n, device=_dev())
+    out = torch.empty(m, n, device=_dev(), dtype=dtype)
+    L.gemm(x, w, out, act=L.ACT_NONE, act_begin=0, act_end=n, bias=bias)
+    assert rel_l2(out.float(), _gemm_ref(x, w) + bias) < TOL[dtype]

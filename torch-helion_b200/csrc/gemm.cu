@@ -40,6 +40,21 @@ struct EpiParams {
   int64_t ss_ld;
 };
 
+// The activation of an activation segment (TH_ACT_*): torch's silu, softplus
+// (threshold 20) and gelu in its erf and tanh forms.
+__device__ __forceinline__ float act_apply(int act, float x) {
+  switch (act) {
+    case TH_ACT_SILU: return silu_f(x);
+    case TH_ACT_SOFTPLUS: return softplus_f(x);
+    case TH_ACT_GELU: return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+    case TH_ACT_GELU_TANH: {
+      const float u = 0.79788456080286536f * (x + 0.044715f * x * x * x);  // sqrt(2/pi) (x + 0.044715 x^3)
+      return 0.5f * x * (1.0f + tanhf(u));
+    }
+    default: return x;
+  }
+}
+
 // Accumulator value at (local row rl, local col j) with the row scale.
 __device__ __forceinline__ float acc_at(const float* tile, int ldt, int rl, int j, float rs) {
   return tile[rl * ldt + j] * rs;
@@ -90,9 +105,9 @@ __device__ void epilogue_tile(const float* tile, int ldt, float* rscale, const E
           } else {
             const int c = oc + e;
             x = acc_at(tile, ldt, rl, jo, rs);
-            if (ep.act != TH_ACT_NONE && c >= ep.act_begin && c < ep.act_end) {
+            if ((ep.act != TH_ACT_NONE || ep.bias) && c >= ep.act_begin && c < ep.act_end) {
               if (ep.bias) x += ep.bias[c - ep.act_begin];
-              x = ep.act == TH_ACT_SILU ? silu_f(x) : softplus_f(x);
+              x = act_apply(ep.act, x);
             }
             if (ep.rope_cos && c >= ep.rope_begin && c < ep.rope_end) {
               const int hd = ep.rope_hd, half = hd >> 1;
@@ -236,13 +251,13 @@ __device__ __forceinline__ void epilogue_row_res(uint32_t tbase, int row, bool r
     tmem_ld32(tbase + c, v);
 #pragma unroll
     for (int e = 0; e < 32; ++e) v[e] *= rs;
-    if (ep.act != TH_ACT_NONE && col < ep.act_end && col + 32 > ep.act_begin) {
+    if ((ep.act != TH_ACT_NONE || ep.bias) && col < ep.act_end && col + 32 > ep.act_begin) {
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         const int cc = col + e;
         if (cc >= ep.act_begin && cc < ep.act_end) {
           float x = v[e] + (ep.bias ? ep.bias[cc - ep.act_begin] : 0.f);
-          v[e] = ep.act == TH_ACT_SILU ? silu_f(x) : softplus_f(x);
+          v[e] = act_apply(ep.act, x);
         }
       }
     }
@@ -304,13 +319,13 @@ __device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_o
     const int col = n0 + c;
 #pragma unroll
     for (int e = 0; e < 32; ++e) v[e] *= rs;
-    if (ep.act != TH_ACT_NONE && col < ep.act_end && col + 32 > ep.act_begin) {
+    if ((ep.act != TH_ACT_NONE || ep.bias) && col < ep.act_end && col + 32 > ep.act_begin) {
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         const int cc = col + e;
         if (cc >= ep.act_begin && cc < ep.act_end) {
           float x = v[e] + (ep.bias ? ep.bias[cc - ep.act_begin] : 0.f);
-          v[e] = ep.act == TH_ACT_SILU ? silu_f(x) : softplus_f(x);
+          v[e] = act_apply(ep.act, x);
         }
       }
     }
@@ -857,7 +872,7 @@ extern "C" int th_gemm(const th_gemm_args* a, void* stream) {
     if (!a->rope_sin || hd <= 0 || hd % 2 || hd > 128 || a->rope_begin % hd || a->rope_end % hd || a->rope_seq <= 0)
       return fail(TH_EINVAL, "th_gemm: bad rope segment");
   }
-  if (a->act != TH_ACT_NONE && a->act != TH_ACT_SILU && a->act != TH_ACT_SOFTPLUS) return fail(TH_EINVAL, "th_gemm: bad act");
+  if (a->act < TH_ACT_NONE || a->act > TH_ACT_GELU_TANH) return fail(TH_EINVAL, "th_gemm: bad act %d", a->act);
   if (a->rs_parts && a->rs_nparts <= 0) return fail(TH_EINVAL, "th_gemm: rs_nparts must be > 0");
   if (a->ss_out && a->ss_ld < (n_out + 63) / 64) return fail(TH_EINVAL, "th_gemm: ss_ld too small");
 

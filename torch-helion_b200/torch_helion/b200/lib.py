@@ -19,7 +19,10 @@ _PKG_ROOT = Path(__file__).resolve().parents[2]  # .../torch-helion_b200
 LIB_PATH = Path(os.environ.get("TH_B200_LIB", _PKG_ROOT / "lib" / "libth_b200.so"))
 
 TH_F32, TH_BF16, TH_F16 = 0, 1, 2
-ACT_NONE, ACT_SILU, ACT_SOFTPLUS = 0, 1, 2
+ACT_NONE, ACT_SILU, ACT_SOFTPLUS, ACT_GELU, ACT_GELU_TANH = 0, 1, 2, 3, 4
+# activation name of a lowered GEMM plan -> TH_ACT_* code
+ACT_CODES = {None: ACT_NONE, "identity": ACT_NONE, "silu": ACT_SILU, "softplus": ACT_SOFTPLUS, "gelu": ACT_GELU,
+             "gelu_tanh": ACT_GELU_TANH}
 _DTYPES = {torch.float32: TH_F32, torch.bfloat16: TH_BF16, torch.float16: TH_F16}
 
 EXPORTED_SYMBOLS = (

@@ -6,7 +6,7 @@ executes one): here a KernelSpec becomes a plan for one ``th_*`` C-ABI call
 (``include/th_b200.h``).  A ``gemm`` spec's epilogue SSA is matched to the
 fused stages of ``th_gemm``:
 
-    out_segment = residual + act(rowscale * acc + bias)        (act: silu/softplus)
+    out_segment = residual + act(rowscale * acc + bias)        (act: silu/softplus/gelu)
                 | residual + rope(rowscale * acc)
                 | residual + silu(rowscale * acc_gate) * (rowscale * acc_up)
 
@@ -44,7 +44,7 @@ class GemmPlan:
     k: int
     rows: int
     rowscale: tuple[float, float] | None = None    # (inv_k, eps)
-    act: str | None = None                         # "silu" | "softplus"
+    act: str | None = None                         # "silu" | "softplus" | "gelu" | "gelu_tanh" | "identity" (bias only)
     bias: str | None = None                        # const tensor [w] of the act segment
     rope: tuple[str, str, int] | None = None       # (cos, sin, head_dim) const tensors [S, d]
     swiglu: tuple[str, str] | None = None          # (gate rhs, up rhs) for an interleaved weight
@@ -137,8 +137,8 @@ def lower_gemm(spec: KernelSpec, tensors: dict[str, TensorType], fp32_outputs: s
             if v is None:
                 continue
         kind, act, bias, rope = "plain", None, None, None
-        if node is not None and node.op in ("silu", "softplus"):
-            act = node.op
+        if node is not None and node.op in ("silu", "softplus", "gelu"):
+            act = node.op if node.op != "gelu" or node.attrs.get("approximate", "none") == "none" else "gelu_tanh"
             v, node = node.inputs[0], ep.get(node.inputs[0])
             if node is not None and node.op == "add" and len(node.inputs) == 2 and "scalar" not in node.attrs:
                 for a, b in (node.inputs, node.inputs[::-1]):
@@ -148,6 +148,14 @@ def lower_gemm(spec: KernelSpec, tensors: dict[str, TensorType], fp32_outputs: s
                         v, node = a, ep.get(a)
                         break
             kind = "act"
+        elif node is not None and node.op == "add" and len(node.inputs) == 2 and "scalar" not in node.attrs:
+            # a bias without an activation (a Linear's bias): an identity activation segment
+            for a, b in (node.inputs, node.inputs[::-1]):
+                if b in args and args[b].role == "const" and tensors[args[b].tensor].numel == width.get(
+                        _acc_below(spec, ep, a, set(accs)), -1):
+                    act, bias, kind = "identity", args[b].tensor, "act"
+                    v, node = a, ep.get(a)
+                    break
         elif node is not None and node.op == "rope":
             x, c, s = node.inputs
             if args.get(c) is None or args.get(s) is None:

@@ -199,11 +199,11 @@ class CompiledProgram:
         col = 0
         for s in p.segments:
             if s.kind == "act":
-                kw.update(act=lib.ACT_SILU if p.act == "silu" else lib.ACT_SOFTPLUS, act_begin=col, act_end=col + s.width)
+                kw.update(act=lib.ACT_CODES[p.act], act_begin=col, act_end=col + s.width)
             if s.kind != "tail":
                 col += s.width
         if n_tail:
-            act_code = lib.ACT_SILU if p.act == "silu" else lib.ACT_SOFTPLUS
+            act_code = lib.ACT_CODES[p.act]
             kw.update(act=act_code, act_begin=n_main_pad, act_end=n_main_pad + n_tail, out2=tail, tail_begin=n_main_pad)
         if p.bias is not None:
             kw["bias"] = self._param(p.bias, "f32vec", torch.float32)

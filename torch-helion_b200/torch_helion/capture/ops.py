@@ -18,7 +18,8 @@ from __future__ import annotations
 
 LAYOUT_OPS = frozenset({"view", "permute", "expand", "clone", "slice", "cat", "cast"})
 BINARY_OPS = frozenset({"add", "sub", "mul", "div", "max", "powf"})
-UNARY_OPS = frozenset({"exp", "log", "neg", "rsqrt", "sigmoid", "silu", "tanh", "square", "sqrt", "log1p", "softplus"})
+UNARY_OPS = frozenset({"exp", "log", "neg", "rsqrt", "sigmoid", "silu", "tanh", "square", "sqrt", "log1p", "softplus",
+                       "erf", "gelu"})
 REDUCE_OPS = frozenset({"row_sum", "row_max", "row_mean", "row_sumsq"})
 SCAN_OPS = frozenset({"row_cumsum"})
 MACRO_OPS = frozenset({"rmsnorm", "rope", "rotate_half", "attention", "softmax", "ssd", "causal_conv1d", "embedding"})
@@ -26,7 +27,7 @@ ANCHOR_OPS = frozenset({"matmul", "batch_matmul", "attention", "ssd", "causal_co
 ELEMENTWISE_OPS = BINARY_OPS | UNARY_OPS
 
 # Ops a B200 GEMM epilogue executes (th_gemm stages); see torch_helion.b200.lower.
-EPILOGUE_OPS = frozenset({"add", "mul", "softplus", "silu", "rope", "broadcast", "powf", "row_sumsq"})
+EPILOGUE_OPS = frozenset({"add", "mul", "softplus", "silu", "gelu", "rope", "broadcast", "powf", "row_sumsq"})
 
 
 def is_elementwise(op: str) -> bool:
