@@ -13,23 +13,20 @@
 //   cum, dt and colf_l = exp(cum_{l|31} - cum_l) dt_l.  This replaces the
 //   separate chunk-state and inter-chunk passes and their fp32 round trips.
 //
-// ssd_scan_mh -- one CTA per (chunk, set of heads, batch), in two passes:
+// ssd_scan_g -- one CTA per (chunk, set of heads, batch), in two passes:
 //   query rows 128-255 (256 keys), then rows 0-127 (128 keys), so every CTA
 //   carries the same work.  The heads of one B/C group share C.B^T, so each
 //   pass computes it once into TMEM and then, head by head:
 //     G = C.B^T * exp(cum_i - cum_j) dt_j  (j <= i), plus D on the diagonal
-//         (CUDA cores: TMEM -> bf16 128B-swizzled shared-memory operand)
-//     Y = G . x + exp(cum_i) (C . S_in)     (tcgen05, two TMEM buffers)
+//         (CUDA cores, TMEM -> packed fp32 pairs -> bf16 back into TMEM)
+//     Y = G . x + exp(cum_i) (C . S_in)     (tcgen05, G the A operand from TMEM)
 //     y = Y * silu(z) -> shared memory -> TMA store, per-head sum of y^2
-//   D on the diagonal of G makes G . x carry the D x skip, so x can be
-//   released as soon as the MMA has read it.
-//   Below-diagonal 32-column blocks use exp(ci - cj) = exp(ci - c_ref)
-//   exp(c_ref - cj) with c_ref the block's last column (both factors <= 1).
+//   D on the diagonal of G makes G . x carry the D x skip.  Sub-diagonal
+//   blocks use exp(ci - cj) = exp(ci - c_ref) exp(c_ref - cj) with c_ref the
+//   32-key block's last column (neither factor overflows).
 //
-// Warp roles (scan): warp 0 TMA producer, warp 1 MMA issuer, warps 2-9 build
-// G and run the epilogue (two warps per TMEM lane quadrant, splitting the
-// columns).  Every wait is bounded; on a timeout the roles skip their work
-// but still pass every named barrier, so the CTA always drains and frees TMEM.
+// Every wait is bounded; on a timeout the roles skip their work but still
+// pass every barrier, so the CTA always drains and frees TMEM.
 #include "common.cuh"
 
 namespace th {
@@ -488,377 +485,15 @@ __global__ void __launch_bounds__(256) ssd_state_pass(th_ssd_args p, int nc, con
 }
 
 // -------------------------------------------------------------------- scan
-// Shared-memory plan of the scan for d_state NS (64, 128 or 256).  B (up to
-// 256 keys) occupies the G region only until C.B^T is in TMEM; with NS = 256
-// it arrives in two 128-state halves through that region, and x | S_in of a
-// head (64 KB) is single-buffered.
-template <int NS>
-struct ScCfg {
-  static constexpr int KAT = NS / 64;                  // 64-wide state atoms
-  static constexpr int KB = KAT < 2 ? KAT : 2;         // B atoms resident at a time
-  static constexpr int C_BYTES = KAT * 128 * 128;      // 128 query rows
-  static constexpr int B_BYTES = KB * CK_L * 128;      // up to 256 keys
-  static constexpr int G_BYTES = 4 * 128 * 128;        // 128 rows x 256 keys
-  static constexpr int BG_BYTES = B_BYTES > G_BYTES ? B_BYTES : G_BYTES;
-  static constexpr int X_BYTES = CK_L * 128;
-  static constexpr int S_BYTES = NS * 128;
-  static constexpr int STAGES = NS > 128 ? 1 : 2;
-  static constexpr int STAGE = X_BYTES + S_BYTES;
-  static constexpr int OFF_C = 0, OFF_B = C_BYTES, OFF_G = OFF_B;  // G replaces B once C.B^T is in TMEM
-  static constexpr int OFF_X = OFF_B + BG_BYTES;                    // stages of x | S_in
-  static constexpr int OFF_Y = OFF_X + STAGES * STAGE;              // z in, y out: 128 rows x 64
-  static constexpr int OFF_SC = OFF_Y + 128 * 128;                  // scalar ring
-  static constexpr int OFF_R = OFF_SC + CK_SR * CK_SCAL * 4;        // row partials of sum y^2
-  static constexpr int OFF_BAR = OFF_R + 4 * 128 * 4;
-  static constexpr int SMEM = 1024 + OFF_BAR + 200;
-  static_assert(SMEM <= 227 * 1024, "shared memory budget");
-  static_assert(OFF_X % 1024 == 0 && OFF_Y % 1024 == 0, "128-byte swizzle atoms");
-};
-
 struct ScMaps {
   CUtensorMap C, B256, B128, X256, X128, S, Y, Z;
 };
-
-constexpr int SC_MATH = 512;  // 16 math warps: 4 per TMEM lane quadrant
-
-
-template <typename T, int NS>
-__global__ void __launch_bounds__(64 + SC_MATH, 1)
-    ssd_scan_mh(const __grid_constant__ ScMaps mp, th_ssd_args p, int nc, int hs, int nsets,
-                const float* __restrict__ scal) {
-  using ScC = ScCfg<NS>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = smem_align<1024>(smem_raw);
-  float* red = reinterpret_cast<float*>(sm + ScC::OFF_R);  // [4][128] row partials of sum y^2
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + ScC::OFF_BAR);
-  uint64_t* cb_full = bar + 0;
-  uint64_t* cb_done = bar + 1;
-  uint64_t* full = bar + 2;      // [2]
-  uint64_t* empty = bar + 4;     // [2]
-  uint64_t* g_full = bar + 6;
-  uint64_t* g_free = bar + 7;
-  uint64_t* y_full = bar + 8;    // [2]
-  uint64_t* y_empty = bar + 10;  // [2]
-  uint64_t* sc_full = bar + 12;  // [CK_SR]
-  uint64_t* sc_free = bar + 16;  // [CK_SR]
-  uint64_t* z_full = bar + 20;
-  uint64_t* y_ready = bar + 21;
-  uint64_t* b_free = bar + 22;  // d_state 256: the first half of B has been read by the C.B^T MMA
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 23);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
-
-  // one CTA per (chunk, head set, batch) does the rows 128-255 (256 keys) and then the rows 0-127
-  // (128 keys) of its heads, so every CTA carries the same work
-  const int hpg = p.heads / p.ngroups;
-  int u = (int)blockIdx.x;
-  const int set = u % (p.ngroups * nsets);
-  u /= p.ngroups * nsets;
-  const int c = u % nc, b = u / nc;
-  const int g = set / nsets, h0 = g * hpg + (set % nsets) * hs;
-  const int hcount = min(hs, g * hpg + hpg - h0);
-  const int s0 = c * CK_L, len = min(CK_L, p.seq - s0);
-  if (hcount <= 0) return;  // nothing to compute (uniform over the CTA)
-  const bool has_s = c > 0, has_z = p.z != nullptr;
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) *abort_flag = 0;
-  if (warp == 1) tmem_alloc(tslot, 512);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tslot;
-  pdl_wait();  // the previous kernel's outputs (this kernel's inputs) are complete
-  pdl_trigger();
-  for (int pass = 0; pass < 2; ++pass) {
-  const int qb = 1 - pass;
-  if (qb * 128 >= len) continue;  // a chunk of at most 128 rows has no second half (uniform)
-  const int nk = qb ? 256 : 128;
-  if (tid == 0) {  // fresh barriers for each pass (the previous pass has fully drained)
-    uint64_t* all = bar;
-    if (pass > 0)
-      for (int i = 0; i < 23; ++i) mbar_inval(&all[i]);  // bar[0..22]; bar[23] holds the TMEM address
-    mbar_init(cb_full, 1);
-    mbar_init(cb_done, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
-      mbar_init(&y_full[i], 1);
-      mbar_init(&y_empty[i], 1);
-    }
-    mbar_init(g_full, 1);
-    mbar_init(g_free, 1);
-    for (int i = 0; i < CK_SR; ++i) { mbar_init(&sc_full[i], 1); mbar_init(&sc_free[i], 1); }
-    mbar_init(z_full, 1);
-    mbar_init(y_ready, 1);
-    mbar_init(b_free, 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  const float* scal_bc = scal + ((int64_t)b * p.heads * nc + c) * CK_SCAL;  // + head * nc * CK_SCAL
-
-  if (warp == 0) {
-    // TMA producer; it also stores each head's y tile and refills the tile with the next head's z
-    if (lane == 0) {
-      const CUtensorMap* tB = qb ? &mp.B256 : &mp.B128;
-      const CUtensorMap* tX = qb ? &mp.X256 : &mp.X128;
-      auto load_xs = [&](int k) {
-        const int s = ScC::STAGES == 2 ? (k & 1) : 0;
-        uint8_t* st = sm + ScC::OFF_X + s * ScC::STAGE;
-        mbar_arrive_expect_tx(&full[s], nk * 128 + (has_s ? ScC::S_BYTES : 0));
-        tma_load_3d(st, tX, &full[s], (h0 + k) * CK_P, s0, b);
-        if (has_s) tma_load_2d(st + ScC::X_BYTES, &mp.S, &full[s], 0, (((b * nc + c) * p.heads) + h0 + k) * NS);
-      };
-      auto load_sc = [&](int k) {
-        const int j = k % CK_SR;
-        mbar_arrive_expect_tx(&sc_full[j], CK_SCAL * 4);
-        bulk_load(sm + ScC::OFF_SC + j * CK_SCAL * 4, scal_bc + (int64_t)(h0 + k) * nc * CK_SCAL, CK_SCAL * 4,
-                  &sc_full[j]);
-      };
-      auto store_y = [&](int k) -> bool {  // y of head k is in the tile
-        if (!mbar_wait(y_ready, k & 1, abort_flag)) return false;
-        tma_store_3d(&mp.Y, sm + ScC::OFF_Y, (h0 + k) * CK_P, s0 + qb * 128, b);
-        bulk_commit();
-        bulk_wait_read0();
-        return true;
-      };
-      mbar_arrive_expect_tx(cb_full, ScC::C_BYTES + ScC::KB * nk * 128);
-      for (int a = 0; a < ScC::KAT; ++a) {
-        tma_load_3d(sm + ScC::OFF_C + a * 128 * 128, &mp.C, cb_full, g * NS + a * 64, s0 + qb * 128, b);
-        if (a < ScC::KB) tma_load_3d(sm + ScC::OFF_B + a * nk * 128, tB, cb_full, g * NS + a * 64, s0, b);
-      }
-      bool ok = true;
-      if constexpr (ScC::KAT > ScC::KB) {  // the second half of B once the MMA has read the first
-        ok = mbar_wait(b_free, 0, abort_flag);
-        if (ok) {
-          mbar_arrive_expect_tx(cb_full, (ScC::KAT - ScC::KB) * nk * 128);
-          for (int a = ScC::KB; a < ScC::KAT; ++a)
-            tma_load_3d(sm + ScC::OFF_B + (a - ScC::KB) * nk * 128, tB, cb_full, g * NS + a * 64, s0, b);
-        }
-      }
-      for (int k = 0; k < min(CK_SR, hcount); ++k) load_sc(k);
-      load_xs(0);
-      for (int k = 0; ok && k < hcount; ++k) {
-        // x | S_in of head k+1 once the MMA of head k+1-STAGES has read its slot
-        if (k + 1 < hcount) {
-          const int prev = k + 1 - ScC::STAGES;  // the head that last used the slot
-          const int ps = ScC::STAGES == 2 ? (prev & 1) : 0, pph = ScC::STAGES == 2 ? ((prev >> 1) & 1) : (prev & 1);
-          if (prev >= 0 && !(ok = mbar_wait(&empty[ps], pph, abort_flag))) break;
-          load_xs(k + 1);
-        }
-        // scalars of head k+4 once G of head k has read them
-        if (k + CK_SR < hcount) {
-          if (!(ok = mbar_wait(&sc_free[k % CK_SR], (k / CK_SR) & 1, abort_flag))) break;
-          load_sc(k + CK_SR);
-        }
-        // y of head k-1 out, z of head k in
-        if (k >= 1 && !(ok = store_y(k - 1))) break;
-        if (has_z) {
-          mbar_arrive_expect_tx(z_full, 128 * 128);
-          tma_load_3d(sm + ScC::OFF_Y, &mp.Z, z_full, (h0 + k) * CK_P, s0 + qb * 128, b);
-        }
-      }
-      if (ok) store_y(hcount - 1);
-      bulk_wait0();
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr int fmt = DT<T>::id == TH_BF16 ? 1 : 0;
-      const uint32_t cA = smem_u32(sm + ScC::OFF_C), bA = smem_u32(sm + ScC::OFF_B), gA = smem_u32(sm + ScC::OFF_G);
-      bool ok = mbar_wait(cb_full, 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        const uint32_t id_cb = make_idesc_f16(128, nk, fmt, 0, 0);
-        for (int kk = 0; kk < NS / 16; ++kk) {
-          if constexpr (ScC::KAT > ScC::KB) {
-            if (kk == ScC::KB * 4) {  // d_state 256: the second half of B replaces the first
-              tc_commit(b_free);
-              if (!(ok = mbar_wait(cb_full, 1, abort_flag))) break;
-              tc_fence_after();
-            }
-          }
-          const int ba = (kk >> 2) & (ScC::KB - 1);  // B atom slot (KB is 1 or 2)
-          const uint64_t ad = make_desc_sw128(cA + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = make_desc_sw128(bA + ba * nk * 128 + (kk & 3) * 32, 16, 1024);
-          tc_mma_f16(tmem, ad, bd, id_cb, kk ? 1u : 0u);
-        }
-        tc_commit(cb_done);
-      }
-      constexpr uint32_t id_y = make_idesc_f16(128, 64, fmt, 0, 1);  // B operand (x, S_in) MN-major
-      for (int k = 0; ok && k < hcount; ++k) {
-        const int s = k & 1, xs = ScC::STAGES == 2 ? s : 0;  // TMEM Y buffer, x | S_in stage
-        const int xph = ScC::STAGES == 2 ? ((k >> 1) & 1) : (k & 1);
-        ok = mbar_wait(&full[xs], xph, abort_flag) && mbar_wait(g_full, k & 1, abort_flag) &&
-             (k < 2 || mbar_wait(&y_empty[s], ((k >> 1) - 1) & 1, abort_flag));
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t yd = tmem + 256 + s * 128;
-        const uint32_t xA = smem_u32(sm + ScC::OFF_X + xs * ScC::STAGE), sA = xA + ScC::X_BYTES;
-        for (int kk = 0; kk < nk / 16; ++kk) {
-          const uint64_t ad = make_desc_sw128(gA + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = make_desc_sw128(xA + kk * 2048, nk * 128, 1024);
-          tc_mma_f16(yd, ad, bd, id_y, kk ? 1u : 0u);
-        }
-        if (has_s) {
-          for (int kk = 0; kk < NS / 16; ++kk) {
-            const uint64_t ad = make_desc_sw128(cA + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = make_desc_sw128(sA + kk * 2048, NS * 128, 1024);
-            tc_mma_f16(yd + 64, ad, bd, id_y, kk ? 1u : 0u);
-          }
-        }
-        tc_commit(g_free);
-        tc_commit(&empty[xs]);
-        tc_commit(&y_full[s]);
-      }
-    }
-  } else {
-    // math threads: quadrant q of TMEM lanes (rows), column quarter cq
-    const int mt = tid - 64;
-    const int q = warp & 3, cq = (warp - 2) >> 2;
-    const int r = q * 32 + lane;      // row within the query half (TMEM lane)
-    const int i = qb * 128 + r;       // row within the chunk
-    const int R = qb * 128 + q * 32;  // first row of this warp
-    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
-    const int bpq = nk / 128;         // 32-column blocks of G per quarter
-    const int64_t trow = (int64_t)b * p.seq + s0 + i;
-    bool ok = true;
-    float e_prev = 0.f, e_cur = 0.f;
-    for (int k = 0; k <= hcount; ++k) {
-      // ---------------------------------------------------------- G for head k
-      if (k < hcount) {
-        const int j = k % CK_SR;
-        if (k == 0) ok = ok && mbar_wait(cb_done, 0, abort_flag);
-        else ok = ok && mbar_wait(g_free, (k - 1) & 1, abort_flag);
-        ok = ok && mbar_wait(&sc_full[j], (k / CK_SR) & 1, abort_flag);
-        ok = __all_sync(0xffffffffu, ok);
-        if (ok) {
-          tc_fence_after();
-          const float* cum = reinterpret_cast<const float*>(sm + ScC::OFF_SC + j * CK_SCAL * 4);
-          const float* dts = cum + CK_L;
-          const float* colf = dts + CK_L;
-          const float Dh = colf[CK_L];
-          const float ci = cum[i];
-          e_cur = __expf(ci);
-          uint8_t* gb = sm + ScC::OFF_G;
-          // this quarter's 32-column blocks (2 heavy / 1 light); per block both TMEM loads, one wait
-          const int jb0 = cq * bpq;
-          for (int bb = 0; bb < bpq; ++bb) {
-            const int j0 = (jb0 + bb) * 32;
-            if (j0 > R) {  // above the diagonal: zeros
-              float zz[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-              for (int e8 = 0; e8 < 32; e8 += 8) store8<T>(reinterpret_cast<T*>(gb + sw128_off(r, j0 + e8, 128)), zz);
-              continue;
-            }
-            uint32_t raw[2][16];
-            tmem_ld16_issue(tl + j0, raw[0]);
-            tmem_ld16_issue(tl + j0 + 16, raw[1]);
-            const float dref = ci - cum[j0 + 31];  // <= 0 below the diagonal block
-            const bool fact = dref < 80.f;         // exp(ci - cj) = exp(ci - c_ref) exp(c_ref - cj) cannot overflow
-            const float rf = __expf(fact ? dref : 0.f);
-            tmem_wait_ld(raw[0]);
-            tmem_wait_ld(raw[1]);
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-              const int jc = j0 + hf * 16;
-              float v[16];
-#pragma unroll
-              for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(raw[hf][e]);
-              if (fact) {
-                const float4* cf4 = reinterpret_cast<const float4*>(colf + jc);  // 16-byte aligned: jc % 16 == 0
-#pragma unroll
-                for (int e4 = 0; e4 < 4; ++e4) {
-                  const float4 cf = cf4[e4];
-                  v[4 * e4 + 0] *= rf * cf.x;
-                  v[4 * e4 + 1] *= rf * cf.y;
-                  v[4 * e4 + 2] *= rf * cf.z;
-                  v[4 * e4 + 3] *= rf * cf.w;
-                }
-              } else {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) v[e] *= __expf(ci - cum[jc + e]) * dts[jc + e];
-              }
-              if (j0 == R) {  // diagonal block: causal mask and the D skip
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                  const int jj = jc + e;
-                  v[e] = jj < i ? v[e] : (jj == i ? v[e] + Dh : 0.f);
-                }
-              }
-#pragma unroll
-              for (int e8 = 0; e8 < 16; e8 += 8)
-                store8<T>(reinterpret_cast<T*>(gb + sw128_off(r, jc + e8, 128)), v + e8);
-            }
-          }
-          fence_proxy_async();
-          tc_fence_before();
-        }
-        named_bar(1, SC_MATH);
-        if (mt == SC_MATH - 1) {  // a thread that issues no global stores: its arrive releases nothing slow
-          mbar_arrive(g_full);
-          mbar_arrive(&sc_free[j]);
-        }
-      }
-      // --------------------------------------------------- epilogue of head k-1
-      if (k >= 1) {
-        const int kh = k - 1, s = kh & 1;
-        const int hh = h0 + kh;
-        if (has_z) ok = ok && mbar_wait(z_full, kh & 1, abort_flag);
-        ok = ok && mbar_wait(&y_full[s], (kh >> 1) & 1, abort_flag);
-        ok = __all_sync(0xffffffffu, ok);
-        float ss = 0.f;
-        if (ok) {
-          uint32_t ry[16], ro[16];
-          tc_fence_after();
-          const uint32_t ya = tl + 256 + s * 128 + cq * 16;
-          tmem_ld16_issue(ya, ry);
-          if (has_s) tmem_ld16_issue(ya + 64, ro);
-          tmem_wait_ld(ry);
-          tmem_wait_ld(ro);
-          tc_fence_before();
-          float yv[16], yo[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) { yv[e] = __uint_as_float(ry[e]); yo[e] = __uint_as_float(ro[e]); }
-          uint8_t* yb = sm + ScC::OFF_Y;  // holds z of this head (when gated); y is written in place
-#pragma unroll
-          for (int c8 = 0; c8 < 2; ++c8) {
-            T* at = reinterpret_cast<T*>(yb + sw128_off(r, cq * 16 + c8 * 8, 128));
-            float zf[8], o[8];
-            if (has_z) load8<T>(at, zf);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              float y = yv[c8 * 8 + e];
-              if (has_s) y += e_prev * yo[c8 * 8 + e];
-              if (has_z) y *= silu_tanh(zf[e]);
-              o[e] = y;
-            }
-            ss += store8_ss<T>(at, o);  // sum of squares of the stored (rounded) values
-          }
-          fence_proxy_async();
-          red[cq * 128 + r] = ss;
-        }
-        named_bar(1, SC_MATH);
-        if (mt == SC_MATH - 1) {
-          mbar_arrive(&y_empty[s]);
-          mbar_arrive(y_ready);
-        }
-        if (ok && cq == 0 && i < len && p.gss)
-          p.gss[trow * p.ldgss + hh] = red[r] + red[128 + r] + red[256 + r] + red[384 + r];
-      }
-      e_prev = e_cur;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();  // this pass has drained: every store, load and MMA is complete
-  tc_fence_after();
-  }  // pass
-  if (warp == 1) tmem_dealloc(tmem, 512);
-}
 
 // ------------------------------------------------------- scan, G in TMEM
 // ssd_scan_g -- the scan with the decay-masked operand G held in tensor
 // memory and separate warp groups for building G and for the epilogue, so
 // head k's epilogue runs while head k+1's G is built and head k+1's MMAs
-// run.  Same CTA decomposition as ssd_scan_mh (chunk, head set, batch; query
+// run.  One CTA per (chunk, head set, batch; query
 // rows 128-255 against 256 keys, then rows 0-127 against 128 keys).
 //
 // TMEM (512 columns): C.B^T fp32 in [0, 256) (one column per key), a ring of
@@ -1288,8 +923,8 @@ __global__ void __maxnreg__(72)
 
 template <typename T, int NS>
 static int ssd_scan_launch(const ScMaps& m, const th_ssd_args* a, int nc, cudaStream_t st) {
-  using Cf = ScCfg<NS>;
-  if (int rc = smem_limit(ssd_scan_mh<T, NS>, Cf::SMEM, "th_ssd(scan, tcgen05 multi-head)")) return rc;
+  using Gf = SgCfg<NS>;
+  if (int rc = smem_limit(ssd_scan_g<T, NS>, Gf::SMEM, "th_ssd(scan, G in TMEM)")) return rc;
   // head sets: about one CTA per SM
   const int hpg = a->heads / a->ngroups;
   const int per = a->batch * nc * a->ngroups;
@@ -1298,17 +933,6 @@ static int ssd_scan_launch(const ScMaps& m, const th_ssd_args* a, int nc, cudaSt
   const int hs = (hpg + nsets - 1) / nsets;
   nsets = (hpg + hs - 1) / hs;
   const int units = per * nsets;
-  static const bool old_scan = [] {  // TH_SSD_SCAN=mh selects the earlier scan (G in shared memory)
-    const char* e = getenv("TH_SSD_SCAN");
-    return e && e[0] == 'm';
-  }();
-  if (old_scan) {
-    launch_pdl(ssd_scan_mh<T, NS>, dim3(units), dim3(64 + SC_MATH), Cf::SMEM, st, m, *a, nc, hs, nsets,
-               reinterpret_cast<const float*>(a->workspace));
-    return TH_OK;
-  }
-  using Gf = SgCfg<NS>;
-  if (int rc = smem_limit(ssd_scan_g<T, NS>, Gf::SMEM, "th_ssd(scan, G in TMEM)")) return rc;
   launch_pdl(ssd_scan_g<T, NS>, dim3(units), dim3(SG_THREADS), Gf::SMEM, st, m, *a, nc, hs, nsets,
              reinterpret_cast<const float*>(a->workspace));
   return TH_OK;
