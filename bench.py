@@ -288,6 +288,8 @@ def main() -> None:
     ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3", "c4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp-chunks", type=int, default=4, help="c3 tensor parallel: row chunks of the all-reduce overlap")
+    ap.add_argument("--tp-comm-sms", type=int, default=24,
+                    help="c3 tensor parallel: SMs the overlapped GEMMs leave to the all-reduces (0 = none)")
     args = ap.parse_args()
 
     if args.impl == "reference":
@@ -316,7 +318,8 @@ def main() -> None:
     res = compile_model(model, (x,), CompileConfig(run_name=f"bench_{args.workload}_r{rank}", device=str(dev),
                                                    verify_passes=False, reference_check=False,
                                                    results_dir=REPO / "results", world_size=world if tp else 1,
-                                                   tp_mode="heads" if tp else None, tp_chunks=args.tp_chunks))
+                                                   tp_mode="heads" if tp else None, tp_chunks=args.tp_chunks,
+                                                   tp_comm_sms=args.tp_comm_sms))
     mod = res.module
     prog = mod.program  # this rank's program (its tensor-parallel shard under TP)
     tokens = x.shape[0] * x.shape[1]
@@ -442,7 +445,8 @@ def main() -> None:
         dt_name = {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[mod.dtype]
         if tp:
             par = (f"tp{n}: heads and FFN columns, NCCL all-reduce after o_proj and after down_proj, "
-                   f"{args.tp_chunks} row chunks overlapping the all-reduces with the GEMMs")
+                   f"{args.tp_chunks} row chunks overlapping the all-reduces with the GEMMs, "
+                   f"which leave {args.tp_comm_sms} SMs to them")
             launch = "eager launches; NCCL all-reduces on a second stream"
             entry = ("CompileResult.streaming_runner -> ShardedStreamingRunner: each rank copies its 1/N of the "
                      "rows in and out of pinned host memory, NCCL all-gather of the input rows, tensor-parallel "

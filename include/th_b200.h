@@ -160,6 +160,9 @@ typedef struct {
   /* 7. sum-of-squares partials of the stored output, one per 64 columns */
   float* ss_out;
   int64_t ss_ld;
+  /* SMs the kernel's persistent grid may occupy (0 = all): leaves the rest to
+   * work that runs beside it, e.g. a collective on another stream */
+  int32_t sm_limit;
 } th_gemm_args;
 int th_gemm(const th_gemm_args* a, void* stream);
 

@@ -757,6 +757,13 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const T* __restrict__ A,
 }
 
 // ------------------------------------------------------------------- host
+// SMs this launch's persistent grid may occupy: all of them, or the caller's
+// sm_limit (at least one CTA pair).
+static int gemm_sms(const th_gemm_args* a) {
+  const int all = sm_count();
+  return a->sm_limit > 0 && a->sm_limit < all ? (a->sm_limit < 2 ? 2 : a->sm_limit) : all;
+}
+
 template <typename T, int BN, int EPI>
 static int launch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st) {
   using C = TcCfg<BN>;
@@ -768,7 +775,7 @@ static int launch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st
   if ((rc = smem_limit(gemm_tc_kernel<T, BN, EPI>, C::SMEM_BYTES, "th_gemm(tcgen05)"))) return rc;
   const int tiles_m = (int)((a->m + C::BM - 1) / C::BM), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n;
-  const int grid = ntiles < sm_count() ? ntiles : sm_count();
+  const int grid = ntiles < gemm_sms(a) ? ntiles : gemm_sms(a);
   launch_pdl(gemm_tc_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb, ep, (int)a->k, tiles_m,
              tiles_n);
   return check_launch("th_gemm(tcgen05)");
@@ -784,7 +791,7 @@ static int launch_tc2(const th_gemm_args* a, const EpiParams& ep, cudaStream_t s
   if (rc) return rc;
   if ((rc = smem_limit(gemm_tc2_kernel<T, BN, EPI>, C::SMEM_BYTES, "th_gemm(tcgen05 pair)"))) return rc;
   const int tiles_m = (int)((a->m + 2 * C::BM - 1) / (2 * C::BM)), tiles_n = (int)((a->n + BN - 1) / BN);
-  const int ntiles = tiles_m * tiles_n, pairs = sm_count() / 2;
+  const int ntiles = tiles_m * tiles_n, pairs = gemm_sms(a) / 2;
   const int grid = 2 * (ntiles < pairs ? ntiles : pairs);
   launch_pdl(gemm_tc2_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb, ep, (int)a->k, tiles_m,
              tiles_n);
@@ -804,7 +811,7 @@ static int pair_mode() {  // TH_GEMM_PAIR: 0 single-CTA kernel, 1 (default) pair
 }
 
 static int pair_width(const th_gemm_args* a) {
-  const int64_t tm = (a->m + 255) / 256, pairs = sm_count() / 2;
+  const int64_t tm = (a->m + 255) / 256, pairs = gemm_sms(a) / 2;
   const bool no192 = a->swiglu || a->rope_cos || a->ss_out;
   const int forced = pair_mode();
   if (forced == 256 || forced == 128 || (forced == 192 && !no192)) return forced;
@@ -834,7 +841,7 @@ static int dispatch_tc2(const th_gemm_args* a, const EpiParams& ep, cudaStream_t
 
 // The pair kernel serves every 2-byte GEMM with more than one 128-row tile
 // (TH_GEMM_PAIR=0 in the environment selects the single-CTA kernel instead).
-static bool use_pair(const th_gemm_args* a) { return pair_mode() != 0 && a->m > 128 && sm_count() >= 2; }
+static bool use_pair(const th_gemm_args* a) { return pair_mode() != 0 && a->m > 128 && gemm_sms(a) >= 2; }
 
 static bool is_al16(const void* p) { return p == nullptr || aligned16(p); }
 
@@ -901,7 +908,7 @@ extern "C" int th_gemm(const th_gemm_args* a, void* stream) {
     return fail(TH_EALIGN, "th_gemm: a/w must be 16-B aligned with lda, ldw multiples of 8");
   bool wide = a->n >= 256 && (!a->rope_cos || 256 % a->rope_head_dim == 0);
   if (wide) {  // narrow tiles when they cut the wave-quantised work by a fifth or more
-    const int64_t tm = (a->m + 127) / 128, sms = sm_count();
+    const int64_t tm = (a->m + 127) / 128, sms = gemm_sms(a);
     const int64_t r256 = (tm * ((a->n + 255) / 256) + sms - 1) / sms, r128 = (tm * ((a->n + 127) / 128) + sms - 1) / sms;
     if (r128 * 128 * 5 <= r256 * 256 * 4) wide = false;
   }

@@ -58,7 +58,7 @@ class GemmArgs(ctypes.Structure):
         ("rope_seq", _i32),
         ("swiglu", _i32), ("residual", _vp), ("ld_res", _i64),
         ("out2", _vp), ("ld_out2", _i64), ("tail_begin", _i32),
-        ("ss_out", _vp), ("ss_ld", _i64),
+        ("ss_out", _vp), ("ss_ld", _i64), ("sm_limit", _i32),
     ]
 
 
@@ -208,7 +208,7 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, rs_parts: torch
          bias: torch.Tensor | None = None, rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
          rope_begin: int = 0, rope_end: int = 0, rope_head_dim: int = 0, swiglu: bool = False,
          residual: torch.Tensor | None = None, out2: torch.Tensor | None = None, tail_begin: int = 0,
-         ss_out: torch.Tensor | None = None) -> torch.Tensor:
+         ss_out: torch.Tensor | None = None, sm_limit: int = 0) -> torch.Tensor:
     """``out = epilogue(a @ w.T)``; see ``th_gemm`` in include/th_b200.h."""
     m, k, lda = _rows(a)
     n, k2, ldw = _rows(w)
@@ -237,6 +237,7 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, *, rs_parts: torch
         args.out2, args.ld_out2, args.tail_begin = out2.data_ptr(), _rows(out2)[2], tail_begin
     if ss_out is not None:
         args.ss_out, args.ss_ld = ss_out.data_ptr(), _rows(ss_out)[2]
+    args.sm_limit = int(sm_limit)
     _check(load().th_gemm(ctypes.byref(args), _stream()), "th_gemm")
     return out
 

@@ -54,7 +54,7 @@ class CompiledProgram:
 
     def __init__(self, program: Program, params: dict[str, torch.Tensor], device: str | torch.device = "cuda",
                  tp_rank: int = 0, tp_world: int = 1, allreduce: Callable[[torch.Tensor], None] | None = None,
-                 shared_params: dict | None = None, tp_chunks: int = 4) -> None:
+                 shared_params: dict | None = None, tp_chunks: int = 4, tp_comm_sms: int = 24) -> None:
         if not torch.cuda.is_available():
             raise lib.B200KernelError("CompiledProgram needs a CUDA device (there is no CPU fallback)")
         lib.load()
@@ -71,6 +71,10 @@ class CompiledProgram:
         self._ssd_ws: torch.Tensor | None = None
         self.tp_rank, self.tp_world, self.allreduce = tp_rank, tp_world, allreduce
         self.tp_chunks = tp_chunks
+        # SMs left to the collectives while the chunked schedule overlaps them with GEMMs: the GEMMs'
+        # persistent grids are capped at (SMs - tp_comm_sms) there, so NCCL's kernels get SMs at once
+        self.tp_comm_sms = tp_comm_sms
+        self._gemm_sm_limit = 0  # read by every GEMM launch when it runs
         self._pipe: tuple | None = None  # chunked tensor-parallel schedule (see _plan_tp_pipeline)
         with torch.cuda.device(self.device):
             self._build()
@@ -231,8 +235,9 @@ class CompiledProgram:
                 kr = dict(kw)
                 for k in row_kw:
                     kr[k] = kw[k][r0:r1]
-                lib.gemm(lhs[r0:r1], W, d[r0:r1], **kr)
-        self.launches.append(KernelLaunch(kname, "gemm", lambda lhs=lhs, W=W, d=d, kw=kw: lib.gemm(lhs, W, d, **kw),
+                lib.gemm(lhs[r0:r1], W, d[r0:r1], sm_limit=self._gemm_sm_limit, **kr)
+        self.launches.append(KernelLaunch(kname, "gemm", lambda lhs=lhs, W=W, d=d, kw=kw: lib.gemm(
+            lhs, W, d, sm_limit=self._gemm_sm_limit, **kw),
                                           fn_rows))
         if self._allreduced(spec):
             buf = out  # the whole (contiguous) buffer; zero-weight pad columns sum to zero
@@ -331,6 +336,14 @@ class CompiledProgram:
         main = torch.cuda.current_stream()
         for l in prefix:
             l.fn()
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self._gemm_sm_limit = max(2, sms - self.tp_comm_sms) if self.tp_comm_sms > 0 else 0
+        try:
+            self._run_chunks(pre, post, bounds, comm, main)
+        finally:
+            self._gemm_sm_limit = 0
+
+    def _run_chunks(self, pre, post, bounds, comm, main) -> None:
 
         def collective(l, r0, r1) -> torch.cuda.Event:
             ready = torch.cuda.Event()

@@ -39,6 +39,7 @@ class CompileConfig:
       world_size / tp_mode  tensor parallelism ("heads" for the Llama block)
       tp_chunks          row chunks of the tensor-parallel part after attention:
                          each chunk's all-reduce overlaps the next chunk's GEMMs
+      tp_comm_sms        SMs the GEMMs of that overlapped part leave to the collectives
       measure_iters      time the forward on the device (0 = skip)
     """
 
@@ -68,6 +69,7 @@ class CompileConfig:
     world_size: int = 1
     tp_mode: str | None = None
     tp_chunks: int = 4
+    tp_comm_sms: int = 24
     measure_iters: int = 0
 
     @property
