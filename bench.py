@@ -288,6 +288,8 @@ def main() -> None:
     ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3", "c4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp-chunks", type=int, default=4, help="c3 tensor parallel: row chunks of the all-reduce overlap")
+    ap.add_argument("--tp-allreduce", choices=["auto", "multimem", "nccl"], default="auto",
+                    help="c3 tensor parallel: all-reduce through NVSwitch multicast (th_allreduce) or NCCL")
     ap.add_argument("--tp-comm-sms", type=int, default=24,
                     help="c3 tensor parallel: SMs the overlapped GEMMs leave to the all-reduces (0 = none)")
     args = ap.parse_args()
@@ -319,7 +321,7 @@ def main() -> None:
                                                    verify_passes=False, reference_check=False,
                                                    results_dir=REPO / "results", world_size=world if tp else 1,
                                                    tp_mode="heads" if tp else None, tp_chunks=args.tp_chunks,
-                                                   tp_comm_sms=args.tp_comm_sms))
+                                                   tp_comm_sms=args.tp_comm_sms, tp_allreduce=args.tp_allreduce))
     mod = res.module
     prog = mod.program  # this rank's program (its tensor-parallel shard under TP)
     tokens = x.shape[0] * x.shape[1]
@@ -444,10 +446,12 @@ def main() -> None:
         cb = None if (args.no_cpu_baseline or n > 1) else cpu_baseline(cfg, model, x)
         dt_name = {torch.bfloat16: "bf16", torch.float16: "fp16", torch.float32: "fp32"}[mod.dtype]
         if tp:
-            par = (f"tp{n}: heads and FFN columns, NCCL all-reduce after o_proj and after down_proj, "
+            how = ("th_allreduce (NVSwitch multicast, in place on symmetric buffers)" if mod._multimem
+                   else "NCCL all-reduce")
+            par = (f"tp{n}: heads and FFN columns, {how} after o_proj and after down_proj, "
                    f"{args.tp_chunks} row chunks overlapping the all-reduces with the GEMMs, "
                    f"which leave {args.tp_comm_sms} SMs to them")
-            launch = "eager launches; NCCL all-reduces on a second stream"
+            launch = f"eager launches; {'th_allreduce kernels' if mod._multimem else 'NCCL all-reduces'} on a second stream"
             entry = ("CompileResult.streaming_runner -> ShardedStreamingRunner: each rank copies its 1/N of the "
                      "rows in and out of pinned host memory, NCCL all-gather of the input rows, tensor-parallel "
                      "forward; copies overlapped with neighbouring forwards")
@@ -479,6 +483,7 @@ def main() -> None:
         }
         if dist is not None:
             line["nccl"] = {"backend": dist.get_backend(), "ranks": dist.get_world_size(),
+                            "tp_allreduce": "multimem" if getattr(mod, "_multimem", False) else "nccl",
                             "nvls_env": os.environ.get("NCCL_NVLS_ENABLE", "unset (NCCL default)"),
                             "nccl_version": ".".join(map(str, torch.cuda.nccl.version()))}
         print(json.dumps(line), flush=True)

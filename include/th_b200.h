@@ -263,6 +263,38 @@ typedef struct {
 } th_embedding_args;
 int th_embedding(const th_embedding_args* a, void* stream);
 
+/* --------------------------------------------------------------- allreduce
+ * In-place sum all-reduce of bytes [offset, offset + bytes) of a symmetric
+ * buffer across `world` ranks on one NVSwitch node, through the switch's
+ * multicast (multimem.ld_reduce / multimem.st; NVLS).  Replaces the NCCL
+ * all-reduce the tensor-parallel Llama block runs after its row-split
+ * projections (the reference has no multi-GPU path; the exchange itself is
+ * the standard Megatron split: o_proj and down_proj partial sums).
+ *
+ * Every rank calls it with the same offset, bytes, dtype and ctas, in the
+ * same order (like any collective), each on its own GPU.  Rank r reduces
+ * slice r (bytes / world) of the range and writes the sum to every rank.
+ * `sig` is this rank's TH_ALLREDUCE_SIGNAL_BYTES signal pad (zeroed once
+ * before the first call, on every rank, before any rank calls), `peer_sig` a
+ * device array of `world` pointers to every rank's pad as mapped in this
+ * process.  bf16 / f16 are summed with fp32 accumulation.  bytes must be a
+ * multiple of 16 x world; `mc + offset` and `sig` 16-byte aligned.  The
+ * handshakes wait at most 2 s: then the device error word reports
+ * TH_DEVERR_MBAR_TIMEOUT and the range is left partly reduced.  ctas: grid
+ * size (0 = 32, at most TH_ALLREDUCE_MAX_CTAS); every rank must pass the same
+ * value.  world == 1 returns at once. */
+#define TH_ALLREDUCE_MAX_CTAS 256
+#define TH_ALLREDUCE_MAX_WORLD 8
+#define TH_ALLREDUCE_SIGNAL_BYTES 20480
+typedef struct {
+  void* mc;               /* multicast address of the buffer (offset 0) */
+  void* const* peer_sig;  /* device array [world] of signal-pad pointers */
+  void* sig;              /* this rank's signal pad */
+  int64_t offset, bytes;
+  int32_t dtype, rank, world, ctas;
+} th_allreduce_args;
+int th_allreduce(const th_allreduce_args* a, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -6,3 +6,4 @@
 #include "attention.cu"
 #include "ssd.cu"
 #include "selftest.cu"
+#include "allreduce.cu"

@@ -97,6 +97,7 @@ def main(argv: list[str] | None = None) -> int:
     p.add_argument("--world-size", type=int, default=1, help="tensor-parallel ranks (launch with torchrun)")
     p.add_argument("--tp-chunks", type=int, default=4)
     p.add_argument("--tp-comm-sms", type=int, default=24, help="SMs the overlapped GEMMs leave to the all-reduces")
+    p.add_argument("--tp-allreduce", choices=["auto", "multimem", "nccl"], default="auto")
     p.add_argument("-v", "--verbose", action="store_true")
     args = p.parse_args(argv)
     logging.basicConfig(level=logging.INFO if args.verbose else logging.WARNING, format="%(asctime)s %(message)s")
@@ -128,7 +129,7 @@ def main(argv: list[str] | None = None) -> int:
                         reference_check=run and not args.no_check and args.world_size == 1,
                         cuda_graph=args.cuda_graph and args.world_size == 1, world_size=args.world_size,
                         tp_mode="heads" if args.world_size > 1 else None, tp_chunks=args.tp_chunks,
-                        tp_comm_sms=args.tp_comm_sms,
+                        tp_comm_sms=args.tp_comm_sms, tp_allreduce=args.tp_allreduce,
                         measure_iters=args.bench)
     res = compile_model(model, (example,), cfg)
     ok = True

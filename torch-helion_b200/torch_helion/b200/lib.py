@@ -28,7 +28,7 @@ _DTYPES = {torch.float32: TH_F32, torch.bfloat16: TH_BF16, torch.float16: TH_F16
 EXPORTED_SYMBOLS = (
     "th_last_error_string", "th_version", "th_device_error", "th_rowstat", "th_rmsnorm", "th_gemm",
     "th_attention", "th_conv1d", "th_ssd_workspace_size", "th_ssd", "th_embedding", "th_ssd_noalloc",
-    "th_selftest_bounded_wait",
+    "th_selftest_bounded_wait", "th_allreduce",
 )
 
 
@@ -46,6 +46,15 @@ class RowstatArgs(ctypes.Structure):
 class RmsnormArgs(ctypes.Structure):
     _fields_ = [("x", _vp), ("ldx", _i64), ("gain", _vp), ("y", _vp), ("ldy", _i64), ("rows", _i64), ("cols", _i64),
                 ("eps", _f32), ("dtype", _i32)]
+
+
+class AllreduceArgs(ctypes.Structure):
+    _fields_ = [("mc", _vp), ("peer_sig", _vp), ("sig", _vp), ("offset", _i64), ("bytes", _i64), ("dtype", _i32),
+                ("rank", _i32), ("world", _i32), ("ctas", _i32)]
+
+
+ALLREDUCE_SIGNAL_BYTES = 20480  # TH_ALLREDUCE_SIGNAL_BYTES
+ALLREDUCE_MAX_CTAS = 256
 
 
 class GemmArgs(ctypes.Structure):
@@ -123,7 +132,8 @@ def load() -> ctypes.CDLL:
         lib.th_ssd_workspace_size.argtypes = [_i32] * 6
         for name, st in (("th_rowstat", RowstatArgs), ("th_rmsnorm", RmsnormArgs), ("th_gemm", GemmArgs),
                          ("th_attention", AttentionArgs), ("th_conv1d", Conv1dArgs), ("th_ssd", SsdArgs),
-                         ("th_ssd_noalloc", SsdArgs), ("th_embedding", EmbeddingArgs)):
+                         ("th_ssd_noalloc", SsdArgs), ("th_embedding", EmbeddingArgs),
+                         ("th_allreduce", AllreduceArgs)):
             fn = getattr(lib, name)
             fn.restype = ctypes.c_int
             fn.argtypes = [ctypes.POINTER(st), _vp]
@@ -181,6 +191,19 @@ def device_error(clear: bool = True) -> int:
 
 
 # ------------------------------------------------------------------ kernels
+def allreduce(mc: int, peer_sig: torch.Tensor, sig: torch.Tensor, offset: int, nbytes: int, dtype: torch.dtype,
+              rank: int, world: int, ctas: int = 0) -> None:
+    """In-place multicast sum all-reduce of bytes [offset, offset + nbytes) of a symmetric buffer
+    (th_allreduce): ``mc`` is the buffer's multicast address, ``peer_sig`` an int64 device tensor of
+    every rank's signal-pad address, ``sig`` this rank's pad (uint8, zeroed before the first call)."""
+    if peer_sig.dtype != torch.int64 or peer_sig.numel() != world or not peer_sig.is_cuda:
+        raise B200KernelError("allreduce: peer_sig must be an int64 CUDA tensor of world entries")
+    if sig.numel() * sig.element_size() < ALLREDUCE_SIGNAL_BYTES:
+        raise B200KernelError(f"allreduce: the signal pad needs {ALLREDUCE_SIGNAL_BYTES} bytes")
+    a = AllreduceArgs(mc, peer_sig.data_ptr(), sig.data_ptr(), offset, nbytes, _DTYPES[dtype], rank, world, ctas)
+    _check(load().th_allreduce(ctypes.byref(a), _stream()), "th_allreduce")
+
+
 def rowstat(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """Per-row sum of squares (fp32)."""
     rows, cols, ld = _rows(x)

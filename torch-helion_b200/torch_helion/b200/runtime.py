@@ -32,6 +32,8 @@ from ..optimizer.opir import KernelArg, Program
 from . import lib
 from .lower import GemmPlan, MacroPlan, fp32_outputs, lower_gemm, lower_macro
 
+# launch kinds that exchange data between the ranks (run on the communication stream when chunked)
+_COLLECTIVES = ("nccl", "allreduce")
 _TORCH_DTYPES = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16, "int64": torch.int64}
 
 
@@ -54,7 +56,8 @@ class CompiledProgram:
 
     def __init__(self, program: Program, params: dict[str, torch.Tensor], device: str | torch.device = "cuda",
                  tp_rank: int = 0, tp_world: int = 1, allreduce: Callable[[torch.Tensor], None] | None = None,
-                 shared_params: dict | None = None, tp_chunks: int = 4, tp_comm_sms: int = 24) -> None:
+                 shared_params: dict | None = None, tp_chunks: int = 4, tp_comm_sms: int = 24,
+                 tp_allreduce: str = "auto") -> None:
         if not torch.cuda.is_available():
             raise lib.B200KernelError("CompiledProgram needs a CUDA device (there is no CPU fallback)")
         lib.load()
@@ -75,6 +78,11 @@ class CompiledProgram:
         # persistent grids are capped at (SMs - tp_comm_sms) there, so NCCL's kernels get SMs at once
         self.tp_comm_sms = tp_comm_sms
         self._gemm_sm_limit = 0  # read by every GEMM launch when it runs
+        if tp_allreduce not in ("auto", "multimem", "nccl"):
+            raise ValueError(f"tp_allreduce must be auto, multimem or nccl, not {tp_allreduce!r}")
+        self.tp_allreduce = tp_allreduce
+        self._multimem = False  # all-reduces through th_allreduce on symmetric buffers (decided in _build)
+        self._symmetric: list = []
         self._pipe: tuple | None = None  # chunked tensor-parallel schedule (see _plan_tp_pipeline)
         with torch.cuda.device(self.device):
             self._build()
@@ -143,6 +151,12 @@ class CompiledProgram:
             cols = t.shape[1] if dt == torch.int64 else _round_up(t.shape[1], 8)
             buf = self._empty(t.shape[0], cols, dt)
             self.views[name] = buf if dt == torch.int64 else buf[:, : t.shape[1]]
+        if self.tp_world > 1 and self.tp_allreduce != "nccl" and any(self._allreduced(k) for k in prog.kernels):
+            from .collectives import multimem_available
+
+            self._multimem = multimem_available(self.device)  # the same answer on every rank
+            if not self._multimem and self.tp_allreduce == "multimem":
+                raise lib.B200KernelError("tp_allreduce='multimem' but this node has no multicast symmetric memory")
         f32 = fp32_outputs(prog)
         plans = {}
         for spec in prog.kernels:
@@ -191,7 +205,16 @@ class CompiledProgram:
         n_tail = p.n_tail
         n_tail_pad = _round_up(n_tail, 8) if n_tail else 0
         W = self._gemm_weight(p, n_main_pad, n_tail_pad)
-        out = self._empty(T, max(n_main_pad, 8), self.dtype)
+        sym = None
+        if self._multimem and self._allreduced(spec):  # reduced in place through NVSwitch multicast
+            from .collectives import SymmetricRows
+
+            sym = SymmetricRows(T, max(n_main_pad, 8), self.dtype, self.device,
+                                ctas=self.tp_comm_sms if self.tp_comm_sms > 0 else 32)
+            self._symmetric.append(sym)
+            out = sym.buf
+        else:
+            out = self._empty(T, max(n_main_pad, 8), self.dtype)
         tail = self._empty(T, n_tail_pad, torch.float32) if n_tail else None
         for tname, (where, c0, c1) in p.outputs.items():
             self.views[tname] = (out if where == "main" else tail)[:, c0:c1]
@@ -239,7 +262,10 @@ class CompiledProgram:
         self.launches.append(KernelLaunch(kname, "gemm", lambda lhs=lhs, W=W, d=d, kw=kw: lib.gemm(
             lhs, W, d, sm_limit=self._gemm_sm_limit, **kw),
                                           fn_rows))
-        if self._allreduced(spec):
+        if sym is not None:
+            self.launches.append(KernelLaunch(f"allreduce({kname})", "allreduce",
+                                              lambda sym=sym, T=T: sym.allreduce_rows(0, T), sym.allreduce_rows))
+        elif self._allreduced(spec):
             buf = out  # the whole (contiguous) buffer; zero-weight pad columns sum to zero
             self.launches.append(KernelLaunch(f"allreduce({kname})", "nccl", lambda buf=buf: self.allreduce(buf),
                                               lambda r0, r1, buf=buf: self.allreduce(buf[r0:r1])))
@@ -314,7 +340,7 @@ class CompiledProgram:
         chunk are a multiple of 128 (whole GEMM row tiles)."""
         if self.tp_world <= 1 or self.tp_chunks <= 1:
             return
-        first = next((i for i, l in enumerate(self.launches) if l.kind == "nccl"), None)
+        first = next((i for i, l in enumerate(self.launches) if l.kind in _COLLECTIVES), None)
         if first is None or first == 0:
             return
         seg = self.launches[first - 1:]
@@ -358,7 +384,7 @@ class CompiledProgram:
         def run(chunk, r0, r1) -> torch.cuda.Event | None:
             last = None
             for l in chunk:
-                if l.kind == "nccl":
+                if l.kind in _COLLECTIVES:
                     last = collective(l, r0, r1)
                 else:
                     if last is not None:  # compute after a collective of the same rows

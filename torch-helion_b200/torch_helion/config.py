@@ -40,6 +40,9 @@ class CompileConfig:
       tp_chunks          row chunks of the tensor-parallel part after attention:
                          each chunk's all-reduce overlaps the next chunk's GEMMs
       tp_comm_sms        SMs the GEMMs of that overlapped part leave to the collectives
+                         (also the grid of the multicast all-reduce kernel)
+      tp_allreduce       "multimem" (th_allreduce on symmetric buffers through NVSwitch
+                         multicast), "nccl", or "auto" (multimem where every rank supports it)
       measure_iters      time the forward on the device (0 = skip)
     """
 
@@ -70,6 +73,7 @@ class CompileConfig:
     tp_mode: str | None = None
     tp_chunks: int = 4
     tp_comm_sms: int = 24
+    tp_allreduce: str = "auto"
     measure_iters: int = 0
 
     @property

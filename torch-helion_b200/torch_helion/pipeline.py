@@ -109,7 +109,7 @@ def device_module(program: Program, params: dict[str, torch.Tensor], config: Com
     sharded, sparams = shard_program(program, params, config.world_size, rank)
     return CompiledProgram(sharded, sparams, config.device, tp_rank=rank, tp_world=config.world_size,
                            allreduce=lambda t: dist.all_reduce(t), tp_chunks=config.tp_chunks,
-                           tp_comm_sms=config.tp_comm_sms)
+                           tp_comm_sms=config.tp_comm_sms, tp_allreduce=config.tp_allreduce)
 
 
 class _Stage:
