@@ -290,8 +290,8 @@ def main() -> None:
     ap.add_argument("--tp-chunks", type=int, default=4, help="c3 tensor parallel: row chunks of the all-reduce overlap")
     ap.add_argument("--tp-allreduce", choices=["auto", "multimem", "nccl"], default="auto",
                     help="c3 tensor parallel: all-reduce through NVSwitch multicast (th_allreduce) or NCCL")
-    ap.add_argument("--tp-comm-sms", type=int, default=24,
-                    help="c3 tensor parallel: SMs the overlapped GEMMs leave to the all-reduces (0 = none)")
+    ap.add_argument("--tp-comm-sms", type=int, default=None,
+                    help="c3 tensor parallel: SMs the overlapped GEMMs leave to the all-reduces (default: by rank count)")
     args = ap.parse_args()
 
     if args.impl == "reference":
@@ -450,7 +450,7 @@ def main() -> None:
                    else "NCCL all-reduce")
             par = (f"tp{n}: heads and FFN columns, {how} after o_proj and after down_proj, "
                    f"{args.tp_chunks} row chunks overlapping the all-reduces with the GEMMs, "
-                   f"which leave {args.tp_comm_sms} SMs to them")
+                   f"which leave {mod.tp_comm_sms} SMs to them")
             launch = f"eager launches; {'th_allreduce kernels' if mod._multimem else 'NCCL all-reduces'} on a second stream"
             entry = ("CompileResult.streaming_runner -> ShardedStreamingRunner: each rank copies its 1/N of the "
                      "rows in and out of pinned host memory, NCCL all-gather of the input rows, tensor-parallel "

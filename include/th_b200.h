@@ -161,7 +161,9 @@ typedef struct {
   float* ss_out;
   int64_t ss_ld;
   /* SMs the kernel's persistent grid may occupy (0 = all): leaves the rest to
-   * work that runs beside it, e.g. a collective on another stream */
+   * work that runs beside it, e.g. a collective on another stream.  Such a
+   * launch does not use programmatic dependent launch, so its CTAs do not
+   * take the free SMs before the previous kernel of the stream ends. */
   int32_t sm_limit;
 } th_gemm_args;
 int th_gemm(const th_gemm_args* a, void* stream);

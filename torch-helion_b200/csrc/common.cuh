@@ -598,10 +598,12 @@ inline int smem_limit(void (*kernel)(KArgs...), size_t bytes, const char* what) 
   return smem_limit_raw(reinterpret_cast<const void*>(kernel), bytes, what);
 }
 
-// Launch `kern` on `st` with programmatic stream serialisation: only for
-// kernels that call pdl_wait() before their first access to global memory.
+// Launch `kern` on `st`, with programmatic stream serialisation when `pdl`
+// (and TH_PDL is not 0): only for kernels that call pdl_wait() before their
+// first access to global memory.
 template <typename... KArgs, typename... Args>
-inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+inline void launch_maybe_pdl(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -611,8 +613,12 @@ inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
   cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  launch_maybe_pdl(true, kern, grid, block, smem, st, static_cast<Args&&>(args)...);
 }
 
 }  // namespace th

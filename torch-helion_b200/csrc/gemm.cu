@@ -776,8 +776,10 @@ static int launch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st
   const int tiles_m = (int)((a->m + C::BM - 1) / C::BM), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n;
   const int grid = ntiles < gemm_sms(a) ? ntiles : gemm_sms(a);
-  launch_pdl(gemm_tc_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb, ep, (int)a->k, tiles_m,
-             tiles_n);
+  // a GEMM kept to part of the GPU launches without PDL, so the SMs it leaves free stay free for the
+  // kernel beside it (with PDL its CTAs would take them early, waiting for the previous kernel)
+  launch_maybe_pdl(a->sm_limit <= 0, gemm_tc_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb, ep,
+                   (int)a->k, tiles_m, tiles_n);
   return check_launch("th_gemm(tcgen05)");
 }
 
@@ -793,8 +795,8 @@ static int launch_tc2(const th_gemm_args* a, const EpiParams& ep, cudaStream_t s
   const int tiles_m = (int)((a->m + 2 * C::BM - 1) / (2 * C::BM)), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n, pairs = gemm_sms(a) / 2;
   const int grid = 2 * (ntiles < pairs ? ntiles : pairs);
-  launch_pdl(gemm_tc2_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb, ep, (int)a->k, tiles_m,
-             tiles_n);
+  launch_maybe_pdl(a->sm_limit <= 0, gemm_tc2_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb, ep,
+                   (int)a->k, tiles_m, tiles_n);
   return check_launch("th_gemm(tcgen05 pair)");
 }
 

@@ -96,7 +96,7 @@ def main(argv: list[str] | None = None) -> int:
     p.add_argument("--cuda-graph", action="store_true", help="replay the forward as one CUDA graph")
     p.add_argument("--world-size", type=int, default=1, help="tensor-parallel ranks (launch with torchrun)")
     p.add_argument("--tp-chunks", type=int, default=4)
-    p.add_argument("--tp-comm-sms", type=int, default=24, help="SMs the overlapped GEMMs leave to the all-reduces")
+    p.add_argument("--tp-comm-sms", type=int, default=None, help="SMs the overlapped GEMMs leave to the all-reduces")
     p.add_argument("--tp-allreduce", choices=["auto", "multimem", "nccl"], default="auto")
     p.add_argument("-v", "--verbose", action="store_true")
     args = p.parse_args(argv)

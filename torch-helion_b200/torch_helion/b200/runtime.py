@@ -56,7 +56,7 @@ class CompiledProgram:
 
     def __init__(self, program: Program, params: dict[str, torch.Tensor], device: str | torch.device = "cuda",
                  tp_rank: int = 0, tp_world: int = 1, allreduce: Callable[[torch.Tensor], None] | None = None,
-                 shared_params: dict | None = None, tp_chunks: int = 4, tp_comm_sms: int = 24,
+                 shared_params: dict | None = None, tp_chunks: int = 4, tp_comm_sms: int | None = None,
                  tp_allreduce: str = "auto") -> None:
         if not torch.cuda.is_available():
             raise lib.B200KernelError("CompiledProgram needs a CUDA device (there is no CPU fallback)")
@@ -74,13 +74,18 @@ class CompiledProgram:
         self._ssd_ws: torch.Tensor | None = None
         self.tp_rank, self.tp_world, self.allreduce = tp_rank, tp_world, allreduce
         self.tp_chunks = tp_chunks
-        # SMs left to the collectives while the chunked schedule overlaps them with GEMMs: the GEMMs'
-        # persistent grids are capped at (SMs - tp_comm_sms) there, so NCCL's kernels get SMs at once
-        self.tp_comm_sms = tp_comm_sms
-        self._gemm_sm_limit = 0  # read by every GEMM launch when it runs
         if tp_allreduce not in ("auto", "multimem", "nccl"):
             raise ValueError(f"tp_allreduce must be auto, multimem or nccl, not {tp_allreduce!r}")
-        self.tp_allreduce = tp_allreduce
+        # Measured on B200 (C3 block, 4 chunks): at 2 ranks the forward is compute-bound and NCCL's
+        # peer-to-peer all-reduce beats the multicast one (505 vs 395 GB/s on 256 MiB), so the GEMMs keep
+        # every SM; from 4 ranks on the all-reduces weigh as much as the GEMMs and the multicast kernel on
+        # 16 SMs of its own overlaps them best (8 ranks: 2.52 ms against 2.69 with 24 SMs and 3.14 over NCCL).
+        wide = tp_world >= 4
+        self.tp_allreduce = tp_allreduce if tp_allreduce != "auto" or wide else "nccl"
+        # SMs left to the collectives while the chunked schedule overlaps them with GEMMs: the GEMMs'
+        # persistent grids are capped at (SMs - tp_comm_sms) there, and th_allreduce runs on that many CTAs
+        self.tp_comm_sms = tp_comm_sms if tp_comm_sms is not None else (16 if wide else 0)
+        self._gemm_sm_limit = 0  # read by every GEMM launch when it runs
         self._multimem = False  # all-reduces through th_allreduce on symmetric buffers (decided in _build)
         self._symmetric: list = []
         self._pipe: tuple | None = None  # chunked tensor-parallel schedule (see _plan_tp_pipeline)
@@ -210,7 +215,7 @@ class CompiledProgram:
             from .collectives import SymmetricRows
 
             sym = SymmetricRows(T, max(n_main_pad, 8), self.dtype, self.device,
-                                ctas=self.tp_comm_sms if self.tp_comm_sms > 0 else 32)
+                                ctas=self.tp_comm_sms if self.tp_comm_sms > 0 else 16)
             self._symmetric.append(sym)
             out = sym.buf
         else:

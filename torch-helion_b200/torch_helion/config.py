@@ -40,9 +40,11 @@ class CompileConfig:
       tp_chunks          row chunks of the tensor-parallel part after attention:
                          each chunk's all-reduce overlaps the next chunk's GEMMs
       tp_comm_sms        SMs the GEMMs of that overlapped part leave to the collectives
-                         (also the grid of the multicast all-reduce kernel)
+                         (also the grid of the multicast all-reduce kernel); None: 16 from
+                         4 ranks on, 0 at 2 ranks
       tp_allreduce       "multimem" (th_allreduce on symmetric buffers through NVSwitch
-                         multicast), "nccl", or "auto" (multimem where every rank supports it)
+                         multicast), "nccl", or "auto" (multimem from 4 ranks on where every
+                         rank supports it, NCCL at 2 ranks)
       measure_iters      time the forward on the device (0 = skip)
     """
 
@@ -72,7 +74,7 @@ class CompileConfig:
     world_size: int = 1
     tp_mode: str | None = None
     tp_chunks: int = 4
-    tp_comm_sms: int = 24
+    tp_comm_sms: int | None = None
     tp_allreduce: str = "auto"
     measure_iters: int = 0
 
