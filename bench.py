@@ -287,6 +287,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3", "c4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--timeline", type=Path, default=None, metavar="PATH",
+                    help="after the timed steps, write rank 0's per-launch event timeline of one forward to PATH")
     ap.add_argument("--tp-chunks", type=int, default=4, help="c3 tensor parallel: row chunks of the all-reduce overlap")
     ap.add_argument("--tp-allreduce", choices=["auto", "multimem", "nccl"], default="auto",
                     help="c3 tensor parallel: all-reduce through NVSwitch multicast (th_allreduce) or NCCL")
@@ -414,10 +416,16 @@ def main() -> None:
         torch.cuda.synchronize()
         ms_e2e = e0.elapsed_time(e1) / args.steps
         del runner
+        if args.timeline is not None:  # every rank runs it (collectives inside); rank 0 writes it
+            flush()
+            marks = mod.timeline()
+            if rank == 0:
+                args.timeline.parent.mkdir(parents=True, exist_ok=True)
+                args.timeline.write_text("".join(f"{t:9.3f}  {name}  rows@{r0}\n" for t, name, r0 in marks))
 
     # ---- per-kernel times and the dominant kernel's roofline
     peaks, peak_src = _peaks()
-    top = max((l for l in mod.launches if l.kind != "nccl"), key=lambda l: ktimes[l.name])
+    top = max((l for l in mod.launches if l.kind not in ("nccl", "allreduce")), key=lambda l: ktimes[l.name])
     work = kernel_work(top, prog, mod)
     ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
     t_top = ktimes[top.name] / 1e3
@@ -435,6 +443,8 @@ def main() -> None:
     tf = REPO / "profiles" / f"traffic_{args.workload}{'_tp' + str(world) if tp else ''}.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(top.name)
+
+    ar_bytes = {l.name: l.nbytes for l in mod.launches if l.kind in ("nccl", "allreduce")}
 
     # ---- aggregate over ranks (max time)
     t = torch.tensor([ms, ms_e2e], device=dev, dtype=torch.float64)
@@ -481,6 +491,13 @@ def main() -> None:
             "kernels_ms": ktimes,
             "cpu_baseline": cb,
         }
+        if tp:
+            # each all-reduce on its own: the bytes it sums over the time it took (algorithm bandwidth)
+            line["collectives"] = {
+                l.name: {"kind": "th_allreduce (NVSwitch multicast)" if l.kind == "allreduce" else "NCCL all_reduce",
+                         "bytes": ar_bytes[l.name], "ms": ktimes[l.name],
+                         "algbw_gbs": ar_bytes[l.name] / ktimes[l.name] / 1e6}
+                for l in mod.launches if l.kind in ("nccl", "allreduce")}
         if dist is not None:
             line["nccl"] = {"backend": dist.get_backend(), "ranks": dist.get_world_size(),
                             "tp_allreduce": "multimem" if getattr(mod, "_multimem", False) else "nccl",

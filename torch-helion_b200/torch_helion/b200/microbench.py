@@ -6,11 +6,18 @@
     python -m torch_helion.b200.microbench gemm --m 8192 --n 3328 --k 768 --vs-torch
     python -m torch_helion.b200.microbench conv --batch 4 --seq 2048 --channels 1792
     python -m torch_helion.b200.microbench rmsnorm --m 8192 --k 768
+    torchrun --nproc-per-node 8 -m torch_helion.b200.microbench allreduce --m 32768 --k 4096 --ctas 16,24,32
 
 Each mode runs 3 warm-up launches and times ``--iters`` launches with CUDA
 events (L2 flushed before each when ``--flush``), printing one JSON line with
 the median time and the kernel's algorithmic throughput.  This is the
 command behind the single-kernel ncu captures.
+
+``allreduce`` (one process per GPU under torchrun) sums a bf16 [m, k] array
+over the ranks with ``th_allreduce`` for every ``--ctas`` grid size and
+with NCCL's ``all_reduce`` on the same bytes, checks that both give the
+same sums, and prints rank 0's line: the max over ranks of each median
+time and the algorithm bandwidth (bytes / time).
 
 ``ssd-sweep`` is the standalone chunked-scan sweep: batch 8, 64 heads of 64,
 one B/C group, chunk 256, d_state in {64, 128, 256} x seqlen in {512, 2048,
@@ -97,9 +104,60 @@ def _ssd_sweep(a) -> None:
             torch.cuda.empty_cache()
 
 
+def _allreduce(a) -> None:
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from .collectives import SymmetricRows, multimem_available
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        if not multimem_available(dev):
+            raise lib.B200KernelError("no multicast symmetric memory on this node")
+        sym = SymmetricRows(a.m, a.k, torch.bfloat16, dev)
+        g = torch.Generator(device=dev).manual_seed(dist.get_rank())
+        src = torch.randn(a.m, a.k, device=dev, generator=g).to(torch.bfloat16)
+        ref = src.clone()
+        dist.all_reduce(ref)
+        sym.buf.copy_(src)
+        torch.cuda.synchronize()
+        dist.barrier()
+        sym.allreduce_rows(0, a.m)
+        torch.cuda.synchronize()
+        same = bool(torch.equal(sym.buf, ref))
+        nbytes = a.m * a.k * 2
+
+        def med(fn) -> float:  # median device time, max over ranks
+            t = torch.tensor([_time(fn, a.iters, False)], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t)
+
+        rows = {"nccl": med(lambda: dist.all_reduce(ref))}
+        for c in (int(v) for v in a.ctas.split(",")):
+            sym.ctas = c
+            rows[f"th_allreduce ctas={c}"] = med(lambda: sym.allreduce_rows(0, a.m))
+        err = lib.device_error()
+        if dist.get_rank() == 0:
+            print(json.dumps({"kernel": "allreduce", "ranks": dist.get_world_size(), "bytes": nbytes,
+                              "same_sums_as_nccl": same, "device_error": err,
+                              "us": {k: v * 1e6 for k, v in rows.items()},
+                              "algbw_gbs": {k: nbytes / v / 1e9 for k, v in rows.items()}}))
+        torch.cuda.synchronize()
+        dist.barrier()
+        del sym
+    finally:
+        dist.destroy_process_group()
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("kernel", choices=["attention", "ssd", "ssd-sweep", "gemm", "conv", "rmsnorm", "rowstat"])
+    ap.add_argument("kernel", choices=["attention", "ssd", "ssd-sweep", "gemm", "conv", "rmsnorm", "rowstat",
+                                       "allreduce"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--hq", type=int, default=32)
@@ -113,6 +171,7 @@ def main(argv=None) -> None:
     ap.add_argument("--k", type=int, default=768)
     ap.add_argument("--channels", type=int, default=1792)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--ctas", default="16,24,32", help="allreduce: th_allreduce grid sizes to time")
     ap.add_argument("--flush", action="store_true")
     ap.add_argument("--no-gate", action="store_true", help="ssd: no silu(z) gate, no D skip, no row sums")
     ap.add_argument("--vs-torch", action="store_true", help="gemm: also time torch.matmul (cuBLAS)")
@@ -122,6 +181,9 @@ def main(argv=None) -> None:
     extra: dict = {}
     if a.kernel == "ssd-sweep":
         _ssd_sweep(a)
+        return
+    if a.kernel == "allreduce":
+        _allreduce(a)
         return
     if a.kernel == "attention":
         t = a.batch * a.seq

@@ -49,6 +49,8 @@ class KernelLaunch:
     # the same launch restricted to rows [r0, r1) of every row-indexed operand
     # (None: the kernel does not decompose by rows, e.g. attention or RoPE)
     fn_rows: Callable[[int, int], None] | None = None
+    # bytes a collective sums per call (0 for compute kernels)
+    nbytes: int = 0
 
 
 class CompiledProgram:
@@ -269,11 +271,13 @@ class CompiledProgram:
                                           fn_rows))
         if sym is not None:
             self.launches.append(KernelLaunch(f"allreduce({kname})", "allreduce",
-                                              lambda sym=sym, T=T: sym.allreduce_rows(0, T), sym.allreduce_rows))
+                                              lambda sym=sym, T=T: sym.allreduce_rows(0, T), sym.allreduce_rows,
+                                              nbytes=T * sym.row_bytes))
         elif self._allreduced(spec):
             buf = out  # the whole (contiguous) buffer; zero-weight pad columns sum to zero
             self.launches.append(KernelLaunch(f"allreduce({kname})", "nccl", lambda buf=buf: self.allreduce(buf),
-                                              lambda r0, r1, buf=buf: self.allreduce(buf[r0:r1])))
+                                              lambda r0, r1, buf=buf: self.allreduce(buf[r0:r1]),
+                                              nbytes=buf.numel() * buf.element_size()))
 
     def _add_macro(self, kname: str, p: MacroPlan, need_ss, ss_by_producer) -> None:
         prog = self.program
@@ -418,6 +422,36 @@ class CompiledProgram:
             return
         for l in self.launches:
             l.fn()
+
+    def timeline(self) -> list[tuple[float, str, int]]:
+        """One eager forward with a CUDA event recorded after every launch on the stream it went to:
+        [(ms from the forward's start to the launch's end, launch name, first row or -1)], sorted by
+        time.  Under tensor parallelism every rank must call it (the collectives run inside)."""
+        marks: list[tuple[str, int, torch.cuda.Event]] = []
+        saved = [(l, l.fn, l.fn_rows) for l in self.launches]
+
+        def mark(name: str, r0: int) -> None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            marks.append((name, r0, e))
+
+        for l, fn, fr in saved:
+            l.fn = lambda fn=fn, name=l.name: (fn(), mark(name, -1))
+            if fr is not None:
+                l.fn_rows = lambda r0, r1, fr=fr, name=l.name: (fr(r0, r1), mark(name, r0))
+        graph, self._graph = self._graph, None
+        try:
+            with torch.cuda.device(self.device):
+                torch.cuda.synchronize()
+                start = torch.cuda.Event(enable_timing=True)
+                start.record()
+                self.launch_all()
+                torch.cuda.synchronize()
+        finally:
+            self._graph = graph
+            for l, fn, fr in saved:
+                l.fn, l.fn_rows = fn, fr
+        return sorted((start.elapsed_time(e), name, r0) for name, r0, e in marks)
 
     def output_views(self) -> list[torch.Tensor]:
         shapes = self.program.metadata.get("output_shapes", {})
