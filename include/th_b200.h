@@ -294,6 +294,13 @@ typedef struct {
   void* sig;              /* this rank's signal pad */
   int64_t offset, bytes;
   int32_t dtype, rank, world, ctas;
+  /* optional row statistics: when sumsq_mc (the multicast address of an fp32
+   * array in symmetric memory, element i = row i of the buffer) is set, every
+   * rank's slice must be whole rows of row_bytes bytes (offset and bytes
+   * multiples of row_bytes, bytes of row_bytes x world); each reduced row's
+   * sum of squares (fp32) is stored to element row of every rank's array */
+  float* sumsq_mc;
+  int64_t row_bytes;
 } th_allreduce_args;
 int th_allreduce(const th_allreduce_args* a, void* stream);
 

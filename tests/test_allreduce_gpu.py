@@ -53,7 +53,7 @@ def _multicast_ok() -> bool:
         return False
 
 
-def _rows_rank(rank, world, port, path, dtype_name):
+def _rows_rank(rank, world, port, path, dtype_name, stats=False):
     _setup(rank, world, port)
     try:
         from torch_helion.b200 import lib
@@ -63,6 +63,7 @@ def _rows_rank(rank, world, port, path, dtype_name):
         dev = torch.device("cuda", rank)
         rows, cols = 1024, 4096
         sym = SymmetricRows(rows, cols, dtype, dev, ctas=24)
+        sym.stats = stats
         g = torch.Generator(device=dev).manual_seed(100 + rank)
         src = torch.randn(rows, cols, device=dev, generator=g).to(dtype)
         sym.buf.copy_(src)
@@ -74,19 +75,22 @@ def _rows_rank(rank, world, port, path, dtype_name):
         torch.cuda.synchronize()
         err = lib.device_error()
         want = torch.stack([e.float() for e in everyone]).sum(0).to(dtype)
-        torch.save({"err": err, "got": sym.buf.float().cpu(), "want": want.float().cpu()}, f"{path}/rank{rank}.pt")
+        torch.save({"err": err, "got": sym.buf.float().cpu(), "want": want.float().cpu(),
+                    "sumsq": sym.sumsq.cpu() if stats else None}, f"{path}/rank{rank}.pt")
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("dtype_name", ["bfloat16", "float32"])
-def test_allreduce_world2(tmp_path, dtype_name):
+@pytest.mark.parametrize("dtype_name,stats", [("bfloat16", False), ("float32", False), ("bfloat16", True)],
+                         ids=["bf16", "fp32", "bf16-rowstats"])
+def test_allreduce_world2(tmp_path, dtype_name, stats):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     if not _multicast_ok():
         pytest.skip("no multicast symmetric memory on this node")
-    mp.start_processes(_rows_rank, args=(2, _free_port(), str(tmp_path), dtype_name), nprocs=2, start_method="spawn")
+    mp.start_processes(_rows_rank, args=(2, _free_port(), str(tmp_path), dtype_name, stats), nprocs=2,
+                       start_method="spawn")
     res = [torch.load(tmp_path / f"rank{r}.pt") for r in range(2)]
     for r in res:
         assert r["err"] == 0
@@ -96,6 +100,10 @@ def test_allreduce_world2(tmp_path, dtype_name):
         ulp = 2.0 ** -7 if dtype_name == "bfloat16" else 2.0 ** -23
         assert torch.allclose(r["got"], r["want"], rtol=ulp, atol=1e-30)
     assert torch.equal(res[0]["got"], res[1]["got"])  # every rank holds the same sums
+    if stats:  # each row's sum of squares of the reduced values, on every rank
+        want_ss = (res[0]["got"].double() ** 2).sum(1)
+        for r in res:
+            assert torch.allclose(r["sumsq"].double(), want_ss, rtol=1e-5, atol=0)
 
 
 def _block_rank(rank, world, port, path, kw):
@@ -111,6 +119,8 @@ def _block_rank(rank, world, port, path, kw):
                                                    world_size=world, tp_mode="heads", reference_check=False,
                                                    verify_passes=False, tp_allreduce="multimem", tp_chunks=2))
         assert res.module._multimem
+        # the second RMSNorm's statistic comes from the all-reduce: one row-statistics launch is left
+        assert sum(n.startswith("rowstat(") for n in res.module.launch_names()) == 1
         out = res.run(x.to(f"cuda:{rank}"))[0].float().cpu()
         torch.cuda.synchronize()
         torch.save(out, f"{path}/rank{rank}.pt")

@@ -17,6 +17,12 @@
 //      buffer (or reads it) before every rank's stores into it have landed and
 //      every rank has finished reading it.
 //
+// With row statistics (`sumsq_mc`), each rank's slice is whole rows: one warp
+// reduces a row, sums the squares of the (rounded) sums in fp32 and stores
+// that row's sum of squares to every rank with one multimem.st -- the
+// statistic the next RMSNorm needs, so no separate row-statistics pass reads
+// the reduced rows again.
+//
 // The epoch is a per-block counter kept in the signal pad (so a captured CUDA
 // graph replays correctly): block b of call k on every rank uses epoch k of
 // block b.  Waits compare with wrap-safe arithmetic and give up after
@@ -33,6 +39,7 @@ namespace th {
 constexpr int kArMaxCtas = TH_ALLREDUCE_MAX_CTAS;
 constexpr int kArMaxWorld = TH_ALLREDUCE_MAX_WORLD;
 constexpr int kArThreads = 512;
+constexpr int kArWarps = kArThreads / 32;
 constexpr int kArUnroll = 4;
 
 // Signal pad layout (uint32 words): [2 phases][kArMaxCtas blocks][kArMaxWorld sources], then the
@@ -45,6 +52,9 @@ struct ArParams {
   uint32_t* sig;                 // this rank's signal pad
   int64_t slice_vecs;            // 16-byte vectors per rank slice
   int32_t rank, world, dtype;
+  float* sumsq_mc;               // row statistics: multicast address of the fp32 [rows] array (or null)
+  int64_t row_vecs;              // 16-byte vectors per row (row statistics)
+  int64_t row0;                  // index of this rank's first row in the sumsq array
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -114,6 +124,61 @@ __device__ __forceinline__ void mm_st(uint8_t* a, uint4 v) {
   }
 }
 
+__device__ __forceinline__ void mm_st_f32(float* a, float v) {
+  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(a), "f"(v) : "memory");
+}
+
+// Sum of squares of the 16-byte vector's elements (fp32).
+template <int DTYPE>
+__device__ __forceinline__ float sumsq16(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (DTYPE == TH_BF16) {
+      const float lo = __uint_as_float(w[i] << 16), hi = __uint_as_float(w[i] & 0xffff0000u);
+      s = fmaf(lo, lo, fmaf(hi, hi, s));
+    } else if constexpr (DTYPE == TH_F16) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      s = fmaf(f.x, f.x, fmaf(f.y, f.y, s));
+    } else {
+      const float f = __uint_as_float(w[i]);
+      s = fmaf(f, f, s);
+    }
+  }
+  return s;
+}
+
+// This rank's slice, one warp per row, with the row's sum of squares stored to every rank.
+template <int DTYPE>
+__device__ __forceinline__ void reduce_rows(const ArParams& p, uint8_t* base) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rows = p.slice_vecs / p.row_vecs;
+  for (int64_t r = (int64_t)blockIdx.x * kArWarps + warp; r < rows; r += (int64_t)gridDim.x * kArWarps) {
+    uint8_t* row = base + r * p.row_vecs * 16;
+    float ss = 0.f;
+    int64_t i = lane;
+    for (; i + (kArUnroll - 1) * 32 < p.row_vecs; i += kArUnroll * 32) {
+      uint4 v[kArUnroll];
+#pragma unroll
+      for (int u = 0; u < kArUnroll; ++u) v[u] = mm_ld_reduce<DTYPE>(row + (i + u * 32) * 16);
+#pragma unroll
+      for (int u = 0; u < kArUnroll; ++u) {
+        mm_st<DTYPE>(row + (i + u * 32) * 16, v[u]);
+        ss += sumsq16<DTYPE>(v[u]);
+      }
+    }
+    for (; i < p.row_vecs; i += 32) {
+      const uint4 v = mm_ld_reduce<DTYPE>(row + i * 16);
+      mm_st<DTYPE>(row + i * 16, v);
+      ss += sumsq16<DTYPE>(v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) mm_st_f32(p.sumsq_mc + p.row0 + r, ss);
+  }
+}
+
 template <int DTYPE>
 __global__ void __launch_bounds__(kArThreads) allreduce_mm_kernel(ArParams p) {
   __shared__ int s_ok;
@@ -128,7 +193,9 @@ __global__ void __launch_bounds__(kArThreads) allreduce_mm_kernel(ArParams p) {
   const uint32_t epoch = s_epoch;
   if (tid < p.world && !ar_handshake(p, 0, tid, epoch)) s_ok = 0;
   __syncthreads();
-  if (s_ok) {
+  if (s_ok && p.sumsq_mc) {
+    reduce_rows<DTYPE>(p, p.mc + (int64_t)p.rank * p.slice_vecs * 16);
+  } else if (s_ok) {
     // rank r's slice, vectors spread over the grid; kArUnroll loads in flight per thread
     uint8_t* base = p.mc + (int64_t)p.rank * p.slice_vecs * 16;
     const int64_t stride = (int64_t)gridDim.x * kArThreads;
@@ -166,6 +233,13 @@ extern "C" int th_allreduce(const th_allreduce_args* a, void* stream) {
     return fail(TH_EALIGN, "th_allreduce: %lld bytes is not a multiple of 16 x world", (long long)a->bytes);
   uint8_t* mc = static_cast<uint8_t*>(a->mc) + a->offset;
   if (!aligned16(mc) || !aligned16(a->sig)) return fail(TH_EALIGN, "th_allreduce: range or signal pad not 16-byte aligned");
+  if (a->sumsq_mc) {  // row statistics: every rank's slice is whole rows
+    if (a->row_bytes <= 0 || a->row_bytes % 16 != 0 || a->offset % a->row_bytes != 0 ||
+        a->bytes % (a->row_bytes * a->world) != 0)
+      return fail(TH_EINVAL, "th_allreduce: row statistics need whole rows per rank (row_bytes %lld, offset %lld, "
+                  "bytes %lld, world %d)", (long long)a->row_bytes, (long long)a->offset, (long long)a->bytes, a->world);
+    if (reinterpret_cast<uintptr_t>(a->sumsq_mc) % 4 != 0) return fail(TH_EALIGN, "th_allreduce: sumsq_mc misaligned");
+  }
   if (a->bytes == 0 || a->world == 1) return TH_OK;
   ArParams p;
   p.mc = mc;
@@ -175,6 +249,9 @@ extern "C" int th_allreduce(const th_allreduce_args* a, void* stream) {
   p.rank = a->rank;
   p.world = a->world;
   p.dtype = a->dtype;
+  p.sumsq_mc = a->sumsq_mc;
+  p.row_vecs = a->sumsq_mc ? a->row_bytes / 16 : 0;
+  p.row0 = a->sumsq_mc ? a->offset / a->row_bytes + (int64_t)a->rank * (a->bytes / a->world / a->row_bytes) : 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (a->dtype) {
     case TH_BF16: allreduce_mm_kernel<TH_BF16><<<ctas, kArThreads, 0, st>>>(p); break;

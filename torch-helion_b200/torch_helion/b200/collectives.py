@@ -36,7 +36,9 @@ def multimem_available(device: torch.device, group=None) -> bool:
 
 class SymmetricRows:
     """A [rows, cols] tensor in symmetric memory with the multicast address and signal pad that
-    ``th_allreduce`` needs.  Creating one is a collective call (every rank, same shape)."""
+    ``th_allreduce`` needs, and an fp32 [rows] array for per-row sums of squares that the
+    all-reduce fills when ``stats`` is set (the next RMSNorm's statistic).  Creating one is a
+    collective call (every rank, same shape)."""
 
     def __init__(self, rows: int, cols: int, dtype: torch.dtype, device: torch.device, group=None, ctas: int = 0):
         import torch.distributed as dist
@@ -45,7 +47,8 @@ class SymmetricRows:
         group = group if group is not None else dist.group.WORLD
         esz = torch.empty((), dtype=dtype).element_size()
         data = (rows * cols * esz + 255) // 256 * 256
-        raw = symm.empty(data + lib.ALLREDUCE_SIGNAL_BYTES, dtype=torch.uint8, device=device)
+        sq = (rows * 4 + 255) // 256 * 256
+        raw = symm.empty(data + sq + lib.ALLREDUCE_SIGNAL_BYTES, dtype=torch.uint8, device=device)
         hdl = symm.rendezvous(raw, group)
         if not hdl.multicast_ptr:
             raise lib.B200KernelError("symmetric memory has no multicast address on this device")
@@ -54,9 +57,13 @@ class SymmetricRows:
         self.rank, self.world = hdl.rank, hdl.world_size
         self.mc = hdl.multicast_ptr + off
         self.dtype, self.row_bytes, self.ctas = dtype, cols * esz, ctas
-        self.sig = raw[data:]
-        self.peer_sig = torch.tensor([p + off + data for p in hdl.buffer_ptrs], dtype=torch.int64, device=device)
+        self.sig = raw[data + sq:]
+        self.peer_sig = torch.tensor([p + off + data + sq for p in hdl.buffer_ptrs], dtype=torch.int64,
+                                     device=device)
         self.buf = raw[: rows * cols * esz].view(dtype).view(rows, cols)
+        self.sumsq = raw[data: data + rows * 4].view(torch.float32)
+        self.sumsq_mc = self.mc + data
+        self.stats = False
         self._raw, self._hdl = raw, hdl  # keep the mapping alive
         self.sig.zero_()
         torch.cuda.synchronize(device)
@@ -67,4 +74,5 @@ class SymmetricRows:
         if not 0 <= r0 <= r1 <= self.buf.shape[0]:
             raise lib.B200KernelError(f"allreduce_rows: rows [{r0}, {r1}) outside [0, {self.buf.shape[0]})")
         lib.allreduce(self.mc, self.peer_sig, self.sig, r0 * self.row_bytes, (r1 - r0) * self.row_bytes, self.dtype,
-                      self.rank, self.world, self.ctas)
+                      self.rank, self.world, self.ctas, sumsq_mc=self.sumsq_mc if self.stats else 0,
+                      row_bytes=self.row_bytes)

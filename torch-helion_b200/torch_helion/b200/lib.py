@@ -50,7 +50,7 @@ class RmsnormArgs(ctypes.Structure):
 
 class AllreduceArgs(ctypes.Structure):
     _fields_ = [("mc", _vp), ("peer_sig", _vp), ("sig", _vp), ("offset", _i64), ("bytes", _i64), ("dtype", _i32),
-                ("rank", _i32), ("world", _i32), ("ctas", _i32)]
+                ("rank", _i32), ("world", _i32), ("ctas", _i32), ("sumsq_mc", _vp), ("row_bytes", _i64)]
 
 
 ALLREDUCE_SIGNAL_BYTES = 20480  # TH_ALLREDUCE_SIGNAL_BYTES
@@ -192,15 +192,18 @@ def device_error(clear: bool = True) -> int:
 
 # ------------------------------------------------------------------ kernels
 def allreduce(mc: int, peer_sig: torch.Tensor, sig: torch.Tensor, offset: int, nbytes: int, dtype: torch.dtype,
-              rank: int, world: int, ctas: int = 0) -> None:
+              rank: int, world: int, ctas: int = 0, sumsq_mc: int = 0, row_bytes: int = 0) -> None:
     """In-place multicast sum all-reduce of bytes [offset, offset + nbytes) of a symmetric buffer
     (th_allreduce): ``mc`` is the buffer's multicast address, ``peer_sig`` an int64 device tensor of
-    every rank's signal-pad address, ``sig`` this rank's pad (uint8, zeroed before the first call)."""
+    every rank's signal-pad address, ``sig`` this rank's pad (uint8, zeroed before the first call).
+    With ``sumsq_mc`` (multicast address of an fp32 per-row array) every reduced row's sum of
+    squares is stored there too; each rank's slice must then be whole rows of ``row_bytes``."""
     if peer_sig.dtype != torch.int64 or peer_sig.numel() != world or not peer_sig.is_cuda:
         raise B200KernelError("allreduce: peer_sig must be an int64 CUDA tensor of world entries")
     if sig.numel() * sig.element_size() < ALLREDUCE_SIGNAL_BYTES:
         raise B200KernelError(f"allreduce: the signal pad needs {ALLREDUCE_SIGNAL_BYTES} bytes")
-    a = AllreduceArgs(mc, peer_sig.data_ptr(), sig.data_ptr(), offset, nbytes, _DTYPES[dtype], rank, world, ctas)
+    a = AllreduceArgs(mc, peer_sig.data_ptr(), sig.data_ptr(), offset, nbytes, _DTYPES[dtype], rank, world, ctas,
+                      sumsq_mc or None, row_bytes)
     _check(load().th_allreduce(ctypes.byref(a), _stream()), "th_allreduce")
 
 

@@ -53,6 +53,24 @@ class KernelLaunch:
     nbytes: int = 0
 
 
+def _chunk_bounds(rows: int, n: int) -> list[tuple[int, int]]:
+    """Row ranges of the ``n`` chunks of the tensor-parallel tail, multiples of 128 rows.
+
+    With three or more chunks the first and the last are half as tall as the
+    rest: the first chunk's all-reduce is the one the compute stream can wait
+    for (only the next chunk's o_proj runs beside it), and the last chunk's
+    all-reduce ends the forward with nothing to hide behind."""
+    w = [0.5] + [1.0] * (n - 2) + [0.5] if n >= 3 else [1.0] * n
+    tiles = (rows + 127) // 128
+    edges, acc = [0], 0.0
+    for i, wi in enumerate(w[:-1]):
+        acc += wi
+        e = int(round(acc / sum(w) * tiles))
+        edges.append(min(max(e, edges[-1] + 1), tiles - (n - 1 - i)))
+    edges.append(tiles)
+    return [(a * 128, min(rows, b * 128)) for a, b in zip(edges, edges[1:])]
+
+
 class CompiledProgram:
     """A Program bound to device memory on one GPU."""
 
@@ -90,6 +108,7 @@ class CompiledProgram:
         self._gemm_sm_limit = 0  # read by every GEMM launch when it runs
         self._multimem = False  # all-reduces through th_allreduce on symmetric buffers (decided in _build)
         self._symmetric: list = []
+        self._sym_views: dict = {}  # tensor name -> the SymmetricRows whose whole row it is
         self._pipe: tuple | None = None  # chunked tensor-parallel schedule (see _plan_tp_pipeline)
         with torch.cuda.device(self.device):
             self._build()
@@ -197,6 +216,13 @@ class CompiledProgram:
         """fp32 [T, nparts] whose row sums are sum(x^2) of tensor ``tname``."""
         if tname in self._ss_parts:
             return self._ss_parts[tname]
+        sym = self._sym_views.get(tname)
+        if sym is not None and sym.world > 1 and 128 % sym.world == 0 and sym.buf.shape[0] % 128 == 0:
+            # the multicast all-reduce that produces the tensor stores each row's sum of squares
+            # (every chunk is whole 128-row tiles, so every rank's slice of a chunk is whole rows)
+            sym.stats = True
+            self._ss_parts[tname] = sym.sumsq.view(-1, 1)
+            return self._ss_parts[tname]
         # no producer writes it: a th_rowstat launch right before the consumer
         x = self.views[tname]
         parts = self._empty(x.shape[0], 1, torch.float32)
@@ -225,6 +251,8 @@ class CompiledProgram:
         tail = self._empty(T, n_tail_pad, torch.float32) if n_tail else None
         for tname, (where, c0, c1) in p.outputs.items():
             self.views[tname] = (out if where == "main" else tail)[:, c0:c1]
+            if sym is not None and where == "main" and c0 == 0 and c1 == out.shape[1]:
+                self._sym_views[tname] = sym
         lhs = self._view(p.lhs)
         kw: dict = {}
         if p.rowscale is not None:
@@ -346,7 +374,8 @@ class CompiledProgram:
         chunk c's all-reduce runs on a communication stream while chunk c+1's
         GEMMs run on the compute stream, and the part after the first all-reduce
         of chunk c waits only for that chunk's all-reduce.  The rows of every
-        chunk are a multiple of 128 (whole GEMM row tiles)."""
+        chunk are a multiple of 128 (whole GEMM row tiles); the first and the
+        last chunk are half as tall as the others (see ``_chunk_bounds``)."""
         if self.tp_world <= 1 or self.tp_chunks <= 1:
             return
         first = next((i for i, l in enumerate(self.launches) if l.kind in _COLLECTIVES), None)
@@ -360,8 +389,7 @@ class CompiledProgram:
         n = min(self.tp_chunks, T // 128)
         if n <= 1:
             return
-        per = (T // n + 127) // 128 * 128
-        bounds = [(r0, min(T, r0 + per)) for r0 in range(0, T, per)]
+        bounds = _chunk_bounds(T, n)
         pre = seg[:2]    # the GEMM and its all-reduce
         post = seg[2:]   # everything after, per chunk
         self._pipe = (self.launches[:first - 1], pre, post, bounds, torch.cuda.Stream(device=self.device))
