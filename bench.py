@@ -418,6 +418,8 @@ def main() -> None:
         del runner
         if args.timeline is not None:  # every rank runs it (collectives inside); rank 0 writes it
             flush()
+            torch.cuda.synchronize()
+            barrier()  # the ranks start the forward together
             marks = mod.timeline()
             if rank == 0:
                 args.timeline.parent.mkdir(parents=True, exist_ok=True)

@@ -202,7 +202,7 @@ def _nccl_rank(rank, world, port, path, kw):
         (x,) = m.example_inputs(seed=1)
         res = compile_model(m, (x,), CompileConfig(run_name=f"tp{rank}", results_dir=path, device=f"cuda:{rank}",
                                                    world_size=world, tp_mode="heads", reference_check=False,
-                                                   verify_passes=False))
+                                                   verify_passes=False, tp_allreduce="nccl"))
         out = res.run(x.to(f"cuda:{rank}"))[0].float().cpu()
         torch.cuda.synchronize()
         torch.save(out, f"{path}/rank{rank}.pt")

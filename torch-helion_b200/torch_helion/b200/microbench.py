@@ -6,14 +6,14 @@
     python -m torch_helion.b200.microbench gemm --m 8192 --n 3328 --k 768 --vs-torch
     python -m torch_helion.b200.microbench conv --batch 4 --seq 2048 --channels 1792
     python -m torch_helion.b200.microbench rmsnorm --m 8192 --k 768
-    torchrun --nproc-per-node 8 -m torch_helion.b200.microbench allreduce --m 32768 --k 4096 --ctas 16,24,32
+    torchrun --nproc-per-node 8 -m torch_helion.b200.microbench allreduce --rows 32768 --cols 4096 --ctas 16,24,32
 
 Each mode runs 3 warm-up launches and times ``--iters`` launches with CUDA
 events (L2 flushed before each when ``--flush``), printing one JSON line with
 the median time and the kernel's algorithmic throughput.  This is the
 command behind the single-kernel ncu captures.
 
-``allreduce`` (one process per GPU under torchrun) sums a bf16 [m, k] array
+``allreduce`` (one process per GPU under torchrun) sums a bf16 [rows, cols] array
 over the ranks with ``th_allreduce`` for every ``--ctas`` grid size and
 with NCCL's ``all_reduce`` on the same bytes, checks that both give the
 same sums, and prints rank 0's line: the max over ranks of each median
@@ -119,18 +119,18 @@ def _allreduce(a) -> None:
     try:
         if not multimem_available(dev):
             raise lib.B200KernelError("no multicast symmetric memory on this node")
-        sym = SymmetricRows(a.m, a.k, torch.bfloat16, dev)
+        sym = SymmetricRows(a.rows, a.cols, torch.bfloat16, dev)
         g = torch.Generator(device=dev).manual_seed(dist.get_rank())
-        src = torch.randn(a.m, a.k, device=dev, generator=g).to(torch.bfloat16)
+        src = torch.randn(a.rows, a.cols, device=dev, generator=g).to(torch.bfloat16)
         ref = src.clone()
         dist.all_reduce(ref)
         sym.buf.copy_(src)
         torch.cuda.synchronize()
         dist.barrier()
-        sym.allreduce_rows(0, a.m)
+        sym.allreduce_rows(0, a.rows)
         torch.cuda.synchronize()
         same = bool(torch.equal(sym.buf, ref))
-        nbytes = a.m * a.k * 2
+        nbytes = a.rows * a.cols * 2
 
         def med(fn) -> float:  # median device time, max over ranks
             t = torch.tensor([_time(fn, a.iters, False)], device=dev, dtype=torch.float64)
@@ -140,7 +140,7 @@ def _allreduce(a) -> None:
         rows = {"nccl": med(lambda: dist.all_reduce(ref))}
         for c in (int(v) for v in a.ctas.split(",")):
             sym.ctas = c
-            rows[f"th_allreduce ctas={c}"] = med(lambda: sym.allreduce_rows(0, a.m))
+            rows[f"th_allreduce ctas={c}"] = med(lambda: sym.allreduce_rows(0, a.rows))
         err = lib.device_error()
         if dist.get_rank() == 0:
             print(json.dumps({"kernel": "allreduce", "ranks": dist.get_world_size(), "bytes": nbytes,
@@ -172,6 +172,9 @@ def main(argv=None) -> None:
     ap.add_argument("--channels", type=int, default=1792)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--ctas", default="16,24,32", help="allreduce: th_allreduce grid sizes to time")
+    # (not --m / --k: under torchrun those would be taken for abbreviations of its own options)
+    ap.add_argument("--rows", type=int, default=32768, help="allreduce: rows of the bf16 array")
+    ap.add_argument("--cols", type=int, default=4096, help="allreduce: columns of the bf16 array")
     ap.add_argument("--flush", action="store_true")
     ap.add_argument("--no-gate", action="store_true", help="ssd: no silu(z) gate, no D skip, no row sums")
     ap.add_argument("--vs-torch", action="store_true", help="gemm: also time torch.matmul (cuBLAS)")

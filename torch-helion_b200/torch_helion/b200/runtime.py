@@ -96,15 +96,15 @@ class CompiledProgram:
         self.tp_chunks = tp_chunks
         if tp_allreduce not in ("auto", "multimem", "nccl"):
             raise ValueError(f"tp_allreduce must be auto, multimem or nccl, not {tp_allreduce!r}")
-        # Measured on B200 (C3 block, 4 chunks): at 2 ranks the forward is compute-bound and NCCL's
-        # peer-to-peer all-reduce beats the multicast one (505 vs 395 GB/s on 256 MiB), so the GEMMs keep
-        # every SM; from 4 ranks on the all-reduces weigh as much as the GEMMs and the multicast kernel on
-        # 16 SMs of its own overlaps them best (8 ranks: 2.52 ms against 2.69 with 24 SMs and 3.14 over NCCL).
-        wide = tp_world >= 4
-        self.tp_allreduce = tp_allreduce if tp_allreduce != "auto" or wide else "nccl"
+        # Measured on B200 (C3 block, 4 chunks): the multicast kernel on 16 SMs of its own overlaps the
+        # GEMMs best -- 8 ranks: 2.52 ms per forward against 2.69 with 24 SMs and 3.14 over NCCL; 2 ranks
+        # (with the row statistics folded into it): 6.64 ms against 7.21 over NCCL with every SM to the
+        # GEMMs.  Where multicast is missing, NCCL runs with every SM left to the GEMMs.
+        self.tp_allreduce = tp_allreduce
         # SMs left to the collectives while the chunked schedule overlaps them with GEMMs: the GEMMs'
         # persistent grids are capped at (SMs - tp_comm_sms) there, and th_allreduce runs on that many CTAs
-        self.tp_comm_sms = tp_comm_sms if tp_comm_sms is not None else (16 if wide else 0)
+        self._comm_sms_arg = tp_comm_sms
+        self.tp_comm_sms = tp_comm_sms if tp_comm_sms is not None else 16
         self._gemm_sm_limit = 0  # read by every GEMM launch when it runs
         self._multimem = False  # all-reduces through th_allreduce on symmetric buffers (decided in _build)
         self._symmetric: list = []
@@ -183,6 +183,8 @@ class CompiledProgram:
             self._multimem = multimem_available(self.device)  # the same answer on every rank
             if not self._multimem and self.tp_allreduce == "multimem":
                 raise lib.B200KernelError("tp_allreduce='multimem' but this node has no multicast symmetric memory")
+        if not self._multimem and self._comm_sms_arg is None:
+            self.tp_comm_sms = 0  # NCCL beside GEMMs on every SM measured best without the multicast kernel
         f32 = fp32_outputs(prog)
         plans = {}
         for spec in prog.kernels:

@@ -40,11 +40,10 @@ class CompileConfig:
       tp_chunks          row chunks of the tensor-parallel part after attention:
                          each chunk's all-reduce overlaps the next chunk's GEMMs
       tp_comm_sms        SMs the GEMMs of that overlapped part leave to the collectives
-                         (also the grid of the multicast all-reduce kernel); None: 16 from
-                         4 ranks on, 0 at 2 ranks
+                         (also the grid of the multicast all-reduce kernel); None: 16 with
+                         the multicast all-reduce, 0 with NCCL
       tp_allreduce       "multimem" (th_allreduce on symmetric buffers through NVSwitch
-                         multicast), "nccl", or "auto" (multimem from 4 ranks on where every
-                         rank supports it, NCCL at 2 ranks)
+                         multicast), "nccl", or "auto" (multimem where every rank supports it)
       measure_iters      time the forward on the device (0 = skip)
     """
 
