@@ -68,14 +68,14 @@ static std::mutex g_tmap_mu;
 static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> g_tmap_cache;
 
 static TmapKey tmap_key(const void* base, int dtype, int rank, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
-                        uint64_t s2, uint32_t b0, uint32_t b1, bool swz) {
+                        uint64_t s2, uint32_t b0, uint32_t b1, int swz) {
   TmapKey k;
   memset(&k, 0, sizeof(k));
   k.base = base;
   k.dims[0] = d0; k.dims[1] = d1; k.dims[2] = d2;
   k.strides[0] = s1; k.strides[1] = s2;
   k.box[0] = b0; k.box[1] = b1;
-  k.dtype = dtype; k.rank = rank; k.swz = swz ? 1 : 0;
+  k.dtype = dtype; k.rank = rank; k.swz = swz;
   return k;
 }
 static bool tmap_lookup(const TmapKey& k, CUtensorMap* out) {
@@ -93,6 +93,11 @@ static void tmap_insert(const TmapKey& k, const CUtensorMap& m) {
 
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  return make_tmap_2d_sw(map, base, dtype, inner, outer, row_stride_bytes, box_inner, box_outer, swizzle128 ? 128 : 0);
+}
+
+int make_tmap_2d_sw(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
+                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, int swizzle_bytes) {
   std::call_once(g_encode_once, [] {
     cudaDriverEntryPointQueryResult q;
     void* fn = nullptr;
@@ -103,7 +108,9 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, 
   if (!g_encode) return fail(TH_ELAUNCH, "cuTensorMapEncodeTiled is not available from the driver");
   if (!aligned16(base)) return fail(TH_EALIGN, "TMA base address %p is not 16-byte aligned", base);
   if (row_stride_bytes % 16) return fail(TH_EALIGN, "TMA row stride %llu B is not a multiple of 16", (unsigned long long)row_stride_bytes);
-  const TmapKey key = tmap_key(base, dtype, 2, inner, outer, 0, row_stride_bytes, 0, box_inner, box_outer, swizzle128);
+  if (swizzle_bytes != 0 && swizzle_bytes != 64 && swizzle_bytes != 128)
+    return fail(TH_EINVAL, "TMA swizzle of %d bytes is not offered here", swizzle_bytes);
+  const TmapKey key = tmap_key(base, dtype, 2, inner, outer, 0, row_stride_bytes, 0, box_inner, box_outer, swizzle_bytes);
   if (tmap_lookup(key, map)) return TH_OK;
   CUtensorMapDataType dt = dtype == TH_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                            : dtype == TH_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -113,7 +120,9 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, 
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                        : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                              : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TH_ELAUNCH, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   tmap_insert(key, *map);
@@ -124,7 +133,7 @@ int make_tmap_3d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, 
                  uint64_t row_stride_bytes, uint64_t plane_stride_bytes, uint32_t box_inner, uint32_t box_rows,
                  bool swizzle128) {
   const TmapKey key = tmap_key(base, dtype, 3, inner, rows, planes, row_stride_bytes, plane_stride_bytes, box_inner,
-                               box_rows, swizzle128);
+                               box_rows, swizzle128 ? 128 : 0);
   if (tmap_lookup(key, map)) return TH_OK;
   CUtensorMap probe;  // resolves the driver entry point once and checks the 2-D part
   int rc = make_tmap_2d(&probe, base, dtype, inner, rows, row_stride_bytes, box_inner, box_rows, swizzle128);

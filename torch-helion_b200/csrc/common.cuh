@@ -578,6 +578,9 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int m, int n, int ab_fmt, 
 // library does not link libcuda directly.
 int make_tmap_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+// The same with a swizzle of 0, 64 or 128 bytes.
+int make_tmap_2d_sw(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
+                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, int swizzle_bytes);
 // 3-D map {inner, rows, planes} (strides in bytes), box {box_inner, box_rows, 1},
 // 128-byte swizzle; rows past `rows` read as zero and are not stored.
 int make_tmap_3d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t rows, uint64_t planes,

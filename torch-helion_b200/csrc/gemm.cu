@@ -11,6 +11,7 @@
 // epilogue (row scale, activation segment, RoPE, SwiGLU, residual, stores,
 // sum-of-squares partials), so the two paths have identical semantics.
 #include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 
@@ -38,6 +39,8 @@ struct EpiParams {
   int tail_begin;  // in output columns; >= n_out means none
   float* ss_out;
   int64_t ss_ld;
+  int tma_store;  // tcgen05 kernels: 32 x 32 output chunks leave through shared memory and a TMA store
+  int d_cols;     // columns of d the TMA store map covers (min(n_out, tail_begin))
 };
 
 // The activation of an activation segment (TH_ACT_*): torch's silu, softplus
@@ -174,6 +177,11 @@ __device__ __forceinline__ int2 tile_coords(int tile, int tiles_m, int tiles_n) 
   return make_int2(g * GM + r % gm, r / gm);  // (row tile, column tile)
 }
 
+// Output staging of the tcgen05 epilogue: every epilogue warp owns two 2 KB
+// buffers (32 rows x 64 bytes) in shared memory after the operand ring.
+constexpr int EPI_WARPS = 8, EPI_BUF_BYTES = 2048;
+constexpr int EPI_STAGE_BYTES = EPI_WARPS * 2 * EPI_BUF_BYTES;
+
 template <int BN>
 struct TcCfg {
   static constexpr int BM = 128, BK = 64;
@@ -183,7 +191,9 @@ struct TcCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + RING_BYTES + 256 /*barriers*/;
+  // ring | barriers (1 KB) | output staging (EPI_STAGE_BYTES)
+  static constexpr int STAGE_OFF = RING_BYTES + 1024;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGE_OFF + EPI_STAGE_BYTES;
 };
 
 // Residual add, store, fp32 tail and sum-of-squares partials of a 32-value
@@ -219,6 +229,88 @@ __device__ __forceinline__ float finish_chunk(float* v, int row, int oc, int n_o
   return ss;
 }
 
+struct OutStage {
+  uint8_t* buf;             // this warp's two buffers
+  const CUtensorMap* map;   // d as [rows, d_cols], box 32 x 32, 64-byte swizzle
+  uint32_t n;               // stores this warp has issued
+};
+
+// 8 values rounded to T and packed into 16 bytes; returns their sum of squares (of the rounded values).
+template <typename T>
+__device__ __forceinline__ float pack8_ss(const float* v, uint4& u) {
+  float s = 0.f;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f;
+    if constexpr (DT<T>::id == TH_BF16) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+      f = __bfloat1622float2(h);
+    } else {
+      __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+      f = __half22float2(h);
+    }
+    s = fmaf(f.x, f.x, fmaf(f.y, f.y, s));
+  }
+  return s;
+}
+
+// A warp's 32 rows x 32 columns of output (lane = row row0 + lane, its 32
+// values from column oc) leave through shared memory and one TMA store:
+// every lane writes its row as four 16-byte pieces in the layout of the
+// map's 64-byte swizzle (piece j of row r at slot j ^ ((r >> 1) & 3), so the
+// 32 rows of one store instruction fall on distinct bank groups eight rows at
+// a time), then lane 0 issues the store.  The buffer written here was last
+// read by the store two calls ago; rows and columns outside d are clipped by
+// the TMA unit.  All 32 lanes must call it.  Returns the lane's sum of
+// squares of the stored values.
+template <typename T>
+__device__ __forceinline__ float stage_store32(const float* v, OutStage& st, int oc, int row0, int lane) {
+  uint8_t* buf = st.buf + (st.n & 1) * EPI_BUF_BYTES;
+  if (lane == 0) bulk_wait_read1();
+  __syncwarp();
+  const uint32_t row_addr = smem_u32(buf) + (uint32_t)lane * 64u;
+  const int sw = (lane >> 1) & 3;
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 u;
+    ss += pack8_ss<T>(v + 8 * j, u);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row_addr + 16u * (uint32_t)(j ^ sw)), "r"(u.x),
+                 "r"(u.y), "r"(u.z), "r"(u.w)
+                 : "memory");
+  }
+  fence_proxy_async();  // the generic-proxy writes above, before the async-proxy read of the store
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(st.map, buf, oc, row0);
+    bulk_commit();
+  }
+  ++st.n;
+  return ss;
+}
+
+// Whether the 32-column chunk at output column oc goes out through stage_store32 (warp-uniform).
+__device__ __forceinline__ bool staged(const EpiParams& ep, int oc) {
+  return ep.tma_store && oc < ep.d_cols && oc + 32 <= ep.tail_begin;
+}
+
+// Residual of a 32-column chunk added to v (16-byte loads of this lane's row).
+template <typename T>
+__device__ __forceinline__ void add_residual32(float* v, int row, int oc, const EpiParams& ep) {
+  const T* res = reinterpret_cast<const T*>(ep.residual) + (int64_t)row * ep.ld_res + oc;
+#pragma unroll
+  for (int e8 = 0; e8 < 4; ++e8) {
+    if (oc + e8 * 8 >= ep.d_cols) break;  // n_out % 8 == 0: a piece is wholly inside or outside
+    float r8[8];
+    load8<T>(res + e8 * 8, r8);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e8 * 8 + e] += r8[e];
+  }
+}
+
 // Epilogue variants compiled as separate kernels (smaller code per kernel).
 constexpr int EPI_ROPE = 1, EPI_SWIGLU = 2, EPI_RES = 4;
 
@@ -238,7 +330,8 @@ __device__ __forceinline__ void res_issue(uint4 (&r)[4], int row, bool row_ok, i
 // first two chunks were issued before the accumulator was ready.
 template <typename T, int NC>
 __device__ __forceinline__ void epilogue_row_res(uint32_t tbase, int row, bool row_ok, float rs, int n0, int cb,
-                                                 const EpiParams& ep, uint4 (&rb)[3][4]) {
+                                                 const EpiParams& ep, uint4 (&rb)[3][4], OutStage& ost, int row0,
+                                                 int lane) {
   const int n_out = ep.n;
   T* d = reinterpret_cast<T*>(ep.d);
   const bool want_ss = ep.ss_out != nullptr;
@@ -261,7 +354,17 @@ __device__ __forceinline__ void epilogue_row_res(uint32_t tbase, int row, bool r
         }
       }
     }
-    if (row_ok) {
+    if (staged(ep, col)) {  // the whole warp: residual from the prefetched registers, then shared memory + TMA
+#pragma unroll
+      for (int e8 = 0; e8 < 4; ++e8) {
+        const uint4 u = rb[ci % 3][e8];
+        const T* rh = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e8 * 8 + e] += to_f32(rh[e]);
+      }
+      const float s32 = stage_store32<T>(v, ost, col, row0, lane);
+      if (want_ss) ss += s32;
+    } else if (row_ok) {
 #pragma unroll
       for (int e8 = 0; e8 < 4; ++e8) {
         const int cc = col + e8 * 8;
@@ -292,7 +395,7 @@ __device__ __forceinline__ void epilogue_row_res(uint32_t tbase, int row, bool r
 // Epilogue of one accumulator row (this thread) of a 128 x BN tile.
 template <typename T, int BN, int EPI>
 __device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_ok, float rs, int n0, int cb, int ce,
-                                             const EpiParams& ep) {
+                                             const EpiParams& ep, OutStage& ost, int row0, int lane) {
   if constexpr ((EPI & EPI_SWIGLU) != 0) {
     const int n_out = ep.n / 2;
     for (int g = cb / 128; g < ce / 128; ++g) {
@@ -304,7 +407,12 @@ __device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_o
 #pragma unroll
         for (int e = 0; e < 32; ++e) gv[e] = silu_f(gv[e] * rs) * (uv[e] * rs);
         const int oc = n0 / 2 + g * 64 + q * 32;
-        if (row_ok) ss += finish_chunk<T>(gv, row, oc, n_out, ep);
+        if (staged(ep, oc)) {
+          const float s32 = stage_store32<T>(gv, ost, oc, row0, lane);
+          if (ep.ss_out) ss += s32;
+        } else if (row_ok) {
+          ss += finish_chunk<T>(gv, row, oc, n_out, ep);
+        }
       }
       const int oc = n0 / 2 + g * 64;
       if (ep.ss_out && row_ok && oc < n_out) ep.ss_out[(int64_t)row * ep.ss_ld + (oc >> 6)] = ss;
@@ -374,7 +482,13 @@ __device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_o
         }
       }
     }
-    if (row_ok) ss += finish_chunk<T>(v, row, col, n_out, ep);
+    if (staged(ep, col)) {
+      if (ep.residual && row_ok) add_residual32<T>(v, row, col, ep);
+      const float s32 = stage_store32<T>(v, ost, col, row0, lane);
+      if (ep.ss_out) ss += s32;
+    } else if (row_ok) {
+      ss += finish_chunk<T>(v, row, col, n_out, ep);
+    }
     if (((c + 32) & 63) == 0) {
       const int g0 = col - 32;  // first column of this 64-column group
       if (ep.ss_out && row_ok && g0 < n_out && g0 < ep.tail_begin) ep.ss_out[(int64_t)row * ep.ss_ld + (g0 >> 6)] = ss;
@@ -390,7 +504,8 @@ __device__ __forceinline__ void epilogue_row(uint32_t tbase, int row, bool row_o
 // Returns false when the wait for the accumulator gave up.
 template <typename T, int BN, int EPI>
 __device__ __forceinline__ bool epilogue_tmem_tile(uint32_t tacc, int warp, int lane, int m0, int n0, uint64_t* tfull,
-                                              uint32_t parity, volatile int* abort_flag, const EpiParams& ep) {
+                                              uint32_t parity, volatile int* abort_flag, const EpiParams& ep,
+                                              OutStage& ost) {
   const int q = warp & 3;  // TMEM lane quarter this warp may read
   const int hh = (warp - 2) >> 2;
   const int rl = q * 32 + lane;
@@ -429,8 +544,9 @@ __device__ __forceinline__ bool epilogue_tmem_tile(uint32_t tacc, int warp, int 
   __syncwarp();
   tc_fence_after();
   const uint32_t tb = tacc + ((uint32_t)(q * 32) << 16);
-  if constexpr ((EPI & EPI_RES) != 0) epilogue_row_res<T, BN / 64>(tb, row, row_ok, rs, n0, cb, ep, rb);
-  else if (ce > cb) epilogue_row<T, BN, EPI>(tb, row, row_ok, rs, n0, cb, ce, ep);
+  const int row0 = m0 + q * 32;  // the warp's first row (its TMEM lane quarter)
+  if constexpr ((EPI & EPI_RES) != 0) epilogue_row_res<T, BN / 64>(tb, row, row_ok, rs, n0, cb, ep, rb, ost, row0, lane);
+  else if (ce > cb) epilogue_row<T, BN, EPI>(tb, row, row_ok, rs, n0, cb, ce, ep, ost, row0, lane);
   tc_fence_before();
   __syncwarp();
   return true;
@@ -438,7 +554,8 @@ __device__ __forceinline__ bool epilogue_tmem_tile(uint32_t tacc, int warp, int 
 
 template <typename T, int BN, int EPI>
 __global__ void __launch_bounds__(320, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiParams ep,
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmD, EpiParams ep,
                    int K, int tiles_m, int tiles_n) {
   using C = TcCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
@@ -469,6 +586,7 @@ __global__ void __launch_bounds__(320, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (ep.tma_store) tma_prefetch_desc(&tmD);
   }
   __syncwarp();
   if (warp == 0) tmem_alloc(tmem_slot, C::TMEM_COLS);  // warp-wide .sync.aligned
@@ -531,16 +649,18 @@ __global__ void __launch_bounds__(320, 1)
       tc_commit(done);  // tracks every MMA this thread issued
     }
   } else {  // ---- epilogue warps 2..9: two per TMEM lane quarter, each one half of the tile's columns
+    OutStage ost{smem + C::STAGE_OFF + (warp - 2) * 2 * EPI_BUF_BYTES, &tmD, 0};
     int i = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++i) {
       const int acc = i & 1, use = i >> 1;
       const int2 tc = tile_coords(tile, tiles_m, tiles_n);
       const int m0 = tc.x * C::BM, n0 = tc.y * BN;
       if (!epilogue_tmem_tile<T, BN, EPI>(tmem + (uint32_t)(acc * BN), warp, lane, m0, n0, &tfull[acc], use & 1,
-                                          abort_flag, ep))
+                                          abort_flag, ep, ost))
         break;
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (lane == 0) bulk_wait0();  // this warp's output stores are complete before the kernel ends
   }
   __syncwarp();
   // teardown: wait (bounded) for the MMAs to retire before freeing TMEM
@@ -572,15 +692,19 @@ struct Tc2Cfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = (BN / 2) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (196 * 1024) / STAGE_BYTES > 8 ? 8 : (196 * 1024) / STAGE_BYTES;
+  // the ring takes what 227 KB leave after the alignment slack, the barriers and the output staging
+  static constexpr int RING_MAX = 227 * 1024 - 2048 - EPI_STAGE_BYTES;
+  static constexpr int STAGES = RING_MAX / STAGE_BYTES > 8 ? 8 : RING_MAX / STAGE_BYTES;
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;  // a power of two
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + RING_BYTES + 256 /*barriers*/;
+  static constexpr int STAGE_OFF = RING_BYTES + 1024;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGE_OFF + EPI_STAGE_BYTES;
 };
 
 template <typename T, int BN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
-    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiParams ep,
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmD, EpiParams ep,
                     int K, int tiles_m, int tiles_n) {
   using C = Tc2Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
@@ -614,6 +738,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (ep.tma_store) tma_prefetch_desc(&tmD);
   }
   __syncwarp();
   if (warp == 0) tmem_alloc_pair(tmem_slot, C::TMEM_COLS);  // the same warp in both CTAs
@@ -684,16 +809,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     }
   } else {  // ---- epilogue warps 2..9 (both CTAs): this CTA's 128 rows of the pair's tile
     const uint32_t tempty0 = cluster_addr(tempty, 0);
+    OutStage ost{smem + C::STAGE_OFF + (warp - 2) * 2 * EPI_BUF_BYTES, &tmD, 0};
     int i = 0;
     for (int tile = pair; tile < ntiles; tile += npairs, ++i) {
       const int acc = i & 1, use = i >> 1;
       const int2 tc = tile_coords(tile, tiles_m, tiles_n);
       const int m0 = tc.x * 2 * C::BM + (int)rank * C::BM, n0 = tc.y * BN;
       if (!epilogue_tmem_tile<T, BN, EPI>(tmem + (uint32_t)(acc * BN), warp, lane, m0, n0, &tfull[acc], use & 1,
-                                          abort_flag, ep))
+                                          abort_flag, ep, ost))
         break;
       if (lane == 0) mbar_arrive_cluster(tempty0 + (uint32_t)(acc * 8));
     }
+    if (lane == 0) bulk_wait0();  // this warp's output stores are complete before the kernel ends
   }
   __syncwarp();
   // teardown: the even CTA waits (bounded) for its MMAs to retire; then neither
@@ -764,39 +891,71 @@ static int gemm_sms(const th_gemm_args* a) {
   return a->sm_limit > 0 && a->sm_limit < all ? (a->sm_limit < 2 ? 2 : a->sm_limit) : all;
 }
 
+// TH_GEMM_TMA_STORE=0: the tcgen05 epilogue stores each lane's row directly instead of staging
+// 32 x 32 chunks in shared memory for a TMA store (for comparisons; read once per process).
+static bool tma_store_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("TH_GEMM_TMA_STORE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Copy of the epilogue parameters with the staged output store set up: d as a [m, d_cols] tensor map
+// (box 32 x 32, 64-byte swizzle, matching stage_store32), where d_cols = min(n_out, tail_begin).
+static int with_out_map(const th_gemm_args* a, const EpiParams& ep, EpiParams* out, CUtensorMap* tm) {
+  *out = ep;
+  const int n_out = a->swiglu ? (int)(a->n / 2) : (int)a->n;
+  out->d_cols = ep.tail_begin < n_out ? ep.tail_begin : n_out;
+  out->tma_store = 0;
+  memset(tm, 0, sizeof(*tm));
+  if (!tma_store_enabled() || !a->d || out->d_cols < 8) return TH_OK;
+  const int rc = make_tmap_2d_sw(tm, a->d, a->dtype, (uint64_t)out->d_cols, (uint64_t)a->m, (uint64_t)a->ldd * 2, 32,
+                                 32, 64);
+  if (rc) return rc;
+  out->tma_store = 1;
+  return TH_OK;
+}
+
 template <typename T, int BN, int EPI>
-static int launch_tc(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st) {
+static int launch_tc(const th_gemm_args* a, const EpiParams& ep0, cudaStream_t st) {
   using C = TcCfg<BN>;
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, a->a, a->dtype, (uint64_t)a->k, (uint64_t)a->m, (uint64_t)a->lda * 2, 64, C::BM, true);
   if (rc) return rc;
   rc = make_tmap_2d(&tb, a->w, a->dtype, (uint64_t)a->k, (uint64_t)a->n, (uint64_t)a->ldw * 2, 64, BN, true);
   if (rc) return rc;
+  CUtensorMap td;
+  EpiParams ep;
+  if ((rc = with_out_map(a, ep0, &ep, &td))) return rc;
   if ((rc = smem_limit(gemm_tc_kernel<T, BN, EPI>, C::SMEM_BYTES, "th_gemm(tcgen05)"))) return rc;
   const int tiles_m = (int)((a->m + C::BM - 1) / C::BM), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n;
   const int grid = ntiles < gemm_sms(a) ? ntiles : gemm_sms(a);
   // a GEMM kept to part of the GPU launches without PDL, so the SMs it leaves free stay free for the
   // kernel beside it (with PDL its CTAs would take them early, waiting for the previous kernel)
-  launch_maybe_pdl(a->sm_limit <= 0, gemm_tc_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb, ep,
-                   (int)a->k, tiles_m, tiles_n);
+  launch_maybe_pdl(a->sm_limit <= 0, gemm_tc_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb, td,
+                   ep, (int)a->k, tiles_m, tiles_n);
   return check_launch("th_gemm(tcgen05)");
 }
 
 template <typename T, int BN, int EPI>
-static int launch_tc2(const th_gemm_args* a, const EpiParams& ep, cudaStream_t st) {
+static int launch_tc2(const th_gemm_args* a, const EpiParams& ep0, cudaStream_t st) {
   using C = Tc2Cfg<BN>;
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, a->a, a->dtype, (uint64_t)a->k, (uint64_t)a->m, (uint64_t)a->lda * 2, 64, C::BM, true);
   if (rc) return rc;
   rc = make_tmap_2d(&tb, a->w, a->dtype, (uint64_t)a->k, (uint64_t)a->n, (uint64_t)a->ldw * 2, 64, BN / 2, true);
   if (rc) return rc;
+  CUtensorMap td;
+  EpiParams ep;
+  if ((rc = with_out_map(a, ep0, &ep, &td))) return rc;
   if ((rc = smem_limit(gemm_tc2_kernel<T, BN, EPI>, C::SMEM_BYTES, "th_gemm(tcgen05 pair)"))) return rc;
   const int tiles_m = (int)((a->m + 2 * C::BM - 1) / (2 * C::BM)), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n, pairs = gemm_sms(a) / 2;
   const int grid = 2 * (ntiles < pairs ? ntiles : pairs);
-  launch_maybe_pdl(a->sm_limit <= 0, gemm_tc2_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb, ep,
-                   (int)a->k, tiles_m, tiles_n);
+  launch_maybe_pdl(a->sm_limit <= 0, gemm_tc2_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb,
+                   td, ep, (int)a->k, tiles_m, tiles_n);
   return check_launch("th_gemm(tcgen05 pair)");
 }
 
@@ -896,6 +1055,7 @@ extern "C" int th_gemm(const th_gemm_args* a, void* stream) {
   ep.swiglu = a->swiglu; ep.residual = a->residual; ep.ld_res = a->ld_res;
   ep.out2 = a->out2; ep.ld_out2 = a->ld_out2; ep.tail_begin = tail;
   ep.ss_out = a->ss_out; ep.ss_ld = a->ss_ld;
+  ep.tma_store = 0; ep.d_cols = tail;  // the tcgen05 launchers set up the staged store
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
   if (a->dtype == TH_F32) {
