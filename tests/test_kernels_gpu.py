@@ -95,6 +95,28 @@ def test_gemm_rowscale_residual_sumsq(L, dtype):
     assert rel_l2(ss, ss_ref) < 1e-5
 
 
+@pytest.mark.parametrize("m,n,k", [(4000, 800, 512), (300, 1000, 256), (8192, 4096, 512), (96, 768, 128)])
+def test_gemm_residual_widths(L, m, n, k):
+    """Residual epilogue across output widths: whole 32-column chunks (the residual arrives by TMA
+    into the staging buffer), a last column tile that is mostly past the output (n = 800), a width
+    that is not a multiple of 32 (per-lane residual loads), ragged rows and a single row tile."""
+    torch.manual_seed(9)
+    dt = torch.bfloat16
+    x = torch.randn(m, k, device=_dev()).to(dt)
+    w = (torch.randn(n, k, device=_dev()) * 0.05).to(dt)
+    res = torch.randn(m, n, device=_dev()).to(dt)
+    out = torch.empty(m, n, device=_dev(), dtype=dt)
+    ss = torch.zeros(m, (n + 63) // 64, device=_dev())
+    L.gemm(x, w, out, residual=res, ss_out=ss)
+    torch.cuda.synchronize()
+    assert L.device_error() == 0
+    assert rel_l2(out.float(), _gemm_ref(x, w) + res.float()) < TOL[dt]
+    o = out.float()
+    pad = (64 - n % 64) % 64
+    ss_ref = F.pad(o, (0, pad)).pow(2).reshape(m, -1, 64).sum(-1)
+    assert rel_l2(ss, ss_ref) < 1e-5
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_gemm_softplus_tail(L, dtype):
     """Mamba in_proj: z | xBC stored in the model dtype, dt = softplus(acc + bias)

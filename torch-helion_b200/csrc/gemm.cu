@@ -41,6 +41,7 @@ struct EpiParams {
   int64_t ss_ld;
   int tma_store;  // tcgen05 kernels: 32 x 32 output chunks leave through shared memory and a TMA store
   int d_cols;     // columns of d the TMA store map covers (min(n_out, tail_begin))
+  int res_tma;    // residual kernels: the residual chunk arrives by TMA into the same staging buffer
 };
 
 // The activation of an activation segment (TH_ACT_*): torch's silu, softplus
@@ -233,6 +234,9 @@ struct OutStage {
   uint8_t* buf;             // this warp's two buffers
   const CUtensorMap* map;   // d as [rows, d_cols], box 32 x 32, 64-byte swizzle
   uint32_t n;               // stores this warp has issued
+  const CUtensorMap* rmap;  // the residual, same geometry (res_tma)
+  uint64_t* bar;            // one mbarrier per buffer: the residual chunk loaded into it has landed
+  uint32_t loads;           // residual loads lane 0 has issued (chunk n's is the n-th)
 };
 
 // 8 values rounded to T and packed into 16 bytes; returns their sum of squares (of the rounded values).
@@ -292,6 +296,54 @@ __device__ __forceinline__ float stage_store32(const float* v, OutStage& st, int
   return ss;
 }
 
+// Lane 0: TMA-load the residual chunk (rows row0.., columns oc..) into buffer b of this warp.
+__device__ __forceinline__ void res_load32(OutStage& st, int b, int oc, int row0) {
+  mbar_arrive_expect_tx(&st.bar[b], EPI_BUF_BYTES);
+  tma_load_2d(st.buf + b * EPI_BUF_BYTES, st.rmap, &st.bar[b], oc, row0);
+  ++st.loads;
+}
+
+// Lane 0, as the warp leaves the epilogue: residual loads it issued that no chunk consumed (after a
+// wait gave up) land before the CTA ends; the wait is bounded as well.
+__device__ __forceinline__ void res_drain(OutStage& st) {
+  volatile int quit = 0;
+  for (uint32_t k = st.n; k < st.loads; ++k)
+    if (!mbar_wait_for(&st.bar[k & 1], (k >> 1) & 1, &quit, 100000000ull)) break;
+}
+
+// stage_store32 for a chunk whose residual sits in the buffer (res_load32): each lane adds its row
+// of the residual and writes the sums back in place, then lane 0 stores the buffer.  `want_ss`: sum
+// of squares of the stored values.  Returns false when the wait for the residual gave up.
+template <typename T>
+__device__ __forceinline__ bool stage_store32_res(float* v, OutStage& st, int oc, int row0, int lane, float& ss,
+                                                  volatile int* abort_flag) {
+  const int b = st.n & 1;
+  uint8_t* buf = st.buf + b * EPI_BUF_BYTES;
+  if (!mbar_wait(&st.bar[b], (st.n >> 1) & 1, abort_flag)) return false;
+  const uint32_t row_addr = smem_u32(buf) + (uint32_t)lane * 64u;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t a = row_addr + 16u * (uint32_t)(j ^ sw);
+    uint4 u;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w) : "r"(a));
+    const T* rh = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[8 * j + e] += to_f32(rh[e]);
+    ss += pack8_ss<T>(v + 8 * j, u);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(u.x), "r"(u.y), "r"(u.z), "r"(u.w)
+                 : "memory");
+  }
+  fence_proxy_async();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(st.map, buf, oc, row0);
+    bulk_commit();
+  }
+  ++st.n;
+  return true;
+}
+
 // Whether the 32-column chunk at output column oc goes out through stage_store32 (warp-uniform).
 __device__ __forceinline__ bool staged(const EpiParams& ep, int oc) {
   return ep.tma_store && oc < ep.d_cols && oc + 32 <= ep.tail_begin;
@@ -329,13 +381,51 @@ __device__ __forceinline__ void res_issue(uint4 (&r)[4], int row, bool row_ok, i
 // the residual of chunk c+2 is in flight while chunk c is stored, and the
 // first two chunks were issued before the accumulator was ready.
 template <typename T, int NC>
-__device__ __forceinline__ void epilogue_row_res(uint32_t tbase, int row, bool row_ok, float rs, int n0, int cb,
+__device__ __forceinline__ bool epilogue_row_res(uint32_t tbase, int row, bool row_ok, float rs, int n0, int cb,
                                                  const EpiParams& ep, uint4 (&rb)[3][4], OutStage& ost, int row0,
-                                                 int lane) {
+                                                 int lane, volatile int* abort_flag) {
   const int n_out = ep.n;
   T* d = reinterpret_cast<T*>(ep.d);
   const bool want_ss = ep.ss_out != nullptr;
   float ss = 0.f;
+  if (ep.res_tma) {
+    // the residual of chunks 0 and 1 was loaded into this warp's two buffers before the accumulator
+    // was ready; chunk ci + 2 is loaded into chunk ci's buffer once chunk ci's store has read it
+    for (int ci = 0; ci < NC; ++ci) {
+      const int c = cb + ci * 32, col = n0 + c;
+      if (col < ep.d_cols) {  // else past the output (last column tile); the sum-of-squares group still closes
+        float v[32];
+        tmem_ld32(tbase + c, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] *= rs;
+        if ((ep.act != TH_ACT_NONE || ep.bias) && col < ep.act_end && col + 32 > ep.act_begin) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int cc = col + e;
+            if (cc >= ep.act_begin && cc < ep.act_end) {
+              float x = v[e] + (ep.bias ? ep.bias[cc - ep.act_begin] : 0.f);
+              v[e] = act_apply(ep.act, x);
+            }
+          }
+        }
+        const int b = ost.n & 1;
+        float s32 = 0.f;
+        if (!stage_store32_res<T>(v, ost, col, row0, lane, s32, abort_flag)) return false;
+        if (want_ss) ss += s32;
+        if (lane == 0 && ci + 2 < NC && col + 64 < ep.d_cols) {
+          bulk_wait_read0();  // the store just issued has read the buffer
+          res_load32(ost, b, col + 64, row0);
+        }
+        __syncwarp();
+      }
+      if ((ci & 1) == 1) {
+        const int g0 = col - 32;
+        if (ep.ss_out && row_ok && g0 < n_out) ep.ss_out[(int64_t)row * ep.ss_ld + (g0 >> 6)] = ss;
+        ss = 0.f;
+      }
+    }
+    return true;
+  }
 #pragma unroll
   for (int ci = 0; ci < NC; ++ci) {
     const int c = cb + ci * 32, col = n0 + c;
@@ -390,6 +480,7 @@ __device__ __forceinline__ void epilogue_row_res(uint32_t tbase, int row, bool r
       ss = 0.f;
     }
   }
+  return true;
 }
 
 // Epilogue of one accumulator row (this thread) of a 128 x BN tile.
@@ -536,17 +627,30 @@ __device__ __forceinline__ bool epilogue_tmem_tile(uint32_t tacc, int warp, int 
     rs = rsqrtf(sacc * ep.rs_inv_k + ep.rs_eps);
   }
   uint4 rb[3][4];
+  const int row0 = m0 + q * 32;  // the warp's first row (its TMEM lane quarter)
   if constexpr ((EPI & EPI_RES) != 0) {
-    res_issue<T>(rb[0], row, row_ok, n0 + cb, ep);
-    res_issue<T>(rb[1], row, row_ok, n0 + cb + 32, ep);
+    if (ep.res_tma) {  // residual chunks 0 and 1 into this warp's two buffers, once earlier stores read them
+      if (lane == 0) {
+        bulk_wait_read0();
+#pragma unroll
+        for (int i = 0; i < 2 && i < BN / 64; ++i)
+          if (n0 + cb + 32 * i < ep.d_cols) res_load32(ost, (ost.n + i) & 1, n0 + cb + 32 * i, row0);
+      }
+      __syncwarp();
+    } else {
+      res_issue<T>(rb[0], row, row_ok, n0 + cb, ep);
+      res_issue<T>(rb[1], row, row_ok, n0 + cb + 32, ep);
+    }
   }
   if (!mbar_wait(tfull, parity, abort_flag)) return false;
   __syncwarp();
   tc_fence_after();
   const uint32_t tb = tacc + ((uint32_t)(q * 32) << 16);
-  const int row0 = m0 + q * 32;  // the warp's first row (its TMEM lane quarter)
-  if constexpr ((EPI & EPI_RES) != 0) epilogue_row_res<T, BN / 64>(tb, row, row_ok, rs, n0, cb, ep, rb, ost, row0, lane);
-  else if (ce > cb) epilogue_row<T, BN, EPI>(tb, row, row_ok, rs, n0, cb, ce, ep, ost, row0, lane);
+  if constexpr ((EPI & EPI_RES) != 0) {
+    if (!epilogue_row_res<T, BN / 64>(tb, row, row_ok, rs, n0, cb, ep, rb, ost, row0, lane, abort_flag)) return false;
+  } else if (ce > cb) {
+    epilogue_row<T, BN, EPI>(tb, row, row_ok, rs, n0, cb, ce, ep, ost, row0, lane);
+  }
   tc_fence_before();
   __syncwarp();
   return true;
@@ -555,7 +659,7 @@ __device__ __forceinline__ bool epilogue_tmem_tile(uint32_t tacc, int warp, int 
 template <typename T, int BN, int EPI>
 __global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmD, EpiParams ep,
+                   const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmR, EpiParams ep,
                    int K, int tiles_m, int tiles_n) {
   using C = TcCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
@@ -567,6 +671,7 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* ebar = reinterpret_cast<uint64_t*>(smem + C::RING_BYTES + 512);  // residual-load barriers, 2 per epilogue warp
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = tiles_m * tiles_n;
@@ -582,11 +687,13 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&tempty[a], 8);  // one arrive per epilogue warp
     }
     mbar_init(done, 1);
+    for (int b = 0; b < 2 * EPI_WARPS; ++b) mbar_init(&ebar[b], 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (ep.tma_store) tma_prefetch_desc(&tmD);
+    if (ep.res_tma) tma_prefetch_desc(&tmR);
   }
   __syncwarp();
   if (warp == 0) tmem_alloc(tmem_slot, C::TMEM_COLS);  // warp-wide .sync.aligned
@@ -649,7 +756,7 @@ __global__ void __launch_bounds__(320, 1)
       tc_commit(done);  // tracks every MMA this thread issued
     }
   } else {  // ---- epilogue warps 2..9: two per TMEM lane quarter, each one half of the tile's columns
-    OutStage ost{smem + C::STAGE_OFF + (warp - 2) * 2 * EPI_BUF_BYTES, &tmD, 0};
+    OutStage ost{smem + C::STAGE_OFF + (warp - 2) * 2 * EPI_BUF_BYTES, &tmD, 0, &tmR, ebar + 2 * (warp - 2), 0};
     int i = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++i) {
       const int acc = i & 1, use = i >> 1;
@@ -660,7 +767,10 @@ __global__ void __launch_bounds__(320, 1)
         break;
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
-    if (lane == 0) bulk_wait0();  // this warp's output stores are complete before the kernel ends
+    if (lane == 0) {
+      if (ep.res_tma) res_drain(ost);
+      bulk_wait0();  // this warp's output stores are complete before the kernel ends
+    }
   }
   __syncwarp();
   // teardown: wait (bounded) for the MMAs to retire before freeing TMEM
@@ -704,7 +814,7 @@ struct Tc2Cfg {
 template <typename T, int BN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmD, EpiParams ep,
+                   const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmR, EpiParams ep,
                     int K, int tiles_m, int tiles_n) {
   using C = Tc2Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
@@ -716,6 +826,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
   uint64_t* done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* ebar = reinterpret_cast<uint64_t*>(smem + C::RING_BYTES + 512);  // residual-load barriers, 2 per epilogue warp
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -734,11 +845,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
       mbar_init(&tempty[a], 16);  // one arrive per epilogue warp of both CTAs
     }
     mbar_init(done, 1);
+    for (int b = 0; b < 2 * EPI_WARPS; ++b) mbar_init(&ebar[b], 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (ep.tma_store) tma_prefetch_desc(&tmD);
+    if (ep.res_tma) tma_prefetch_desc(&tmR);
   }
   __syncwarp();
   if (warp == 0) tmem_alloc_pair(tmem_slot, C::TMEM_COLS);  // the same warp in both CTAs
@@ -809,7 +922,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     }
   } else {  // ---- epilogue warps 2..9 (both CTAs): this CTA's 128 rows of the pair's tile
     const uint32_t tempty0 = cluster_addr(tempty, 0);
-    OutStage ost{smem + C::STAGE_OFF + (warp - 2) * 2 * EPI_BUF_BYTES, &tmD, 0};
+    OutStage ost{smem + C::STAGE_OFF + (warp - 2) * 2 * EPI_BUF_BYTES, &tmD, 0, &tmR, ebar + 2 * (warp - 2), 0};
     int i = 0;
     for (int tile = pair; tile < ntiles; tile += npairs, ++i) {
       const int acc = i & 1, use = i >> 1;
@@ -820,7 +933,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
         break;
       if (lane == 0) mbar_arrive_cluster(tempty0 + (uint32_t)(acc * 8));
     }
-    if (lane == 0) bulk_wait0();  // this warp's output stores are complete before the kernel ends
+    if (lane == 0) {
+      if (ep.res_tma) res_drain(ost);
+      bulk_wait0();  // this warp's output stores are complete before the kernel ends
+    }
   }
   __syncwarp();
   // teardown: the even CTA waits (bounded) for its MMAs to retire; then neither
@@ -901,19 +1017,38 @@ static bool tma_store_enabled() {
   return on;
 }
 
+// TH_GEMM_TMA_RES=0: residual kernels load the residual with per-lane 16-byte loads instead of TMA.
+static bool tma_res_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("TH_GEMM_TMA_RES");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 // Copy of the epilogue parameters with the staged output store set up: d as a [m, d_cols] tensor map
-// (box 32 x 32, 64-byte swizzle, matching stage_store32), where d_cols = min(n_out, tail_begin).
-static int with_out_map(const th_gemm_args* a, const EpiParams& ep, EpiParams* out, CUtensorMap* tm) {
+// (box 32 x 32, 64-byte swizzle, matching stage_store32), where d_cols = min(n_out, tail_begin); and,
+// when every output chunk is staged (d_cols % 32 == 0, no fp32 tail), the residual as a map of the same
+// geometry for stage_store32_res.
+static int with_out_map(const th_gemm_args* a, const EpiParams& ep, EpiParams* out, CUtensorMap* tm,
+                        CUtensorMap* tr) {
   *out = ep;
   const int n_out = a->swiglu ? (int)(a->n / 2) : (int)a->n;
   out->d_cols = ep.tail_begin < n_out ? ep.tail_begin : n_out;
   out->tma_store = 0;
+  out->res_tma = 0;
   memset(tm, 0, sizeof(*tm));
+  memset(tr, 0, sizeof(*tr));
   if (!tma_store_enabled() || !a->d || out->d_cols < 8) return TH_OK;
-  const int rc = make_tmap_2d_sw(tm, a->d, a->dtype, (uint64_t)out->d_cols, (uint64_t)a->m, (uint64_t)a->ldd * 2, 32,
-                                 32, 64);
+  int rc = make_tmap_2d_sw(tm, a->d, a->dtype, (uint64_t)out->d_cols, (uint64_t)a->m, (uint64_t)a->ldd * 2, 32, 32, 64);
   if (rc) return rc;
   out->tma_store = 1;
+  if (a->residual && !a->swiglu && tma_res_enabled() && out->d_cols % 32 == 0 && ep.tail_begin >= n_out) {
+    rc = make_tmap_2d_sw(tr, a->residual, a->dtype, (uint64_t)out->d_cols, (uint64_t)a->m, (uint64_t)a->ld_res * 2, 32,
+                         32, 64);
+    if (rc) return rc;
+    out->res_tma = 1;
+  }
   return TH_OK;
 }
 
@@ -925,9 +1060,9 @@ static int launch_tc(const th_gemm_args* a, const EpiParams& ep0, cudaStream_t s
   if (rc) return rc;
   rc = make_tmap_2d(&tb, a->w, a->dtype, (uint64_t)a->k, (uint64_t)a->n, (uint64_t)a->ldw * 2, 64, BN, true);
   if (rc) return rc;
-  CUtensorMap td;
+  CUtensorMap td, tr;
   EpiParams ep;
-  if ((rc = with_out_map(a, ep0, &ep, &td))) return rc;
+  if ((rc = with_out_map(a, ep0, &ep, &td, &tr))) return rc;
   if ((rc = smem_limit(gemm_tc_kernel<T, BN, EPI>, C::SMEM_BYTES, "th_gemm(tcgen05)"))) return rc;
   const int tiles_m = (int)((a->m + C::BM - 1) / C::BM), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n;
@@ -935,7 +1070,7 @@ static int launch_tc(const th_gemm_args* a, const EpiParams& ep0, cudaStream_t s
   // a GEMM kept to part of the GPU launches without PDL, so the SMs it leaves free stay free for the
   // kernel beside it (with PDL its CTAs would take them early, waiting for the previous kernel)
   launch_maybe_pdl(a->sm_limit <= 0, gemm_tc_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb, td,
-                   ep, (int)a->k, tiles_m, tiles_n);
+                   tr, ep, (int)a->k, tiles_m, tiles_n);
   return check_launch("th_gemm(tcgen05)");
 }
 
@@ -947,15 +1082,15 @@ static int launch_tc2(const th_gemm_args* a, const EpiParams& ep0, cudaStream_t 
   if (rc) return rc;
   rc = make_tmap_2d(&tb, a->w, a->dtype, (uint64_t)a->k, (uint64_t)a->n, (uint64_t)a->ldw * 2, 64, BN / 2, true);
   if (rc) return rc;
-  CUtensorMap td;
+  CUtensorMap td, tr;
   EpiParams ep;
-  if ((rc = with_out_map(a, ep0, &ep, &td))) return rc;
+  if ((rc = with_out_map(a, ep0, &ep, &td, &tr))) return rc;
   if ((rc = smem_limit(gemm_tc2_kernel<T, BN, EPI>, C::SMEM_BYTES, "th_gemm(tcgen05 pair)"))) return rc;
   const int tiles_m = (int)((a->m + 2 * C::BM - 1) / (2 * C::BM)), tiles_n = (int)((a->n + BN - 1) / BN);
   const int ntiles = tiles_m * tiles_n, pairs = gemm_sms(a) / 2;
   const int grid = 2 * (ntiles < pairs ? ntiles : pairs);
   launch_maybe_pdl(a->sm_limit <= 0, gemm_tc2_kernel<T, BN, EPI>, dim3(grid), dim3(320), C::SMEM_BYTES, st, ta, tb,
-                   td, ep, (int)a->k, tiles_m, tiles_n);
+                   td, tr, ep, (int)a->k, tiles_m, tiles_n);
   return check_launch("th_gemm(tcgen05 pair)");
 }
 
@@ -1055,7 +1190,7 @@ extern "C" int th_gemm(const th_gemm_args* a, void* stream) {
   ep.swiglu = a->swiglu; ep.residual = a->residual; ep.ld_res = a->ld_res;
   ep.out2 = a->out2; ep.ld_out2 = a->ld_out2; ep.tail_begin = tail;
   ep.ss_out = a->ss_out; ep.ss_ld = a->ss_ld;
-  ep.tma_store = 0; ep.d_cols = tail;  // the tcgen05 launchers set up the staged store
+  ep.tma_store = 0; ep.d_cols = tail; ep.res_tma = 0;  // the tcgen05 launchers set up the staged store
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
   if (a->dtype == TH_F32) {

@@ -178,6 +178,7 @@ def main(argv=None) -> None:
     ap.add_argument("--flush", action="store_true")
     ap.add_argument("--no-gate", action="store_true", help="ssd: no silu(z) gate, no D skip, no row sums")
     ap.add_argument("--vs-torch", action="store_true", help="gemm: also time torch.matmul (cuBLAS)")
+    ap.add_argument("--residual", action="store_true", help="gemm: add a residual [m, n] in the epilogue")
     a = ap.parse_args(argv)
     torch.manual_seed(0)
     dev, bf = "cuda", torch.bfloat16
@@ -204,7 +205,11 @@ def main(argv=None) -> None:
         x = torch.randn(a.m, a.k, device=dev).to(bf)
         w = (torch.randn(a.n, a.k, device=dev) * 0.02).to(bf)
         d = torch.empty(a.m, a.n, device=dev, dtype=bf)
-        fn = lambda: lib.gemm(x, w, d)
+        if a.residual:  # the row-parallel projections' epilogue: + residual
+            res = torch.randn(a.m, a.n, device=dev).to(bf)
+            fn = lambda: lib.gemm(x, w, d, residual=res)
+        else:
+            fn = lambda: lib.gemm(x, w, d)
         work, unit = 2.0 * a.m * a.n * a.k, "TFLOP/s"
         if a.vs_torch:  # cuBLAS through torch on the same operands, for comparison
             extra["torch_us"] = _time(lambda: torch.matmul(x, w.t()), a.iters, a.flush) * 1e6
