@@ -178,9 +178,14 @@ class CompiledProgram:
             buf = self._empty(t.shape[0], cols, dt)
             self.views[name] = buf if dt == torch.int64 else buf[:, : t.shape[1]]
         if self.tp_world > 1 and self.tp_allreduce != "nccl" and any(self._allreduced(k) for k in prog.kernels):
+            import torch.distributed as dist
+
             from .collectives import multimem_available
 
-            self._multimem = multimem_available(self.device)  # the same answer on every rank
+            # only over a process group of this program's ranks; otherwise the caller's all-reduce
+            # (e.g. a stand-in that runs one rank's shard alone) is used
+            grouped = dist.is_available() and dist.is_initialized() and dist.get_world_size() == self.tp_world
+            self._multimem = grouped and multimem_available(self.device)  # the same answer on every rank
             if not self._multimem and self.tp_allreduce == "multimem":
                 raise lib.B200KernelError("tp_allreduce='multimem' but this node has no multicast symmetric memory")
         if not self._multimem and self._comm_sms_arg is None:
