@@ -1095,9 +1095,13 @@ static int launch_tc2(const th_gemm_args* a, const EpiParams& ep0, cudaStream_t 
 }
 
 // Tile width of the pair kernel: the one with the least wave-quantised work,
-// rounds x (BN + 32) (the 32 stands for a tile's fixed cost).  192 is offered
-// only where no 64-column group (SwiGLU block, RoPE head, sum-of-squares
-// group) may straddle the epilogue's column halves.
+// rounds x (BN + 320).  The 320 is fitted to B200 timings: a tile costs far
+// more than its width suggests at narrow widths (32768 x 3584 x 4096: 1071 /
+// 778 / 660 us at BN 128 / 192 / 256, i.e. 49 / 33 / 25 rounds; 8192 x 3352 x
+// 768: 69.6 / 53.3 / 49.2 us), so 256 wins unless it leaves a whole round
+// nearly empty (8192 x 768 x 1536: 192 at 30.7 us against 31.6).  192 is
+// offered only where no 64-column group (SwiGLU block, RoPE head,
+// sum-of-squares group) may straddle the epilogue's column halves.
 static int pair_mode() {  // TH_GEMM_PAIR: 0 single-CTA kernel, 1 (default) pair kernel, 128/192/256 its width
   static const int env = [] {
     const char* e = getenv("TH_GEMM_PAIR");
@@ -1116,7 +1120,7 @@ static int pair_width(const th_gemm_args* a) {
   for (int bn : {256, 192, 128}) {
     if (bn == 192 && no192) continue;
     const int64_t rounds = (tm * ((a->n + bn - 1) / bn) + pairs - 1) / pairs;
-    const int64_t cost = rounds * (bn + 32);
+    const int64_t cost = rounds * (bn + 320);
     if (cost < best_cost) best_cost = cost, best = bn;
   }
   return best;
