@@ -179,6 +179,8 @@ def main(argv=None) -> None:
     ap.add_argument("--no-gate", action="store_true", help="ssd: no silu(z) gate, no D skip, no row sums")
     ap.add_argument("--vs-torch", action="store_true", help="gemm: also time torch.matmul (cuBLAS)")
     ap.add_argument("--residual", action="store_true", help="gemm: add a residual [m, n] in the epilogue")
+    ap.add_argument("--swiglu", action="store_true",
+                    help="gemm: row-scaled SwiGLU epilogue (gate/up interleaved in 64-column blocks), output [m, n/2]")
     a = ap.parse_args(argv)
     torch.manual_seed(0)
     dev, bf = "cuda", torch.bfloat16
@@ -204,10 +206,13 @@ def main(argv=None) -> None:
     elif a.kernel == "gemm":
         x = torch.randn(a.m, a.k, device=dev).to(bf)
         w = (torch.randn(a.n, a.k, device=dev) * 0.02).to(bf)
-        d = torch.empty(a.m, a.n, device=dev, dtype=bf)
+        d = torch.empty(a.m, a.n // 2 if a.swiglu else a.n, device=dev, dtype=bf)
         if a.residual:  # the row-parallel projections' epilogue: + residual
             res = torch.randn(a.m, a.n, device=dev).to(bf)
             fn = lambda: lib.gemm(x, w, d, residual=res)
+        elif a.swiglu:  # the MLP's gate|up epilogue: RMSNorm row scale from 64-column partial sums, SwiGLU
+            parts = torch.rand(a.m, (a.k + 63) // 64, device=dev) * 64.0
+            fn = lambda: lib.gemm(x, w, d, rs_parts=parts, rs_inv_k=1.0 / a.k, rs_eps=1e-5, swiglu=True)
         else:
             fn = lambda: lib.gemm(x, w, d)
         work, unit = 2.0 * a.m * a.n * a.k, "TFLOP/s"
