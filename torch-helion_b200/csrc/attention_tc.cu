@@ -311,6 +311,329 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
+// ---------------------------------------------------------------------------
+// attention_tc2q_kernel: two 128-row query tiles per CTA share every K/V
+// block, so the tensor core works on one tile while the other tile's softmax
+// runs (ping-pong).  320 threads:
+//   warp 0     TMA: both query tiles once, then K_i and V_i (K and V rings)
+//   warp 1     MMA, issued in the order
+//                S0(i) = Q0 K_i^T, O1 += P1(i-1) V(i-1), S1(i) = Q1 K_i^T, O0 += P0(i) V(i)
+//              so that while softmax 0 works on S0(i) the tensor core runs tile 1's
+//              product and score block, and the other way round.  P_t(i) lives in
+//              the last 64 columns of its S_t buffer (bf16 pairs) and is read by
+//              the P.V MMA from TMEM; S_t(i+1) is issued after O_t += P_t(i) V(i)
+//              by the same thread, and the tcgen05.mma operations of one thread
+//              run in issue order, so the product has read P_t(i) before S_t(i+1)
+//              overwrites it.
+//   warps 2-5  softmax of tile 0, warps 6-9 of tile 1 (warp w serves TMEM lane
+//              quadrant w % 4, so each tile covers all four): one thread per query
+//              row (its TMEM lane); online softmax in the log2 domain with a lazy
+//              rescale of O_t (only when the running max grows by more than 2^8).
+//              O_t is idle while the softmax of block i runs: O_t += P_t(i-1) V(i-1)
+//              was issued before S_t(i), and the commit that signalled S_t(i)
+//              covers every earlier MMA of the issuing thread.  After the last
+//              block the same threads normalise O_t and store it.
+// Causal masking: tile 0 stops one KV block before tile 1 (that block lies wholly
+// above its diagonal); diagonal blocks are masked per element.
+// TMEM: S0 [0,128), S1 [128,256), O0 [256, 256+D), O1 [256+D, 256+2D).
+template <int D>
+struct At2Cfg {
+  static constexpr int BM = 128, BN = 128;
+  static constexpr int DA = D / 64;
+  static constexpr int Q_BYTES = BM * D * 2;  // one query tile
+  static constexpr int KV_BYTES = BN * D * 2;
+  // K and V ring depths; at D = 64 the deeper K ring also keeps one CTA per SM (each takes all of TMEM)
+  static constexpr int KS = D == 64 ? 3 : 2, VS = 3;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = 2 * Q_BYTES;
+  static constexpr int OFF_V = OFF_K + KS * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + VS * KV_BYTES;
+  static constexpr int SMEM = 1024 + OFF_BAR + 256;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(SMEM > 227 * 1024 / 2, "one CTA per SM");
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(320, 1)
+    attention_tc2q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, th_attention_args p) {
+  using C = At2Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_align<1024>(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;           // [KS]
+  uint64_t* k_empty = k_full + C::KS;    // [KS]
+  uint64_t* v_full = k_empty + C::KS;    // [VS]
+  uint64_t* v_empty = v_full + C::VS;    // [VS]
+  uint64_t* s_full = v_empty + C::VS;    // [2] per tile
+  uint64_t* p_full = s_full + 2;         // [2] per tile (its 4 softmax warps arrive)
+  uint64_t* o_done = p_full + 2;         // [2] per tile: its last P.V product is complete
+  uint64_t* mma_done = o_done + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = (p.seq + 2 * C::BM - 1) / (2 * C::BM);
+  const int qb = nqb - 1 - (int)blockIdx.x;  // heaviest (most KV blocks) first when causal
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.hq / p.hkv);
+  const int q0 = qb * 2 * C::BM;
+  const int64_t row0 = (int64_t)b * p.seq;
+  const int nkv_all = (p.seq + C::BN - 1) / C::BN;
+  // KV blocks of each tile (the causal bound of its last row)
+  const int nkv0 = p.causal ? min(nkv_all, (q0 + C::BM - 1) / C::BN + 1) : nkv_all;
+  const int nkv1 = p.causal ? min(nkv_all, (q0 + 2 * C::BM - 1) / C::BN + 1) : nkv_all;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::KS; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1); }
+    for (int s = 0; s < C::VS; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_done[t], 1);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  __syncwarp();
+  if (warp == 0) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  pdl_wait();  // the previous kernel's outputs (this kernel's inputs) are complete
+  pdl_trigger();
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ------------------------------------------- TMA
+      mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
+      for (int t = 0; t < 2; ++t)
+        for (int a = 0; a < C::DA; ++a)
+          tma_load_2d(sm + C::OFF_Q + t * C::Q_BYTES + a * C::BM * 128, &tmQ, q_full, h * D + a * 64,
+                      (int)(row0 + q0 + t * C::BM));
+      for (int i = 0; i < nkv1; ++i) {
+        const int ks = i % C::KS, vs = i % C::VS;
+        if (!mbar_wait(&k_empty[ks], ((i / C::KS) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&k_full[ks], C::KV_BYTES);
+        for (int a = 0; a < C::DA; ++a)
+          tma_load_2d(sm + C::OFF_K + ks * C::KV_BYTES + a * C::BN * 128, &tmK, &k_full[ks], hk * D + a * 64,
+                      (int)(row0 + i * C::BN));
+        if (!mbar_wait(&v_empty[vs], ((i / C::VS) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&v_full[vs], C::KV_BYTES);
+        for (int a = 0; a < C::DA; ++a)
+          tma_load_2d(sm + C::OFF_V + vs * C::KV_BYTES + a * C::BN * 128, &tmV, &v_full[vs], hk * D + a * 64,
+                      (int)(row0 + i * C::BN));
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ------------------------------------------- MMA
+      constexpr int fmt = DT<T>::id == TH_BF16 ? 1 : 0;
+      constexpr uint32_t id_s = make_idesc_f16(128, C::BN, fmt, 0, 0);
+      constexpr uint32_t id_o = make_idesc_f16(128, D, fmt, 0, 1);  // V: MN-major
+      auto issue_s = [&](int t, int i) {  // S_t = Q_t K_i^T
+        const uint32_t qa = smem_u32(sm + C::OFF_Q + t * C::Q_BYTES);
+        const uint32_t ka = smem_u32(sm + C::OFF_K + (i % C::KS) * C::KV_BYTES);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (uint32_t)((k >> 2) * C::BM * 128 + (k & 3) * 32);
+          const uint32_t koff = (uint32_t)((k >> 2) * C::BN * 128 + (k & 3) * 32);
+          tc_mma_f16(tmem + t * 128, make_desc_sw128(qa + off, 16, 1024), make_desc_sw128(ka + koff, 16, 1024), id_s,
+                     k ? 1u : 0u);
+        }
+        tc_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int i) {  // O_t += P_t V_i; keys 2c, 2c+1 of P_t in column 64 + c of S_t
+        const uint32_t va = smem_u32(sm + C::OFF_V + (i % C::VS) * C::KV_BYTES);
+#pragma unroll
+        for (int k = 0; k < C::BN / 16; ++k)
+          tc_mma_f16_ts(tO + (uint32_t)(t * D), tmem + (uint32_t)(t * 128 + 64 + k * 8),
+                        make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o, (i | k) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag);
+      for (int i = 0; ok && i < nkv1; ++i) {
+        if (!(ok = mbar_wait(&k_full[i % C::KS], (i / C::KS) & 1, abort_flag))) break;
+        tc_fence_after();
+        if (i < nkv0) issue_s(0, i);
+        if (i > 0) {  // tile 1's product of the previous block, then its scores of this one
+          if (!(ok = mbar_wait(&p_full[1], (i - 1) & 1, abort_flag))) break;
+          tc_fence_after();
+          issue_pv(1, i - 1);
+          tc_commit(&v_empty[(i - 1) % C::VS]);  // tile 1 is the last reader of V_{i-1}
+        }
+        issue_s(1, i);
+        tc_commit(&k_empty[i % C::KS]);  // ... and of K_i
+        if (i < nkv0) {
+          if (!(ok = mbar_wait(&v_full[i % C::VS], (i / C::VS) & 1, abort_flag) &&
+                     mbar_wait(&p_full[0], i & 1, abort_flag)))
+            break;
+          tc_fence_after();
+          issue_pv(0, i);
+          if (i == nkv0 - 1) tc_commit(&o_done[0]);
+        }
+      }
+      if (ok) {  // tile 1's last product (its V was not waited for when tile 0 stopped a block early)
+        const int i = nkv1 - 1;
+        ok = (i < nkv0 || mbar_wait(&v_full[i % C::VS], (i / C::VS) & 1, abort_flag)) &&
+             mbar_wait(&p_full[1], i & 1, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          issue_pv(1, i);
+          tc_commit(&v_empty[i % C::VS]);
+          tc_commit(&o_done[1]);
+        }
+      }
+      tc_commit(mma_done);
+    }
+  } else {  // ---------------------------------------------- softmax + epilogue, one thread per row
+    const int t = (warp - 2) >> 2;       // query tile
+    const int q4 = warp & 3;             // TMEM lane quadrant
+    const int r = q4 * 32 + lane;        // row within the tile (TMEM lane)
+    const int qt = q0 + t * C::BM;       // first query of the tile
+    const int qi = qt + r;               // this row's query position
+    const int nkv = t ? nkv1 : nkv0;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t tS = tmem + lane_off + (uint32_t)(t * 128);  // S_t / P_t row
+    const uint32_t tOr = tO + lane_off + (uint32_t)(t * D);       // O_t row
+    const float sl2 = p.scale * 1.4426950408889634f;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      ok = __all_sync(0xffffffffu, ok && mbar_wait(&s_full[t], j & 1, abort_flag));
+      if (ok) {
+        tc_fence_after();
+        // Two passes over the 128 scores so that at most 96 are held at once: the max over key
+        // chunks 0-1, then 2-3 (which stay in registers), then P of chunks 2, 3 and of 0, 1 read
+        // again from TMEM.  P of key chunk c goes to columns 64 + 16c, over the scores of chunks
+        // 2-3, which are in registers by then; chunks 0-1 are never overwritten.
+        const int k0 = j * C::BN;
+        const bool edge = (p.causal && k0 + C::BN - 1 > qt) || k0 + C::BN > p.seq;  // diagonal or ragged
+        auto mask = [&](uint32_t(&v)[32], int c) {
+          if (edge) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int kj = k0 + c * 32 + e;
+              if (kj >= p.seq || (p.causal && kj > qi)) v[e] = __float_as_uint(-INFINITY);
+            }
+          }
+        };
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        auto vmax = [&](const uint32_t(&v)[32]) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) m4[e & 3] = fmaxf(m4[e & 3], __uint_as_float(v[e]));
+        };
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld32_issue(tS, r0);
+        tmem_ld32_issue(tS + 32, r1);
+        tmem_wait_ld32(r0);
+        tmem_wait_ld32(r1);
+        mask(r0, 0);
+        mask(r1, 1);
+        vmax(r0);
+        vmax(r1);
+        tmem_ld32_issue(tS + 64, r2);
+        tmem_ld32_issue(tS + 96, r3);
+        tmem_wait_ld32(r2);
+        tmem_wait_ld32(r3);
+        mask(r2, 2);
+        mask(r3, 3);
+        vmax(r2);
+        vmax(r3);
+        const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;  // the scale is positive
+        // the reference max moves only when the row max grows by more than 2^8 (lazy rescale)
+        const float m_new = fmaxf(m_ref, mx);
+        const bool rescale = j > 0 && m_new > m_ref + 8.0f;
+        const float m_use = (j == 0 || rescale) ? m_new : m_ref;
+        const float mref = (m_use == -INFINITY) ? 0.f : m_use;  // fully masked row: P = 0
+        float l4[4] = {0.f, 0.f, 0.f, 0.f};
+        auto emit = [&](const uint32_t(&v)[32], int c) {  // exp2, row sum, bf16 pairs to P columns 64 + 16c
+          uint32_t pk[16];
+#pragma unroll
+          for (int w = 0; w < 16; ++w) {
+            const float p0 = ex2_fast(fmaf(__uint_as_float(v[2 * w]), sl2, -mref));
+            const float p1 = ex2_fast(fmaf(__uint_as_float(v[2 * w + 1]), sl2, -mref));
+            l4[w & 3] += p0 + p1;
+            pk[w] = pack2<T>(p0, p1);
+          }
+          tmem_st16_nowait(tS + 64 + c * 16, pk);
+        };
+        emit(r2, 2);
+        tmem_ld32_issue(tS, r0);  // chunk 0 again, while chunk 3 becomes P
+        emit(r3, 3);
+        tmem_wait_ld32(r0);
+        tmem_ld32_issue(tS + 32, r1);
+        mask(r0, 0);
+        emit(r0, 0);
+        tmem_wait_ld32(r1);
+        mask(r1, 1);
+        emit(r1, 1);
+        // O_t is idle (see above) until this block's P is signalled: rescale it in place, after the
+        // scores have left the registers
+        const float f = rescale ? ex2_fast(m_ref - m_new) : 1.f;
+        if (__any_sync(0xffffffffu, rescale)) {
+          for (int c = 0; c < D; c += 16) {
+            uint32_t o[16];
+            tmem_ld16_issue(tOr + c, o);
+            tmem_wait_ld(o);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+            tmem_st16_nowait(tOr + c, o);
+          }
+        }
+        tmem_wait_st();
+        l = fmaf(l, f, (l4[0] + l4[1]) + (l4[2] + l4[3]));
+        m_ref = m_use;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    // epilogue: O_t / l once the tile's last product is complete
+    if (ok) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&o_done[t], 0, abort_flag));
+      tc_fence_after();
+    }
+    if (ok) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* orow = reinterpret_cast<T*>(p.o) + (row0 + qi) * p.ldo + (int64_t)h * D;
+      for (int c = 0; c < D; c += 32) {
+        float o[32];
+        tmem_ld32(tOr + c, o);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] *= inv;
+        if (qi < p.seq) {
+#pragma unroll
+          for (int e8 = 0; e8 < 32; e8 += 8) store8<T>(orow + c + e8, o + e8);
+        }
+      }
+    }
+  }
+  __syncwarp();
+  if (threadIdx.x == 64) {  // TMEM must be idle before it is freed
+    volatile int dummy = 0;
+    mbar_wait(mma_done, 0, &dummy);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// TH_ATTN_TILES=2 selects the two-tile kernel (default: one tile per CTA)
+static bool attn_two_tiles() {
+  static const bool v = [] {
+    const char* e = getenv("TH_ATTN_TILES");
+    return e && e[0] == '2';
+  }();
+  return v;
+}
+
 // bf16/fp16, head_dim 64/128, 16-byte aligned rows; returns 1 (not taken) otherwise.
 template <typename T>
 static int attention_tc_try(const th_attention_args* a, cudaStream_t st, int* rc) {
@@ -326,6 +649,18 @@ static int attention_tc_try(const th_attention_args* a, cudaStream_t st, int* rc
   if (!r) r = make_tmap_2d(&tk, a->k, a->dtype, (uint64_t)a->hkv * D, (uint64_t)T_, (uint64_t)a->ldk * 2, 64, 128, true);
   if (!r) r = make_tmap_2d(&tv, a->v, a->dtype, (uint64_t)a->hkv * D, (uint64_t)T_, (uint64_t)a->ldv * 2, 64, 128, true);
   if (r) { *rc = r; return 0; }
+  if (attn_two_tiles()) {
+    const dim3 grid2((unsigned)((a->seq + 255) / 256), (unsigned)a->hq, (unsigned)a->batch);
+    if (D == 128) {
+      if ((*rc = smem_limit(attention_tc2q_kernel<T, 128>, At2Cfg<128>::SMEM, "th_attention(tcgen05, 2 tiles)"))) return 0;
+      launch_pdl(attention_tc2q_kernel<T, 128>, grid2, dim3(320), At2Cfg<128>::SMEM, st, tq, tk, tv, *a);
+    } else {
+      if ((*rc = smem_limit(attention_tc2q_kernel<T, 64>, At2Cfg<64>::SMEM, "th_attention(tcgen05, 2 tiles)"))) return 0;
+      launch_pdl(attention_tc2q_kernel<T, 64>, grid2, dim3(320), At2Cfg<64>::SMEM, st, tq, tk, tv, *a);
+    }
+    *rc = check_launch("th_attention(tcgen05, 2 tiles)");
+    return 0;
+  }
   dim3 grid((unsigned)((a->seq + 127) / 128), (unsigned)a->hq, (unsigned)a->batch);
   if (D == 128) {
     if ((*rc = smem_limit(attention_tc_kernel<T, 128>, AtCfg<128>::SMEM, "th_attention(tcgen05)"))) return 0;
