@@ -510,17 +510,17 @@ __global__ void __launch_bounds__(320, 1)
         tc_fence_after();
         // Two passes over the 128 scores so that at most 96 are held at once: the max over key
         // chunks 0-1, then 2-3 (which stay in registers), then P of chunks 2, 3 and of 0, 1 read
-        // again from TMEM.  P of key chunk c goes to columns 64 + 16c, over the scores of chunks
+        // again from TMEM (in a diagonal or ragged block, masked before they were stored back).  P of key chunk c goes to columns 64 + 16c, over the scores of chunks
         // 2-3, which are in registers by then; chunks 0-1 are never overwritten.
         const int k0 = j * C::BN;
         const bool edge = (p.causal && k0 + C::BN - 1 > qt) || k0 + C::BN > p.seq;  // diagonal or ragged
+        // keys k0 + e with e >= nvalid are masked: past the sequence, or after this row when causal
+        const int nvalid = min(p.seq, p.causal ? qi + 1 : p.seq) - k0;
         auto mask = [&](uint32_t(&v)[32], int c) {
           if (edge) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int kj = k0 + c * 32 + e;
-              if (kj >= p.seq || (p.causal && kj > qi)) v[e] = __float_as_uint(-INFINITY);
-            }
+            for (int e = 0; e < 32; ++e)
+              if (c * 32 + e >= nvalid) v[e] = __float_as_uint(-INFINITY);
           }
         };
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -533,8 +533,12 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld32_issue(tS + 32, r1);
         tmem_wait_ld32(r0);
         tmem_wait_ld32(r1);
-        mask(r0, 0);
-        mask(r1, 1);
+        if (edge) {  // masked scores of chunks 0-1 go back to TMEM, so their second read needs no mask
+          mask(r0, 0);
+          mask(r1, 1);
+          tmem_st32_nowait(tS, r0);
+          tmem_st32_nowait(tS + 32, r1);
+        }
         vmax(r0);
         vmax(r1);
         tmem_ld32_issue(tS + 64, r2);
@@ -563,15 +567,14 @@ __global__ void __launch_bounds__(320, 1)
           }
           tmem_st16_nowait(tS + 64 + c * 16, pk);
         };
+        if (edge) tmem_wait_st();  // the masked chunks 0-1 are in TMEM before they are read again
         emit(r2, 2);
         tmem_ld32_issue(tS, r0);  // chunk 0 again, while chunk 3 becomes P
         emit(r3, 3);
         tmem_wait_ld32(r0);
         tmem_ld32_issue(tS + 32, r1);
-        mask(r0, 0);
         emit(r0, 0);
         tmem_wait_ld32(r1);
-        mask(r1, 1);
         emit(r1, 1);
         // O_t is idle (see above) until this block's P is signalled: rescale it in place, after the
         // scores have left the registers
