@@ -353,7 +353,7 @@ struct At2Cfg {
   static_assert(SMEM > 227 * 1024 / 2, "one CTA per SM");
 };
 
-template <typename T, int D>
+template <typename T, int D, int EMU>
 __global__ void __launch_bounds__(320, 1)
     attention_tc2q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, th_attention_args p) {
@@ -508,9 +508,9 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu, ok && mbar_wait(&s_full[t], j & 1, abort_flag));
       if (ok) {
         tc_fence_after();
-        // Two passes over the 128 scores so that at most 96 are held at once: the max over key
-        // chunks 0-1, then 2-3 (which stay in registers), then P of chunks 2, 3 and of 0, 1 read
-        // again from TMEM (in a diagonal or ragged block, masked before they were stored back).  P of key chunk c goes to columns 64 + 16c, over the scores of chunks
+        // Two passes over the 128 scores: all four key chunks loaded for the max, chunks 2-3 kept,
+        // then P of chunks 2, 3 and of 0, 1 read again from TMEM (in a diagonal or ragged block,
+        // masked before they were stored back).  P of key chunk c goes to columns 64 + 16c, over the scores of chunks
         // 2-3, which are in registers by then; chunks 0-1 are never overwritten.
         const int k0 = j * C::BN;
         const bool edge = (p.causal && k0 + C::BN - 1 > qt) || k0 + C::BN > p.seq;  // diagonal or ragged
@@ -531,6 +531,8 @@ __global__ void __launch_bounds__(320, 1)
         uint32_t r0[32], r1[32], r2[32], r3[32];
         tmem_ld32_issue(tS, r0);
         tmem_ld32_issue(tS + 32, r1);
+        tmem_ld32_issue(tS + 64, r2);
+        tmem_ld32_issue(tS + 96, r3);
         tmem_wait_ld32(r0);
         tmem_wait_ld32(r1);
         if (edge) {  // masked scores of chunks 0-1 go back to TMEM, so their second read needs no mask
@@ -541,8 +543,6 @@ __global__ void __launch_bounds__(320, 1)
         }
         vmax(r0);
         vmax(r1);
-        tmem_ld32_issue(tS + 64, r2);
-        tmem_ld32_issue(tS + 96, r3);
         tmem_wait_ld32(r2);
         tmem_wait_ld32(r3);
         mask(r2, 2);
@@ -555,14 +555,23 @@ __global__ void __launch_bounds__(320, 1)
         const bool rescale = j > 0 && m_new > m_ref + 8.0f;
         const float m_use = (j == 0 || rescale) ? m_new : m_ref;
         const float mref = (m_use == -INFINITY) ? 0.f : m_use;  // fully masked row: P = 0
-        float l4[4] = {0.f, 0.f, 0.f, 0.f};
-        auto emit = [&](const uint32_t(&v)[32], int c) {  // exp2, row sum, bf16 pairs to P columns 64 + 16c
+        const uint64_t sl2p = f2_pack(sl2, sl2), nmp = f2_pack(-mref, -mref);
+        uint64_t lp[2] = {0ull, 0ull};  // packed partial row sums (0ull is +0.0f, +0.0f)
+        // exp2 (EMU of every 16 pairs on the FMA pipe, the rest on the special-function unit),
+        // row sum, bf16 pairs to P columns 64 + 16c
+        auto emit = [&](const uint32_t(&v)[32], int c) {
           uint32_t pk[16];
 #pragma unroll
           for (int w = 0; w < 16; ++w) {
-            const float p0 = ex2_fast(fmaf(__uint_as_float(v[2 * w]), sl2, -mref));
-            const float p1 = ex2_fast(fmaf(__uint_as_float(v[2 * w + 1]), sl2, -mref));
-            l4[w & 3] += p0 + p1;
+            float a0, a1, p0, p1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(v[2 * w]), __uint_as_float(v[2 * w + 1])), sl2p, nmp), a0, a1);
+            if (EMU > 0 && (w * EMU) % 16 < EMU) {
+              ex2_poly2(a0, a1, p0, p1);
+            } else {
+              p0 = ex2_fast(a0);
+              p1 = ex2_fast(a1);
+            }
+            lp[w & 1] = f2_add(lp[w & 1], f2_pack(p0, p1));
             pk[w] = pack2<T>(p0, p1);
           }
           tmem_st16_nowait(tS + 64 + c * 16, pk);
@@ -590,7 +599,10 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         tmem_wait_st();
-        l = fmaf(l, f, (l4[0] + l4[1]) + (l4[2] + l4[3]));
+        float l0, l1, l2, l3;
+        f2_unpack(lp[0], l0, l1);
+        f2_unpack(lp[1], l2, l3);
+        l = fmaf(l, f, (l0 + l1) + (l2 + l3));
         m_ref = m_use;
       }
       tc_fence_before();
@@ -637,6 +649,24 @@ static bool attn_two_tiles() {
   return v;
 }
 
+// TH_ATTN_EMU=4|8: that many of every 16 exponential pairs of the two-tile kernel on the FMA pipe
+static int attn_emu() {
+  static const int v = [] {
+    const char* e = getenv("TH_ATTN_EMU");
+    return e ? atoi(e) : 0;
+  }();
+  return v;
+}
+
+template <typename T, int D, int EMU>
+static int attention_tc2q_launch(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk,
+                                 const CUtensorMap& tv, const th_attention_args* a) {
+  if (int rc = smem_limit(attention_tc2q_kernel<T, D, EMU>, At2Cfg<D>::SMEM, "th_attention(tcgen05, 2 tiles)"))
+    return rc;
+  launch_pdl(attention_tc2q_kernel<T, D, EMU>, grid, dim3(320), At2Cfg<D>::SMEM, st, tq, tk, tv, *a);
+  return check_launch("th_attention(tcgen05, 2 tiles)");
+}
+
 // bf16/fp16, head_dim 64/128, 16-byte aligned rows; returns 1 (not taken) otherwise.
 template <typename T>
 static int attention_tc_try(const th_attention_args* a, cudaStream_t st, int* rc) {
@@ -654,14 +684,16 @@ static int attention_tc_try(const th_attention_args* a, cudaStream_t st, int* rc
   if (r) { *rc = r; return 0; }
   if (attn_two_tiles()) {
     const dim3 grid2((unsigned)((a->seq + 255) / 256), (unsigned)a->hq, (unsigned)a->batch);
+    const int emu = attn_emu();
     if (D == 128) {
-      if ((*rc = smem_limit(attention_tc2q_kernel<T, 128>, At2Cfg<128>::SMEM, "th_attention(tcgen05, 2 tiles)"))) return 0;
-      launch_pdl(attention_tc2q_kernel<T, 128>, grid2, dim3(320), At2Cfg<128>::SMEM, st, tq, tk, tv, *a);
+      if (emu == 4) *rc = attention_tc2q_launch<T, 128, 4>(grid2, st, tq, tk, tv, a);
+      else if (emu == 8) *rc = attention_tc2q_launch<T, 128, 8>(grid2, st, tq, tk, tv, a);
+      else *rc = attention_tc2q_launch<T, 128, 0>(grid2, st, tq, tk, tv, a);
     } else {
-      if ((*rc = smem_limit(attention_tc2q_kernel<T, 64>, At2Cfg<64>::SMEM, "th_attention(tcgen05, 2 tiles)"))) return 0;
-      launch_pdl(attention_tc2q_kernel<T, 64>, grid2, dim3(320), At2Cfg<64>::SMEM, st, tq, tk, tv, *a);
+      if (emu == 4) *rc = attention_tc2q_launch<T, 64, 4>(grid2, st, tq, tk, tv, a);
+      else if (emu == 8) *rc = attention_tc2q_launch<T, 64, 8>(grid2, st, tq, tk, tv, a);
+      else *rc = attention_tc2q_launch<T, 64, 0>(grid2, st, tq, tk, tv, a);
     }
-    *rc = check_launch("th_attention(tcgen05, 2 tiles)");
     return 0;
   }
   dim3 grid((unsigned)((a->seq + 127) / 128), (unsigned)a->hq, (unsigned)a->batch);
