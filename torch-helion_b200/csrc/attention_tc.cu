@@ -353,7 +353,7 @@ struct At2Cfg {
   static_assert(SMEM > 227 * 1024 / 2, "one CTA per SM");
 };
 
-template <typename T, int D, int EMU, bool RL>
+template <typename T, int D, int EMU>
 __global__ void __launch_bounds__(320, 1)
     attention_tc2q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, th_attention_args p) {
@@ -508,19 +508,20 @@ __global__ void __launch_bounds__(320, 1)
       ok = __all_sync(0xffffffffu, ok && mbar_wait(&s_full[t], j & 1, abort_flag));
       if (ok) {
         tc_fence_after();
-        // All four 32-column chunks of the row's scores are loaded for the row max.  With RL, chunks
-        // 2-3 stay in registers and chunks 0-1 are read again from TMEM for P (masked chunks of a
-        // diagonal or ragged block are stored back masked first), so at most 96 scores are live;
-        // without RL all 128 stay in registers.  P of key chunk c goes to columns 64 + 16c, over
-        // scores that are in registers by then; chunks 0-1 are never overwritten.
+        // Two passes over the 128 scores: all four key chunks loaded for the max, chunks 2-3 kept,
+        // then P of chunks 2, 3 and of 0, 1 read again from TMEM (in a diagonal or ragged block,
+        // masked before they were stored back).  P of key chunk c goes to columns 64 + 16c, over the scores of chunks
+        // 2-3, which are in registers by then; chunks 0-1 are never overwritten.
         const int k0 = j * C::BN;
         const bool edge = (p.causal && k0 + C::BN - 1 > qt) || k0 + C::BN > p.seq;  // diagonal or ragged
         // keys k0 + e with e >= nvalid are masked: past the sequence, or after this row when causal
         const int nvalid = min(p.seq, p.causal ? qi + 1 : p.seq) - k0;
         auto mask = [&](uint32_t(&v)[32], int c) {
+          if (edge) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c * 32 + e >= nvalid) v[e] = __float_as_uint(-INFINITY);
+            for (int e = 0; e < 32; ++e)
+              if (c * 32 + e >= nvalid) v[e] = __float_as_uint(-INFINITY);
+          }
         };
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         auto vmax = [&](const uint32_t(&v)[32]) {
@@ -534,22 +535,18 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld32_issue(tS + 96, r3);
         tmem_wait_ld32(r0);
         tmem_wait_ld32(r1);
-        if (edge) {
+        if (edge) {  // masked scores of chunks 0-1 go back to TMEM, so their second read needs no mask
           mask(r0, 0);
           mask(r1, 1);
-          if constexpr (RL) {  // chunks 0-1 are read again below: store them back masked
-            tmem_st32_nowait(tS, r0);
-            tmem_st32_nowait(tS + 32, r1);
-          }
+          tmem_st32_nowait(tS, r0);
+          tmem_st32_nowait(tS + 32, r1);
         }
         vmax(r0);
         vmax(r1);
         tmem_wait_ld32(r2);
         tmem_wait_ld32(r3);
-        if (edge) {
-          mask(r2, 2);
-          mask(r3, 3);
-        }
+        mask(r2, 2);
+        mask(r3, 3);
         vmax(r2);
         vmax(r3);
         const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;  // the scale is positive
@@ -579,22 +576,15 @@ __global__ void __launch_bounds__(320, 1)
           }
           tmem_st16_nowait(tS + 64 + c * 16, pk);
         };
-        if constexpr (RL) {
-          if (edge) tmem_wait_st();  // the masked chunks 0-1 are in TMEM before they are read again
-          emit(r2, 2);
-          tmem_ld32_issue(tS, r0);  // chunk 0 again, while chunk 3 becomes P
-          emit(r3, 3);
-          tmem_wait_ld32(r0);
-          tmem_ld32_issue(tS + 32, r1);
-          emit(r0, 0);
-          tmem_wait_ld32(r1);
-          emit(r1, 1);
-        } else {
-          emit(r2, 2);
-          emit(r3, 3);
-          emit(r0, 0);
-          emit(r1, 1);
-        }
+        if (edge) tmem_wait_st();  // the masked chunks 0-1 are in TMEM before they are read again
+        emit(r2, 2);
+        tmem_ld32_issue(tS, r0);  // chunk 0 again, while chunk 3 becomes P
+        emit(r3, 3);
+        tmem_wait_ld32(r0);
+        tmem_ld32_issue(tS + 32, r1);
+        emit(r0, 0);
+        tmem_wait_ld32(r1);
+        emit(r1, 1);
         // O_t is idle (see above) until this block's P is signalled: rescale it in place, after the
         // scores have left the registers
         const float f = rescale ? ex2_fast(m_ref - m_new) : 1.f;
@@ -659,18 +649,8 @@ static bool attn_two_tiles() {
   return v;
 }
 
-// TH_ATTN_RELOAD=0: the two-tile kernel keeps all 128 scores of a row in registers instead of reading
-// half of them again from TMEM
-static bool attn_reload() {
-  static const bool v = [] {
-    const char* e = getenv("TH_ATTN_RELOAD");
-    return !(e && e[0] == '0');
-  }();
-  return v;
-}
-
-// How many of every 16 exponential pairs of the two-tile kernel run on the FMA pipe: TH_ATTN_EMU=0|4,
-// default 4 (C3 attention, B8 S4096 causal: 1166 / 1141 us; 8 of 16 measured 1147 us)
+// How many of every 16 exponential pairs of the two-tile kernel run on the FMA pipe: TH_ATTN_EMU=0|4|8,
+// default 4 (C3 attention, B8 S4096 causal: 1166 / 1141 / 1147 us for 0 / 4 / 8)
 static int attn_emu() {
   static const int v = [] {
     const char* e = getenv("TH_ATTN_EMU");
@@ -679,12 +659,12 @@ static int attn_emu() {
   return v;
 }
 
-template <typename T, int D, int EMU, bool RL>
+template <typename T, int D, int EMU>
 static int attention_tc2q_launch(dim3 grid, cudaStream_t st, const CUtensorMap& tq, const CUtensorMap& tk,
                                  const CUtensorMap& tv, const th_attention_args* a) {
-  if (int rc = smem_limit(attention_tc2q_kernel<T, D, EMU, RL>, At2Cfg<D>::SMEM, "th_attention(tcgen05, 2 tiles)"))
+  if (int rc = smem_limit(attention_tc2q_kernel<T, D, EMU>, At2Cfg<D>::SMEM, "th_attention(tcgen05, 2 tiles)"))
     return rc;
-  launch_pdl(attention_tc2q_kernel<T, D, EMU, RL>, grid, dim3(320), At2Cfg<D>::SMEM, st, tq, tk, tv, *a);
+  launch_pdl(attention_tc2q_kernel<T, D, EMU>, grid, dim3(320), At2Cfg<D>::SMEM, st, tq, tk, tv, *a);
   return check_launch("th_attention(tcgen05, 2 tiles)");
 }
 
@@ -706,15 +686,14 @@ static int attention_tc_try(const th_attention_args* a, cudaStream_t st, int* rc
   if (attn_two_tiles()) {
     const dim3 grid2((unsigned)((a->seq + 255) / 256), (unsigned)a->hq, (unsigned)a->batch);
     const int emu = attn_emu();
-    const bool rl = attn_reload();
     if (D == 128) {
-      if (emu == 0) *rc = attention_tc2q_launch<T, 128, 0, true>(grid2, st, tq, tk, tv, a);
-      else if (!rl) *rc = attention_tc2q_launch<T, 128, 4, false>(grid2, st, tq, tk, tv, a);
-      else *rc = attention_tc2q_launch<T, 128, 4, true>(grid2, st, tq, tk, tv, a);
+      if (emu == 4) *rc = attention_tc2q_launch<T, 128, 4>(grid2, st, tq, tk, tv, a);
+      else if (emu == 8) *rc = attention_tc2q_launch<T, 128, 8>(grid2, st, tq, tk, tv, a);
+      else *rc = attention_tc2q_launch<T, 128, 0>(grid2, st, tq, tk, tv, a);
     } else {
-      if (emu == 0) *rc = attention_tc2q_launch<T, 64, 0, true>(grid2, st, tq, tk, tv, a);
-      else if (!rl) *rc = attention_tc2q_launch<T, 64, 4, false>(grid2, st, tq, tk, tv, a);
-      else *rc = attention_tc2q_launch<T, 64, 4, true>(grid2, st, tq, tk, tv, a);
+      if (emu == 4) *rc = attention_tc2q_launch<T, 64, 4>(grid2, st, tq, tk, tv, a);
+      else if (emu == 8) *rc = attention_tc2q_launch<T, 64, 8>(grid2, st, tq, tk, tv, a);
+      else *rc = attention_tc2q_launch<T, 64, 0>(grid2, st, tq, tk, tv, a);
     }
     return 0;
   }
