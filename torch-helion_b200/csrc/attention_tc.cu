@@ -318,6 +318,8 @@ __global__ void __launch_bounds__(320, 1)
 //   warp 0     TMA: both query tiles once, then K_i and V_i (K and V rings)
 //   warp 1     MMA, issued in the order
 //                S0(i) = Q0 K_i^T, O1 += P1(i-1) V(i-1), S1(i) = Q1 K_i^T, O0 += P0(i) V(i)
+//              (each product in two halves: keys 64-127 once the softmax has signalled
+//              that half of P, then keys 0-63)
 //              so that while softmax 0 works on S0(i) the tensor core runs tile 1's
 //              product and score block, and the other way round.  P_t(i) lives in
 //              the last 64 columns of its S_t buffer (bf16 pairs) and is read by
@@ -367,8 +369,9 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* v_full = k_empty + C::KS;    // [VS]
   uint64_t* v_empty = v_full + C::VS;    // [VS]
   uint64_t* s_full = v_empty + C::VS;    // [2] per tile
-  uint64_t* p_full = s_full + 2;         // [2] per tile (its 4 softmax warps arrive)
-  uint64_t* o_done = p_full + 2;         // [2] per tile: its last P.V product is complete
+  uint64_t* p_full = s_full + 2;         // [2] per tile (its 4 softmax warps arrive): all of P
+  uint64_t* p_half = p_full + 2;         // [2] per tile: P of keys 64-127 (and O_t rescaled)
+  uint64_t* o_done = p_half + 2;         // [2] per tile: its last P.V product is complete
   uint64_t* mma_done = o_done + 2;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
@@ -392,6 +395,7 @@ __global__ void __launch_bounds__(320, 1)
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 4);
+      mbar_init(&p_half[t], 4);
       mbar_init(&o_done[t], 1);
     }
     mbar_init(mma_done, 1);
@@ -449,12 +453,24 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc_commit(&s_full[t]);
       };
-      auto issue_pv = [&](int t, int i) {  // O_t += P_t V_i; keys 2c, 2c+1 of P_t in column 64 + c of S_t
+      // O_t += P_t V_i; keys 2c, 2c+1 of P_t in column 64 + c of S_t.  Keys 64-127 go first, as soon
+      // as the softmax has signalled that half, then keys 0-63 (the first product issued for a
+      // tile starts the accumulator)
+      auto issue_pv = [&](int t, int i) -> bool {
         const uint32_t va = smem_u32(sm + C::OFF_V + (i % C::VS) * C::KV_BYTES);
+        if (!mbar_wait(&p_half[t], i & 1, abort_flag)) return false;
+        tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < C::BN / 16; ++k)
+        for (int k = 4; k < 8; ++k)
           tc_mma_f16_ts(tO + (uint32_t)(t * D), tmem + (uint32_t)(t * 128 + 64 + k * 8),
-                        make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o, (i | k) ? 1u : 0u);
+                        make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o, (i > 0 || k > 4) ? 1u : 0u);
+        if (!mbar_wait(&p_full[t], i & 1, abort_flag)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma_f16_ts(tO + (uint32_t)(t * D), tmem + (uint32_t)(t * 128 + 64 + k * 8),
+                        make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o, 1u);
+        return true;
       };
       bool ok = mbar_wait(q_full, 0, abort_flag);
       for (int i = 0; ok && i < nkv1; ++i) {
@@ -462,29 +478,20 @@ __global__ void __launch_bounds__(320, 1)
         tc_fence_after();
         if (i < nkv0) issue_s(0, i);
         if (i > 0) {  // tile 1's product of the previous block, then its scores of this one
-          if (!(ok = mbar_wait(&p_full[1], (i - 1) & 1, abort_flag))) break;
-          tc_fence_after();
-          issue_pv(1, i - 1);
+          if (!(ok = issue_pv(1, i - 1))) break;
           tc_commit(&v_empty[(i - 1) % C::VS]);  // tile 1 is the last reader of V_{i-1}
         }
         issue_s(1, i);
         tc_commit(&k_empty[i % C::KS]);  // ... and of K_i
         if (i < nkv0) {
-          if (!(ok = mbar_wait(&v_full[i % C::VS], (i / C::VS) & 1, abort_flag) &&
-                     mbar_wait(&p_full[0], i & 1, abort_flag)))
-            break;
-          tc_fence_after();
-          issue_pv(0, i);
+          if (!(ok = mbar_wait(&v_full[i % C::VS], (i / C::VS) & 1, abort_flag) && issue_pv(0, i))) break;
           if (i == nkv0 - 1) tc_commit(&o_done[0]);
         }
       }
       if (ok) {  // tile 1's last product (its V was not waited for when tile 0 stopped a block early)
         const int i = nkv1 - 1;
-        ok = (i < nkv0 || mbar_wait(&v_full[i % C::VS], (i / C::VS) & 1, abort_flag)) &&
-             mbar_wait(&p_full[1], i & 1, abort_flag);
+        ok = (i < nkv0 || mbar_wait(&v_full[i % C::VS], (i / C::VS) & 1, abort_flag)) && issue_pv(1, i);
         if (ok) {
-          tc_fence_after();
-          issue_pv(1, i);
           tc_commit(&v_empty[i % C::VS]);
           tc_commit(&o_done[1]);
         }
@@ -580,13 +587,7 @@ __global__ void __launch_bounds__(320, 1)
         emit(r2, 2);
         tmem_ld32_issue(tS, r0);  // chunk 0 again, while chunk 3 becomes P
         emit(r3, 3);
-        tmem_wait_ld32(r0);
-        tmem_ld32_issue(tS + 32, r1);
-        emit(r0, 0);
-        tmem_wait_ld32(r1);
-        emit(r1, 1);
-        // O_t is idle (see above) until this block's P is signalled: rescale it in place, after the
-        // scores have left the registers
+        // O_t is idle (see above) until this block's first half of P is signalled: rescale it in place
         const float f = rescale ? ex2_fast(m_ref - m_new) : 1.f;
         if (__any_sync(0xffffffffu, rescale)) {
           for (int c = 0; c < D; c += 16) {
@@ -598,6 +599,15 @@ __global__ void __launch_bounds__(320, 1)
             tmem_st16_nowait(tOr + c, o);
           }
         }
+        tmem_wait_st();  // P of keys 64-127 (and O_t) in TMEM: the product may start on that half
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_half[t]);
+        tmem_wait_ld32(r0);
+        tmem_ld32_issue(tS + 32, r1);
+        emit(r0, 0);
+        tmem_wait_ld32(r1);
+        emit(r1, 1);
         tmem_wait_st();
         float l0, l1, l2, l3;
         f2_unpack(lp[0], l0, l1);
@@ -607,7 +617,10 @@ __global__ void __launch_bounds__(320, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
+      if (lane == 0) {
+        if (!ok) mbar_arrive(&p_half[t]);  // (sent mid-block when the block ran)
+        mbar_arrive(&p_full[t]);
+      }
     }
     // epilogue: O_t / l once the tile's last product is complete
     if (ok) {
