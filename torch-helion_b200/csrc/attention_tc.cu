@@ -318,8 +318,8 @@ __global__ void __launch_bounds__(320, 1)
 //   warp 0     TMA: both query tiles once, then K_i and V_i (K and V rings)
 //   warp 1     MMA, issued in the order
 //                S0(i) = Q0 K_i^T, O1 += P1(i-1) V(i-1), S1(i) = Q1 K_i^T, O0 += P0(i) V(i)
-//              (each product in parts: keys 64-127 once the softmax has signalled that
-//              half of P, then keys 0-63; TH_ATTN_PV=4 issues it per quarter)
+//              (each product in two halves: keys 64-127 once the softmax has signalled
+//              that half of P, then keys 0-63)
 //              so that while softmax 0 works on S0(i) the tensor core runs tile 1's
 //              product and score block, and the other way round.  P_t(i) lives in
 //              the last 64 columns of its S_t buffer (bf16 pairs) and is read by
@@ -358,7 +358,7 @@ struct At2Cfg {
 template <typename T, int D, int EMU>
 __global__ void __launch_bounds__(320, 1)
     attention_tc2q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                          const __grid_constant__ CUtensorMap tmV, th_attention_args p, int pv_parts) {
+                          const __grid_constant__ CUtensorMap tmV, th_attention_args p) {
   using C = At2Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_align<1024>(smem_raw);
@@ -369,10 +369,9 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* v_full = k_empty + C::KS;    // [VS]
   uint64_t* v_empty = v_full + C::VS;    // [VS]
   uint64_t* s_full = v_empty + C::VS;    // [2] per tile
-  // [2][4] per tile (its 4 softmax warps arrive): quarter q of P stored (keys 64-95, 96-127, 0-31,
-  // 32-63 in that order; O_t rescaled before the first)
-  uint64_t* p_q = s_full + 2;
-  uint64_t* o_done = p_q + 8;            // [2] per tile: its last P.V product is complete
+  uint64_t* p_full = s_full + 2;         // [2] per tile (its 4 softmax warps arrive): all of P
+  uint64_t* p_half = p_full + 2;         // [2] per tile: P of keys 64-127 (and O_t rescaled)
+  uint64_t* o_done = p_half + 2;         // [2] per tile: its last P.V product is complete
   uint64_t* mma_done = o_done + 2;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
@@ -395,7 +394,8 @@ __global__ void __launch_bounds__(320, 1)
     for (int s = 0; s < C::VS; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      for (int q = 0; q < 4; ++q) mbar_init(&p_q[t * 4 + q], 4);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&p_half[t], 4);
       mbar_init(&o_done[t], 1);
     }
     mbar_init(mma_done, 1);
@@ -453,27 +453,23 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc_commit(&s_full[t]);
       };
-      // O_t += P_t V_i; keys 2c, 2c+1 of P_t in column 64 + c of S_t, in the order the softmax stores
-      // them (keys 64-95, 96-127, 0-31, 32-63: k-steps 4-5, 6-7, 0-1, 2-3), each part as soon as it
-      // is signalled: pv_parts 2 waits for quarters 1 and 3, 4 for every quarter.  The first product
-      // issued for a tile starts the accumulator.
+      // O_t += P_t V_i; keys 2c, 2c+1 of P_t in column 64 + c of S_t.  Keys 64-127 go first, as soon
+      // as the softmax has signalled that half, then keys 0-63 (the first product issued for a
+      // tile starts the accumulator)
       auto issue_pv = [&](int t, int i) -> bool {
         const uint32_t va = smem_u32(sm + C::OFF_V + (i % C::VS) * C::KV_BYTES);
+        if (!mbar_wait(&p_half[t], i & 1, abort_flag)) return false;
+        tc_fence_after();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          if (pv_parts != 4 && !(q & 1)) continue;
-          if (!mbar_wait(&p_q[t * 4 + q], i & 1, abort_flag)) return false;
-          tc_fence_after();
-          const int q0 = pv_parts == 4 ? q : q - 1;  // first quarter this wait covers
-          for (int qx = q0; qx <= q; ++qx)
+        for (int k = 4; k < 8; ++k)
+          tc_mma_f16_ts(tO + (uint32_t)(t * D), tmem + (uint32_t)(t * 128 + 64 + k * 8),
+                        make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o, (i > 0 || k > 4) ? 1u : 0u);
+        if (!mbar_wait(&p_full[t], i & 1, abort_flag)) return false;
+        tc_fence_after();
 #pragma unroll
-            for (int kk = 0; kk < 2; ++kk) {
-              const int k = (qx * 2 + 4 + kk) & 7;
-              tc_mma_f16_ts(tO + (uint32_t)(t * D), tmem + (uint32_t)(t * 128 + 64 + k * 8),
-                            make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o,
-                            (i > 0 || qx > 0 || kk > 0) ? 1u : 0u);
-            }
-        }
+        for (int k = 0; k < 4; ++k)
+          tc_mma_f16_ts(tO + (uint32_t)(t * D), tmem + (uint32_t)(t * 128 + 64 + k * 8),
+                        make_desc_sw128(va + k * 16 * 128, C::BN * 128, 1024), id_o, 1u);
         return true;
       };
       bool ok = mbar_wait(q_full, 0, abort_flag);
@@ -587,8 +583,11 @@ __global__ void __launch_bounds__(320, 1)
           }
           tmem_st16_nowait(tS + 64 + c * 16, pk);
         };
-        // O_t is idle (see above) until the first quarter of this block's P is signalled: rescale it
-        // in place first
+        if (edge) tmem_wait_st();  // the masked chunks 0-1 are in TMEM before they are read again
+        emit(r2, 2);
+        tmem_ld32_issue(tS, r0);  // chunk 0 again, while chunk 3 becomes P
+        emit(r3, 3);
+        // O_t is idle (see above) until this block's first half of P is signalled: rescale it in place
         const float f = rescale ? ex2_fast(m_ref - m_new) : 1.f;
         if (__any_sync(0xffffffffu, rescale)) {
           for (int c = 0; c < D; c += 16) {
@@ -600,36 +599,27 @@ __global__ void __launch_bounds__(320, 1)
             tmem_st16_nowait(tOr + c, o);
           }
         }
-        auto signal = [&](int q) {  // quarter q of P (and everything stored before it) is in TMEM
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&p_q[t * 4 + q]);
-        };
-        if (edge) tmem_wait_st();  // the masked chunks 0-1 are in TMEM before they are read again
-        emit(r2, 2);
-        signal(0);
-        tmem_ld32_issue(tS, r0);  // chunks 0-1 again, while chunk 3 becomes P
-        tmem_ld32_issue(tS + 32, r1);
-        emit(r3, 3);
-        signal(1);
+        tmem_wait_st();  // P of keys 64-127 (and O_t) in TMEM: the product may start on that half
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_half[t]);
         tmem_wait_ld32(r0);
-        tmem_wait_ld32(r1);
+        tmem_ld32_issue(tS + 32, r1);
         emit(r0, 0);
-        signal(2);
+        tmem_wait_ld32(r1);
         emit(r1, 1);
-        signal(3);
+        tmem_wait_st();
         float l0, l1, l2, l3;
         f2_unpack(lp[0], l0, l1);
         f2_unpack(lp[1], l2, l3);
         l = fmaf(l, f, (l0 + l1) + (l2 + l3));
         m_ref = m_use;
       }
-      if (!ok) {  // (sent during the block when it ran)
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0)
-          for (int q = 0; q < 4; ++q) mbar_arrive(&p_q[t * 4 + q]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (!ok) mbar_arrive(&p_half[t]);  // (sent mid-block when the block ran)
+        mbar_arrive(&p_full[t]);
       }
     }
     // epilogue: O_t / l once the tile's last product is complete
@@ -663,15 +653,6 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-// P.V products of the two-tile kernel issued in TH_ATTN_PV=2 halves (default) or 4 quarters
-static int attn_pv_parts() {
-  static const int v = [] {
-    const char* e = getenv("TH_ATTN_PV");
-    return e && e[0] == '4' ? 4 : 2;
-  }();
-  return v;
-}
-
 // TH_ATTN_TILES=1 selects the one-tile kernel (default: two tiles per CTA)
 static bool attn_two_tiles() {
   static const bool v = [] {
@@ -681,8 +662,8 @@ static bool attn_two_tiles() {
   return v;
 }
 
-// How many of every 16 exponential pairs of the two-tile kernel run on the FMA pipe: TH_ATTN_EMU=0|4,
-// default 4 (C3 attention, B8 S4096 causal: 1166 / 1141 us; 8 of 16 measured 1147 us)
+// How many of every 16 exponential pairs of the two-tile kernel run on the FMA pipe: TH_ATTN_EMU=0|4|8,
+// default 4 (C3 attention, B8 S4096 causal: 1166 / 1141 / 1147 us for 0 / 4 / 8)
 static int attn_emu() {
   static const int v = [] {
     const char* e = getenv("TH_ATTN_EMU");
@@ -696,7 +677,7 @@ static int attention_tc2q_launch(dim3 grid, cudaStream_t st, const CUtensorMap& 
                                  const CUtensorMap& tv, const th_attention_args* a) {
   if (int rc = smem_limit(attention_tc2q_kernel<T, D, EMU>, At2Cfg<D>::SMEM, "th_attention(tcgen05, 2 tiles)"))
     return rc;
-  launch_pdl(attention_tc2q_kernel<T, D, EMU>, grid, dim3(320), At2Cfg<D>::SMEM, st, tq, tk, tv, *a, attn_pv_parts());
+  launch_pdl(attention_tc2q_kernel<T, D, EMU>, grid, dim3(320), At2Cfg<D>::SMEM, st, tq, tk, tv, *a);
   return check_launch("th_attention(tcgen05, 2 tiles)");
 }
 
@@ -719,11 +700,13 @@ static int attention_tc_try(const th_attention_args* a, cudaStream_t st, int* rc
     const dim3 grid2((unsigned)((a->seq + 255) / 256), (unsigned)a->hq, (unsigned)a->batch);
     const int emu = attn_emu();
     if (D == 128) {
-      if (emu == 0) *rc = attention_tc2q_launch<T, 128, 0>(grid2, st, tq, tk, tv, a);
-      else *rc = attention_tc2q_launch<T, 128, 4>(grid2, st, tq, tk, tv, a);
+      if (emu == 4) *rc = attention_tc2q_launch<T, 128, 4>(grid2, st, tq, tk, tv, a);
+      else if (emu == 8) *rc = attention_tc2q_launch<T, 128, 8>(grid2, st, tq, tk, tv, a);
+      else *rc = attention_tc2q_launch<T, 128, 0>(grid2, st, tq, tk, tv, a);
     } else {
-      if (emu == 0) *rc = attention_tc2q_launch<T, 64, 0>(grid2, st, tq, tk, tv, a);
-      else *rc = attention_tc2q_launch<T, 64, 4>(grid2, st, tq, tk, tv, a);
+      if (emu == 4) *rc = attention_tc2q_launch<T, 64, 4>(grid2, st, tq, tk, tv, a);
+      else if (emu == 8) *rc = attention_tc2q_launch<T, 64, 8>(grid2, st, tq, tk, tv, a);
+      else *rc = attention_tc2q_launch<T, 64, 0>(grid2, st, tq, tk, tv, a);
     }
     return 0;
   }
