@@ -1,6 +1,9 @@
-// tcgen05 flash attention (forward) for bf16/fp16, head_dim 64 or 128.
+// tcgen05 flash attention (forward) for bf16/fp16, head_dim 64 or 128, in two
+// kernels: attention_tc2q_kernel (two 128-row query tiles per CTA, ping-pong on
+// the tensor core; the default, described above its definition) and
+// attention_tc_kernel below (one tile per CTA; TH_ATTN_TILES=1).
 //
-// One CTA = 128 query rows of one (batch, query head); KV blocks of 128 rows.
+// attention_tc_kernel: one CTA = 128 query rows of one (batch, query head); KV blocks of 128 rows.
 // 320 threads, warp-specialised:
 //   warp 0    TMA: the Q tile once, then K and V tiles into separate 3-stage rings, in
 //             the order the MMA warp consumes them (K_0, K_1, V_0, K_2, V_1, ...), so
