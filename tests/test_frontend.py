@@ -159,6 +159,71 @@ def test_legality_rejects_unbuilt_head_dim(tmp_path):
     assert not rep.ok and "head_dim" in str(rep)
 
 
+def _mutate(prog, kind, rule):
+    """One structural fault of the named rule planted in a copy of a legal program."""
+    import copy
+
+    from torch_helion.capture.opgraph import TensorType
+
+    prog = copy.deepcopy(prog)
+    spec = next(k for k in prog.kernels if k.kind == kind)
+    T = prog.tensors
+    if rule == "operands":
+        spec.args[0].tensor = "no_such_tensor"
+    elif rule == "gemm-shape":
+        spec.k_extent += 8
+    elif rule == "dtype":
+        rhs = next(a for a in spec.args if a.role == "rhs")
+        t = T[rhs.tensor]
+        T[rhs.tensor] = TensorType(t.shape, "float16" if t.dtype != "float16" else "bfloat16")
+    elif rule == "attention":
+        spec.attrs["kv_heads"] = 3
+    elif rule == "ssd":
+        spec.attrs["ngroups"] = 3
+    elif rule == "conv":
+        w = next(a for a in spec.args if a.role == "w")
+        t = T[w.tensor]
+        T[w.tensor] = TensorType((t.shape[0] + 8, t.shape[1]), t.dtype)
+    elif rule == "lowering":
+        spec.attrs["width"] = 7
+    return prog
+
+
+@pytest.mark.parametrize("model,kind,rule", [("llama", "gemm", "operands"), ("llama", "gemm", "gemm-shape"),
+                                             ("llama", "gemm", "dtype"), ("llama", "attention", "attention"),
+                                             ("mamba", "ssd", "ssd"), ("mamba", "causal_conv1d", "conv"),
+                                             ("mamba", "causal_conv1d", "lowering")])
+def test_legality_rules_name_the_broken_rule(tmp_path, model, kind, rule):
+    """Every structural rule of the B200 legality check fires on a planted
+    fault and names itself; the unmodified program is legal."""
+    from torch_helion.optimizer.legality import check_program
+
+    _, m, args = (_llama if model == "llama" else _mamba)(dtype=torch.bfloat16)
+    prog = _compile(m, args, tmp_path).program
+    assert check_program(prog).ok
+    rep = check_program(_mutate(prog, kind, rule))
+    assert not rep.ok
+    assert rule in {v.rule for v in rep.violations}, str(rep)
+
+
+def test_legality_notes_name_the_device_path(tmp_path):
+    """Legal kernels on slower device paths are listed as notes (fp32 GEMMs
+    on the SIMT kernel, head_dim 32 attention on the SIMT flash kernel, a
+    chunk-64 scan on the three-pass path) and in the plan report."""
+    from torch_helion.optimizer.legality import check_program
+
+    _, m, args = _llama()
+    res = _compile(m, args, tmp_path)
+    notes = check_program(res.program).notes
+    assert any("fp32 GEMM" in n for n in notes) and any("SIMT flash" in n for n in notes)
+    plan_md = next(res.run_dir.rglob("plan.md")).read_text()
+    assert "## Device paths" in plan_md and "SIMT flash" in plan_md
+    _, m, args = _mamba(dtype=torch.bfloat16)
+    notes = check_program(_compile(m, args, tmp_path / "m").program).notes
+    assert any("three-pass scan" in n for n in notes)
+    assert not any("GEMM" in n for n in notes)  # bf16 GEMMs of 256 rows take the CTA-pair kernel
+
+
 def test_unknown_backend_raises():
     from torch_helion import CompileConfig, compile_model
 

@@ -32,6 +32,7 @@ from .codegen.emit import emit_program
 from .config import CompileConfig
 from .cost_models.b200 import B200Spec
 from .optimizer.evaluate import max_rel_err, rel_l2
+from .optimizer.legality import check_program
 from .optimizer.opir import Program
 from .optimizer.passes import canonicalize
 from .optimizer.planner import PlanResult, plan
@@ -265,6 +266,9 @@ def plan_report(result: PlanResult, hw: B200Spec, config: CompileConfig) -> str:
         est = f"{c.total_us:,.1f}" if c.legal else "-"
         lines.append(f"| {c.index} | {len(c.program.kernels) if c.program else '-'} | {est} | {'yes' if c.legal else 'no'} | {note} |")
     lines += ["", "## Chosen program", "", "```", result.program.summary(), "```"]
+    notes = check_program(result.program).notes
+    if notes:  # legal kernels that run on a slower device path
+        lines += ["", "## Device paths", ""] + [f"- {n}" for n in notes]
     return "\n".join(lines)
 
 
