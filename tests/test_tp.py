@@ -59,6 +59,23 @@ def _lockstep(shards, x):
     return envs[0][prog.outputs[0]].reshape(x.shape)
 
 
+@pytest.mark.parametrize("rows,n", [(32768, 4), (32768, 8), (8192, 3), (1000, 4), (256, 2), (384, 3)])
+def test_chunk_bounds_cover_rows_in_whole_tiles(rows, n):
+    """The tensor-parallel tail's row chunks: contiguous, covering every row
+    once, every boundary on a 128-row GEMM tile, no empty chunk, and with
+    three or more chunks the first and last about half as tall as the rest."""
+    from torch_helion.b200.runtime import _chunk_bounds
+
+    b = _chunk_bounds(rows, n)
+    assert len(b) == n and b[0][0] == 0 and b[-1][1] == rows
+    assert all(r1 == s0 for (_, r1), (s0, _) in zip(b, b[1:]))
+    assert all(r0 < r1 and r0 % 128 == 0 for r0, r1 in b)
+    if n >= 3 and rows >= 128 * 4 * n:
+        mid = [r1 - r0 for r0, r1 in b[1:-1]]
+        for r0, r1 in (b[0], b[-1]):
+            assert abs((r1 - r0) - min(mid) / 2) <= 128
+
+
 def test_shard_structure(tmp_path):
     from torch_helion.b200.tp import shard_program
 
